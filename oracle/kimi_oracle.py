@@ -1,0 +1,555 @@
+"""TEST INFRASTRUCTURE ONLY: a restatement of the reference's Kimi K3 decode-step oracle.
+
+The reference (garv901/kimi-k3-goalbox) specifies one decode step per tensor-parallel rank as a
+PyTorch program in `megabench/tasks/kimi.py`, with helpers in `megabench/tasks/common.py`,
+`megabench/tasks/quantization.py` and `megabench/tasks/distributed.py`. This module restates that
+program with the same arithmetic (same dtypes, same rounding points, same torch reductions) so that,
+on CPU, it reproduces the reference's outputs bit for bit (pinned by `tests/golden`). It is the
+checker for the CUDA path and the timed CPU baseline; the product never calls it.
+
+A `case` here is the dict the reference's `Case.to_dict()` produces (keys `id`, `gpus`, `tp`, `ep`,
+`params`, ...).
+"""
+
+from __future__ import annotations
+
+import hashlib
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+# kimi.py:38-40 -- the oracle band constants
+BAND = 2.0
+FLOOR = 2e-3
+ROUTE_FLOOR = 1e-3
+
+# quantization.py:8-9 -- E2M1 code -> value (bit 3 is the sign)
+E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0,
+               -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0)
+
+
+def stream_seed(seed: int, name: str) -> int:
+    """Per-tensor generator seed: blake2b-64 of "seed:name", little endian (tasks/distributed.py:25-26)."""
+    digest = hashlib.blake2b(f"{seed}:{name}".encode(), digest_size=8).digest()
+    return int.from_bytes(digest, "little")
+
+
+def _params(case) -> dict:
+    return case["params"]
+
+
+def is_mla(case, layer: int) -> bool:
+    """Gated-MLA layers are 3, 7, 11, ... and the last layer (kimi.py:44-45)."""
+    return (layer + 1) % 4 == 0 or layer == _params(case)["layers"] - 1
+
+
+def mla_layer_ids(case) -> list[int]:
+    return [l for l in range(_params(case)["layers"]) if is_mla(case, l)]
+
+
+def kda_layer_ids(case) -> list[int]:
+    return [l for l in range(_params(case)["layers"]) if not is_mla(case, l)]
+
+
+def tensor_specs(case) -> dict:
+    """Per-rank weight tensors: name -> (shape, dtype, fan_in, split over TP) (kimi.py:72-122)."""
+    p, tp = _params(case), case["tp"]
+    h, lh, d, H = p["hidden"], p["latent_hidden"], p["head_dim"], p["q_heads"]
+    L, V = p["layers"], p["vocab"]
+    qdim = H * d
+    for n in (H, V, p["intermediate"], p["dense_intermediate"]):
+        if n % tp:
+            raise ValueError("Kimi attention heads, vocabulary and FFN intermediate must divide TP")
+    if (p["intermediate"] // tp) % 32:
+        raise ValueError("MXFP4 down-projection shards must align to groups of 32")
+    bf, f32, u8 = torch.bfloat16, torch.float32, torch.uint8
+    specs = {
+        "embed": ((V // tp, h), bf, h, True),
+        "lm_head": ((V // tp, h), bf, h, True),
+        "fnorm": ((h,), bf, 0, False),
+        "output_res_norm": ((h,), bf, 0, False),
+        "output_res_proj": ((h,), bf, h, False),
+    }
+    for name in ("ln1", "ln2", "attention_res_norm", "mlp_res_norm"):
+        specs[name] = ((L, h), bf, 0, False)
+    for name in ("attention_res_proj", "mlp_res_proj"):
+        specs[name] = ((L, h), bf, h, False)
+    hr = H // tp
+    for layer in range(L):
+        pre = f"l{layer}_"
+        if is_mla(case, layer):
+            qr, kr = p["q_lora_rank"], p["kv_lora_rank"]
+            nr, rd, vd = p["qk_nope_dim"], p["qk_rope_dim"], p["v_head_dim"]
+            specs.update({
+                pre + "qa": ((qr, h), bf, h, False),
+                pre + "qb": ((hr * (nr + rd), qr), bf, qr, True),
+                pre + "ka": ((kr + rd, h), bf, h, False),
+                pre + "kb": ((hr * (nr + vd), kr), bf, kr, True),
+                pre + "o": ((h, hr * vd), bf, H * vd, True),
+                pre + "output_gate": ((hr * vd, h), bf, h, True),
+                pre + "qn": ((qr,), bf, 0, False),
+                pre + "kn": ((kr,), bf, 0, False),
+            })
+        else:
+            for name in ("q", "k", "v", "output_gate"):
+                specs[pre + name] = ((qdim // tp, h), bf, h, True)
+            specs.update({
+                pre + "o": ((h, qdim // tp), bf, qdim, True),
+                pre + "fa": ((d, h), bf, h, False),
+                pre + "fb": ((qdim // tp, d), bf, d, True),
+                pre + "beta": ((hr, h), bf, h, True),
+                pre + "onorm": ((d,), f32, 0, False),
+                pre + "A_log": ((hr,), f32, 0, True),
+                pre + "dt_bias": ((qdim // tp,), f32, 0, True),
+                pre + "conv_weight": ((3, qdim // tp, p["conv_kernel"]), f32, p["conv_kernel"], True),
+            })
+        if layer < p["first_dense"]:
+            inter = p["dense_intermediate"] // tp
+            specs.update({
+                pre + "gate": ((inter, h), bf, h, True),
+                pre + "up": ((inter, h), bf, h, True),
+                pre + "down": ((h, inter), bf, p["dense_intermediate"], True),
+            })
+        else:
+            E, inter = p["experts"], p["intermediate"] // tp
+            shared = p["intermediate"] * p["shared_experts"] // tp
+            specs.update({
+                pre + "latent_down": ((lh, h), bf, h, False),
+                pre + "latent_up": ((h, lh), bf, lh, False),
+                pre + "latent_norm": ((lh,), bf, 0, False),
+                pre + "router": ((E, h), bf, h, False),
+                pre + "router_bias": ((E,), f32, 0, False),
+                pre + "gate_blocks": ((E, inter, lh // 32, 16), u8, lh, True),
+                pre + "gate_scales": ((E, inter, lh // 32), u8, 0, True),
+                pre + "up_blocks": ((E, inter, lh // 32, 16), u8, lh, True),
+                pre + "up_scales": ((E, inter, lh // 32), u8, 0, True),
+                pre + "down_blocks": ((E, lh, inter // 32, 16), u8, p["intermediate"], True),
+                pre + "down_scales": ((E, lh, inter // 32), u8, 0, True),
+                pre + "shared_gate": ((shared, h), bf, h, True),
+                pre + "shared_up": ((shared, h), bf, h, True),
+                pre + "shared_down": ((h, shared), bf, p["intermediate"] * p["shared_experts"], True),
+            })
+    return specs
+
+
+def _gaussian(seed, stream, shape, std, device, dtype=torch.bfloat16, mean=0.0):
+    """kimi.py:56-58: FP32 normal draws from a per-stream generator, scaled, shifted, then cast."""
+    gen = torch.Generator(device=device).manual_seed(stream_seed(seed, stream))
+    return (torch.randn(shape, generator=gen, device=device) * std + mean).to(dtype)
+
+
+def _mxfp4_random(seed, stream, shape, fan_in, device):
+    """kimi.py:61-69: uniform E2M1 bytes and E8M0 exponents near 1/(2.93*sqrt(fan_in))."""
+    gen = torch.Generator(device=device).manual_seed(stream_seed(seed, stream))
+    *lead, cols = shape
+    codes = torch.randint(0, 256, (*lead, cols // 32, 16), generator=gen, device=device, dtype=torch.uint8)
+    centre = round(-torch.log2(torch.tensor(2.93 * fan_in ** 0.5)).item())
+    jitter = torch.randint(0, 3, (*lead, cols // 32), generator=gen, device=device)
+    return codes, (127 + centre - 1 + jitter).to(torch.uint8)
+
+
+def synthetic_weights(case, seed: int, device, rank: int) -> dict:
+    """kimi.py:125-144: fresh seeded weights; split tensors use the stream `name@rank`."""
+    out = {}
+    for name, (shape, dtype, fan_in, split) in tensor_specs(case).items():
+        stream = f"{name}@{rank}" if split else name
+        if name.endswith("_scales"):
+            continue
+        if name.endswith("_blocks"):
+            base = name[: -len("_blocks")]
+            out[name], out[base + "_scales"] = _mxfp4_random(
+                seed, stream, shape[:-2] + (shape[-2] * 32,), fan_in, device)
+        elif name.endswith("A_log"):
+            out[name] = _gaussian(seed, stream, shape, 0.5, device, dtype)
+        elif name.endswith("dt_bias"):
+            out[name] = _gaussian(seed, stream, shape, 1.0, device, dtype, mean=-4.0)
+        elif name.endswith("router_bias"):
+            out[name] = _gaussian(seed, stream, shape, 0.01, device, dtype)
+        elif fan_in == 0:
+            out[name] = _gaussian(seed, stream, shape, 0.1, device, dtype, mean=1.0)
+        else:
+            out[name] = _gaussian(seed, stream, shape, fan_in ** -0.5, device, dtype)
+    return out
+
+
+def make_state(case, seed: int, device, rank: int) -> dict:
+    """kimi.py:164-182: tokens, reset flags, MLA latent/rope caches, KDA conv and recurrent states."""
+    p, tp, B = _params(case), case["tp"], _params(case)["batch"]
+    gen = torch.Generator(device=device).manual_seed(stream_seed(seed, "token"))
+    state = {"token": torch.randint(0, p["vocab"], (B,), generator=gen, device=device),
+             "reset": torch.rand((B,), generator=gen, device=device) < 0.25}
+    state["reset"][0] = False
+    if B == 1:
+        state["reset"][0] = seed % 3 == 0
+    hr, d = p["q_heads"] // tp, p["head_dim"]
+    qdim = p["q_heads"] * d // tp
+    for layer in range(p["layers"]):
+        pre = f"l{layer}_"
+        if is_mla(case, layer):
+            state[pre + "kv_cache"] = _gaussian(seed, pre + "kv_cache", (B, p["context"], p["kv_lora_rank"]), 1.0, device)
+            state[pre + "pe_cache"] = _gaussian(seed, pre + "pe_cache", (B, p["context"], p["qk_rope_dim"]), 1.0, device)
+        else:
+            state[pre + "conv_state"] = _gaussian(seed, f"{pre}conv_state@{rank}", (B, 3, qdim, p["conv_kernel"]), 1.0, device)
+            state[pre + "recurrent_state"] = _gaussian(seed, f"{pre}recurrent@{rank}", (B, hr, d, d), 0.05, device, torch.float32)
+    return state
+
+
+def make_inputs(case, seed: int, device, rank: int = 0) -> dict:
+    """kimi.py:185-191 (synthetic source only): weights | state for one rank."""
+    if case["ep"] != 1 or case["gpus"] != case["tp"] or not 0 <= rank < case["gpus"]:
+        raise ValueError("Kimi requires one TP group spanning all ranks")
+    if _params(case).get("checkpoint"):
+        raise ValueError("real-checkpoint cases are not generated by the oracle restatement")
+    return synthetic_weights(case, seed, device, rank) | make_state(case, seed, device, rank)
+
+
+def decode_mxfp4(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """quantization.py:40-51: E2M1 nibbles (low nibble first) times 2**(scale-127); scale 255 is NaN."""
+    if codes.dtype != torch.uint8 or scales.dtype != torch.uint8:
+        raise ValueError("MXFP4 blocks and E8M0 scales must be uint8")
+    if codes.shape[:-1] != scales.shape or codes.shape[-1] != 16:
+        raise ValueError("invalid MXFP4 block/scale geometry")
+    table = torch.tensor(E2M1_VALUES, device=codes.device, dtype=torch.float32)
+    nibbles = torch.stack((codes & 15, codes >> 4), dim=-1).flatten(-2)
+    values = torch.ldexp(table[nibbles.long()], scales.int()[..., None] - 127)
+    values = values.masked_fill(scales[..., None] == 255, torch.nan)
+    return values.flatten(-2)
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """common.py:13-21 (plain form): FP32 normalise, cast to x's dtype, multiply by the weight in that dtype."""
+    xf = x.float()
+    scaled = xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps)
+    return scaled.to(x.dtype) * weight.to(x.dtype)
+
+
+def situ(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """kimi.py:194-196: 4*tanh(g/4)*sigmoid(g) * 25*tanh(u/25), in FP32."""
+    g, u = gate.float(), up.float()
+    return 4 * torch.tanh(g / 4) * g.sigmoid() * (25 * torch.tanh(u / 25))
+
+
+def block_mix(prefix, blocks, norm, proj, cast):
+    """kimi.py:199-204: softmax over [blocks..., prefix] of rms(v).(norm*proj), mixing in FP32."""
+    stacked = torch.stack([*blocks, prefix]).float()
+    keys = stacked * torch.rsqrt(stacked.square().mean(-1, keepdim=True) + 1e-5)
+    logits = (keys * (norm.float() * proj.float())).sum(-1)
+    weights = logits.softmax(0)
+    return cast((weights[..., None] * stacked).sum(0))
+
+
+def kda_update(q, k, v, g, beta, A_log, dt_bias, state):
+    """kimi.py:207-215: one gated delta-rule token per row; state is V-first [.., H, V, K] in FP32."""
+    qf = q.float() * torch.rsqrt(q.float().square().sum(-1, keepdim=True) + 1e-6) / q.shape[-1] ** 0.5
+    kf = k.float() * torch.rsqrt(k.float().square().sum(-1, keepdim=True) + 1e-6)
+    decay = (-5 * torch.sigmoid(A_log.float().exp()[:, None] * (g.float() + dt_bias.float()))).exp()
+    s = state.float() * decay[..., None, :]
+    err = v.float() - torch.einsum("...hvk,...hk->...hv", s, kf)
+    s = s + torch.einsum("...hv,...hk->...hvk", err * beta.float().sigmoid()[..., None], kf)
+    return torch.einsum("...hvk,...hk->...hv", s, qf), s
+
+
+def _tp_sum(value, group):
+    """kimi.py:343-347: FP32 SUM all-reduce, then back to the value's dtype."""
+    acc = value.float().clone()
+    dist.all_reduce(acc, group=group)
+    return acc.to(value.dtype)
+
+
+def _argmax_sharded(logits, offset, group, serial):
+    """kimi.py:218-227: global argmax of vocabulary-sharded logits; the lowest index wins ties."""
+    if serial:
+        return logits.argmax(-1)
+    best = logits.max(-1).values.clone()
+    dist.all_reduce(best, op=dist.ReduceOp.MAX, group=group)
+    index = torch.arange(logits.shape[-1], device=logits.device) + offset
+    token = torch.where(logits == best[:, None], index, torch.iinfo(torch.int64).max).min(-1).values
+    dist.all_reduce(token, op=dist.ReduceOp.MIN, group=group)
+    return token
+
+
+def _rank_context(case, serial, tp_rank, group):
+    if serial:
+        if (case["gpus"], case["tp"], case["ep"]) != (1, 1, 1):
+            raise ValueError("serial validation requires unsharded geometry")
+        return 0, None
+    if tp_rank is None:
+        tp_rank = dist.get_rank() % case["tp"]
+    return tp_rank, group
+
+
+def reference(case, values, *, serial=None, fp32=False, routes=None, tp_rank=None, group=None, trace=None):
+    """One decode step for one rank (kimi.py:230-340).
+
+    fp32=False is the BF16 serving oracle; fp32=True recomputes with FP32 activations. `routes`
+    [L, B, topk] forces the MoE expert sets and adds `route_shortfall` [L, B]. `tp_rank`/`group`
+    name this rank's TP position and process group when not serial (default: WORLD, rank % tp).
+    `trace`, if a dict, receives per-layer intermediates (debugging aid for the CUDA path).
+    """
+    serial = case["gpus"] == 1 if serial is None else serial
+    tp_rank, group = _rank_context(case, serial, tp_rank, group)
+    reduce = (lambda t: t) if serial else (lambda t: _tp_sum(t, group))
+    act = torch.float32 if fp32 else torch.bfloat16
+    cast = lambda t: t.to(act)
+    p, tp = _params(case), case["tp"]
+    d, hr, B = p["head_dim"], p["q_heads"] // tp, p["batch"]
+    chunk = p["vocab"] // tp
+    offset = tp_rank * chunk
+    device = values["token"].device
+    rec = (lambda k, t: trace.__setitem__(k, t.detach().clone())) if trace is not None else (lambda k, t: None)
+
+    def proj(name, x):
+        return cast(x) @ cast(values[name]).T
+
+    token, reset = values["token"], values["reset"]
+    mine = (token >= offset) & (token < offset + chunk)
+    prefix = torch.where(mine[:, None], values["embed"][(token - offset).clamp(0, chunk - 1)], 0)
+    prefix = cast(reduce(prefix))
+    rec("embed", prefix)
+    blocks, kv_out, pe_out, state_out, conv_out, chosen, shortfall = [], [], [], [], [], [], []
+    keep = ~reset
+    for layer in range(p["layers"]):
+        pre = f"l{layer}_"
+        hidden = block_mix(prefix, blocks, values["attention_res_norm"][layer],
+                           values["attention_res_proj"][layer], cast) if blocks else prefix
+        if layer % p["attn_res_block_size"] == 0:
+            blocks.append(prefix)
+            prefix = None
+        x = rms_norm(hidden, values["ln1"][layer], 1e-5)
+        rec(pre + "x_attn", x)
+        if is_mla(case, layer):
+            kr, nr, rd, vd = p["kv_lora_rank"], p["qk_nope_dim"], p["qk_rope_dim"], p["v_head_dim"]
+            q = proj(pre + "qb", rms_norm(proj(pre + "qa", x), values[pre + "qn"], 1e-6)).view(B, hr, nr + rd)
+            raw = proj(pre + "ka", x)
+            latent = rms_norm(raw[:, :kr], values[pre + "kn"], 1e-6)
+            pe = raw[:, kr:]
+            kv_out.append(latent)
+            pe_out.append(pe)
+            kb = cast(values[pre + "kb"]).view(hr, nr + vd, kr)
+            absorbed = torch.einsum("bhd,hdc->bhc", q[..., :nr], kb[:, :nr])
+            rec(pre + "q", q)
+            rec(pre + "absorbed", absorbed)
+            rows = []
+            for b in range(B):
+                lat, pos = latent[b:b + 1], pe[b:b + 1]
+                if keep[b]:
+                    lat = torch.cat((cast(values[pre + "kv_cache"][b]), lat))
+                    pos = torch.cat((cast(values[pre + "pe_cache"][b]), pos))
+                scores = (absorbed[b].float() @ lat.float().T + q[b, :, nr:].float() @ pos.float().T) / (nr + rd) ** 0.5
+                rows.append(cast(scores.softmax(-1)) @ lat)
+            mixed = torch.stack(rows)
+            rec(pre + "attn_latent", mixed)
+            out = torch.einsum("bhc,hdc->bhd", mixed, kb[:, nr:]).flatten(1)
+            out = out * proj(pre + "output_gate", x).sigmoid()
+            rec(pre + "attn_in", out)
+            attention = cast(reduce(proj(pre + "o", out)))
+        else:
+            raw = torch.stack([proj(pre + n, x) for n in ("q", "k", "v")], 1)
+            old = values[pre + "conv_state"] * keep[:, None, None, None]
+            window = torch.cat((cast(old[..., 1:]), raw[..., None]), -1)
+            conv_out.append(window)
+            q, k, v = cast(F.silu((window.float() * values[pre + "conv_weight"].float()).sum(-1))).view(B, 3, hr, d).unbind(1)
+            gate = proj(pre + "fb", proj(pre + "fa", x)).view(B, hr, d)
+            beta = proj(pre + "beta", x)
+            state = values[pre + "recurrent_state"] * keep[:, None, None, None]
+            out, new_state = kda_update(q, k, v, gate, beta, values[pre + "A_log"],
+                                        values[pre + "dt_bias"].view(hr, d), state)
+            state_out.append(new_state)
+            out = cast(out).float()
+            out = out * torch.rsqrt(out.square().mean(-1, keepdim=True) + 1e-5) * values[pre + "onorm"].float()
+            out = cast(out * proj(pre + "output_gate", x).view(B, hr, d).float().sigmoid())
+            rec(pre + "attn_in", out.flatten(1))
+            attention = cast(reduce(proj(pre + "o", out.flatten(1))))
+        rec(pre + "attn", attention)
+        prefix = attention if prefix is None else prefix + attention
+        hidden = block_mix(prefix, blocks, values["mlp_res_norm"][layer], values["mlp_res_proj"][layer], cast)
+        x = rms_norm(hidden, values["ln2"][layer], 1e-5)
+        rec(pre + "x_mlp", x)
+        if layer < p["first_dense"]:
+            out = cast(reduce(proj(pre + "down", cast(situ(proj(pre + "gate", x), proj(pre + "up", x))))))
+            chosen.append(torch.full((B, p["topk"]), -1, device=device, dtype=torch.int64))
+            shortfall.append(torch.zeros(B, device=device))
+        else:
+            scores = (x.float() @ values[pre + "router"].float().T).sigmoid()
+            biased = scores + values[pre + "router_bias"].float()
+            top = biased.topk(p["topk"], -1).indices
+            if routes is not None:
+                top = routes[layer].to(device=device, dtype=torch.int64)
+                kth = biased.topk(p["topk"], -1).values[:, -1]
+                shortfall.append((kth - biased.gather(1, top).min(-1).values).clamp_min(0))
+            w = scores.gather(1, top)
+            w = w / (w.sum(-1, keepdim=True) + 1e-20)
+            chosen.append(top.sort(-1).values)
+            latent = proj(pre + "latent_down", x)
+            rec(pre + "latent", latent)
+            total = torch.zeros(B, p["latent_hidden"], device=device)
+            for expert in top.unique().tolist():
+                rows, slots = (top == expert).nonzero(as_tuple=True)
+
+                def wt(kind, e=expert):
+                    return decode_mxfp4(values[f"{pre}{kind}_blocks"][e], values[f"{pre}{kind}_scales"][e]).to(act)
+
+                y = cast(cast(situ(latent[rows] @ wt("gate").T, latent[rows] @ wt("up").T)) @ wt("down").T)
+                total.index_add_(0, rows, y.float() * w[rows, slots, None])
+            rec(pre + "expert_sum_local", total)
+            total = reduce(total)
+            routed = proj(pre + "latent_up", rms_norm(cast(total), values[pre + "latent_norm"], 1e-5))
+            shared = reduce(proj(pre + "shared_down", cast(situ(proj(pre + "shared_gate", x),
+                                                                 proj(pre + "shared_up", x)))))
+            rec(pre + "routed", routed)
+            rec(pre + "shared", cast(shared))
+            out = routed + cast(shared)
+        rec(pre + "mlp", out)
+        prefix = prefix + out
+        rec(pre + "prefix", prefix)
+    hidden = block_mix(prefix, blocks, values["output_res_norm"], values["output_res_proj"], cast)
+    x = rms_norm(hidden, values["fnorm"], 1e-5)
+    rec("x_head", x)
+    logits = proj("lm_head", x).float()
+    length = torch.where(reset, 1, p["context"] + 1).to(torch.int64)
+    stack = lambda items: torch.stack(items) if items else torch.zeros(0, device=device)
+    result = {"logits": logits, "next_token": _argmax_sharded(logits, offset, group, serial),
+              "kv_write": stack(kv_out), "pe_write": stack(pe_out),
+              "recurrent_state": stack(state_out), "conv_state": stack(conv_out),
+              "expert_ids": torch.stack(chosen), "cache_length": length}
+    if routes is not None:
+        result["route_shortfall"] = torch.stack(shortfall)
+    return result
+
+
+def _group_sum(t, group, serial):
+    if not serial:
+        dist.all_reduce(t, group=group)
+    return t
+
+
+def routes_valid(case, routes, expected) -> bool:
+    """kimi.py:358-367: ids in range and distinct per row; dense layers carry -1 exactly as expected."""
+    p, dense = _params(case), _params(case)["first_dense"]
+    if not torch.equal(routes[:dense], expected[:dense]):
+        return False
+    moe = routes[dense:]
+    if bool(((moe < 0) | (moe >= p["experts"])).any()):
+        return False
+    ordered = moe.sort(-1).values
+    return not bool((ordered[..., 1:] == ordered[..., :-1]).any())
+
+
+def compare(case, values, expected, actual, *, serial=None, tp_rank=None, group=None):
+    """The oracle band grader (kimi.py:370-462). Returns details; raises AssertionError on failure."""
+    if not isinstance(actual, dict) or set(actual) != set(expected):
+        raise AssertionError(f"output keys: expected {sorted(expected)}, got "
+                             f"{sorted(actual) if isinstance(actual, dict) else type(actual)}")
+    for name, want in expected.items():
+        got = actual[name]
+        if not isinstance(got, torch.Tensor):
+            raise AssertionError(f"{name}: output must be a Tensor")
+        if got.shape != want.shape or got.dtype != want.dtype or got.device != want.device:
+            raise AssertionError(f"{name}: expected {tuple(want.shape)} {want.dtype} on {want.device}, "
+                                 f"got {tuple(got.shape)} {got.dtype} on {got.device}")
+    serial = case["gpus"] == 1 if serial is None else serial
+    tp_rank, group = _rank_context(case, serial, tp_rank, group)
+    routes = actual["expert_ids"].long()
+    ordered = routes.sort(-1).values
+    checksum = (ordered * torch.arange(1, ordered.numel() + 1, device=ordered.device).view(ordered.shape)).sum()
+    flags = torch.tensor([0 if routes_valid(case, routes, expected["expert_ids"]) else 1,
+                          int(checksum), -int(checksum),
+                          0 if torch.equal(routes.sort(-1).values, expected["expert_ids"]) else 1],
+                         device=routes.device, dtype=torch.int64)
+    if not serial:
+        dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=group)
+    if flags[0] or int(flags[1]) != -int(flags[2]):
+        raise AssertionError("expert_ids: ids out of range, repeated in a row, wrong in a dense layer, "
+                             "or different between ranks")
+    kw = dict(serial=serial, fp32=True, tp_rank=tp_rank, group=group)
+    truth_o = reference(case, values, routes=expected["expert_ids"], **kw)
+    truth_c = truth_o if not flags[3] else reference(case, values, routes=routes, **kw)
+    details, failures = {}, []
+    for name in ("logits", "kv_write", "pe_write", "recurrent_state", "conv_state"):
+        ref_o, ref_c = truth_o[name].float(), truth_c[name].float()
+        oracle, got = expected[name].float(), actual[name].float()
+        rows = ref_o.shape[0] if name == "logits" else 1
+        ref_o, ref_c, oracle, got = (t.reshape(rows, -1) for t in (ref_o, ref_c, oracle, got))
+        if not torch.isfinite(got).all():
+            failures.append(f"{name}: non-finite values")
+        sums = torch.stack([(oracle - ref_o).square().sum(-1), ref_o.square().sum(-1),
+                            (got - ref_c).square().sum(-1), ref_c.square().sum(-1)])
+        sums = _group_sum(sums.double(), group, serial)
+        oracle_err = (sums[0] / sums[1].clamp_min(1e-30)).sqrt()
+        cand_err = (sums[2] / sums[3].clamp_min(1e-30)).sqrt()
+        limit = BAND * oracle_err + FLOOR
+        details[name] = {"candidate_rel_l2_max": float(cand_err.max()),
+                         "oracle_rel_l2_max": float(oracle_err.max()),
+                         "worst_ratio": float((cand_err / limit).max())}
+        if bool((cand_err > limit).any()) or not torch.isfinite(cand_err).all():
+            failures.append(f"{name}: {details[name]}")
+    ref = truth_c["logits"].float()
+    chunk = ref.shape[-1]
+    offset = 0 if serial else tp_rank * chunk
+    stats = torch.stack([ref.max(-1).values,
+                         (expected["logits"].float() - truth_o["logits"].float()).abs().max(-1).values])
+    if not serial:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX, group=group)
+    token = actual["next_token"].long()
+    mine = (token >= offset) & (token < offset + chunk)
+    picked = torch.where(mine, ref.gather(1, (token - offset).clamp(0, chunk - 1)[:, None])[:, 0], -torch.inf)
+    if not serial:
+        dist.all_reduce(picked, op=dist.ReduceOp.MAX, group=group)
+    bad = picked < stats[0] - 2 * stats[1]
+    details["next_token"] = {"rows_outside_tie_margin": int(bad.sum()),
+                             "rows_differing_from_fp32_argmax": int((token != truth_c["next_token"]).sum())}
+    if bad.any():
+        failures.append(f"next_token: {details['next_token']}")
+    oracle_short = float(truth_o["route_shortfall"].max()) if truth_o["route_shortfall"].numel() else 0.0
+    cand_short = truth_c["route_shortfall"]
+    allowed = BAND * oracle_short + ROUTE_FLOOR
+    details["expert_ids"] = {"candidate_max_shortfall": float(cand_short.max()) if cand_short.numel() else 0.0,
+                             "oracle_max_shortfall": oracle_short, "allowed": allowed,
+                             "sets_differing_from_oracle": int((routes.sort(-1).values != expected["expert_ids"]).any(-1).sum())}
+    if cand_short.numel() and bool((cand_short > allowed).any()):
+        failures.append(f"expert_ids: {details['expert_ids']}")
+    mismatch = int((actual["cache_length"] != expected["cache_length"]).sum())
+    details["cache_length"] = {"mismatched_elements": mismatch}
+    if mismatch:
+        failures.append(f"cache_length: {mismatch} mismatches")
+    if failures:
+        raise AssertionError("; ".join(failures))
+    return details
+
+
+def snapshot(inputs: dict) -> dict:
+    """Input-mutation detector in the spirit of harness/correctness.py:13-45 (host copy or device checksums)."""
+    out = {}
+    for name, value in inputs.items():
+        value = value.detach()
+        nbytes = value.numel() * value.element_size()
+        if nbytes <= 1 << 26 or not value.is_contiguous() or nbytes % 4:
+            out[name] = value.to("cpu", copy=True)
+            continue
+        words = value.reshape(-1).view(torch.uint8).view(torch.int32)
+        total = torch.zeros(2, dtype=torch.int64, device=value.device)
+        step = 1 << 26
+        weight = (torch.arange(step, device=value.device, dtype=torch.int64) % 65521) + 1
+        for start in range(0, words.numel(), step):
+            part = words[start:start + step].to(torch.int64)
+            total[0] += part.sum()
+            total[1] += (part * weight[:part.numel()]).sum()
+        out[name] = total.cpu()
+    return out
+
+
+def check_unchanged(inputs: dict, before: dict) -> None:
+    after = snapshot(inputs)
+    for name in inputs:
+        if not torch.equal(after[name], before[name]):
+            raise AssertionError(f"candidate mutated input {name}")
+
+
+def serial_rank_view(case):
+    """A TP1 case dict that runs exactly one TP rank's arithmetic serially (reductions become identity)."""
+    p, tp = dict(_params(case)), case["tp"]
+    for key in ("q_heads", "vocab", "intermediate", "dense_intermediate"):
+        p[key] //= tp
+    return dict(case, id=case["id"] + "-rank-equivalent", gpus=1, tp=1, params=p)
+
