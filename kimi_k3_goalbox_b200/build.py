@@ -1,0 +1,89 @@
+"""Build libkk3.so (the sm_100a decode-step kernels and their C ABI) in-tree with nvcc.
+
+    python -m kimi_k3_goalbox_b200.build [--force] [-j N]
+
+Objects go to `_build/` at the repository root, the shared library to `kimi_k3_goalbox_b200/_lib/libkk3.so`.
+Translation units are compiled in parallel and only when a source or header is newer than the object.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+BUILD = ROOT / "_build"
+LIB = PKG / "_lib" / "libkk3.so"
+UNITS = ["kk3_host.cu", "kk3_kernel_nt1.cu", "kk3_kernel_nt2.cu", "kk3_kernel_nt4.cu", "kk3_kernel_nt8.cu"]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xptxas", "-v", f"-I{ROOT / 'include'}"]
+
+
+def nvcc() -> str:
+    found = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not Path(found).exists():
+        raise RuntimeError("nvcc not found: the CUDA 12.9 toolkit is required to build libkk3.so")
+    return found
+
+
+def _deps() -> list[Path]:
+    return sorted(CSRC.glob("*.cuh")) + [ROOT / "include" / "kk3.h"]
+
+
+def _stale(obj: Path, src: Path) -> bool:
+    if not obj.exists():
+        return True
+    t = obj.stat().st_mtime
+    return any(p.stat().st_mtime > t for p in [src, *_deps()])
+
+
+def _compile(unit: str, force: bool) -> tuple[str, str]:
+    src, obj = CSRC / unit, BUILD / (unit + ".o")
+    if not force and not _stale(obj, src):
+        return unit, "up to date"
+    cmd = [nvcc(), *ARCH, *FLAGS, "-c", str(src), "-o", str(obj)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {unit}:\n{res.stderr}")
+    (BUILD / (unit + ".ptxas.txt")).write_text(res.stderr)
+    return unit, "compiled"
+
+
+def build(force: bool = False, jobs: int | None = None, verbose: bool = True) -> Path:
+    BUILD.mkdir(exist_ok=True)
+    LIB.parent.mkdir(exist_ok=True)
+    jobs = jobs or min(len(UNITS), os.cpu_count() or 1)
+    with ThreadPoolExecutor(jobs) as pool:
+        results = list(pool.map(lambda u: _compile(u, force), UNITS))
+    objs = [BUILD / (u + ".o") for u in UNITS]
+    relink = force or not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs)
+    if relink:
+        cmd = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(LIB)]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"link failed:\n{res.stderr}")
+    if verbose:
+        for unit, state in results:
+            print(f"  {unit}: {state}")
+        print(f"  {LIB.relative_to(ROOT)}: {'linked' if relink else 'up to date'}")
+    return LIB
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-j", type=int, default=None)
+    args = ap.parse_args(argv)
+    build(force=args.force, jobs=args.j)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,298 @@
+// kk3_common.cuh - shared device types and PTX helpers for the sm_100a Kimi K3 decode-step kernel.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/kk3.h"
+
+#define KK3_DEV __device__ __forceinline__
+
+namespace kk3 {
+
+typedef __nv_bfloat16 bf16;
+
+constexpr int kThreads = 512;          // one CTA per SM, 16 warps
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxBatch = 64;
+constexpr int kMaxTp = 8;
+constexpr int kMaxTopk = 32;
+constexpr int kMaxExperts = 1024;
+constexpr int kMaxPtrs = KK3_GLOBAL_SLOTS + 96 * KK3_LAYER_SLOTS;   // 3104 slots: up to 96 layers
+constexpr int kMlaPos = 32;            // cache positions per attention sub-tile
+
+// device error word values (also the host-visible status)
+constexpr int kErrTimeout = 1;
+constexpr int kErrDevice = 2;
+
+// ---------------------------------------------------------------------------------------------
+// Geometry and scratch layout, copied into the kernel parameters.
+
+struct Geo {
+  int L, B, h, lh, inter, dinter, sinter, hr, d, qr, kr, nr, rd, vd, V, E, K, ctx, conv, bs, first_dense;
+  int tp, rank;
+  int qdim;          // hr * d
+  int nmla, nkda;    // layer counts
+  int nblk;          // block-vector capacity
+  long long timeout_ns;
+  int mla_chunks;    // split-K chunks per batch row of the MLA attention
+  int mla_chunk_len; // positions per chunk (multiple of kMlaPos)
+  long long fix_bank; // floats per stream-K partial bank (two banks: two GEMV passes may share a phase)
+  int cnt_bank;       // counters per stream-K counter bank
+  int mla_mt;         // 16-row head tiles of the MLA attention (ceil(hr / 16))
+};
+
+// scratch buffers (device pointers owned by the context)
+struct Scratch {
+  bf16* prefix;       // [B, h]
+  bf16* blocks;       // [nblk, B, h]
+  bf16* xa;           // [B, h]   normalised attention input
+  bf16* xm;           // [B, h]   normalised MLP input
+  bf16* qkv;          // [B, 3*qdim] KDA q,k,v projections (or MLA qa [B,qr] + ka [B,576])
+  bf16* og;           // [B, qdim] output-gate projection
+  bf16* fa;           // [B, d]
+  bf16* beta;         // [B, hr]
+  bf16* attn_in;      // [B, hr*vd] input of the o projection
+  bf16* mla_qan;      // [B, qr]
+  bf16* mla_q;        // [B, hr*(nr+rd)]
+  bf16* absorbed;     // [B, hr, kr]
+  float* mla_part;    // [B, chunks, hr, kr+2]
+  bf16* dense_act;    // [B, dinter]
+  float* scores;      // [B, E] sigmoid router scores (FP32)
+  bf16* latent;       // [B, lh]
+  __half* latent_p;   // [B, lh] FP16, group-permuted for the MXFP4 tensor-core path
+  bf16* shared_act;   // [B, sinter]
+  int* route_ids;     // [B, K] sorted expert ids of the current layer
+  float* route_w;     // [B, K] renormalised weights (same order)
+  int* pair_row;      // [B*K] pair -> batch row, grouped by expert
+  int* pair_slot;     // [B*K] pair -> slot j
+  int* chunk_info;    // [1 + B*K*3]: count, then (expert, first pair, pairs) per expert chunk of <= 8 pairs
+  __half* act_p;      // [B*K, inter] FP16 permuted expert activations
+  bf16* out_slot;     // [B, K, lh] per-slot expert outputs
+  bf16* x3;           // [B, lh] latent_norm(expert_sum)
+  bf16* shared_red;   // [B, h] reduced shared-expert output
+  float* expert_sum;  // [B, lh] FP32 (diagnostics copy of the local sum)
+  float* fix_part;    // [2 * warps_total, 16 * 64 * 2] stream-K partial tiles
+  int* fix_cnt;       // [max tiles] stream-K arrival counters
+  unsigned long long* argmax_key; // [B]
+  unsigned* bar;      // [2] grid barrier: count, generation
+  int* err;           // device error word (mapped host memory)
+  int* phase_count;   // number of grid phases of the last complete step
+};
+
+// One-shot exchange buffers, symmetric across ranks (this rank's and peers' mapped copies).
+struct Comm {
+  unsigned char* base[kMaxTp];   // per rank, this rank's view of rank r's exchange buffer
+  long long flag_off;            // byte offset of the flag array [B][tp] (u32)
+  long long data_off[2];         // byte offset of the two parity data regions
+  long long region_bytes;        // bytes per parity region
+  // sub-regions inside a parity region, byte offsets (each [tp][B][width])
+  long long att_off, exp_off, shd_off, key_off;
+};
+
+struct StepArgs {
+  Geo g;
+  Scratch s;
+  Comm comm;
+  unsigned epoch;       // step counter (1, 2, ...), orders the peer flags
+  int stop_phase;       // debug: return after this many grid phases (-1: run everything)
+  int nptr;
+  const void* ptr[kMaxPtrs];
+};
+
+// ---------------------------------------------------------------------------------------------
+// small helpers
+
+KK3_DEV unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+KK3_DEV unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+KK3_DEV unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+KK3_DEV void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+KK3_DEV int ld_volatile_int(const int* p) { return *(volatile const int*)p; }
+
+// streaming 16-byte weight load: read-only path, no L1 allocation
+KK3_DEV uint4 ldg_stream16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+KK3_DEV unsigned ldg_nc32(const void* p) {
+  unsigned v;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+KK3_DEV unsigned ldg_nc8(const void* p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.u8 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+// activation load: coherent global load (data written earlier in this kernel, ordered by a grid barrier)
+KK3_DEV uint4 ld_act16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+// L2-only load for data another CTA may have written after this SM cached the line
+KK3_DEV float ld_cg_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+
+KK3_DEV float bf2f(bf16 v) { return __bfloat162float(v); }
+KK3_DEV bf16 f2bf(float v) { return __float2bfloat16_rn(v); }
+KK3_DEV float round_bf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+KK3_DEV float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// E8M0 scale byte -> 2^(s-127) in FP32; 255 is NaN (megabench/tasks/quantization.py:49-50)
+KK3_DEV float e8m0_to_f32(unsigned s) {
+  float v = __uint_as_float(s << 23);
+  v = (s == 0u) ? 5.877471754111438e-39f : v;
+  v = (s == 255u) ? __uint_as_float(0x7fc00000u) : v;
+  return v;
+}
+
+// Eight E2M1 nibbles of one 32-bit word -> four FP16x2 registers holding the exact E2M1 values.
+// Register j holds nibbles (j, j+4): the layout expected by the permuted activation operand.
+// The nibble's 3 magnitude bits land in the FP16 exponent/mantissa boundary (value * 2^-14, exact
+// for every code, including the subnormal 0.5 -> 2^-15), then one FP16x2 multiply by 2^14 restores it.
+KK3_DEV void e2m1x8_to_f16(unsigned w, unsigned (&r)[4]) {
+  const unsigned mag = 0x0E000E00u, sgn = 0x80008000u;
+  unsigned a = ((w << 9) & mag) | ((w << 12) & sgn);
+  unsigned b = ((w << 5) & mag) | ((w << 8) & sgn);
+  unsigned c = ((w << 1) & mag) | ((w << 4) & sgn);
+  unsigned d = ((w >> 3) & mag) | (w & sgn);
+  const __half2 k = __halves2half2(__ushort_as_half(0x7400), __ushort_as_half(0x7400));   // 16384
+  __half2 ha = __hmul2(*reinterpret_cast<__half2*>(&a), k);
+  __half2 hb = __hmul2(*reinterpret_cast<__half2*>(&b), k);
+  __half2 hc = __hmul2(*reinterpret_cast<__half2*>(&c), k);
+  __half2 hd = __hmul2(*reinterpret_cast<__half2*>(&d), k);
+  r[0] = *reinterpret_cast<unsigned*>(&ha);
+  r[1] = *reinterpret_cast<unsigned*>(&hb);
+  r[2] = *reinterpret_cast<unsigned*>(&hc);
+  r[3] = *reinterpret_cast<unsigned*>(&hd);
+}
+
+// position of element k inside its 8-element group in the permuted FP16 activation layout:
+// order [k0,k4,k1,k5,k2,k6,k3,k7]
+KK3_DEV int perm8(int k) { return (k & ~7) | ((k & 3) << 1) | ((k >> 2) & 1); }
+
+// D = A*B + C, m16n8k16, BF16 inputs, FP32 accumulate
+KK3_DEV void mma_bf16(float (&d)[4], unsigned a0, unsigned a1, unsigned a2, unsigned a3, unsigned b0, unsigned b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+KK3_DEV void mma_f16(float (&d)[4], unsigned a0, unsigned a1, unsigned a2, unsigned a3, unsigned b0, unsigned b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+KK3_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+KK3_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// CTA-wide sum of one float (all threads get the result). `red` needs kWarps floats of shared memory.
+KK3_DEV float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < kWarps ? red[lane] : 0.0f;
+  return warp_sum(t);
+}
+
+// pointer-table access
+template <typename T>
+KK3_DEV const T* gptr(const StepArgs& a, int slot) { return reinterpret_cast<const T*>(a.ptr[slot]); }
+template <typename T>
+KK3_DEV const T* lptr(const StepArgs& a, int layer, int slot) {
+  return reinterpret_cast<const T*>(a.ptr[KK3_GLOBAL_SLOTS + layer * KK3_LAYER_SLOTS + slot]);
+}
+template <typename T>
+KK3_DEV T* gout(const StepArgs& a, int slot) { return reinterpret_cast<T*>(const_cast<void*>(a.ptr[slot])); }
+
+KK3_DEV void set_error(const StepArgs& a, int code) { atomicCAS(a.s.err, 0, code); }
+KK3_DEV bool failed(const StepArgs& a) { return ld_volatile_int(a.s.err) != 0; }
+
+// Bounded grid-wide barrier (sense reversal on a generation counter). Returns false when the wait ran
+// past the timeout or another CTA already reported an error; the kernel then unwinds.
+KK3_DEV bool grid_sync(const StepArgs& a) {
+  __shared__ int ok_flag;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned* count = a.s.bar;
+    unsigned* gen = a.s.bar + 1;
+    int ok = 1;
+    unsigned my_gen = ld_acquire_gpu(gen);
+    __threadfence();
+    unsigned arrived = atomicAdd(count, 1u);
+    if (arrived == gridDim.x - 1) {
+      atomicExch(count, 0u);
+      __threadfence();
+      atomicAdd(gen, 1u);
+    } else {
+      const unsigned long long t0 = globaltimer();
+      while (ld_acquire_gpu(gen) == my_gen) {
+        if (failed(a) || globaltimer() - t0 > (unsigned long long)a.g.timeout_ns) {
+          set_error(a, kErrTimeout);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    __threadfence();
+    if (failed(a)) ok = 0;
+    ok_flag = ok;
+  }
+  __syncthreads();
+  return ok_flag != 0;
+}
+
+// Wait (thread-level) until *flag >= want (system scope). Returns false on timeout / error.
+KK3_DEV bool wait_flag_sys(const StepArgs& a, const unsigned* flag, unsigned want) {
+  const unsigned long long t0 = globaltimer();
+  while ((int)(ld_acquire_sys(flag) - want) < 0) {
+    if (failed(a) || globaltimer() - t0 > (unsigned long long)a.g.timeout_ns) {
+      set_error(a, kErrTimeout);
+      return false;
+    }
+    __nanosleep(32);
+  }
+  return true;
+}
+
+}  // namespace kk3

@@ -1,0 +1,387 @@
+// kk3_host.cu - the C ABI declared in include/kk3.h: context set-up, peer mapping, launch, status.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+
+#include "kk3_phases.cuh"
+
+namespace kk3 {
+// one instantiation per batch tile count, each in its own translation unit (kk3_kernel_nt*.cu)
+#define KK3_DECL(n)                                                  \
+  cudaError_t prepare_nt##n(size_t smem, int* occupancy);           \
+  cudaError_t launch_nt##n(const StepArgs* args, int grid, size_t smem, cudaStream_t stream);
+KK3_DECL(1)
+KK3_DECL(2)
+KK3_DECL(4)
+KK3_DECL(8)
+#undef KK3_DECL
+
+static cudaError_t prepare_kernel(int nt, size_t smem, int* occ) {
+  switch (nt) {
+    case 1: return prepare_nt1(smem, occ);
+    case 2: return prepare_nt2(smem, occ);
+    case 4: return prepare_nt4(smem, occ);
+    default: return prepare_nt8(smem, occ);
+  }
+}
+static cudaError_t launch_kernel(int nt, const StepArgs* a, int grid, size_t smem, cudaStream_t st) {
+  switch (nt) {
+    case 1: return launch_nt1(a, grid, smem, st);
+    case 2: return launch_nt2(a, grid, smem, st);
+    case 4: return launch_nt4(a, grid, smem, st);
+    default: return launch_nt8(a, grid, smem, st);
+  }
+}
+}  // namespace kk3
+
+using namespace kk3;
+
+struct kk3_ctx {
+  kk3_config cfg;
+  Geo g;
+  Scratch s;
+  Comm comm;
+  int sms = 0, grid = 0, nt = 1;
+  size_t smem = 0;
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  void* comm_local = nullptr;
+  size_t comm_bytes = 0;
+  void* peer_open[kMaxTp] = {};
+  int* err_host = nullptr;
+  int* err_dev = nullptr;
+  unsigned epoch = 0;
+  int failed = 0;
+  int peers_open = 0;
+  StepArgs* args = nullptr;
+  size_t buf_bytes[KK3_BUF_COUNT] = {};
+  void* buf_ptr[KK3_BUF_COUNT] = {};
+};
+
+static int cuda_fail(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return KK3_OK;
+  fprintf(stderr, "kk3: %s failed: %s\n", what, cudaGetErrorString(e));
+  return KK3_ERR_CUDA;
+}
+#define KK3_CUDA(call)                                 \
+  do {                                                 \
+    int rc_ = cuda_fail((call), #call);                \
+    if (rc_ != KK3_OK) return rc_;                     \
+  } while (0)
+
+extern "C" int kk3_table_size(const kk3_config* cfg) {
+  if (!cfg || cfg->layers < 1) return KK3_ERR_ARG;
+  return KK3_GLOBAL_SLOTS + cfg->layers * KK3_LAYER_SLOTS;
+}
+
+extern "C" const char* kk3_error_string(int code) {
+  switch (code) {
+    case KK3_OK: return "ok";
+    case KK3_ERR_ARG: return "bad argument or pointer table";
+    case KK3_ERR_UNSUPPORTED: return "geometry not supported by the sm_100a kernels";
+    case KK3_ERR_CUDA: return "CUDA runtime call failed";
+    case KK3_ERR_TIMEOUT: return "in-kernel wait exceeded its bound (a peer or CTA never arrived)";
+    case KK3_ERR_DEVICE: return "in-kernel consistency check failed";
+    case KK3_ERR_PEERS: return "tensor-parallel peers are not open";
+    case KK3_ERR_FAILED: return "context failed earlier; rebuild it";
+    default: return "unknown kk3 error";
+  }
+}
+
+static int validate(const kk3_config* c) {
+  if (!c) return KK3_ERR_ARG;
+  const bool ok =
+      c->layers >= 1 && c->layers <= 96 && c->batch >= 1 && c->batch <= kMaxBatch && c->head_dim == 128 &&
+      c->qk_nope_dim == 128 && c->v_head_dim == 128 && c->qk_rope_dim == 64 && c->kv_lora_rank == 512 &&
+      c->conv_kernel == 4 && c->topk >= 1 && c->topk <= kMaxTopk && c->experts >= c->topk &&
+      c->experts <= kMaxExperts && c->heads >= 1 && c->heads <= 96 && c->tp >= 1 && c->tp <= kMaxTp &&
+      c->rank >= 0 && c->rank < c->tp && c->hidden % 64 == 0 && c->hidden <= 8192 && c->latent_hidden % 64 == 0 &&
+      c->latent_hidden <= 8192 && c->q_lora_rank % 64 == 0 && c->inter_shard % 64 == 0 && c->inter_shard > 0 &&
+      c->dense_inter_shard % 64 == 0 && c->shared_inter_shard % 64 == 0 && c->vocab_shard >= 1 &&
+      c->context >= 1 && c->attn_res_block_size >= 1 && c->first_dense >= 0 &&
+      (c->layers + c->attn_res_block_size - 1) / c->attn_res_block_size <= kMaxBlocks - 1 &&
+      (long long)c->heads * 128 % 64 == 0 && (long long)c->vocab_shard * c->batch < (1ll << 31);
+  return ok ? KK3_OK : KK3_ERR_UNSUPPORTED;
+}
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
+  if (!out) return KK3_ERR_ARG;
+  *out = nullptr;
+  int rc = validate(cfg);
+  if (rc != KK3_OK) return rc;
+  KK3_CUDA(cudaSetDevice(cfg->device));
+  kk3_ctx* x = new (std::nothrow) kk3_ctx();
+  if (!x) return KK3_ERR_CUDA;
+  x->cfg = *cfg;
+  Geo& g = x->g;
+  memset(&g, 0, sizeof(g));
+  g.L = cfg->layers; g.B = cfg->batch; g.h = cfg->hidden; g.lh = cfg->latent_hidden; g.inter = cfg->inter_shard;
+  g.dinter = cfg->dense_inter_shard; g.sinter = cfg->shared_inter_shard; g.hr = cfg->heads; g.d = cfg->head_dim;
+  g.qr = cfg->q_lora_rank; g.kr = cfg->kv_lora_rank; g.nr = cfg->qk_nope_dim; g.rd = cfg->qk_rope_dim;
+  g.vd = cfg->v_head_dim; g.V = cfg->vocab_shard; g.E = cfg->experts; g.K = cfg->topk; g.ctx = cfg->context;
+  g.conv = cfg->conv_kernel; g.bs = cfg->attn_res_block_size; g.first_dense = cfg->first_dense; g.tp = cfg->tp;
+  g.rank = cfg->rank; g.qdim = g.hr * g.d;
+  for (int l = 0; l < g.L; ++l) {
+    if (((l + 1) % 4 == 0) || l == g.L - 1) ++g.nmla; else ++g.nkda;
+  }
+  g.nblk = (g.L + g.bs - 1) / g.bs;
+  g.timeout_ns = cfg->timeout_ns > 0 ? cfg->timeout_ns : 10000000000ll;
+  g.mla_mt = (g.hr + 15) / 16;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, cfg->device) != cudaSuccess) { delete x; return KK3_ERR_CUDA; }
+  x->sms = prop.multiProcessorCount;
+  x->grid = x->sms;
+  x->nt = g.B <= 8 ? 1 : (g.B <= 16 ? 2 : (g.B <= 32 ? 4 : 8));
+  {
+    int chunks = x->grid / g.B;
+    chunks = chunks < 1 ? 1 : (chunks > 64 ? 64 : chunks);
+    int len = (g.ctx + 1 + chunks - 1) / chunks;
+    len = (len + kMlaPos - 1) / kMlaPos * kMlaPos;
+    g.mla_chunk_len = len;
+    g.mla_chunks = (g.ctx + 1 + len - 1) / len;
+  }
+  const long long gw = (long long)x->grid * kWarps;
+  g.fix_bank = 2ll * gw * (2 * x->nt * 128);
+  {
+    long long tiles = 0, t;
+    auto mx = [&](long long v) { tiles = v > tiles ? v : tiles; };
+    mx((3ll * g.qdim + g.qdim + g.d + g.hr + 15 * 6) / 16 + 6);
+    mx((long long)(g.qr + g.kr + g.rd + g.hr * g.vd) / 16 + 3);
+    mx((long long)g.hr * (g.nr + g.rd) / 16 + 1);
+    mx(g.h / 16 + 1);
+    mx((long long)(g.dinter + 15) / 16 + 1);
+    mx((long long)(g.E + g.lh + 30) / 16 + 2);
+    mx((long long)(g.sinter + 15) / 16 + 1);
+    mx((long long)(g.V + 15) / 16 + 1);
+    t = (long long)g.B * g.K * ((g.inter > g.lh ? g.inter : g.lh) / 16);
+    mx(t);
+    g.cnt_bank = (int)tiles;
+  }
+  // scratch layout
+  struct Item { void** p; size_t bytes; };
+  const size_t B = g.B;
+  size_t qkv_w = (size_t)3 * g.qdim > (size_t)(g.qr + g.kr + g.rd) ? (size_t)3 * g.qdim : (size_t)(g.qr + g.kr + g.rd);
+  Scratch& s = x->s;
+  unsigned* bar = nullptr;
+  int* phase_count = nullptr;
+  Item items[] = {
+      {(void**)&s.prefix, B * g.h * 2}, {(void**)&s.blocks, (size_t)g.nblk * B * g.h * 2},
+      {(void**)&s.xa, B * g.h * 2}, {(void**)&s.xm, B * g.h * 2}, {(void**)&s.qkv, B * qkv_w * 2},
+      {(void**)&s.og, B * (size_t)g.qdim * 2}, {(void**)&s.fa, B * g.d * 2}, {(void**)&s.beta, B * g.hr * 2},
+      {(void**)&s.attn_in, B * (size_t)g.hr * g.vd * 2}, {(void**)&s.mla_qan, B * g.qr * 2},
+      {(void**)&s.mla_q, B * (size_t)g.hr * (g.nr + g.rd) * 2}, {(void**)&s.absorbed, B * (size_t)g.hr * g.kr * 2},
+      {(void**)&s.mla_part, B * (size_t)g.mla_chunks * g.hr * (g.kr + 2) * 4},
+      {(void**)&s.dense_act, B * (size_t)(g.dinter > 0 ? g.dinter : 64) * 2}, {(void**)&s.scores, B * g.E * 4},
+      {(void**)&s.latent, B * g.lh * 2}, {(void**)&s.latent_p, B * g.lh * 2},
+      {(void**)&s.shared_act, B * (size_t)(g.sinter > 0 ? g.sinter : 64) * 2}, {(void**)&s.route_ids, B * g.K * 4},
+      {(void**)&s.route_w, B * g.K * 4}, {(void**)&s.pair_row, B * g.K * 4}, {(void**)&s.pair_slot, B * g.K * 4},
+      {(void**)&s.chunk_info, (1 + B * g.K * 3) * 4}, {(void**)&s.act_p, B * g.K * (size_t)g.inter * 2},
+      {(void**)&s.out_slot, B * g.K * (size_t)g.lh * 2}, {(void**)&s.x3, B * g.lh * 2},
+      {(void**)&s.shared_red, B * g.h * 2}, {(void**)&s.expert_sum, B * g.lh * 4},
+      {(void**)&s.fix_part, (size_t)g.fix_bank * 2 * 4}, {(void**)&s.fix_cnt, (size_t)g.cnt_bank * 2 * 4},
+      {(void**)&s.argmax_key, B * 8}, {(void**)&bar, 64}, {(void**)&phase_count, 64},
+  };
+  size_t total = 0;
+  for (auto& it : items) total += align_up(it.bytes, 256);
+  x->scratch_bytes = total;
+  if (cudaMalloc(&x->scratch, total) != cudaSuccess) { delete x; return KK3_ERR_CUDA; }
+  if (cudaMemset(x->scratch, 0, total) != cudaSuccess) { cudaFree(x->scratch); delete x; return KK3_ERR_CUDA; }
+  {
+    size_t off = 0;
+    for (auto& it : items) {
+      *it.p = (char*)x->scratch + off;
+      off += align_up(it.bytes, 256);
+    }
+  }
+  s.bar = bar;
+  s.phase_count = phase_count;
+  // device error word in mapped host memory, readable without synchronising
+  if (cudaHostAlloc((void**)&x->err_host, 64, cudaHostAllocMapped) != cudaSuccess) {
+    cudaFree(x->scratch); delete x; return KK3_ERR_CUDA;
+  }
+  memset(x->err_host, 0, 64);
+  if (cudaHostGetDevicePointer((void**)&x->err_dev, x->err_host, 0) != cudaSuccess) {
+    cudaFreeHost(x->err_host); cudaFree(x->scratch); delete x; return KK3_ERR_CUDA;
+  }
+  s.err = x->err_dev;
+  // exchange buffer: flags [B][tp] u32, then two parity regions {att bf16 [tp][B][h], exp f32 [tp][B][lh],
+  // shd bf16 [tp][B][h], key u64 [tp][B]}
+  Comm& c = x->comm;
+  memset(&c, 0, sizeof(c));
+  const size_t tp = g.tp;
+  c.flag_off = 0;
+  size_t off = align_up(B * tp * 4, 256);
+  c.att_off = 0;
+  size_t r = align_up(tp * B * g.h * 2, 256);
+  c.exp_off = r;
+  r += align_up(tp * B * g.lh * 4, 256);
+  c.shd_off = r;
+  r += align_up(tp * B * g.h * 2, 256);
+  c.key_off = r;
+  r += align_up(tp * B * 8, 256);
+  c.region_bytes = r;
+  c.data_off[0] = off;
+  c.data_off[1] = off + r;
+  x->comm_bytes = off + 2 * r;
+  if (cudaMalloc(&x->comm_local, x->comm_bytes) != cudaSuccess ||
+      cudaMemset(x->comm_local, 0, x->comm_bytes) != cudaSuccess) {
+    cudaFreeHost(x->err_host); cudaFree(x->scratch); delete x; return KK3_ERR_CUDA;
+  }
+  for (int i = 0; i < kMaxTp; ++i) c.base[i] = nullptr;
+  c.base[g.rank] = (unsigned char*)x->comm_local;
+  x->peers_open = g.tp == 1;
+  // shared memory: the largest phase (MLA attention with all head tiles, or row buffers)
+  const int HR = g.mla_mt * 16;
+  size_t sm_mla = (size_t)(HR + 2 * kMlaPos) * kRowK * 2 + (size_t)HR * kRowS * 4 + (size_t)HR * kRowP * 2 + 3 * HR * 4 + 64;
+  size_t sm_row = (512 + (size_t)(g.h > g.lh ? g.h : g.lh)) * 4 + 64;
+  size_t sm_abs = ((size_t)g.B * 128 + 4 * 16 * 128) * 4;
+  size_t sm_route = ((size_t)g.B * g.K + 4 * kMaxExperts) * 4;
+  size_t sm = sm_mla;
+  sm = sm_row > sm ? sm_row : sm;
+  sm = sm_abs > sm ? sm_abs : sm;
+  sm = sm_route > sm ? sm_route : sm;
+  x->smem = align_up(sm, 128);
+  if (x->smem > (size_t)prop.sharedMemPerBlockOptin) {
+    kk3_free(x);
+    return KK3_ERR_UNSUPPORTED;
+  }
+  int occ = 0;
+  if (prepare_kernel(x->nt, x->smem, &occ) != cudaSuccess || occ < 1) {
+    kk3_free(x);
+    return KK3_ERR_UNSUPPORTED;
+  }
+  x->args = new (std::nothrow) StepArgs();
+  if (!x->args) { kk3_free(x); return KK3_ERR_CUDA; }
+  // diagnostics table
+  void* bp[KK3_BUF_COUNT] = {s.prefix, s.xa, s.xm, s.attn_in, s.scores, s.latent, s.shared_act, s.x3, s.route_w,
+                             s.qkv, s.mla_q, s.absorbed, s.absorbed, s.expert_sum, s.blocks, x->comm_local};
+  size_t bb[KK3_BUF_COUNT] = {B * g.h * 2, B * g.h * 2, B * g.h * 2, B * (size_t)g.hr * g.vd * 2, B * g.E * 4,
+                              B * g.lh * 2, B * (size_t)g.sinter * 2, B * g.lh * 2, B * g.K * 4, B * qkv_w * 2,
+                              B * (size_t)g.hr * (g.nr + g.rd) * 2, B * (size_t)g.hr * g.kr * 2,
+                              B * (size_t)g.hr * g.kr * 2, B * g.lh * 4, (size_t)g.nblk * B * g.h * 2, x->comm_bytes};
+  for (int i = 0; i < KK3_BUF_COUNT; ++i) { x->buf_ptr[i] = bp[i]; x->buf_bytes[i] = bb[i]; }
+  *out = x;
+  return KK3_OK;
+}
+
+extern "C" int kk3_ipc_handle(kk3_ctx* x, void* handle64) {
+  if (!x || !handle64) return KK3_ERR_ARG;
+  KK3_CUDA(cudaSetDevice(x->cfg.device));
+  cudaIpcMemHandle_t h;
+  KK3_CUDA(cudaIpcGetMemHandle(&h, x->comm_local));
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  memcpy(handle64, &h, 64);
+  return KK3_OK;
+}
+
+extern "C" int kk3_open_peers(kk3_ctx* x, const void* handles) {
+  if (!x || !handles) return KK3_ERR_ARG;
+  KK3_CUDA(cudaSetDevice(x->cfg.device));
+  for (int r = 0; r < x->g.tp; ++r) {
+    if (r == x->g.rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, (const char*)handles + 64 * r, 64);
+    void* p = nullptr;
+    KK3_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    x->peer_open[r] = p;
+    x->comm.base[r] = (unsigned char*)p;
+  }
+  x->peers_open = 1;
+  return KK3_OK;
+}
+
+// Single-process testing aid: use an existing device allocation as rank r's exchange buffer.
+extern "C" int kk3_debug_set_peer(kk3_ctx* x, int r, void* device_ptr) {
+  if (!x || r < 0 || r >= x->g.tp || r == x->g.rank || !device_ptr) return KK3_ERR_ARG;
+  x->comm.base[r] = (unsigned char*)device_ptr;
+  int all = 1;
+  for (int i = 0; i < x->g.tp; ++i) all &= x->comm.base[i] != nullptr;
+  x->peers_open = all;
+  return KK3_OK;
+}
+
+extern "C" size_t kk3_exchange_bytes(kk3_ctx* x) { return x ? x->comm_bytes : 0; }
+
+static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int stop_phase) {
+  if (!x || !table) return KK3_ERR_ARG;
+  if (x->failed) return KK3_ERR_FAILED;
+  if (!x->peers_open) return KK3_ERR_PEERS;
+  const int need = KK3_GLOBAL_SLOTS + x->g.L * KK3_LAYER_SLOTS;
+  if (n != need || n > kMaxPtrs) return KK3_ERR_ARG;
+  if (*x->err_host != 0) {
+    x->failed = 1;
+    return KK3_ERR_FAILED;
+  }
+  StepArgs* a = x->args;
+  a->g = x->g;
+  a->s = x->s;
+  a->comm = x->comm;
+  a->epoch = ++x->epoch;
+  a->stop_phase = stop_phase;
+  a->nptr = n;
+  memcpy(a->ptr, table, sizeof(void*) * n);
+  cudaError_t e = launch_kernel(x->nt, a, x->grid, x->smem, (cudaStream_t)stream);
+  return cuda_fail(e, "cudaLaunchCooperativeKernel(kk3_step_kernel)");
+}
+
+extern "C" int kk3_step(kk3_ctx* x, const void* const* table, int n, void* stream) {
+  return launch(x, table, n, stream, -1);
+}
+
+extern "C" int kk3_debug_step(kk3_ctx* x, const void* const* table, int n, void* stream, int stop_phase) {
+  return launch(x, table, n, stream, stop_phase < 0 ? -1 : stop_phase);
+}
+
+extern "C" int kk3_status(kk3_ctx* x) {
+  if (!x) return KK3_ERR_ARG;
+  const int e = *(volatile int*)x->err_host;
+  if (e == kErrTimeout) { x->failed = 1; return KK3_ERR_TIMEOUT; }
+  if (e != 0) { x->failed = 1; return KK3_ERR_DEVICE; }
+  return KK3_OK;
+}
+
+extern "C" int kk3_phase_count(kk3_ctx* x) {
+  if (!x) return KK3_ERR_ARG;
+  int v = 0;
+  if (cudaMemcpy(&v, x->s.phase_count, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return KK3_ERR_CUDA;
+  return v;
+}
+
+extern "C" int kk3_debug_buffer(kk3_ctx* x, int id, void** ptr, size_t* bytes) {
+  if (!x || id < 0 || id >= KK3_BUF_COUNT || !ptr || !bytes) return KK3_ERR_ARG;
+  *ptr = x->buf_ptr[id];
+  *bytes = x->buf_bytes[id];
+  return KK3_OK;
+}
+
+extern "C" int kk3_debug_copy(kk3_ctx* x, int id, void* dst, size_t bytes) {
+  if (!x || id < 0 || id >= KK3_BUF_COUNT || !dst || bytes > x->buf_bytes[id]) return KK3_ERR_ARG;
+  KK3_CUDA(cudaSetDevice(x->cfg.device));
+  KK3_CUDA(cudaMemcpy(dst, x->buf_ptr[id], bytes, cudaMemcpyDeviceToDevice));
+  return KK3_OK;
+}
+
+extern "C" void kk3_free(kk3_ctx* x) {
+  if (!x) return;
+  cudaSetDevice(x->cfg.device);
+  for (int r = 0; r < kMaxTp; ++r)
+    if (x->peer_open[r]) cudaIpcCloseMemHandle(x->peer_open[r]);
+  if (x->comm_local) cudaFree(x->comm_local);
+  if (x->scratch) cudaFree(x->scratch);
+  if (x->err_host) cudaFreeHost(x->err_host);
+  delete x->args;
+  delete x;
+}
+
+extern "C" int kk3_launch_config(kk3_ctx* x, int* grid, int* threads, size_t* smem) {
+  if (!x) return KK3_ERR_ARG;
+  if (grid) *grid = x->grid;
+  if (threads) *threads = kThreads;
+  if (smem) *smem = x->smem;
+  return KK3_OK;
+}

@@ -1,0 +1,20 @@
+// kk3_kernel_nt4.cu - step kernel instantiation for batches of up to 32 rows (4 MMA n-tile(s) of 8),
+// with its own launch helpers so no translation unit references another unit's kernel.
+#include <cuda_runtime.h>
+
+#include "kk3_kernel.cuh"
+
+namespace kk3 {
+
+cudaError_t prepare_nt4(size_t smem, int* occupancy) {
+  cudaError_t e = cudaFuncSetAttribute(kk3_step_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occupancy, kk3_step_kernel<4>, kThreads, smem);
+}
+
+cudaError_t launch_nt4(const StepArgs* args, int grid, size_t smem, cudaStream_t stream) {
+  void* params[] = {const_cast<StepArgs*>(args)};
+  return cudaLaunchCooperativeKernel((const void*)kk3_step_kernel<4>, dim3(grid), dim3(kThreads), params, smem, stream);
+}
+
+}  // namespace kk3

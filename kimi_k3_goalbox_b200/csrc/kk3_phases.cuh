@@ -1,0 +1,679 @@
+// kk3_phases.cuh - the non-GEMV phases of the decode step: per-row residual mixing and norms, the
+// one-shot tensor-parallel exchanges, KDA (gated delta rule), MLA (absorbed latent attention, split-K),
+// routing.
+#pragma once
+
+#include "kk3_gemv.cuh"
+
+namespace kk3 {
+
+// ------------------------------------------------------------------------------------------------
+// One-shot exchange over NVLink peer memory. Rank r writes its partial for batch row b into slot [r] of
+// every rank's region; the writer then publishes flag [b][r] = seq on every rank (release, system scope);
+// the reader acquires all tp flags of row b and sums the slots in rank order (FP32, kimi.py:343-347), so
+// every rank obtains bit-identical sums. Data regions alternate by exchange parity; flags carry a
+// monotonically increasing sequence number, so nothing is ever cleared.
+
+KK3_DEV unsigned* flag_ptr(const StepArgs& a, int dst, int b, int src) {
+  return reinterpret_cast<unsigned*>(a.comm.base[dst] + a.comm.flag_off) + (size_t)b * a.g.tp + src;
+}
+
+// called by a whole CTA after its writes of row b (all threads), tp > 1 only
+KK3_DEV void xch_signal_row(const StepArgs& a, int b, unsigned seq) {
+  __threadfence_system();
+  __syncthreads();
+  if ((int)threadIdx.x < a.g.tp) st_release_sys(flag_ptr(a, threadIdx.x, b, a.g.rank), seq);
+}
+
+KK3_DEV bool xch_wait_row(const StepArgs& a, int b, unsigned seq) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if ((int)threadIdx.x < a.g.tp) {
+    if (!wait_flag_sys(a, flag_ptr(a, a.g.rank, b, threadIdx.x), seq)) ok = 0;
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+// local region (this rank's buffer), parity p, byte offset `off`
+template <typename T>
+KK3_DEV const T* xlocal(const StepArgs& a, int parity, long long off) {
+  return reinterpret_cast<const T*>(a.comm.base[a.g.rank] + a.comm.data_off[parity] + off);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Row phase: block attention residual (kimi.py:199-204) followed by RMSNorm (common.py:13-21).
+// hidden = softmax_i(rms(v_i) . (norm*proj)) mixing of [blocks..., prefix] in FP32, cast to BF16;
+// out = bf16(bf16(hidden * rsqrt(mean(hidden^2) + eps)) * ln).
+
+constexpr int kMaxBlocks = 9;
+
+KK3_DEV void mix_and_norm(const StepArgs& a, int b, int nb, const bf16* norm, const bf16* proj, const bf16* ln,
+                          float eps, bf16* out_row, float* hbuf, float* red) {
+  const Geo& g = a.g;
+  const int tid = threadIdx.x;
+  const bf16* prefix = a.s.prefix + (size_t)b * g.h;
+  if (nb > 0) {
+    const int n = nb + 1;
+    float ss[kMaxBlocks + 1], dt[kMaxBlocks + 1];
+#pragma unroll
+    for (int i = 0; i <= kMaxBlocks; ++i) ss[i] = dt[i] = 0.0f;
+    for (int e = tid; e < g.h; e += kThreads) {
+      const float np = bf2f(norm[e]) * bf2f(proj[e]);
+#pragma unroll
+      for (int i = 0; i <= kMaxBlocks; ++i) {
+        if (i < n) {
+          const bf16* vec = (i < nb) ? a.s.blocks + ((size_t)i * g.B + b) * g.h : prefix;
+          const float v = bf2f(vec[e]);
+          ss[i] += v * v;
+          dt[i] += v * np;
+        }
+      }
+    }
+    // reduce 2n values over the CTA: warp sums, then per-warp partials in shared memory
+    float* part = red;   // [kWarps][2 * (kMaxBlocks+1)]
+    const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+    for (int i = 0; i <= kMaxBlocks; ++i) {
+      if (i < n) {
+        const float s1 = warp_sum(ss[i]), s2 = warp_sum(dt[i]);
+        if (lane == 0) {
+          part[warp * 2 * (kMaxBlocks + 1) + 2 * i] = s1;
+          part[warp * 2 * (kMaxBlocks + 1) + 2 * i + 1] = s2;
+        }
+      }
+    }
+    __syncthreads();
+    float* prob = red + kWarps * 2 * (kMaxBlocks + 1);   // [kMaxBlocks+1]
+    if (tid == 0) {
+      float logit[kMaxBlocks + 1];
+      float mx = -INFINITY;
+      for (int i = 0; i < n; ++i) {
+        float s1 = 0.0f, s2 = 0.0f;
+        for (int w = 0; w < kWarps; ++w) {
+          s1 += part[w * 2 * (kMaxBlocks + 1) + 2 * i];
+          s2 += part[w * 2 * (kMaxBlocks + 1) + 2 * i + 1];
+        }
+        logit[i] = s2 * rsqrtf(s1 / (float)g.h + 1e-5f);
+        mx = fmaxf(mx, logit[i]);
+      }
+      float tot = 0.0f;
+      for (int i = 0; i < n; ++i) {
+        logit[i] = expf(logit[i] - mx);
+        tot += logit[i];
+      }
+      for (int i = 0; i < n; ++i) prob[i] = logit[i] / tot;
+    }
+    __syncthreads();
+    float ssh = 0.0f;
+    for (int e = tid; e < g.h; e += kThreads) {
+      float acc = 0.0f;
+      for (int i = 0; i < n; ++i) {
+        const bf16* vec = (i < nb) ? a.s.blocks + ((size_t)i * g.B + b) * g.h : prefix;
+        acc += prob[i] * bf2f(vec[e]);
+      }
+      const float hv = round_bf(acc);
+      hbuf[e] = hv;
+      ssh += hv * hv;
+    }
+    const float tot = block_sum(ssh, red + kWarps * 2 * (kMaxBlocks + 1) + kMaxBlocks + 1);
+    const float rs = rsqrtf(tot / (float)g.h + eps);
+    for (int e = tid; e < g.h; e += kThreads) out_row[e] = f2bf(round_bf(hbuf[e] * rs) * bf2f(ln[e]));
+  } else {
+    float ssh = 0.0f;
+    for (int e = tid; e < g.h; e += kThreads) {
+      const float hv = bf2f(prefix[e]);
+      ssh += hv * hv;
+    }
+    const float tot = block_sum(ssh, red);
+    const float rs = rsqrtf(tot / (float)g.h + eps);
+    for (int e = tid; e < g.h; e += kThreads) out_row[e] = f2bf(round_bf(bf2f(prefix[e]) * rs) * bf2f(ln[e]));
+  }
+  __syncthreads();
+}
+
+// RMSNorm of one BF16 row of width n (common.py:13-21)
+KK3_DEV void rms_row(const bf16* in, const bf16* w, int n, float eps, bf16* out, float* red) {
+  float ss = 0.0f;
+  for (int e = threadIdx.x; e < n; e += kThreads) {
+    const float v = bf2f(in[e]);
+    ss += v * v;
+  }
+  const float tot = block_sum(ss, red);
+  const float rs = rsqrtf(tot / (float)n + eps);
+  for (int e = threadIdx.x; e < n; e += kThreads) out[e] = f2bf(round_bf(bf2f(in[e]) * rs) * bf2f(w[e]));
+  __syncthreads();
+}
+
+// Sum the tp BF16 partials of row b in an exchange sub-region (FP32, rank order) and round to BF16.
+KK3_DEV float xch_sum_bf16(const StepArgs& a, int parity, long long off, int b, int width, int e) {
+  const bf16* base = xlocal<bf16>(a, parity, off);
+  float acc = 0.0f;
+  for (int src = 0; src < a.g.tp; ++src) acc += bf2f(base[((size_t)src * a.g.B + b) * width + e]);
+  return round_bf(acc);
+}
+
+// ------------------------------------------------------------------------------------------------
+// KDA: one CTA per (batch row, head). Short convolution (kimi.py:286-289), f_a/f_b gate (:290),
+// beta (:291), gated delta rule on the V-first FP32 state (:207-215), gated per-head RMSNorm (:296-298).
+
+KK3_DEV void kda_item(const StepArgs& a, int layer, int kidx, int b, int hh, float* sm) {
+  const Geo& g = a.g;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int D = g.qdim, dh = 128;
+  float* sq = sm;            // [128] q after conv
+  float* sk = sm + 128;      // [128] k after conv
+  float* sv = sm + 256;      // [128] v after conv
+  float* decay = sm + 384;   // [128]
+  float* qn = sm + 512;      // [128]
+  float* kn = sm + 640;      // [128]
+  float* outv = sm + 768;    // [128]
+  float* fa = sm + 896;      // [128]
+  float* misc = sm + 1024;   // [32]
+  const bool keep = !reinterpret_cast<const bool*>(a.ptr[KK3_RESET])[b];
+  const bf16* conv_in = lptr<bf16>(a, layer, KK3_KDA_CONV_STATE);
+  const float* cw = lptr<float>(a, layer, KK3_KDA_CONV_WEIGHT);
+  bf16* conv_out = gout<bf16>(a, KK3_OUT_CONV_STATE) + (size_t)kidx * g.B * 3 * D * 4;
+  if (tid < 128) fa[tid] = bf2f(a.s.fa[(size_t)b * dh + tid]);
+  __syncthreads();
+  if (tid < 384) {
+    const int i = tid >> 7, dd = tid & 127, ch = hh * dh + dd;
+    const float raw = bf2f(a.s.qkv[((size_t)b * 3 + i) * D + ch]);
+    const size_t off = (((size_t)b * 3 + i) * D + ch) * 4;
+    float w1 = 0.0f, w2 = 0.0f, w3 = 0.0f;
+    if (keep) {
+      w1 = bf2f(conv_in[off + 1]);
+      w2 = bf2f(conv_in[off + 2]);
+      w3 = bf2f(conv_in[off + 3]);
+    }
+    bf16* co = conv_out + off;
+    co[0] = f2bf(w1);
+    co[1] = f2bf(w2);
+    co[2] = f2bf(w3);
+    co[3] = f2bf(raw);
+    const float* cwi = cw + ((size_t)i * D + ch) * 4;
+    const float s = w1 * cwi[0] + w2 * cwi[1] + w3 * cwi[2] + raw * cwi[3];
+    const float act = round_bf(s * sigmoidf_(s));
+    (i == 0 ? sq : (i == 1 ? sk : sv))[dd] = act;
+  } else {
+    const int dd = tid - 384, ch = hh * dh + dd;
+    const bf16* fb = lptr<bf16>(a, layer, KK3_KDA_FB) + (size_t)ch * dh;
+    float acc = 0.0f;
+    for (int e = 0; e < dh; e += 8) {
+      const uint4 w = *reinterpret_cast<const uint4*>(fb + e);
+      const bf16* wv = reinterpret_cast<const bf16*>(&w);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc += bf2f(wv[q]) * fa[e + q];
+    }
+    const float gate = round_bf(acc);
+    const float A = expf(lptr<float>(a, layer, KK3_KDA_A_LOG)[hh]);
+    const float dtb = lptr<float>(a, layer, KK3_KDA_DT_BIAS)[ch];
+    decay[dd] = expf(-5.0f * sigmoidf_(A * (gate + dtb)));
+  }
+  __syncthreads();
+  if (warp < 2) {
+    const float* src = warp == 0 ? sq : sk;
+    float v[4], ss = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      v[q] = src[lane * 4 + q];
+      ss += v[q] * v[q];
+    }
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss + 1e-6f);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (warp == 0) qn[lane * 4 + q] = v[q] * rs / 11.313708498984761f;
+      else kn[lane * 4 + q] = v[q] * rs;
+    }
+  } else if (warp == 2 && lane == 0) {
+    misc[0] = sigmoidf_(bf2f(a.s.beta[(size_t)b * g.hr + hh]));
+  }
+  __syncthreads();
+  const float sb = misc[0];
+  const float4 dk = *reinterpret_cast<const float4*>(decay + lane * 4);
+  const float4 kk = *reinterpret_cast<const float4*>(kn + lane * 4);
+  const float4 qq = *reinterpret_cast<const float4*>(qn + lane * 4);
+  const float* st_in = lptr<float>(a, layer, KK3_KDA_RECURRENT_STATE) + (((size_t)b * g.hr + hh) * dh) * dh;
+  float* st_out = gout<float>(a, KK3_OUT_RECURRENT_STATE) + ((((size_t)kidx * g.B + b) * g.hr + hh) * dh) * dh;
+  for (int v = warp * 8; v < warp * 8 + 8; ++v) {
+    float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (keep) s = *reinterpret_cast<const float4*>(st_in + (size_t)v * dh + lane * 4);
+    s.x *= dk.x; s.y *= dk.y; s.z *= dk.z; s.w *= dk.w;
+    const float pred = warp_sum(s.x * kk.x + s.y * kk.y + s.z * kk.z + s.w * kk.w);
+    const float err = (sv[v] - pred) * sb;
+    s.x += err * kk.x; s.y += err * kk.y; s.z += err * kk.z; s.w += err * kk.w;
+    const float o = warp_sum(s.x * qq.x + s.y * qq.y + s.z * qq.z + s.w * qq.w);
+    *reinterpret_cast<float4*>(st_out + (size_t)v * dh + lane * 4) = s;
+    if (lane == 0) outv[v] = o;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float o[4], ss = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      o[q] = round_bf(outv[lane * 4 + q]);
+      ss += o[q] * o[q];
+    }
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss / 128.0f + 1e-5f);
+    const float* onorm = lptr<float>(a, layer, KK3_KDA_ONORM);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int v = lane * 4 + q;
+      const float gt = sigmoidf_(bf2f(a.s.og[(size_t)b * D + hh * dh + v]));
+      a.s.attn_in[(size_t)b * D + hh * dh + v] = f2bf(o[q] * rs * onorm[v] * gt);
+    }
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------------------------------------------
+// MLA (kimi.py:263-283), absorbed latent form.
+
+// absorbed[b, h, c] = bf16(sum_d q[b, h, d] * kb[h*256 + d, c]), d < nr   (kimi.py:271-272)
+KK3_DEV void mla_absorb_item(const StepArgs& a, int layer, int hh, int cq, float* sm) {
+  const Geo& g = a.g;
+  const int tid = threadIdx.x;
+  const int c = cq * 128 + (tid & 127), dq = tid >> 7;   // 4 quarters of the 128 nope dims
+  const bf16* kb = lptr<bf16>(a, layer, KK3_MLA_KB);
+  float* qs = sm;                  // [B][128]
+  float* part = sm + g.B * 128;    // [4][16][128]
+  for (int i = tid; i < g.B * 128; i += kThreads) {
+    const int b = i >> 7, d = i & 127;
+    qs[i] = bf2f(a.s.mla_q[((size_t)b * g.hr + hh) * (g.nr + g.rd) + d]);
+  }
+  __syncthreads();
+  for (int b0 = 0; b0 < g.B; b0 += 16) {
+    float acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+    for (int d = dq * 32; d < dq * 32 + 32; ++d) {
+      const float w = bf2f(kb[((size_t)hh * (g.nr + g.vd) + d) * g.kr + c]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (b0 + i < g.B) acc[i] += qs[(b0 + i) * 128 + d] * w;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) part[(dq * 16 + i) * 128 + (tid & 127)] = acc[i];
+    __syncthreads();
+    if (dq == 0) {
+      for (int i = 0; i < 16 && b0 + i < g.B; ++i) {
+        const float s = part[(0 * 16 + i) * 128 + (tid & 127)] + part[(1 * 16 + i) * 128 + (tid & 127)] +
+                        part[(2 * 16 + i) * 128 + (tid & 127)] + part[(3 * 16 + i) * 128 + (tid & 127)];
+        a.s.absorbed[(((size_t)(b0 + i)) * g.hr + hh) * g.kr + c] = f2bf(s);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// shared-memory layout of one attention item
+constexpr int kRowK = 584;   // padded row (elements) of a cached position: 512 latent + 64 rope + 8 pad
+constexpr int kRowP = 40;    // padded row of the BF16 probability tile (32 positions + 8)
+constexpr int kRowS = 33;    // padded row of the FP32 score tile
+
+KK3_DEV unsigned smem_u32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+
+KK3_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+KK3_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+KK3_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+KK3_DEV void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+KK3_DEV void ldsm_x4(unsigned (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_u32(p)));
+}
+KK3_DEV void ldsm_x2(unsigned (&r)[2], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_u32(p)));
+}
+KK3_DEV void ldsm_x2_t(unsigned (&r)[2], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1]) : "r"(smem_u32(p)));
+}
+
+// stage positions [t0, t0+32) of row b (cache rows, the new token at t == ctx, zero beyond T)
+KK3_DEV void mla_stage(const StepArgs& a, int layer, int midx, int b, int t0, int T, bf16* dst) {
+  const Geo& g = a.g;
+  const bf16* kv = lptr<bf16>(a, layer, KK3_MLA_KV_CACHE);
+  const bf16* pe = lptr<bf16>(a, layer, KK3_MLA_PE_CACHE);
+  const bf16* kvw = gout<bf16>(a, KK3_OUT_KV_WRITE) + ((size_t)midx * g.B + b) * g.kr;
+  const bf16* pew = gout<bf16>(a, KK3_OUT_PE_WRITE) + ((size_t)midx * g.B + b) * g.rd;
+  const bool keep = !reinterpret_cast<const bool*>(a.ptr[KK3_RESET])[b];
+  for (int i = threadIdx.x; i < kMlaPos * 72; i += kThreads) {
+    const int tl = i / 72, q = i % 72, t = t0 + tl;
+    bf16* d = dst + tl * kRowK + q * 8;
+    // position index in the attended sequence: cache rows first (keep rows only), then the new token
+    const int ncache = keep ? g.ctx : 0;
+    if (t >= T) {
+      *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
+    } else if (t < ncache) {
+      const bf16* src = q < 64 ? kv + ((size_t)b * g.ctx + t) * g.kr + q * 8 : pe + ((size_t)b * g.ctx + t) * g.rd + (q - 64) * 8;
+      cp_async16(d, src);
+    } else {
+      const bf16* src = q < 64 ? kvw + q * 8 : pew + (q - 64) * 8;
+      *reinterpret_cast<uint4*>(d) = ld_act16(src);
+    }
+  }
+  cp_async_commit();
+}
+
+// One split-K item: batch row b, positions [p0, p1) of its attended sequence (T = ctx+1 or 1).
+// Writes (m, l, O[kr]) per head for the combine phase (flash-decoding with online softmax).
+KK3_DEV void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int chunk, int p0, int p1, int T,
+                             unsigned char* smem) {
+  const Geo& g = a.g;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, r = lane >> 2, c = lane & 3;
+  const int MT = g.mla_mt, HR = MT * 16;
+  const int qk = g.kr + g.rd;   // 576
+  bf16* Qs = reinterpret_cast<bf16*>(smem);                   // [HR][kRowK]
+  bf16* Ks = Qs + HR * kRowK;                                 // [2][32][kRowK]
+  float* Ss = reinterpret_cast<float*>(Ks + 2 * kMlaPos * kRowK);   // [HR][kRowS]
+  bf16* Ps = reinterpret_cast<bf16*>(Ss + HR * kRowS);        // [HR][kRowP]
+  float* mrun = reinterpret_cast<float*>(Ps + HR * kRowP);    // [HR]
+  float* lrun = mrun + HR;                                    // [HR]
+  float* alpha = lrun + HR;                                   // [HR]
+  const float scale = rsqrtf((float)(g.nr + g.rd));
+  // Q rows: absorbed (512) | q rope (64); zero for padded heads
+  for (int i = tid; i < HR * 72; i += kThreads) {
+    const int hh = i / 72, q = i % 72;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (hh < g.hr) {
+      if (q < 64) v = ld_act16(a.s.absorbed + (((size_t)b * g.hr + hh) * g.kr) + q * 8);
+      else v = ld_act16(a.s.mla_q + ((size_t)b * g.hr + hh) * (g.nr + g.rd) + g.nr + (q - 64) * 8);
+    }
+    *reinterpret_cast<uint4*>(Qs + hh * kRowK + q * 8) = v;
+  }
+  for (int i = tid; i < HR; i += kThreads) {
+    mrun[i] = -INFINITY;
+    lrun[i] = 0.0f;
+  }
+  // O accumulators: warp w owns latent dims [32w, 32w+32) for every head tile
+  float O[6][4][4];
+#pragma unroll
+  for (int mt = 0; mt < 6; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) O[mt][nt][i] = 0.0f;
+
+  const int nsub = (p1 - p0 + kMlaPos - 1) / kMlaPos;
+  mla_stage(a, layer, midx, b, p0, p1 < T ? p1 : T, Ks);
+  for (int s = 0; s < nsub; ++s) {
+    const int t0 = p0 + s * kMlaPos;
+    bf16* Kc = Ks + (s & 1) * kMlaPos * kRowK;
+    if (s + 1 < nsub) {
+      mla_stage(a, layer, midx, b, t0 + kMlaPos, p1 < T ? p1 : T, Ks + ((s + 1) & 1) * kMlaPos * kRowK);
+      cp_async_wait_one();
+    } else {
+      cp_async_wait_all();
+    }
+    __syncthreads();
+    // S = Q K^T over 576 dims: items (head tile, 8-position n-tile)
+    for (int it = warp; it < MT * 4; it += kWarps) {
+      const int mt = it >> 2, nt = it & 3;
+      float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int k0 = 0; k0 < qk; k0 += 16) {
+        unsigned af[4], bfr[2];
+        ldsm_x4(af, Qs + (mt * 16 + (lane & 15)) * kRowK + k0 + (lane >> 4) * 8);
+        ldsm_x2(bfr, Kc + (nt * 8 + (lane & 7)) * kRowK + k0 + ((lane >> 3) & 1) * 8);
+        mma_bf16(sacc, af[0], af[1], af[2], af[3], bfr[0], bfr[1]);
+      }
+      Ss[(mt * 16 + r) * kRowS + nt * 8 + 2 * c] = sacc[0] * scale;
+      Ss[(mt * 16 + r) * kRowS + nt * 8 + 2 * c + 1] = sacc[1] * scale;
+      Ss[(mt * 16 + r + 8) * kRowS + nt * 8 + 2 * c] = sacc[2] * scale;
+      Ss[(mt * 16 + r + 8) * kRowS + nt * 8 + 2 * c + 1] = sacc[3] * scale;
+    }
+    __syncthreads();
+    // online softmax, one warp per head row, one lane per position
+    for (int hh = warp; hh < HR; hh += kWarps) {
+      const bool valid = (t0 + lane) < p1 && (t0 + lane) < T && hh < g.hr;
+      const float sv = valid ? Ss[hh * kRowS + lane] : -INFINITY;
+      const float mt_ = warp_max(sv);
+      const float mold = mrun[hh];
+      const float mnew = fmaxf(mold, mt_);
+      const float p = valid ? expf(sv - mnew) : 0.0f;
+      const float ps = warp_sum(p);
+      Ps[hh * kRowP + lane] = f2bf(p);
+      if (lane == 0) {
+        const float al = (mold == -INFINITY) ? 0.0f : expf(mold - mnew);
+        alpha[hh] = (mnew == -INFINITY) ? 1.0f : al;
+        lrun[hh] = lrun[hh] * alpha[hh] + ps;
+        mrun[hh] = mnew;
+      }
+    }
+    __syncthreads();
+    // O = O * alpha + P V over this sub-tile: warp w owns dims [32w, 32w+32)
+#pragma unroll
+    for (int mt = 0; mt < 6; ++mt) {
+      if (mt < MT) {
+        const float a0 = alpha[mt * 16 + r], a1 = alpha[mt * 16 + r + 8];
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          O[mt][nt][0] *= a0; O[mt][nt][1] *= a0; O[mt][nt][2] *= a1; O[mt][nt][3] *= a1;
+        }
+      }
+    }
+#pragma unroll
+    for (int k0 = 0; k0 < kMlaPos; k0 += 16) {
+      unsigned bfr[4][2];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) ldsm_x2_t(bfr[nt], Kc + (k0 + (lane & 15)) * kRowK + warp * 32 + nt * 8);
+#pragma unroll
+      for (int mt = 0; mt < 6; ++mt) {
+        if (mt < MT) {
+          unsigned af[4];
+          ldsm_x4(af, Ps + (mt * 16 + (lane & 15)) * kRowP + k0 + (lane >> 4) * 8);
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) mma_bf16(O[mt][nt], af[0], af[1], af[2], af[3], bfr[nt][0], bfr[nt][1]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // write the partial: [b][chunk][h] x (m, l, O[512])
+  const int stride = g.kr + 2;
+  float* base = a.s.mla_part + (((size_t)b * g.mla_chunks + chunk) * g.hr) * stride;
+  for (int hh = tid; hh < g.hr; hh += kThreads) {
+    base[(size_t)hh * stride] = mrun[hh];
+    base[(size_t)hh * stride + 1] = lrun[hh];
+  }
+#pragma unroll
+  for (int mt = 0; mt < 6; ++mt) {
+    if (mt < MT) {
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int hh = mt * 16 + r + 8 * (i >> 1);
+          const int col = warp * 32 + nt * 8 + 2 * c + (i & 1);
+          if (hh < g.hr) base[(size_t)hh * stride + 2 + col] = O[mt][nt][i];
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Combine the split-K partials of (b, h), apply kb's value half and the sigmoid output gate
+// (kimi.py:280-282): out[d] = bf16(bf16(sum_c lat[c] * kb[h*256+128+d, c]) * bf16(sigmoid(og))).
+KK3_DEV void mla_combine_item(const StepArgs& a, int layer, int b, int hh, float* sm) {
+  const Geo& g = a.g;
+  const int tid = threadIdx.x;
+  const bool keep = !reinterpret_cast<const bool*>(a.ptr[KK3_RESET])[b];
+  const int nck = keep ? g.mla_chunks : 1;
+  const int stride = g.kr + 2;
+  const float* base = a.s.mla_part + (((size_t)b * g.mla_chunks) * g.hr + hh) * stride;
+  const size_t cstride = (size_t)g.hr * stride;
+  float* lat = sm;              // [512]
+  float* wgt = sm + 512;        // [chunks]
+  float* misc = sm + 512 + 64;  // [2]
+  if (tid == 0) {
+    float M = -INFINITY;
+    for (int i = 0; i < nck; ++i) M = fmaxf(M, ld_cg_f32(base + i * cstride));
+    float Lsum = 0.0f;
+    for (int i = 0; i < nck; ++i) {
+      const float m = ld_cg_f32(base + i * cstride);
+      const float w = (m == -INFINITY) ? 0.0f : expf(m - M);
+      wgt[i] = w;
+      Lsum += w * ld_cg_f32(base + i * cstride + 1);
+    }
+    misc[0] = 1.0f / Lsum;
+  }
+  __syncthreads();
+  for (int cc = tid; cc < g.kr; cc += kThreads) {
+    float acc = 0.0f;
+    for (int i = 0; i < nck; ++i) acc += wgt[i] * ld_cg_f32(base + i * cstride + 2 + cc);
+    lat[cc] = round_bf(acc * misc[0]);
+  }
+  __syncthreads();
+  // the attended latent (kimi.py:280) replaces the absorbed query in scratch, for diagnostics
+  for (int cc = tid; cc < g.kr; cc += kThreads)
+    a.s.absorbed[(((size_t)b) * g.hr + hh) * g.kr + cc] = f2bf(lat[cc]);
+  // value projection: 4 threads per output dim, 128 latent dims each
+  const bf16* kb = lptr<bf16>(a, layer, KK3_MLA_KB);
+  const int dv = tid >> 2, part = tid & 3;
+  float acc = 0.0f;
+  if (dv < g.vd) {
+    const bf16* row = kb + ((size_t)hh * (g.nr + g.vd) + g.nr + dv) * g.kr + part * 128;
+    for (int e = 0; e < 128; e += 8) {
+      const uint4 w = *reinterpret_cast<const uint4*>(row + e);
+      const bf16* wv = reinterpret_cast<const bf16*>(&w);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc += bf2f(wv[q]) * lat[part * 128 + e + q];
+    }
+  }
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+  if (dv < g.vd && part == 0) {
+    const float o = round_bf(acc);
+    const float gt = round_bf(sigmoidf_(bf2f(a.s.og[(size_t)b * g.hr * g.vd + hh * g.vd + dv])));
+    a.s.attn_in[(size_t)b * g.hr * g.vd + hh * g.vd + dv] = f2bf(o * gt);
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------------------------------------------
+// Routing (kimi.py:308-316) for all rows, by one CTA: FP32 sigmoid scores + bias, top-k (lowest index
+// wins ties), weights renormalised over the unbiased scores, ids sorted ascending. Then group the
+// (row, slot) pairs by expert into chunks of <= 8 pairs for the MXFP4 phases.
+KK3_DEV void route_all(const StepArgs& a, int layer, int moe_idx, unsigned char* smem) {
+  const Geo& g = a.g;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int* ids = reinterpret_cast<int*>(smem);            // [B*K]
+  int* cnt = ids + g.B * g.K;                          // [E]
+  int* off = cnt + kMaxExperts;                        // [E]
+  int* fill = off + kMaxExperts;                       // [E]
+  int* coff = fill + kMaxExperts;                      // [E] chunk offsets
+  const float* bias = lptr<float>(a, layer, KK3_MOE_ROUTER_BIAS);
+  long long* out_ids = gout<long long>(a, KK3_OUT_EXPERT_IDS) + (size_t)layer * g.B * g.K;
+  for (int e = tid; e < g.E; e += kThreads) {
+    cnt[e] = 0;
+    fill[e] = 0;
+  }
+  for (int b = warp; b < g.B; b += kWarps) {
+    const float* sc = a.s.scores + (size_t)b * g.E;
+    // candidates: biased score (NaN scores count as -inf); taken or padded entries are NaN, which never wins
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int e = lane + 32 * i;
+      const float x = e < g.E ? sc[e] + bias[e] : __int_as_float(0x7fc00000);
+      v[i] = (e < g.E && x != x) ? -INFINITY : x;
+    }
+    int mine = -1;   // lane j < K keeps the j-th selected expert
+    for (int j = 0; j < g.K; ++j) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int e = lane + 32 * i;
+        if (v[i] > bv || (v[i] == bv && e < bi)) {
+          bv = v[i];
+          bi = e;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if (lane == j) mine = bi;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i == (bi >> 5) && (bi & 31) == lane) v[i] = __int_as_float(0x7fc00000);
+    }
+    // sort the K ids ascending: rank of each
+    int rank = 0;
+    for (int j = 0; j < g.K; ++j) {
+      const int other = __shfl_sync(0xffffffffu, mine, j);
+      if (lane < g.K && other < mine) ++rank;
+    }
+    const float w = lane < g.K ? sc[mine] : 0.0f;
+    const float wsum = warp_sum(w);
+    if (lane < g.K) {
+      a.s.route_ids[b * g.K + rank] = mine;
+      a.s.route_w[b * g.K + rank] = w / (wsum + 1e-20f);
+      out_ids[(size_t)b * g.K + rank] = (long long)mine;
+      ids[b * g.K + rank] = mine;
+    }
+  }
+  __syncthreads();
+  const int npairs = g.B * g.K;
+  for (int i = tid; i < npairs; i += kThreads) atomicAdd(&cnt[ids[i]], 1);
+  __syncthreads();
+  if (warp == 0) {
+    // exclusive scans over experts of pair counts and chunk counts (one warp, 32 experts per step)
+    int run = 0, crun = 0;
+    for (int e0 = 0; e0 < g.E; e0 += 32) {
+      const int e = e0 + lane;
+      const int n = e < g.E ? cnt[e] : 0;
+      const int nc = (n + 7) / 8;
+      int incl = n, cincl = nc;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t1 = __shfl_up_sync(0xffffffffu, incl, o);
+        const int t2 = __shfl_up_sync(0xffffffffu, cincl, o);
+        if (lane >= o) {
+          incl += t1;
+          cincl += t2;
+        }
+      }
+      if (e < g.E) {
+        off[e] = run + incl - n;
+        coff[e] = crun + cincl - nc;
+      }
+      run += __shfl_sync(0xffffffffu, incl, 31);
+      crun += __shfl_sync(0xffffffffu, cincl, 31);
+    }
+    if (lane == 0) a.s.chunk_info[0] = crun;
+  }
+  __syncthreads();
+  for (int i = tid; i < npairs; i += kThreads) {
+    const int e = ids[i];
+    const int pos = off[e] + atomicAdd(&fill[e], 1);
+    a.s.pair_row[pos] = i / g.K;
+    a.s.pair_slot[pos] = i % g.K;
+  }
+  for (int e = tid; e < g.E; e += kThreads) {
+    const int n = cnt[e];
+    for (int q = 0; q * 8 < n; ++q) {
+      const int ci = coff[e] + q;
+      a.s.chunk_info[1 + ci * 3] = e;
+      a.s.chunk_info[2 + ci * 3] = off[e] + q * 8;
+      a.s.chunk_info[3 + ci * 3] = (n - q * 8) < 8 ? (n - q * 8) : 8;
+    }
+  }
+  (void)moe_idx;
+  __threadfence();
+  __syncthreads();
+}
+
+}  // namespace kk3

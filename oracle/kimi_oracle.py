@@ -279,6 +279,180 @@ def _rank_context(case, serial, tp_rank, group):
     return tp_rank, group
 
 
+class _Step:
+    """Mutable state of one decode step while the oracle walks the layers (kimi.py:249-340)."""
+
+    def __init__(self, case, values, serial, fp32, routes, tp_rank, group, trace):
+        self.case, self.values, self.routes = case, values, routes
+        self.serial = case["gpus"] == 1 if serial is None else serial
+        self.tp_rank, self.group = _rank_context(case, self.serial, tp_rank, group)
+        self.act = torch.float32 if fp32 else torch.bfloat16
+        self.p = _params(case)
+        self.device = values["token"].device
+        self.trace = trace
+        self.blocks, self.kv_out, self.pe_out, self.state_out = [], [], [], []
+        self.conv_out, self.chosen, self.shortfall = [], [], []
+        self.prefix = None
+        self.keep = ~values["reset"]
+
+    def cast(self, t):
+        return t.to(self.act)
+
+    def reduce(self, t):
+        return t if self.serial else _tp_sum(t, self.group)
+
+    def rec(self, key, t):
+        if self.trace is not None:
+            self.trace[key] = t.detach().clone()
+
+    def proj(self, name, x):
+        return self.cast(x) @ self.cast(self.values[name]).T
+
+
+def _embed(st):
+    """kimi.py:249-252: masked gather of this rank's vocabulary shard, TP sum."""
+    chunk = st.p["vocab"] // st.case["tp"]
+    offset = st.tp_rank * chunk
+    token = st.values["token"]
+    mine = (token >= offset) & (token < offset + chunk)
+    rows = torch.where(mine[:, None], st.values["embed"][(token - offset).clamp(0, chunk - 1)], 0)
+    st.prefix = st.cast(st.reduce(rows))
+    st.rec("embed", st.prefix)
+
+
+def _mla_attention(st, layer, x):
+    """kimi.py:263-283 (gated MLA, absorbed latent form, no rotary)."""
+    p, v, pre = st.p, st.values, f"l{layer}_"
+    B, hr = p["batch"], p["q_heads"] // st.case["tp"]
+    kr, nr, rd, vd = p["kv_lora_rank"], p["qk_nope_dim"], p["qk_rope_dim"], p["v_head_dim"]
+    q = st.proj(pre + "qb", rms_norm(st.proj(pre + "qa", x), v[pre + "qn"], 1e-6)).view(B, hr, nr + rd)
+    raw = st.proj(pre + "ka", x)
+    latent = rms_norm(raw[:, :kr], v[pre + "kn"], 1e-6)
+    pe = raw[:, kr:]
+    st.kv_out.append(latent)
+    st.pe_out.append(pe)
+    kb = st.cast(v[pre + "kb"]).view(hr, nr + vd, kr)
+    absorbed = torch.einsum("bhd,hdc->bhc", q[..., :nr], kb[:, :nr])
+    st.rec(pre + "q", q)
+    st.rec(pre + "absorbed", absorbed)
+    rows = []
+    for b in range(B):
+        lat, pos = latent[b:b + 1], pe[b:b + 1]
+        if st.keep[b]:
+            lat = torch.cat((st.cast(v[pre + "kv_cache"][b]), lat))
+            pos = torch.cat((st.cast(v[pre + "pe_cache"][b]), pos))
+        scores = (absorbed[b].float() @ lat.float().T + q[b, :, nr:].float() @ pos.float().T) / (nr + rd) ** 0.5
+        rows.append(st.cast(scores.softmax(-1)) @ lat)
+    mixed = torch.stack(rows)
+    st.rec(pre + "attn_latent", mixed)
+    out = torch.einsum("bhc,hdc->bhd", mixed, kb[:, nr:]).flatten(1)
+    out = out * st.proj(pre + "output_gate", x).sigmoid()
+    st.rec(pre + "attn_in", out)
+    return st.cast(st.reduce(st.proj(pre + "o", out)))
+
+
+def _kda_attention(st, layer, x):
+    """kimi.py:285-299 (short conv, f_a/f_b gate, beta, gated delta rule, gated per-head norm)."""
+    p, v, pre = st.p, st.values, f"l{layer}_"
+    B, hr, d = p["batch"], p["q_heads"] // st.case["tp"], p["head_dim"]
+    raw = torch.stack([st.proj(pre + n, x) for n in ("q", "k", "v")], 1)
+    old = v[pre + "conv_state"] * st.keep[:, None, None, None]
+    window = torch.cat((st.cast(old[..., 1:]), raw[..., None]), -1)
+    st.conv_out.append(window)
+    q, k, val = st.cast(F.silu((window.float() * v[pre + "conv_weight"].float()).sum(-1))).view(B, 3, hr, d).unbind(1)
+    gate = st.proj(pre + "fb", st.proj(pre + "fa", x)).view(B, hr, d)
+    beta = st.proj(pre + "beta", x)
+    state = v[pre + "recurrent_state"] * st.keep[:, None, None, None]
+    out, new_state = kda_update(q, k, val, gate, beta, v[pre + "A_log"], v[pre + "dt_bias"].view(hr, d), state)
+    st.state_out.append(new_state)
+    out = st.cast(out).float()
+    out = out * torch.rsqrt(out.square().mean(-1, keepdim=True) + 1e-5) * v[pre + "onorm"].float()
+    out = st.cast(out * st.proj(pre + "output_gate", x).view(B, hr, d).float().sigmoid())
+    st.rec(pre + "attn_in", out.flatten(1))
+    return st.cast(st.reduce(st.proj(pre + "o", out.flatten(1))))
+
+
+def _moe(st, layer, x):
+    """kimi.py:307-328 (router, top-k with bias, MXFP4 routed experts in the latent space, shared experts)."""
+    p, v, pre, act = st.p, st.values, f"l{layer}_", st.act
+    B = p["batch"]
+    scores = (x.float() @ v[pre + "router"].float().T).sigmoid()
+    biased = scores + v[pre + "router_bias"].float()
+    top = biased.topk(p["topk"], -1).indices
+    if st.routes is not None:
+        top = st.routes[layer].to(device=st.device, dtype=torch.int64)
+        kth = biased.topk(p["topk"], -1).values[:, -1]
+        st.shortfall.append((kth - biased.gather(1, top).min(-1).values).clamp_min(0))
+    w = scores.gather(1, top)
+    w = w / (w.sum(-1, keepdim=True) + 1e-20)
+    st.chosen.append(top.sort(-1).values)
+    latent = st.proj(pre + "latent_down", x)
+    st.rec(pre + "latent", latent)
+    total = torch.zeros(B, p["latent_hidden"], device=st.device)
+    for expert in top.unique().tolist():
+        rows, slots = (top == expert).nonzero(as_tuple=True)
+
+        def wt(kind, e=expert):
+            return decode_mxfp4(v[f"{pre}{kind}_blocks"][e], v[f"{pre}{kind}_scales"][e]).to(act)
+
+        y = st.cast(st.cast(situ(latent[rows] @ wt("gate").T, latent[rows] @ wt("up").T)) @ wt("down").T)
+        total.index_add_(0, rows, y.float() * w[rows, slots, None])
+    st.rec(pre + "expert_sum_local", total)
+    total = st.reduce(total)
+    routed = st.proj(pre + "latent_up", rms_norm(st.cast(total), v[pre + "latent_norm"], 1e-5))
+    shared = st.reduce(st.proj(pre + "shared_down", st.cast(situ(st.proj(pre + "shared_gate", x),
+                                                                 st.proj(pre + "shared_up", x)))))
+    st.rec(pre + "routed", routed)
+    st.rec(pre + "shared", st.cast(shared))
+    return routed + st.cast(shared)
+
+
+def _layer(st, layer):
+    """One decoder layer (kimi.py:256-329): block residual, attention, block residual, FFN."""
+    p, v, pre = st.p, st.values, f"l{layer}_"
+    hidden = block_mix(st.prefix, st.blocks, v["attention_res_norm"][layer], v["attention_res_proj"][layer],
+                       st.cast) if st.blocks else st.prefix
+    if layer % p["attn_res_block_size"] == 0:
+        st.blocks.append(st.prefix)
+        st.prefix = None
+    x = rms_norm(hidden, v["ln1"][layer], 1e-5)
+    st.rec(pre + "x_attn", x)
+    attention = _mla_attention(st, layer, x) if is_mla(st.case, layer) else _kda_attention(st, layer, x)
+    st.rec(pre + "attn", attention)
+    st.prefix = attention if st.prefix is None else st.prefix + attention
+    hidden = block_mix(st.prefix, st.blocks, v["mlp_res_norm"][layer], v["mlp_res_proj"][layer], st.cast)
+    x = rms_norm(hidden, v["ln2"][layer], 1e-5)
+    st.rec(pre + "x_mlp", x)
+    if layer < p["first_dense"]:
+        out = st.cast(st.reduce(st.proj(pre + "down", st.cast(situ(st.proj(pre + "gate", x), st.proj(pre + "up", x))))))
+        st.chosen.append(torch.full((p["batch"], p["topk"]), -1, device=st.device, dtype=torch.int64))
+        st.shortfall.append(torch.zeros(p["batch"], device=st.device))
+    else:
+        out = _moe(st, layer, x)
+    st.rec(pre + "mlp", out)
+    st.prefix = st.prefix + out
+    st.rec(pre + "prefix", st.prefix)
+
+
+def _head(st):
+    """kimi.py:330-340: output block residual, final norm, LM head, greedy token, outputs."""
+    p, v = st.p, st.values
+    chunk = p["vocab"] // st.case["tp"]
+    hidden = block_mix(st.prefix, st.blocks, v["output_res_norm"], v["output_res_proj"], st.cast)
+    x = rms_norm(hidden, v["fnorm"], 1e-5)
+    st.rec("x_head", x)
+    logits = st.proj("lm_head", x).float()
+    length = torch.where(v["reset"], 1, p["context"] + 1).to(torch.int64)
+    stack = lambda items: torch.stack(items) if items else torch.zeros(0, device=st.device)
+    result = {"logits": logits, "next_token": _argmax_sharded(logits, st.tp_rank * chunk, st.group, st.serial),
+              "kv_write": stack(st.kv_out), "pe_write": stack(st.pe_out),
+              "recurrent_state": stack(st.state_out), "conv_state": stack(st.conv_out),
+              "expert_ids": torch.stack(st.chosen), "cache_length": length}
+    if st.routes is not None:
+        result["route_shortfall"] = torch.stack(st.shortfall)
+    return result
+
+
 def reference(case, values, *, serial=None, fp32=False, routes=None, tp_rank=None, group=None, trace=None):
     """One decode step for one rank (kimi.py:230-340).
 
@@ -287,135 +461,31 @@ def reference(case, values, *, serial=None, fp32=False, routes=None, tp_rank=Non
     name this rank's TP position and process group when not serial (default: WORLD, rank % tp).
     `trace`, if a dict, receives per-layer intermediates (debugging aid for the CUDA path).
     """
-    serial = case["gpus"] == 1 if serial is None else serial
-    tp_rank, group = _rank_context(case, serial, tp_rank, group)
-    reduce = (lambda t: t) if serial else (lambda t: _tp_sum(t, group))
-    act = torch.float32 if fp32 else torch.bfloat16
-    cast = lambda t: t.to(act)
-    p, tp = _params(case), case["tp"]
-    d, hr, B = p["head_dim"], p["q_heads"] // tp, p["batch"]
-    chunk = p["vocab"] // tp
-    offset = tp_rank * chunk
-    device = values["token"].device
-    rec = (lambda k, t: trace.__setitem__(k, t.detach().clone())) if trace is not None else (lambda k, t: None)
+    st = _Step(case, values, serial, fp32, routes, tp_rank, group, trace)
+    _embed(st)
+    for layer in range(st.p["layers"]):
+        _layer(st, layer)
+    return _head(st)
 
-    def proj(name, x):
-        return cast(x) @ cast(values[name]).T
 
-    token, reset = values["token"], values["reset"]
-    mine = (token >= offset) & (token < offset + chunk)
-    prefix = torch.where(mine[:, None], values["embed"][(token - offset).clamp(0, chunk - 1)], 0)
-    prefix = cast(reduce(prefix))
-    rec("embed", prefix)
-    blocks, kv_out, pe_out, state_out, conv_out, chosen, shortfall = [], [], [], [], [], [], []
-    keep = ~reset
-    for layer in range(p["layers"]):
-        pre = f"l{layer}_"
-        hidden = block_mix(prefix, blocks, values["attention_res_norm"][layer],
-                           values["attention_res_proj"][layer], cast) if blocks else prefix
-        if layer % p["attn_res_block_size"] == 0:
-            blocks.append(prefix)
-            prefix = None
-        x = rms_norm(hidden, values["ln1"][layer], 1e-5)
-        rec(pre + "x_attn", x)
-        if is_mla(case, layer):
-            kr, nr, rd, vd = p["kv_lora_rank"], p["qk_nope_dim"], p["qk_rope_dim"], p["v_head_dim"]
-            q = proj(pre + "qb", rms_norm(proj(pre + "qa", x), values[pre + "qn"], 1e-6)).view(B, hr, nr + rd)
-            raw = proj(pre + "ka", x)
-            latent = rms_norm(raw[:, :kr], values[pre + "kn"], 1e-6)
-            pe = raw[:, kr:]
-            kv_out.append(latent)
-            pe_out.append(pe)
-            kb = cast(values[pre + "kb"]).view(hr, nr + vd, kr)
-            absorbed = torch.einsum("bhd,hdc->bhc", q[..., :nr], kb[:, :nr])
-            rec(pre + "q", q)
-            rec(pre + "absorbed", absorbed)
-            rows = []
-            for b in range(B):
-                lat, pos = latent[b:b + 1], pe[b:b + 1]
-                if keep[b]:
-                    lat = torch.cat((cast(values[pre + "kv_cache"][b]), lat))
-                    pos = torch.cat((cast(values[pre + "pe_cache"][b]), pos))
-                scores = (absorbed[b].float() @ lat.float().T + q[b, :, nr:].float() @ pos.float().T) / (nr + rd) ** 0.5
-                rows.append(cast(scores.softmax(-1)) @ lat)
-            mixed = torch.stack(rows)
-            rec(pre + "attn_latent", mixed)
-            out = torch.einsum("bhc,hdc->bhd", mixed, kb[:, nr:]).flatten(1)
-            out = out * proj(pre + "output_gate", x).sigmoid()
-            rec(pre + "attn_in", out)
-            attention = cast(reduce(proj(pre + "o", out)))
-        else:
-            raw = torch.stack([proj(pre + n, x) for n in ("q", "k", "v")], 1)
-            old = values[pre + "conv_state"] * keep[:, None, None, None]
-            window = torch.cat((cast(old[..., 1:]), raw[..., None]), -1)
-            conv_out.append(window)
-            q, k, v = cast(F.silu((window.float() * values[pre + "conv_weight"].float()).sum(-1))).view(B, 3, hr, d).unbind(1)
-            gate = proj(pre + "fb", proj(pre + "fa", x)).view(B, hr, d)
-            beta = proj(pre + "beta", x)
-            state = values[pre + "recurrent_state"] * keep[:, None, None, None]
-            out, new_state = kda_update(q, k, v, gate, beta, values[pre + "A_log"],
-                                        values[pre + "dt_bias"].view(hr, d), state)
-            state_out.append(new_state)
-            out = cast(out).float()
-            out = out * torch.rsqrt(out.square().mean(-1, keepdim=True) + 1e-5) * values[pre + "onorm"].float()
-            out = cast(out * proj(pre + "output_gate", x).view(B, hr, d).float().sigmoid())
-            rec(pre + "attn_in", out.flatten(1))
-            attention = cast(reduce(proj(pre + "o", out.flatten(1))))
-        rec(pre + "attn", attention)
-        prefix = attention if prefix is None else prefix + attention
-        hidden = block_mix(prefix, blocks, values["mlp_res_norm"][layer], values["mlp_res_proj"][layer], cast)
-        x = rms_norm(hidden, values["ln2"][layer], 1e-5)
-        rec(pre + "x_mlp", x)
-        if layer < p["first_dense"]:
-            out = cast(reduce(proj(pre + "down", cast(situ(proj(pre + "gate", x), proj(pre + "up", x))))))
-            chosen.append(torch.full((B, p["topk"]), -1, device=device, dtype=torch.int64))
-            shortfall.append(torch.zeros(B, device=device))
-        else:
-            scores = (x.float() @ values[pre + "router"].float().T).sigmoid()
-            biased = scores + values[pre + "router_bias"].float()
-            top = biased.topk(p["topk"], -1).indices
-            if routes is not None:
-                top = routes[layer].to(device=device, dtype=torch.int64)
-                kth = biased.topk(p["topk"], -1).values[:, -1]
-                shortfall.append((kth - biased.gather(1, top).min(-1).values).clamp_min(0))
-            w = scores.gather(1, top)
-            w = w / (w.sum(-1, keepdim=True) + 1e-20)
-            chosen.append(top.sort(-1).values)
-            latent = proj(pre + "latent_down", x)
-            rec(pre + "latent", latent)
-            total = torch.zeros(B, p["latent_hidden"], device=device)
-            for expert in top.unique().tolist():
-                rows, slots = (top == expert).nonzero(as_tuple=True)
-
-                def wt(kind, e=expert):
-                    return decode_mxfp4(values[f"{pre}{kind}_blocks"][e], values[f"{pre}{kind}_scales"][e]).to(act)
-
-                y = cast(cast(situ(latent[rows] @ wt("gate").T, latent[rows] @ wt("up").T)) @ wt("down").T)
-                total.index_add_(0, rows, y.float() * w[rows, slots, None])
-            rec(pre + "expert_sum_local", total)
-            total = reduce(total)
-            routed = proj(pre + "latent_up", rms_norm(cast(total), values[pre + "latent_norm"], 1e-5))
-            shared = reduce(proj(pre + "shared_down", cast(situ(proj(pre + "shared_gate", x),
-                                                                 proj(pre + "shared_up", x)))))
-            rec(pre + "routed", routed)
-            rec(pre + "shared", cast(shared))
-            out = routed + cast(shared)
-        rec(pre + "mlp", out)
-        prefix = prefix + out
-        rec(pre + "prefix", prefix)
-    hidden = block_mix(prefix, blocks, values["output_res_norm"], values["output_res_proj"], cast)
-    x = rms_norm(hidden, values["fnorm"], 1e-5)
-    rec("x_head", x)
-    logits = proj("lm_head", x).float()
-    length = torch.where(reset, 1, p["context"] + 1).to(torch.int64)
-    stack = lambda items: torch.stack(items) if items else torch.zeros(0, device=device)
-    result = {"logits": logits, "next_token": _argmax_sharded(logits, offset, group, serial),
-              "kv_write": stack(kv_out), "pe_write": stack(pe_out),
-              "recurrent_state": stack(state_out), "conv_state": stack(conv_out),
-              "expert_ids": torch.stack(chosen), "cache_length": length}
-    if routes is not None:
-        result["route_shortfall"] = torch.stack(shortfall)
-    return result
+def timed_sample(case, values, part):
+    """CPU-baseline sample: run one part of the BF16 step serially and return its wall time in seconds.
+    `part` is 'embed+head' or a layer index; the blocks/prefix context is a plausible stand-in (the cost of a
+    layer does not depend on it)."""
+    import time
+    st = _Step(case, values, True, False, None, 0, None, None)
+    _embed(st)
+    if part == "embed+head":
+        t0 = time.perf_counter()
+        _embed(st)
+        st.blocks = [st.prefix]
+        _head(st)
+        return time.perf_counter() - t0
+    layer = int(part)
+    st.blocks = [st.prefix]
+    t0 = time.perf_counter()
+    _layer(st, layer)
+    return time.perf_counter() - t0
 
 
 def _group_sum(t, group, serial):

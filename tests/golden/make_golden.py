@@ -113,6 +113,13 @@ def main(ref_root: str) -> None:
         torch.save(fx, HERE / f'{name}.pt')
     tp2 = tp_fixture(make_case(select_cases, dev, TINY, 2, gpus=2), 5, ref_root)
     torch.save(tp2, HERE / 'tiny_tp2_b2_s5.pt')
+    # the reference's HBM floor model (megabench/sol.py) on every case of its table
+    import json
+    from megabench.sol import estimate_case
+    sol = {c.id: {'minimum_bytes': estimate_case(c)['minimum_bytes'],
+                  'components': {x['name']: x['bytes'] for x in estimate_case(c)['components']}}
+           for c in select_cases('all')}
+    (HERE / 'sol_reference.json').write_text(json.dumps(sol, indent=1) + '\n')
     for path in sorted(HERE.glob('*.pt')):
         print(path.name, path.stat().st_size)
 
