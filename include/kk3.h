@@ -128,6 +128,12 @@ void kk3_free(kk3_ctx* ctx);
 /* Like kk3_step, but the kernel returns after `stop_phase` grid-wide phases (stop_phase < 0: all). */
 int kk3_debug_step(kk3_ctx* ctx, const void* const* table, int table_size, void* stream, int stop_phase);
 
+/* Run only phases [start_phase, stop_phase) (stop_phase < 0: to the end); earlier phases are skipped
+ * entirely, so their scratch results must already be in place (e.g. from a previous full step). Used to
+ * time and profile one phase in isolation. */
+int kk3_debug_phases(kk3_ctx* ctx, const void* const* table, int table_size, void* stream, int start_phase,
+                     int stop_phase);
+
 /* Number of grid-wide phases one step runs (known after the first step). */
 int kk3_phase_count(kk3_ctx* ctx);
 
@@ -135,7 +141,9 @@ int kk3_phase_count(kk3_ctx* ctx);
 enum kk3_debug_buffer_id {
     KK3_BUF_PREFIX = 0, KK3_BUF_XA, KK3_BUF_XM, KK3_BUF_ATTN_IN, KK3_BUF_SCORES, KK3_BUF_LATENT,
     KK3_BUF_SHARED_ACT, KK3_BUF_X3, KK3_BUF_ROUTE_W, KK3_BUF_QKV, KK3_BUF_MLA_Q, KK3_BUF_ABSORBED,
-    KK3_BUF_ATTN_LAT, KK3_BUF_EXPERT_SUM, KK3_BUF_BLOCKS, KK3_BUF_EXCHANGE, KK3_BUF_COUNT
+    KK3_BUF_ATTN_LAT, KK3_BUF_EXPERT_SUM, KK3_BUF_BLOCKS, KK3_BUF_EXCHANGE,
+    KK3_BUF_PHASE_TS, /* u64 globaltimer (ns) at kernel start and at the end of every grid phase */
+    KK3_BUF_COUNT
 };
 int kk3_debug_buffer(kk3_ctx* ctx, int id, void** ptr, size_t* bytes);
 

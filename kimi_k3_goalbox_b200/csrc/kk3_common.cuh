@@ -21,6 +21,7 @@ constexpr int kMaxTopk = 32;
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxPtrs = KK3_GLOBAL_SLOTS + 96 * KK3_LAYER_SLOTS;   // 3104 slots: up to 96 layers
 constexpr int kMlaPos = 32;            // cache positions per attention sub-tile
+constexpr int kMaxPhases = 2048;       // phase timestamp capacity (a 96-layer step has ~1500 phases)
 
 // device error word values (also the host-visible status)
 constexpr int kErrTimeout = 1;
@@ -61,14 +62,14 @@ struct Scratch {
   bf16* dense_act;    // [B, dinter]
   float* scores;      // [B, E] sigmoid router scores (FP32)
   bf16* latent;       // [B, lh]
-  __half* latent_p;   // [B, lh] FP16, group-permuted for the MXFP4 tensor-core path
+  __half* latent_p;   // [B, lh] FP16 copy of the latent: the activation operand of the MXFP4 experts
   bf16* shared_act;   // [B, sinter]
   int* route_ids;     // [B, K] sorted expert ids of the current layer
   float* route_w;     // [B, K] renormalised weights (same order)
   int* pair_row;      // [B*K] pair -> batch row, grouped by expert
   int* pair_slot;     // [B*K] pair -> slot j
   int* chunk_info;    // [1 + B*K*3]: count, then (expert, first pair, pairs) per expert chunk of <= 8 pairs
-  __half* act_p;      // [B*K, inter] FP16 permuted expert activations
+  __half* act_p;      // [B*K, inter] FP16 expert activations (operand of the down projection)
   bf16* out_slot;     // [B, K, lh] per-slot expert outputs
   bf16* x3;           // [B, lh] latent_norm(expert_sum)
   bf16* shared_red;   // [B, h] reduced shared-expert output
@@ -77,8 +78,10 @@ struct Scratch {
   int* fix_cnt;       // [max tiles] stream-K arrival counters
   unsigned long long* argmax_key; // [B]
   unsigned* bar;      // [2] grid barrier: count, generation
-  int* err;           // device error word (mapped host memory)
+  int* err;           // device error word, polled by every wait (device memory: cheap to poll)
+  int* err_host;      // host-visible copy in mapped host memory, written only when an error is raised
   int* phase_count;   // number of grid phases of the last complete step
+  unsigned long long* phase_ts;  // [kMaxPhases + 1] globaltimer at kernel start and at the end of each phase
 };
 
 // One-shot exchange buffers, symmetric across ranks (this rank's and peers' mapped copies).
@@ -97,6 +100,7 @@ struct StepArgs {
   Comm comm;
   unsigned epoch;       // step counter (1, 2, ...), orders the peer flags
   int stop_phase;       // debug: return after this many grid phases (-1: run everything)
+  int start_phase;      // debug: skip the work (and barriers) of phases before this one (0: run everything)
   int nptr;
   const void* ptr[kMaxPtrs];
 };
@@ -173,31 +177,6 @@ KK3_DEV float e8m0_to_f32(unsigned s) {
   return v;
 }
 
-// Eight E2M1 nibbles of one 32-bit word -> four FP16x2 registers holding the exact E2M1 values.
-// Register j holds nibbles (j, j+4): the layout expected by the permuted activation operand.
-// The nibble's 3 magnitude bits land in the FP16 exponent/mantissa boundary (value * 2^-14, exact
-// for every code, including the subnormal 0.5 -> 2^-15), then one FP16x2 multiply by 2^14 restores it.
-KK3_DEV void e2m1x8_to_f16(unsigned w, unsigned (&r)[4]) {
-  const unsigned mag = 0x0E000E00u, sgn = 0x80008000u;
-  unsigned a = ((w << 9) & mag) | ((w << 12) & sgn);
-  unsigned b = ((w << 5) & mag) | ((w << 8) & sgn);
-  unsigned c = ((w << 1) & mag) | ((w << 4) & sgn);
-  unsigned d = ((w >> 3) & mag) | (w & sgn);
-  const __half2 k = __halves2half2(__ushort_as_half(0x7400), __ushort_as_half(0x7400));   // 16384
-  __half2 ha = __hmul2(*reinterpret_cast<__half2*>(&a), k);
-  __half2 hb = __hmul2(*reinterpret_cast<__half2*>(&b), k);
-  __half2 hc = __hmul2(*reinterpret_cast<__half2*>(&c), k);
-  __half2 hd = __hmul2(*reinterpret_cast<__half2*>(&d), k);
-  r[0] = *reinterpret_cast<unsigned*>(&ha);
-  r[1] = *reinterpret_cast<unsigned*>(&hb);
-  r[2] = *reinterpret_cast<unsigned*>(&hc);
-  r[3] = *reinterpret_cast<unsigned*>(&hd);
-}
-
-// position of element k inside its 8-element group in the permuted FP16 activation layout:
-// order [k0,k4,k1,k5,k2,k6,k3,k7]
-KK3_DEV int perm8(int k) { return (k & ~7) | ((k & 3) << 1) | ((k >> 2) & 1); }
-
 // D = A*B + C, m16n8k16, BF16 inputs, FP32 accumulate
 KK3_DEV void mma_bf16(float (&d)[4], unsigned a0, unsigned a1, unsigned a2, unsigned a3, unsigned b0, unsigned b1) {
   asm volatile(
@@ -244,7 +223,12 @@ KK3_DEV const T* lptr(const StepArgs& a, int layer, int slot) {
 template <typename T>
 KK3_DEV T* gout(const StepArgs& a, int slot) { return reinterpret_cast<T*>(const_cast<void*>(a.ptr[slot])); }
 
-KK3_DEV void set_error(const StepArgs& a, int code) { atomicCAS(a.s.err, 0, code); }
+KK3_DEV void set_error(const StepArgs& a, int code) {
+  if (atomicCAS(a.s.err, 0, code) == 0) {
+    *reinterpret_cast<volatile int*>(a.s.err_host) = code;
+    __threadfence_system();
+  }
+}
 KK3_DEV bool failed(const StepArgs& a) { return ld_volatile_int(a.s.err) != 0; }
 
 // Bounded grid-wide barrier (sense reversal on a generation counter). Returns false when the wait ran

@@ -12,9 +12,12 @@
 // router must agree bit for bit across tensor-parallel ranks). The finishing warp runs the fused epilogue
 // (BF16 rounding where the reference rounds, sigmoid, SiLU-like `situ`, argmax keys, peer exchange stores).
 //
-// Weights are permuted along k in registers: lane (r = lane/4, c = lane%4) loads 16 contiguous bytes of rows
-// r and r+8 at k = 64s + 8c and 64s + 32 + 8c, so one warp load covers 64 contiguous bytes per row; the
+// Weights are permuted along k in registers: lane (r = lane/4, c = lane%4) owns 16 contiguous bytes of rows
+// r and r+8 at k = 64s + 8c and 64s + 32 + 8c, so one warp covers 64 contiguous bytes per row; the
 // activation operand is read with the same permutation, which leaves the dot product unchanged.
+// Bytes in flight: every warp streams its unit range through a private ring of cp.async stages in shared
+// memory (6 k-steps deep, 2 KB each), so ~190 KB per SM are outstanding without holding registers; the
+// producer cursor runs continuously across tile boundaries.
 #pragma once
 
 #include "kk3_common.cuh"
@@ -25,7 +28,7 @@ enum Epi : int {
   EPI_STORE_BF16 = 0,   // out bf16 [col, ldo]
   EPI_SIGMOID_F32,      // out f32 [col, ldo] = sigmoid(acc)         (router scores, kimi.py:308)
   EPI_SITU,             // dual job: out bf16 = situ(bf16 gate, bf16 up) (kimi.py:194-196, :304, :326)
-  EPI_LATENT,           // out bf16 [col, ldo] and out2 f16 permuted copy for the MXFP4 path
+  EPI_LATENT,           // out bf16 [col, ldo] and out2 an FP16 copy for the MXFP4 path
   EPI_LOGITS,           // out f32 [col, ldo] = bf16-rounded logits, argmax keys (kimi.py:331, :218-227)
   EPI_ROUTED,           // prefix[col, row] += bf16(bf16(acc) + shared_red[col, row]) (kimi.py:325-329)
   EPI_EXCHANGE,         // bf16(acc) into every rank's exchange region [src][col][row] (kimi.py:343-347)
@@ -47,44 +50,42 @@ constexpr int kMaxJobs = 8;
 
 KK3_DEV long long owner_of(long long u, long long U, long long GW) { return ((u + 1) * GW - 1) / U; }
 
+KK3_DEV void cp_async16_g(void* smem_dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(smem_dst)),
+               "l"(src) : "memory");
+}
+KK3_DEV void cp_async_commit_g() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+KK3_DEV void cp_async_wait_g() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// One 64-wide k-step of a 16-row tile: A fragments from this lane's ring slot, activations from global.
 template <int NT, int MT>
-KK3_DEV void mma_rows_bf16(const bf16* const (&wa)[MT], const bf16* const (&wb)[MT], const bf16* __restrict__ x,
-                           int ldx, int ncols, int ks0, int ks1, float (&acc)[MT][NT][4]) {
+KK3_DEV void mma_step_bf16(const uint4* __restrict__ slot, const bf16* __restrict__ x, int ldx, int ncols, int ks,
+                           float (&acc)[MT][NT][4]) {
   const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
-  const bf16* xr[NT];
-  bool xv[NT];
+  uint4 A0[MT], A1[MT], B0[MT], B1[MT];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    A0[mt] = slot[(mt * 4 + 0) * 32 + lane];
+    A1[mt] = slot[(mt * 4 + 1) * 32 + lane];
+    B0[mt] = slot[(mt * 4 + 2) * 32 + lane];
+    B1[mt] = slot[(mt * 4 + 3) * 32 + lane];
+  }
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int n = nt * 8 + r;
-    xv[nt] = n < ncols;
-    xr[nt] = x + (size_t)(xv[nt] ? n : 0) * ldx + 8 * c;
-  }
-  constexpr int kUnroll = (NT * MT <= 2) ? 4 : ((NT * MT <= 4) ? 2 : 1);
-#pragma unroll kUnroll
-  for (int ks = ks0; ks < ks1; ++ks) {
-    const int k0 = ks * 64 + 8 * c;
-    uint4 A0[MT], A1[MT], B0[MT], B1[MT];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      A0[mt] = ldg_stream16(wa[mt] + k0);
-      A1[mt] = ldg_stream16(wa[mt] + k0 + 32);
-      B0[mt] = ldg_stream16(wb[mt] + k0);
-      B1[mt] = ldg_stream16(wb[mt] + k0 + 32);
+    uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
+    if (n < ncols) {
+      const bf16* xr = x + (size_t)n * ldx + ks * 64 + 8 * c;
+      X0 = ld_act16(xr);
+      X1 = ld_act16(xr + 32);
     }
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
-      if (xv[nt]) {
-        X0 = ld_act16(xr[nt] + ks * 64);
-        X1 = ld_act16(xr[nt] + ks * 64 + 32);
-      }
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        mma_bf16(acc[mt][nt], A0[mt].x, B0[mt].x, A0[mt].y, B0[mt].y, X0.x, X0.y);
-        mma_bf16(acc[mt][nt], A0[mt].z, B0[mt].z, A0[mt].w, B0[mt].w, X0.z, X0.w);
-        mma_bf16(acc[mt][nt], A1[mt].x, B1[mt].x, A1[mt].y, B1[mt].y, X1.x, X1.y);
-        mma_bf16(acc[mt][nt], A1[mt].z, B1[mt].z, A1[mt].w, B1[mt].w, X1.z, X1.w);
-      }
+    for (int mt = 0; mt < MT; ++mt) {
+      mma_bf16(acc[mt][nt], A0[mt].x, B0[mt].x, A0[mt].y, B0[mt].y, X0.x, X0.y);
+      mma_bf16(acc[mt][nt], A0[mt].z, B0[mt].z, A0[mt].w, B0[mt].w, X0.z, X0.w);
+      mma_bf16(acc[mt][nt], A1[mt].x, B1[mt].x, A1[mt].y, B1[mt].y, X1.x, X1.y);
+      mma_bf16(acc[mt][nt], A1[mt].z, B1[mt].z, A1[mt].w, B1[mt].w, X1.z, X1.w);
     }
   }
 }
@@ -163,7 +164,7 @@ KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const 
         case EPI_LATENT: {
           const bf16 b = f2bf(v);
           reinterpret_cast<bf16*>(j.out)[o] = b;
-          reinterpret_cast<__half*>(j.out2)[(size_t)col * j.ldo + perm8(row)] = __float2half_rn(bf2f(b));
+          reinterpret_cast<__half*>(j.out2)[(size_t)col * j.ldo + row] = __float2half_rn(bf2f(b));
           break;
         }
         case EPI_ROUTED: {
@@ -188,104 +189,162 @@ KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const 
   }
 }
 
+// Deterministic combination of a tile split over warps first..lastw (see the file comment). `acc` is this
+// warp's partial; slot 0/1 of a warp holds its first/other partial tile. Returns true (with the complete
+// tile in `acc`) when this warp arrived last and must run the epilogue.
+template <int NV>
+KK3_DEV bool stream_k_fixup(const StepArgs& a, float* part_base, int* cnt, long long gw, bool first_seg,
+                            long long tile_beg, long long first, long long lastw, long long U, long long GW,
+                            float (&acc)[NV]) {
+  const int lane = threadIdx.x & 31;
+  float* slot = part_base + (size_t)(gw * 2 + (first_seg ? 0 : 1)) * (NV * 32);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) slot[i * 32 + lane] = acc[i];
+  __threadfence();
+  __syncwarp();
+  int old = 0;
+  if (lane == 0) old = atomicAdd(cnt, 1);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if (old != (int)(lastw - first)) return false;
+  __threadfence();
+  float sum[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) sum[i] = 0.0f;
+  for (long long w = first; w <= lastw; ++w) {
+    if (w == gw) {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) sum[i] += acc[i];
+    } else {
+      const long long wbeg = U * w / GW;
+      const float* ps = part_base + (size_t)(w * 2 + (wbeg >= tile_beg ? 0 : 1)) * (NV * 32);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) sum[i] += ld_cg_f32(ps + i * 32 + lane);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) acc[i] = sum[i];
+  if (lane == 0) atomicExch(cnt, 0);
+  return true;
+}
+
+// position of a unit in a job list
+struct Cursor {
+  int ji, tile, ks;
+};
+
+KK3_DEV Cursor locate(const GemvJob* jobs, long long u) {
+  Cursor c;
+  c.ji = 0;
+  while (u >= jobs[c.ji].ubase + (long long)jobs[c.ji].tiles * jobs[c.ji].ksteps) ++c.ji;
+  const long long local = u - jobs[c.ji].ubase;
+  c.tile = (int)(local / jobs[c.ji].ksteps);
+  c.ks = (int)(local % jobs[c.ji].ksteps);
+  return c;
+}
+
+KK3_DEV void advance(Cursor& c, const GemvJob* jobs) {
+  if (++c.ks == jobs[c.ji].ksteps) {
+    c.ks = 0;
+    if (++c.tile == jobs[c.ji].tiles) {
+      c.tile = 0;
+      ++c.ji;
+    }
+  }
+}
+
+// stage this lane's 16-byte pieces of one unit (rows r, r+8; k = 64ks + 8c and +32) into its ring slot
+template <int MT>
+KK3_DEV void issue_bf16(const GemvJob& j, const Cursor& c, uint4* slot) {
+  const int lane = threadIdx.x & 31, r = lane >> 2, cc = lane & 3;
+  int ra = c.tile * 16 + r, rb = ra + 8;
+  ra = ra < j.rows ? ra : j.rows - 1;
+  rb = rb < j.rows ? rb : j.rows - 1;
+  const int k0 = c.ks * 64 + 8 * cc;
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    const bf16* base = (mt == 0) ? j.w : j.w2;
+    const bf16* pa = base + (size_t)ra * j.K + k0;
+    const bf16* pb = base + (size_t)rb * j.K + k0;
+    cp_async16_g(slot + (mt * 4 + 0) * 32 + lane, pa);
+    cp_async16_g(slot + (mt * 4 + 1) * 32 + lane, pa + 32);
+    cp_async16_g(slot + (mt * 4 + 2) * 32 + lane, pb);
+    cp_async16_g(slot + (mt * 4 + 3) * 32 + lane, pb + 32);
+  }
+}
+
+constexpr int kGemvSmemPerWarp = 12 * 1024;   // ring bytes per warp (6 stages x 2 KB, or 3 x 4 KB)
+
 // Run a list of dense BF16 jobs with warp-level stream-K over CTAs [cta_lo, cta_hi).
 template <int NT, int MT>
 KK3_DEV void run_gemv(const StepArgs& a, const GemvJob* jobs, int njobs, int cta_lo, int cta_hi, int parity,
                          int bank = 0) {
   if ((int)blockIdx.x < cta_lo || (int)blockIdx.x >= cta_hi) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 2;
-  const GemvJob& last = jobs[njobs - 1];
-  const long long U = last.ubase + (long long)last.tiles * last.ksteps;
+  extern __shared__ __align__(16) unsigned char kk3_dyn_smem[];
+  constexpr int S = (MT == 1) ? 6 : 3;   // ring depth in units
+  constexpr int kSlotVec = MT * 4 * 32;  // uint4 per unit slot
+  const int warp = threadIdx.x >> 5;
+  const GemvJob& lastj = jobs[njobs - 1];
+  const long long U = lastj.ubase + (long long)lastj.tiles * lastj.ksteps;
   long long GW = (long long)(cta_hi - cta_lo) * kWarps;
   GW = GW < U ? GW : U;
   const long long gw = (long long)(blockIdx.x - cta_lo) * kWarps + warp;
   if (U == 0 || gw >= GW) return;
   const long long ubeg = U * gw / GW, uend = U * (gw + 1) / GW;
-  constexpr int kSlot = MT * NT * 128;   // floats per partial tile
-  float* my_slot0 = a.s.fix_part + bank * a.g.fix_bank + (size_t)(gw * 2) * kSlot;
-  int ji = 0;
-  for (long long u = ubeg; u < uend;) {
-    while (u >= jobs[ji].ubase + (long long)jobs[ji].tiles * jobs[ji].ksteps) ++ji;
-    const GemvJob& j = jobs[ji];
-    const long long local = u - j.ubase;
-    const int tile = (int)(local / j.ksteps);
-    const int ks0 = (int)(local % j.ksteps);
-    const long long tile_beg = j.ubase + (long long)tile * j.ksteps, tile_end = tile_beg + j.ksteps;
-    const long long seg_end = uend < tile_end ? uend : tile_end;
-    const int ks1 = ks0 + (int)(seg_end - u);
+  uint4* ring = reinterpret_cast<uint4*>(kk3_dyn_smem + (size_t)warp * kGemvSmemPerWarp);
+  float* part_base = a.s.fix_part + bank * a.g.fix_bank;
+  int* cnt_base = a.s.fix_cnt + bank * a.g.cnt_bank;
 
-    const bf16* wa[MT];
-    const bf16* wb[MT];
-    {
-      int ra = tile * 16 + r, rb = ra + 8;
-      ra = ra < j.rows ? ra : j.rows - 1;
-      rb = rb < j.rows ? rb : j.rows - 1;
+  Cursor pc = locate(jobs, ubeg);
+  Cursor cc = pc;
+  long long pu = ubeg;
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const bf16* base = (mt == 0) ? j.w : j.w2;
-        wa[mt] = base + (size_t)ra * j.K;
-        wb[mt] = base + (size_t)rb * j.K;
-      }
+  for (int i = 0; i < S - 1; ++i) {
+    if (pu < uend) {
+      issue_bf16<MT>(jobs[pc.ji], pc, ring + (int)((pu - ubeg) % S) * kSlotVec);
+      advance(pc, jobs);
+      ++pu;
     }
-    float acc[MT][NT][4];
+    cp_async_commit_g();
+  }
+  float acc[MT][NT][4];
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+  for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[mt][nt][i] = 0.0f;
-    mma_rows_bf16<NT, MT>(wa, wb, j.x, j.ldx, j.ncols, ks0, ks1, acc);
-
-    const long long first = owner_of(tile_beg, U, GW), lastw = owner_of(tile_end - 1, U, GW);
-    if (first == lastw) {
-      gemv_epilogue<NT, MT>(a, j, tile, acc, parity);
-    } else {
-      float* slot = my_slot0 + (u == ubeg ? 0 : kSlot);
+      for (int i = 0; i < 4; ++i) acc[mt][nt][i] = 0.0f;
+  long long seg_start = ubeg;
+  for (long long u = ubeg; u < uend; ++u) {
+    if (pu < uend) {
+      issue_bf16<MT>(jobs[pc.ji], pc, ring + (int)((pu - ubeg) % S) * kSlotVec);
+      advance(pc, jobs);
+      ++pu;
+    }
+    cp_async_commit_g();
+    cp_async_wait_g<S - 1>();
+    const GemvJob& j = jobs[cc.ji];
+    mma_step_bf16<NT, MT>(ring + (int)((u - ubeg) % S) * kSlotVec, j.x, j.ldx, j.ncols, cc.ks, acc);
+    if (cc.ks == j.ksteps - 1 || u == uend - 1) {
+      const long long tile_beg = j.ubase + (long long)cc.tile * j.ksteps;
+      const long long first = owner_of(tile_beg, U, GW), lastw = owner_of(tile_beg + j.ksteps - 1, U, GW);
+      bool done = first == lastw;
+      if (!done) {
+        done = stream_k_fixup<MT * NT * 4>(a, part_base, cnt_base + j.tile0 + cc.tile, gw, seg_start == ubeg,
+                                           tile_beg, first, lastw, U, GW,
+                                           *reinterpret_cast<float(*)[MT * NT * 4]>(&acc[0][0][0]));
+      }
+      if (done) gemv_epilogue<NT, MT>(a, j, cc.tile, acc, parity);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) slot[((mt * NT + nt) * 4 + i) * 32 + lane] = acc[mt][nt][i];
-      __threadfence();
-      __syncwarp();
-      int old = 0;
-      if (lane == 0) old = atomicAdd(a.s.fix_cnt + bank * a.g.cnt_bank + j.tile0 + tile, 1);
-      old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == (int)(lastw - first)) {
-        __threadfence();
-        float sum[MT][NT][4];
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) sum[mt][nt][i] = 0.0f;
-        for (long long w = first; w <= lastw; ++w) {
-          if (w == gw) {
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) sum[mt][nt][i] += acc[mt][nt][i];
-          } else {
-            const long long wbeg = U * w / GW;
-            const float* ps = a.s.fix_part + bank * a.g.fix_bank + (size_t)(w * 2 + (wbeg >= tile_beg ? 0 : 1)) * kSlot;
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) sum[mt][nt][i] += ld_cg_f32(ps + ((mt * NT + nt) * 4 + i) * 32 + lane);
-          }
-        }
-        gemv_epilogue<NT, MT>(a, j, tile, sum, parity);
-        if (lane == 0) atomicExch(a.s.fix_cnt + bank * a.g.cnt_bank + j.tile0 + tile, 0);
-      }
+          for (int i = 0; i < 4; ++i) acc[mt][nt][i] = 0.0f;
+      seg_start = u + 1;
     }
-    u = seg_end;
+    advance(cc, jobs);
   }
+  cp_async_wait_g<0>();
 }
 
 // Finalise job unit bases / tile counts (all threads compute identical values).
@@ -306,35 +365,6 @@ KK3_DEV void prepare_jobs(GemvJob* jobs, int njobs) {
 // MXFP4 routed experts (e2m1 codes [rows, K/32, 16] + E8M0 scales [rows, K/32], kimi.py:116-119).
 // One n-tile of <= 8 (expert, token) pairs per unit; the 32-wide scale groups are applied to the FP32
 // accumulator exactly (one zero-initialised 2-step MMA per group, then acc += t * 2^(s-127)).
-
-template <int MT>
-KK3_DEV void mma_rows_fp4(const uint8_t* const (&ca)[MT], const uint8_t* const (&cb)[MT],
-                          const uint8_t* const (&sa)[MT], const uint8_t* const (&sb)[MT],
-                          const __half* xrow, int ks0, int ks1, float (&acc)[MT][4]) {
-  const int lane = threadIdx.x & 31, c = lane & 3;
-#pragma unroll 2
-  for (int g = ks0 * 2; g < ks1 * 2; ++g) {
-    uint4 X = make_uint4(0, 0, 0, 0);
-    if (xrow) X = ld_act16(xrow + g * 32 + 8 * c);
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      const unsigned wa = ldg_nc32(ca[mt] + g * 16 + 4 * c);
-      const unsigned wb = ldg_nc32(cb[mt] + g * 16 + 4 * c);
-      const float fa = e8m0_to_f32(ldg_nc8(sa[mt] + g));
-      const float fb = e8m0_to_f32(ldg_nc8(sb[mt] + g));
-      unsigned ra[4], rb[4];
-      e2m1x8_to_f16(wa, ra);
-      e2m1x8_to_f16(wb, rb);
-      float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      mma_f16(t, ra[0], rb[0], ra[1], rb[1], X.x, X.y);
-      mma_f16(t, ra[2], rb[2], ra[3], rb[3], X.z, X.w);
-      acc[mt][0] = fmaf(t[0], fa, acc[mt][0]);
-      acc[mt][1] = fmaf(t[1], fa, acc[mt][1]);
-      acc[mt][2] = fmaf(t[2], fb, acc[mt][2]);
-      acc[mt][3] = fmaf(t[3], fb, acc[mt][3]);
-    }
-  }
-}
 
 struct ExpertPhase {
   const uint8_t* codes[2];   // gate/up blocks (MT=2) or down blocks (MT=1), expert 0
@@ -358,7 +388,7 @@ KK3_DEV void expert_epilogue(const StepArgs& a, const ExpertPhase& ph, int first
     if (MT == 2) {
       const float g = round_bf(acc[0][i]), u = round_bf(acc[MT - 1][i]);
       const float act = round_bf(situ_f(g, u));
-      a.s.act_p[(size_t)p * a.g.inter + perm8(row)] = __float2half_rn(act);
+      a.s.act_p[(size_t)p * a.g.inter + row] = __float2half_rn(act);
     } else {
       int b = a.s.pair_row[p], slot = a.s.pair_slot[p];
       b = b < 0 ? 0 : (b >= a.g.B ? a.g.B - 1 : b);
@@ -368,12 +398,37 @@ KK3_DEV void expert_epilogue(const StepArgs& a, const ExpertPhase& ph, int first
   }
 }
 
-// Stream-K over (expert chunk, tile, k-step) units. Chunks come from the routing phase.
+// E2M1 pairs -> FP16 pairs with the sm_100a hardware conversion: byte j of w -> register j holding
+// (low nibble, high nibble) = elements (2j, 2j+1).
+KK3_DEV void e2m1x8_cvt(unsigned w, unsigned (&r)[4]) {
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(w));
+}
+
+KK3_DEV unsigned lds32(const unsigned char* p) { return *reinterpret_cast<const unsigned*>(p); }
+
+constexpr int kFp4Row = 48;                 // staged bytes per row and unit (32 used; 48 keeps LDS conflict-free)
+constexpr int kFp4Slot = 16 * kFp4Row;      // one matrix, one unit
+
+struct ExpertCursor {
+  int chunk, tile, ks;
+};
+
+// Stream-K over (expert chunk, tile, k-step) units. Chunks come from the routing phase. A unit is a
+// 16-row tile x 64 k (two E2M1 groups); the warp's 32 lanes stage its 16 rows x 32 bytes per matrix with
+// one 16-byte cp.async each into a ring (8 deep for gate+up, 16 for down), then every quad reads its
+// rows' 4-byte quarters, converts E2M1 -> FP16 in hardware, and applies the E8M0 scale per group in FP32.
 template <int MT>
 KK3_DEV void run_experts(const StepArgs& a, const ExpertPhase& ph) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 2;
+  extern __shared__ __align__(16) unsigned char kk3_dyn_smem[];
+  constexpr int S = (MT == 2) ? 8 : 16;
+  constexpr int kSlot = MT * kFp4Slot;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
+  const int npk = a.g.B * a.g.K;
   int nchunks = ld_volatile_int(a.s.chunk_info);
-  nchunks = nchunks < 0 ? 0 : (nchunks > a.g.B * a.g.K ? a.g.B * a.g.K : nchunks);
+  nchunks = nchunks < 0 ? 0 : (nchunks > npk ? npk : nchunks);
   const long long per_chunk = (long long)ph.tiles * ph.ksteps;
   const long long U = (long long)nchunks * per_chunk;
   if (U == 0) return;
@@ -382,100 +437,140 @@ KK3_DEV void run_experts(const StepArgs& a, const ExpertPhase& ph) {
   const long long gw = (long long)blockIdx.x * kWarps + warp;
   if (gw >= GW) return;
   const long long ubeg = U * gw / GW, uend = U * (gw + 1) / GW;
-  constexpr int kSlot = MT * 128;
-  float* my_slot0 = a.s.fix_part + (size_t)(gw * 2) * kSlot;
-  for (long long u = ubeg; u < uend;) {
-    const int chunk = (int)(u / per_chunk);
-    const long long local = u - (long long)chunk * per_chunk;
-    const int tile = (int)(local / ph.ksteps);
-    const int ks0 = (int)(local % ph.ksteps);
-    const long long tile_beg = (long long)chunk * per_chunk + (long long)tile * ph.ksteps;
-    const long long tile_end = tile_beg + ph.ksteps;
-    const long long seg_end = uend < tile_end ? uend : tile_end;
-    const int ks1 = ks0 + (int)(seg_end - u);
-    // routing-table values are clamped so that a routing fault can never address outside the buffers
-    const int npk = a.g.B * a.g.K;
-    int expert = a.s.chunk_info[1 + chunk * 3];
-    int first_pair = a.s.chunk_info[2 + chunk * 3];
-    int npairs = a.s.chunk_info[3 + chunk * 3];
-    expert = expert < 0 ? 0 : (expert >= a.g.E ? a.g.E - 1 : expert);
-    first_pair = first_pair < 0 ? 0 : (first_pair >= npk ? npk - 1 : first_pair);
-    npairs = npairs < 0 ? 0 : (npairs > 8 ? 8 : npairs);
-    npairs = first_pair + npairs > npk ? npk - first_pair : npairs;
+  unsigned char* ring = kk3_dyn_smem + (size_t)warp * kGemvSmemPerWarp;
+  float* part_base = a.s.fix_part;
+  const int rowbytes = ph.K / 2, sbytes = ph.K / 32;
 
-    const uint8_t* ca[MT];
-    const uint8_t* cb[MT];
-    const uint8_t* sa[MT];
-    const uint8_t* sb[MT];
-    {
-      const int ra = tile * 16 + r, rb = ra + 8;   // rows are multiples of 16 for expert matrices
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const uint8_t* cbase = ph.codes[mt] + (size_t)expert * ph.expert_codes;
-        const uint8_t* sbase = ph.scales[mt] + (size_t)expert * ph.expert_scales;
-        ca[mt] = cbase + (size_t)ra * (ph.K / 2);
-        cb[mt] = cbase + (size_t)rb * (ph.K / 2);
-        sa[mt] = sbase + (size_t)ra * (ph.K / 32);
-        sb[mt] = sbase + (size_t)rb * (ph.K / 32);
+  auto chunk_expert = [&](int chunk) {
+    int e = a.s.chunk_info[1 + chunk * 3];
+    return e < 0 ? 0 : (e >= a.g.E ? a.g.E - 1 : e);
+  };
+  auto at = [&](long long u) {
+    ExpertCursor q;
+    q.chunk = (int)(u / per_chunk);
+    const long long local = u - (long long)q.chunk * per_chunk;
+    q.tile = (int)(local / ph.ksteps);
+    q.ks = (int)(local % ph.ksteps);
+    return q;
+  };
+  auto step = [&](ExpertCursor& q) {
+    if (++q.ks == ph.ksteps) {
+      q.ks = 0;
+      if (++q.tile == ph.tiles) {
+        q.tile = 0;
+        ++q.chunk;
       }
     }
-    const __half* xrow = nullptr;
-    if (r < npairs) {
-      const int p = first_pair + r;
-      int prow = a.s.pair_row[p];
-      prow = prow < 0 ? 0 : (prow >= a.g.B ? a.g.B - 1 : prow);
-      xrow = (MT == 2) ? a.s.latent_p + (size_t)prow * a.g.lh : a.s.act_p + (size_t)p * a.g.inter;
+  };
+  // staging: lane -> (row = lane/2, 16-byte half = lane%2) of every matrix
+  const int srow = lane >> 1, shalf = lane & 1;
+  auto issue = [&](const ExpertCursor& q, unsigned char* slot) {
+    const int e = chunk_expert(q.chunk);
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const uint8_t* src = ph.codes[mt] + (size_t)e * ph.expert_codes + (size_t)(q.tile * 16 + srow) * rowbytes +
+                           q.ks * 32 + shalf * 16;
+      cp_async16_g(slot + mt * kFp4Slot + srow * kFp4Row + shalf * 16, src);
     }
-    float acc[MT][4];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[mt][i] = 0.0f;
-    mma_rows_fp4<MT>(ca, cb, sa, sb, xrow, ks0, ks1, acc);
+  };
 
-    const long long first = owner_of(tile_beg, U, GW), lastw = owner_of(tile_end - 1, U, GW);
-    const int gtile = chunk * ph.tiles + tile;
-    if (first == lastw) {
-      expert_epilogue<MT>(a, ph, first_pair, npairs, tile, acc);
-    } else {
-      float* slot = my_slot0 + (u == ubeg ? 0 : kSlot);
+  ExpertCursor pc = at(ubeg), cc = pc;
+  long long pu = ubeg;
+#pragma unroll
+  for (int i = 0; i < S - 1; ++i) {
+    if (pu < uend) {
+      issue(pc, ring + (int)((pu - ubeg) % S) * kSlot);
+      step(pc);
+      ++pu;
+    }
+    cp_async_commit_g();
+  }
+  float acc[MT][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[mt][i] = 0.0f;
+  long long seg_start = ubeg;
+  int cur_chunk = -1, expert = 0, first_pair = 0, npairs = 0;
+  const __half* xrow = nullptr;
+  for (long long u = ubeg; u < uend; ++u) {
+    __syncwarp();   // every lane is done with the slot the next issue overwrites
+    if (pu < uend) {
+      issue(pc, ring + (int)((pu - ubeg) % S) * kSlot);
+      step(pc);
+      ++pu;
+    }
+    cp_async_commit_g();
+    if (cc.chunk != cur_chunk) {
+      cur_chunk = cc.chunk;
+      expert = chunk_expert(cur_chunk);
+      first_pair = a.s.chunk_info[2 + cur_chunk * 3];
+      npairs = a.s.chunk_info[3 + cur_chunk * 3];
+      first_pair = first_pair < 0 ? 0 : (first_pair >= npk ? npk - 1 : first_pair);
+      npairs = npairs < 0 ? 0 : (npairs > 8 ? 8 : npairs);
+      npairs = first_pair + npairs > npk ? npk - first_pair : npairs;
+      xrow = nullptr;
+      if (r < npairs) {
+        const int p = first_pair + r;
+        int prow = a.s.pair_row[p];
+        prow = prow < 0 ? 0 : (prow >= a.g.B ? a.g.B - 1 : prow);
+        xrow = (MT == 2) ? a.s.latent_p + (size_t)prow * a.g.lh : a.s.act_p + (size_t)p * a.g.inter;
+      }
+    }
+    // scales of rows r, r+8 for the unit's two groups, and the activations
+    const int rowa = cc.tile * 16 + r;
+    unsigned sa[MT], sb[MT];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const uint8_t* sbase = ph.scales[mt] + (size_t)expert * ph.expert_scales + cc.ks * 2;
+      sa[mt] = *reinterpret_cast<const unsigned short*>(sbase + (size_t)rowa * sbytes);
+      sb[mt] = *reinterpret_cast<const unsigned short*>(sbase + (size_t)(rowa + 8) * sbytes);
+    }
+    uint4 X[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+    if (xrow) {
+      X[0] = ld_act16(xrow + cc.ks * 64 + 8 * c);
+      X[1] = ld_act16(xrow + cc.ks * 64 + 32 + 8 * c);
+    }
+    cp_async_wait_g<S - 1>();
+    __syncwarp();
+    const unsigned char* slot = ring + (int)((u - ubeg) % S) * kSlot;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        const unsigned wa = lds32(slot + mt * kFp4Slot + r * kFp4Row + g * 16 + 4 * c);
+        const unsigned wb = lds32(slot + mt * kFp4Slot + (r + 8) * kFp4Row + g * 16 + 4 * c);
+        unsigned ra[4], rb[4];
+        e2m1x8_cvt(wa, ra);
+        e2m1x8_cvt(wb, rb);
+        float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        mma_f16(t, ra[0], rb[0], ra[1], rb[1], X[g].x, X[g].y);
+        mma_f16(t, ra[2], rb[2], ra[3], rb[3], X[g].z, X[g].w);
+        const float fa = e8m0_to_f32((sa[mt] >> (8 * g)) & 0xffu);
+        const float fb = e8m0_to_f32((sb[mt] >> (8 * g)) & 0xffu);
+        acc[mt][0] = fmaf(t[0], fa, acc[mt][0]);
+        acc[mt][1] = fmaf(t[1], fa, acc[mt][1]);
+        acc[mt][2] = fmaf(t[2], fb, acc[mt][2]);
+        acc[mt][3] = fmaf(t[3], fb, acc[mt][3]);
+      }
+    }
+    if (cc.ks == ph.ksteps - 1 || u == uend - 1) {
+      const long long tile_beg = (long long)cc.chunk * per_chunk + (long long)cc.tile * ph.ksteps;
+      const long long first = owner_of(tile_beg, U, GW), lastw = owner_of(tile_beg + ph.ksteps - 1, U, GW);
+      bool done = first == lastw;
+      if (!done)
+        done = stream_k_fixup<MT * 4>(a, part_base, a.s.fix_cnt + cc.chunk * ph.tiles + cc.tile, gw, seg_start == ubeg,
+                                      tile_beg, first, lastw, U, GW, *reinterpret_cast<float(*)[MT * 4]>(&acc[0][0]));
+      if (done) expert_epilogue<MT>(a, ph, first_pair, npairs, cc.tile, acc);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) slot[(mt * 4 + i) * 32 + lane] = acc[mt][i];
-      __threadfence();
-      __syncwarp();
-      int old = 0;
-      if (lane == 0) old = atomicAdd(a.s.fix_cnt + gtile, 1);
-      old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == (int)(lastw - first)) {
-        __threadfence();
-        float sum[MT][4];
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) sum[mt][i] = 0.0f;
-        for (long long w = first; w <= lastw; ++w) {
-          if (w == gw) {
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-              for (int i = 0; i < 4; ++i) sum[mt][i] += acc[mt][i];
-          } else {
-            const long long wbeg = U * w / GW;
-            const float* ps = a.s.fix_part + (size_t)(w * 2 + (wbeg >= tile_beg ? 0 : 1)) * kSlot;
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-              for (int i = 0; i < 4; ++i) sum[mt][i] += ld_cg_f32(ps + (mt * 4 + i) * 32 + lane);
-          }
-        }
-        expert_epilogue<MT>(a, ph, first_pair, npairs, tile, sum);
-        if (lane == 0) atomicExch(a.s.fix_cnt + gtile, 0);
-      }
+        for (int i = 0; i < 4; ++i) acc[mt][i] = 0.0f;
+      seg_start = u + 1;
     }
-    u = seg_end;
+    step(cc);
   }
+  cp_async_wait_g<0>();
 }
 
 }  // namespace kk3

@@ -184,7 +184,8 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
       {(void**)&s.out_slot, B * g.K * (size_t)g.lh * 2}, {(void**)&s.x3, B * g.lh * 2},
       {(void**)&s.shared_red, B * g.h * 2}, {(void**)&s.expert_sum, B * g.lh * 4},
       {(void**)&s.fix_part, (size_t)g.fix_bank * 2 * 4}, {(void**)&s.fix_cnt, (size_t)g.cnt_bank * 2 * 4},
-      {(void**)&s.argmax_key, B * 8}, {(void**)&bar, 64}, {(void**)&phase_count, 64},
+      {(void**)&s.argmax_key, B * 8}, {(void**)&bar, 64}, {(void**)&phase_count, 64}, {(void**)&s.err, 64},
+      {(void**)&s.phase_ts, (kMaxPhases + 1) * 8},
   };
   size_t total = 0;
   for (auto& it : items) total += align_up(it.bytes, 256);
@@ -208,7 +209,7 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   if (cudaHostGetDevicePointer((void**)&x->err_dev, x->err_host, 0) != cudaSuccess) {
     cudaFreeHost(x->err_host); cudaFree(x->scratch); delete x; return KK3_ERR_CUDA;
   }
-  s.err = x->err_dev;
+  s.err_host = x->err_dev;
   // exchange buffer: flags [B][tp] u32, then two parity regions {att bf16 [tp][B][h], exp f32 [tp][B][lh],
   // shd bf16 [tp][B][h], key u64 [tp][B]}
   Comm& c = x->comm;
@@ -241,7 +242,9 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   size_t sm_row = (512 + (size_t)(g.h > g.lh ? g.h : g.lh)) * 4 + 64;
   size_t sm_abs = ((size_t)g.B * 128 + 4 * 16 * 128) * 4;
   size_t sm_route = ((size_t)g.B * g.K + 4 * kMaxExperts) * 4;
+  size_t sm_gemv = (size_t)kWarps * kGemvSmemPerWarp;   // per-warp cp.async rings of the GEMV phases
   size_t sm = sm_mla;
+  sm = sm_gemv > sm ? sm_gemv : sm;
   sm = sm_row > sm ? sm_row : sm;
   sm = sm_abs > sm ? sm_abs : sm;
   sm = sm_route > sm ? sm_route : sm;
@@ -259,11 +262,13 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   if (!x->args) { kk3_free(x); return KK3_ERR_CUDA; }
   // diagnostics table
   void* bp[KK3_BUF_COUNT] = {s.prefix, s.xa, s.xm, s.attn_in, s.scores, s.latent, s.shared_act, s.x3, s.route_w,
-                             s.qkv, s.mla_q, s.absorbed, s.absorbed, s.expert_sum, s.blocks, x->comm_local};
+                             s.qkv, s.mla_q, s.absorbed, s.absorbed, s.expert_sum, s.blocks, x->comm_local,
+                             s.phase_ts};
   size_t bb[KK3_BUF_COUNT] = {B * g.h * 2, B * g.h * 2, B * g.h * 2, B * (size_t)g.hr * g.vd * 2, B * g.E * 4,
                               B * g.lh * 2, B * (size_t)g.sinter * 2, B * g.lh * 2, B * g.K * 4, B * qkv_w * 2,
                               B * (size_t)g.hr * (g.nr + g.rd) * 2, B * (size_t)g.hr * g.kr * 2,
-                              B * (size_t)g.hr * g.kr * 2, B * g.lh * 4, (size_t)g.nblk * B * g.h * 2, x->comm_bytes};
+                              B * (size_t)g.hr * g.kr * 2, B * g.lh * 4, (size_t)g.nblk * B * g.h * 2, x->comm_bytes,
+                              (size_t)(kMaxPhases + 1) * 8};
   for (int i = 0; i < KK3_BUF_COUNT; ++i) { x->buf_ptr[i] = bp[i]; x->buf_bytes[i] = bb[i]; }
   *out = x;
   return KK3_OK;
@@ -307,7 +312,7 @@ extern "C" int kk3_debug_set_peer(kk3_ctx* x, int r, void* device_ptr) {
 
 extern "C" size_t kk3_exchange_bytes(kk3_ctx* x) { return x ? x->comm_bytes : 0; }
 
-static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int stop_phase) {
+static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int stop_phase, int start_phase) {
   if (!x || !table) return KK3_ERR_ARG;
   if (x->failed) return KK3_ERR_FAILED;
   if (!x->peers_open) return KK3_ERR_PEERS;
@@ -323,6 +328,7 @@ static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int
   a->comm = x->comm;
   a->epoch = ++x->epoch;
   a->stop_phase = stop_phase;
+  a->start_phase = start_phase < 0 ? 0 : start_phase;
   a->nptr = n;
   memcpy(a->ptr, table, sizeof(void*) * n);
   cudaError_t e = launch_kernel(x->nt, a, x->grid, x->smem, (cudaStream_t)stream);
@@ -330,11 +336,16 @@ static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int
 }
 
 extern "C" int kk3_step(kk3_ctx* x, const void* const* table, int n, void* stream) {
-  return launch(x, table, n, stream, -1);
+  return launch(x, table, n, stream, -1, 0);
 }
 
 extern "C" int kk3_debug_step(kk3_ctx* x, const void* const* table, int n, void* stream, int stop_phase) {
-  return launch(x, table, n, stream, stop_phase < 0 ? -1 : stop_phase);
+  return launch(x, table, n, stream, stop_phase < 0 ? -1 : stop_phase, 0);
+}
+
+extern "C" int kk3_debug_phases(kk3_ctx* x, const void* const* table, int n, void* stream, int start_phase,
+                                int stop_phase) {
+  return launch(x, table, n, stream, stop_phase < 0 ? -1 : stop_phase, start_phase);
 }
 
 extern "C" int kk3_status(kk3_ctx* x) {

@@ -246,15 +246,18 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   int phase = 0;
   unsigned xi = 0;
   const unsigned seq0 = a.epoch * 1024u;
-#define KK3_PHASE_END()                          \
-  do {                                           \
-    if (!grid_sync(a)) return;                   \
-    ++phase;                                     \
-    if (phase == a.stop_phase) return;           \
+#define KK3_RUN (phase >= a.start_phase)
+#define KK3_PHASE_END()                                                                      \
+  do {                                                                                       \
+    if (KK3_RUN && !grid_sync(a)) return;                                                    \
+    ++phase;                                                                                 \
+    if (blockIdx.x == 0 && threadIdx.x == 0 && phase <= kMaxPhases) a.s.phase_ts[phase] = globaltimer(); \
+    if (phase == a.stop_phase) return;                                                       \
   } while (0)
 
+  if (blockIdx.x == 0 && threadIdx.x == 0) a.s.phase_ts[0] = globaltimer();
   // embedding (kimi.py:249-252)
-  phase_embed(a, seq0 + xi, xi & 1, fsm);
+  if (KK3_RUN) phase_embed(a, seq0 + xi, xi & 1, fsm);
   int pending = PEND_EMBED;
   bool pend_signal = false;
   unsigned pend_x = xi++;
@@ -264,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   for (int l = 0; l < g.L; ++l) {
     const bool mla = layer_is_mla(g, l);
     // attention prologue (kimi.py:257-262)
-    if (!phase_attn_prologue(a, l, nb, pending, pend_signal, seq0 + pend_x, pend_x & 1, fsm)) return;
+    if (KK3_RUN && !phase_attn_prologue(a, l, nb, pending, pend_signal, seq0 + pend_x, pend_x & 1, fsm)) return;
     pending = PEND_NONE;
     if (l % g.bs == 0) ++nb;
     KK3_PHASE_END();
@@ -283,10 +286,11 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         jobs[i].K = g.h; jobs[i].x = a.s.xa; jobs[i].ldx = g.h; jobs[i].ncols = g.B; jobs[i].epi = EPI_STORE_BF16;
       }
       prepare_jobs(jobs, 6);
-      run_gemv<NT, 1>(a, jobs, 6, 0, gridDim.x, 0);
+      if (KK3_RUN) run_gemv<NT, 1>(a, jobs, 6, 0, gridDim.x, 0);
       KK3_PHASE_END();
       // short conv + gated delta rule (kimi.py:286-299)
-      for (int it = blockIdx.x; it < g.B * g.hr; it += gridDim.x) kda_item(a, l, kidx, it / g.hr, it % g.hr, fsm);
+      if (KK3_RUN)
+        for (int it = blockIdx.x; it < g.B * g.hr; it += gridDim.x) kda_item(a, l, kidx, it / g.hr, it % g.hr, fsm);
       ++kidx;
       KK3_PHASE_END();
     } else {
@@ -301,22 +305,23 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         jobs[i].K = g.h; jobs[i].x = a.s.xa; jobs[i].ldx = g.h; jobs[i].ncols = g.B; jobs[i].epi = EPI_STORE_BF16;
       }
       prepare_jobs(jobs, 3);
-      run_gemv<NT, 1>(a, jobs, 3, 0, gridDim.x, 0);
+      if (KK3_RUN) run_gemv<NT, 1>(a, jobs, 3, 0, gridDim.x, 0);
       KK3_PHASE_END();
-      phase_mla_rows(a, l, midx, fsm);
+      if (KK3_RUN) phase_mla_rows(a, l, midx, fsm);
       KK3_PHASE_END();
       // q_b (kimi.py:265)
       GemvJob qb = {};
       qb.w = lptr<bf16>(a, l, KK3_MLA_QB); qb.rows = g.hr * (g.nr + g.rd); qb.K = g.qr; qb.x = a.s.mla_qan;
       qb.ldx = g.qr; qb.ncols = g.B; qb.epi = EPI_STORE_BF16; qb.out = a.s.mla_q; qb.ldo = g.hr * (g.nr + g.rd);
       prepare_jobs(&qb, 1);
-      run_gemv<NT, 1>(a, &qb, 1, 0, gridDim.x, 0);
+      if (KK3_RUN) run_gemv<NT, 1>(a, &qb, 1, 0, gridDim.x, 0);
       KK3_PHASE_END();
       // absorbed query (kimi.py:271-272)
-      for (int it = blockIdx.x; it < g.hr * 4; it += gridDim.x) mla_absorb_item(a, l, it / 4, it % 4, fsm);
+      if (KK3_RUN)
+        for (int it = blockIdx.x; it < g.hr * 4; it += gridDim.x) mla_absorb_item(a, l, it / 4, it % 4, fsm);
       KK3_PHASE_END();
       // split-K attention over [cache, new token] (kimi.py:274-280)
-      {
+      if (KK3_RUN) {
         const bool* reset = gptr<bool>(a, KK3_RESET);
         int total = 0;
         for (int b = 0; b < g.B; ++b) total += reset[b] ? 1 : g.mla_chunks;
@@ -335,7 +340,8 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         }
       }
       KK3_PHASE_END();
-      for (int it = blockIdx.x; it < g.B * g.hr; it += gridDim.x) mla_combine_item(a, l, it / g.hr, it % g.hr, fsm);
+      if (KK3_RUN)
+        for (int it = blockIdx.x; it < g.B * g.hr; it += gridDim.x) mla_combine_item(a, l, it / g.hr, it % g.hr, fsm);
       ++midx;
       KK3_PHASE_END();
     }
@@ -345,13 +351,13 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
       o.w = lptr<bf16>(a, l, KK3_KDA_O); o.rows = g.h; o.K = g.hr * g.vd; o.x = a.s.attn_in; o.ldx = g.hr * g.vd;
       o.ncols = g.B; o.epi = EPI_EXCHANGE; o.ldo = g.h; o.aux_off = a.comm.att_off;
       prepare_jobs(&o, 1);
-      run_gemv<NT, 1>(a, &o, 1, 0, gridDim.x, xi & 1);
+      if (KK3_RUN) run_gemv<NT, 1>(a, &o, 1, 0, gridDim.x, xi & 1);
       if (g.tp > 1) __threadfence_system();
     }
     const unsigned x_att = xi++;
     KK3_PHASE_END();
     const int nb_after = nb;
-    if (!phase_mlp_prologue(a, l, nb_after, seq0 + x_att, x_att & 1, fsm)) return;
+    if (KK3_RUN && !phase_mlp_prologue(a, l, nb_after, seq0 + x_att, x_att & 1, fsm)) return;
     KK3_PHASE_END();
     if (l < g.first_dense) {
       // dense FFN (kimi.py:304)
@@ -359,13 +365,13 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
       gu.w = lptr<bf16>(a, l, KK3_DENSE_GATE); gu.w2 = lptr<bf16>(a, l, KK3_DENSE_UP); gu.rows = g.dinter; gu.K = g.h;
       gu.x = a.s.xm; gu.ldx = g.h; gu.ncols = g.B; gu.epi = EPI_SITU; gu.out = a.s.dense_act; gu.ldo = g.dinter;
       prepare_jobs(&gu, 1);
-      run_gemv<NT, 2>(a, &gu, 1, 0, gridDim.x, 0);
+      if (KK3_RUN) run_gemv<NT, 2>(a, &gu, 1, 0, gridDim.x, 0);
       KK3_PHASE_END();
       GemvJob dn = {};
       dn.w = lptr<bf16>(a, l, KK3_DENSE_DOWN); dn.rows = g.h; dn.K = g.dinter; dn.x = a.s.dense_act; dn.ldx = g.dinter;
       dn.ncols = g.B; dn.epi = EPI_EXCHANGE; dn.ldo = g.h; dn.aux_off = a.comm.att_off;
       prepare_jobs(&dn, 1);
-      run_gemv<NT, 1>(a, &dn, 1, 0, gridDim.x, xi & 1);
+      if (KK3_RUN) run_gemv<NT, 1>(a, &dn, 1, 0, gridDim.x, xi & 1);
       if (g.tp > 1) __threadfence_system();
       pending = PEND_DENSE;
       pend_signal = true;
@@ -382,16 +388,17 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         j0[i].K = g.h; j0[i].x = a.s.xm; j0[i].ldx = g.h; j0[i].ncols = g.B;
       }
       prepare_jobs(j0, 2);
-      run_gemv<NT, 1>(a, j0, 2, 0, gridDim.x, 0, 0);
+      if (KK3_RUN) run_gemv<NT, 1>(a, j0, 2, 0, gridDim.x, 0, 0);
       GemvJob j1 = {};
       j1.w = lptr<bf16>(a, l, KK3_MOE_SHARED_GATE); j1.w2 = lptr<bf16>(a, l, KK3_MOE_SHARED_UP); j1.rows = g.sinter;
       j1.K = g.h; j1.x = a.s.xm; j1.ldx = g.h; j1.ncols = g.B; j1.epi = EPI_SITU; j1.out = a.s.shared_act; j1.ldo = g.sinter;
       prepare_jobs(&j1, 1);
-      run_gemv<NT, 2>(a, &j1, 1, 0, gridDim.x, 0, 1);
+      if (KK3_RUN) run_gemv<NT, 2>(a, &j1, 1, 0, gridDim.x, 0, 1);
       KK3_PHASE_END();
       // routing on CTA 0 while the other CTAs run the shared-expert down projection (kimi.py:309-316, :326)
       const unsigned x_moe = xi++;
-      if (blockIdx.x == 0) {
+      if (!KK3_RUN) {
+      } else if (blockIdx.x == 0) {
         route_all(a, l, l - g.first_dense, smem);
       } else {
         GemvJob sd = {};
@@ -411,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         ph.scales[1] = lptr<uint8_t>(a, l, KK3_MOE_UP_SCALES);
         ph.rows = g.inter; ph.K = g.lh; ph.tiles = g.inter / 16; ph.ksteps = g.lh / 64;
         ph.expert_codes = (long long)g.inter * g.lh / 2; ph.expert_scales = (long long)g.inter * g.lh / 32;
-        run_experts<2>(a, ph);
+        if (KK3_RUN) run_experts<2>(a, ph);
       }
       KK3_PHASE_END();
       {
@@ -420,27 +427,27 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         ph.scales[0] = ph.scales[1] = lptr<uint8_t>(a, l, KK3_MOE_DOWN_SCALES);
         ph.rows = g.lh; ph.K = g.inter; ph.tiles = g.lh / 16; ph.ksteps = g.inter / 64;
         ph.expert_codes = (long long)g.lh * g.inter / 2; ph.expert_scales = (long long)g.lh * g.inter / 32;
-        run_experts<1>(a, ph);
+        if (KK3_RUN) run_experts<1>(a, ph);
       }
       KK3_PHASE_END();
-      if (!phase_moe_combine(a, l, seq0 + x_moe, x_moe & 1, fsm)) return;
+      if (KK3_RUN && !phase_moe_combine(a, l, seq0 + x_moe, x_moe & 1, fsm)) return;
       KK3_PHASE_END();
       // latent up + shared + residual (kimi.py:325-329)
       GemvJob up = {};
       up.w = lptr<bf16>(a, l, KK3_MOE_LATENT_UP); up.rows = g.h; up.K = g.lh; up.x = a.s.x3; up.ldx = g.lh;
       up.ncols = g.B; up.epi = EPI_ROUTED; up.out = a.s.prefix; up.aux = a.s.shared_red; up.ldo = g.h;
       prepare_jobs(&up, 1);
-      run_gemv<NT, 1>(a, &up, 1, 0, gridDim.x, 0);
+      if (KK3_RUN) run_gemv<NT, 1>(a, &up, 1, 0, gridDim.x, 0);
       KK3_PHASE_END();
     }
   }
   // head (kimi.py:330-334)
   if (pending != PEND_NONE) {
     // the last layer was dense: fold its exchange into prefix first
-    if (!phase_fold_pending(a, pending, pend_signal, seq0 + pend_x, pend_x & 1)) return;
+    if (KK3_RUN && !phase_fold_pending(a, pending, pend_signal, seq0 + pend_x, pend_x & 1)) return;
     KK3_PHASE_END();
   }
-  phase_head_prologue(a, nb, fsm);
+  if (KK3_RUN) phase_head_prologue(a, nb, fsm);
   KK3_PHASE_END();
   {
     GemvJob hd = {};
@@ -448,13 +455,17 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
     hd.epi = EPI_LOGITS; hd.out = gout<float>(a, KK3_OUT_LOGITS); hd.ldo = g.V; hd.aux = a.s.argmax_key;
     hd.aux_off = (long long)g.rank * g.V;
     prepare_jobs(&hd, 1);
-    run_gemv<NT, 1>(a, &hd, 1, 0, gridDim.x, 0);
+    if (KK3_RUN) run_gemv<NT, 1>(a, &hd, 1, 0, gridDim.x, 0);
   }
   KK3_PHASE_END();
   const unsigned x_key = xi++;
-  if (!phase_argmax(a, seq0 + x_key, x_key & 1)) return;
-  if (blockIdx.x == 0 && threadIdx.x == 0) *a.s.phase_count = phase + 1;
+  if (KK3_RUN && !phase_argmax(a, seq0 + x_key, x_key & 1)) return;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (phase + 1 <= kMaxPhases) a.s.phase_ts[phase + 1] = globaltimer();
+    *a.s.phase_count = phase + 1;
+  }
 #undef KK3_PHASE_END
+#undef KK3_RUN
 }
 
 }  // namespace kk3

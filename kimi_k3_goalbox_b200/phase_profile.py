@@ -1,0 +1,193 @@
+"""Per-phase timing of the persistent decode-step kernel.
+
+    python -m kimi_k3_goalbox_b200.phase_profile [--case ID] [--batch B] [--reps N] [--json out.json]
+
+The step is one cooperative launch walking a fixed program of grid-wide phases. CTA 0 stamps %globaltimer at
+kernel start and after every grid barrier (KK3_BUF_PHASE_TS), so one full step yields the in-step time of
+every phase including its barrier and tail. For comparison each phase is also timed alone:
+kk3_debug_phases(start, stop) runs only phases [start, stop) (skipped phases do no work and no barrier), so
+phase i alone costs t([i, i+1)) - t(no phase) (CUDA events, median of N repetitions). Each phase also gets its algorithmic HBM
+bytes (weights, cache and state it must read or write once), so the table reports achieved GB/s per phase
+(the reference measures per-kernel GB/s with Nsight Compute, megabench/integrations/ncu_profile_case.py).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+import sys
+
+import torch
+
+from . import cases, synthetic
+from .cases import is_mla
+from .runtime import StepContext
+
+
+def phase_program(params: dict) -> list[tuple[str, int]]:
+    """Grid-phase sequence of the step kernel (csrc/kk3_kernel.cuh): index i ends at stop_phase i+1."""
+    L, fd = params["layers"], params["first_dense"]
+    prog = [("embed", -1)]
+    for l in range(L):
+        prog.append(("attn_prologue", l))
+        if is_mla(params, l):
+            prog += [("mla_proj", l), ("mla_rows", l), ("mla_qb", l), ("mla_absorb", l), ("mla_attend", l),
+                     ("mla_combine", l)]
+        else:
+            prog += [("kda_proj", l), ("kda", l)]
+        prog += [("o_proj", l), ("mlp_prologue", l)]
+        if l < fd:
+            prog += [("dense_gate_up", l), ("dense_down", l)]
+        else:
+            prog += [("moe_in", l), ("route", l), ("experts_gate_up", l), ("experts_down", l), ("moe_combine", l),
+                     ("latent_up", l)]
+    if L <= fd:
+        prog.append(("fold", -1))
+    prog += [("head_prologue", -1), ("lm_head", -1), ("argmax", -1)]
+    return prog
+
+
+def phase_bytes(case: dict, distinct_experts: float | None = None) -> list[int]:
+    """Algorithmic HBM bytes of each phase (same accounting as the reference's floor model, split by phase)."""
+    p, tp = case["params"], case["tp"]
+    B, h, lh, d, H = p["batch"], p["hidden"], p["latent_hidden"], p["head_dim"], p["q_heads"]
+    hr, qd = H // tp, H * d // tp
+    qr, kr, nr, rd, vd = p["q_lora_rank"], p["kv_lora_rank"], p["qk_nope_dim"], p["qk_rope_dim"], p["v_head_dim"]
+    E, k, ctx = p["experts"], p["topk"], p["context"]
+    inter, sh, di = p["intermediate"] // tp, p["intermediate"] * p["shared_experts"] // tp, p["dense_intermediate"] // tp
+    dist = distinct_experts if distinct_experts is not None else E * (1 - (1 - k / E) ** B)
+    fp4 = lambda r, c: r * c // 2 + r * c // 32
+    out = []
+    for name, l in phase_program(p):
+        b = 0
+        if name == "embed":
+            b = B * h * 2
+        elif name == "kda_proj":
+            b = 2 * h * (4 * qd + d + hr)
+        elif name == "kda":
+            b = 2 * qd * d + B * (2 * hr * d * d * 4 + 2 * 3 * qd * 4 * 2) + 3 * qd * 4 * 4
+        elif name == "mla_proj":
+            b = 2 * h * (qr + kr + rd + hr * vd)
+        elif name == "mla_qb":
+            b = 2 * hr * (nr + rd) * qr
+        elif name == "mla_absorb":
+            b = 2 * hr * nr * kr
+        elif name == "mla_attend":
+            b = B * ctx * (kr + rd) * 2
+        elif name == "mla_combine":
+            b = 2 * hr * vd * kr
+        elif name == "o_proj":
+            b = 2 * h * hr * vd
+        elif name == "dense_gate_up":
+            b = 2 * 2 * di * h
+        elif name == "dense_down":
+            b = 2 * h * di
+        elif name == "moe_in":
+            b = 2 * h * (E + lh + 2 * sh)
+        elif name == "route":
+            b = 2 * h * sh
+        elif name == "experts_gate_up":
+            b = int(dist * 2 * fp4(inter, lh))
+        elif name == "experts_down":
+            b = int(dist * fp4(lh, inter))
+        elif name == "latent_up":
+            b = 2 * h * lh
+        elif name == "lm_head":
+            b = 2 * (p["vocab"] // tp) * h + B * (p["vocab"] // tp) * 4
+        out.append(b)
+    return out
+
+
+def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[dict]:
+    torch.cuda.set_device(device)
+    with torch.inference_mode():
+        values = synthetic.make_inputs(case, seed, torch.device("cuda", device))
+        ctx = StepContext(case, device=device)
+        try:
+            out = ctx.allocate_outputs()
+            ctx._bind_inputs(values)
+            ctx.bind_outputs(out)
+            prog = phase_program(case["params"])
+            stream = torch.cuda.current_stream()
+            for _ in range(3):
+                ctx.launch(stream.cuda_stream)
+            torch.cuda.synchronize()
+            ctx.check()
+            flush = torch.empty(64 << 22, dtype=torch.float32, device=torch.device("cuda", device))   # 1 GiB > L2
+
+            def timed(start, stop):
+                ts = []
+                for _ in range(reps):
+                    flush.zero_()   # evict the 126 MB L2 so an isolated phase streams its weights from HBM
+                    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s.record(stream)
+                    ctx.launch(stream.cuda_stream, stop_phase=stop, start_phase=start)
+                    e.record(stream)
+                    e.synchronize()
+                    ts.append(s.elapsed_time(e) * 1000.0)
+                return statistics.median(ts)
+
+            full = timed(0, -1)
+            # in-step breakdown: globaltimer stamps written at every grid barrier of one full step
+            flush.zero_()
+            ctx.launch(stream.cuda_stream)
+            torch.cuda.synchronize()
+            ts = ctx.debug_buffer(16, torch.int64, (len(prog) + 1,)).cpu().tolist()
+            instep = [(ts[i + 1] - ts[i]) / 1000.0 for i in range(len(prog))]
+            empty = timed(len(prog) + 1, -1)      # walks the program, runs no phase: launch cost
+            alone = [max(timed(i, i + 1 if i + 1 < len(prog) else -1) - empty, 1e-3) for i in range(len(prog))]
+            ctx.check()
+        finally:
+            ctx.close()
+    nbytes = phase_bytes(case)
+    rows = [{"phase": -1, "name": "full_step", "layer": -1, "us": round(full, 2), "bytes": 0, "GBps": None},
+            {"phase": -1, "name": "empty_launch", "layer": -1, "us": round(empty, 2), "bytes": 0, "GBps": None}]
+    for i, (name, layer) in enumerate(prog):
+        dt = instep[i]
+        rows.append({"phase": i, "name": name, "layer": layer, "us": round(dt, 2), "alone_us": round(alone[i], 2),
+                     "bytes": nbytes[i], "GBps": round(nbytes[i] / (dt * 1e-6) / 1e9, 1) if nbytes[i] and dt > 0 else None})
+    return rows
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--case", default="kimi-k3-dev-l4-tp1-b8-s8192")
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--rank-equivalent", action="store_true", help="one TP rank of --case as a TP1 geometry")
+    ap.add_argument("--reps", type=int, default=5)
+    ap.add_argument("--json", default=None)
+    args = ap.parse_args(argv)
+    case = cases.get_case(args.case)
+    case["params"].pop("checkpoint", None)
+    if args.rank_equivalent and case["tp"] > 1:
+        tp = case["tp"]
+        for key in ("q_heads", "vocab", "intermediate", "dense_intermediate"):
+            case["params"][key] //= tp
+        case.update(gpus=1, tp=1, id=case["id"] + "-rank-equivalent")
+    elif case["tp"] > 1:
+        raise SystemExit("multi-rank cases: pass --rank-equivalent (one rank's shapes on one GPU)")
+    if args.batch:
+        case = cases.variant(case, batch=args.batch)
+    rows = profile(case, args.reps)
+    head, rows = rows[:2], rows[2:]
+    total = sum(r["us"] for r in rows)
+    print(f"{case['id']}: full step {head[0]['us']:.1f} us (events), empty launch {head[1]['us']:.1f} us, "
+          f"in-step phases sum to {total:.1f} us (globaltimer), alone-sum {sum(r['alone_us'] for r in rows):.1f} us")
+    agg: dict[str, list] = {}
+    for r in rows:
+        a = agg.setdefault(r["name"], [0.0, 0])
+        a[0] += r["us"]
+        a[1] += r["bytes"]
+    for name, (us, b) in sorted(agg.items(), key=lambda kv: -kv[1][0]):
+        gbps = f"{b / (us * 1e-6) / 1e9:8.1f} GB/s" if b and us > 0 else "        -     "
+        print(f"  {name:18s} {us:9.1f} us  {100 * us / total:5.1f}%  {gbps}")
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump({"case": case["id"], "full_us": head[0]["us"], "empty_launch_us": head[1]["us"],
+                       "sum_alone_us": total, "phases": rows}, f, indent=1)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

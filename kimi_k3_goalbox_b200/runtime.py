@@ -68,6 +68,7 @@ def load_library() -> ctypes.CDLL:
         lib.kk3_open_peers.argtypes = [vp, vp]
         lib.kk3_step.argtypes = [vp, vp, i32, vp]
         lib.kk3_debug_step.argtypes = [vp, vp, i32, vp, i32]
+        lib.kk3_debug_phases.argtypes = [vp, vp, i32, vp, i32, i32]
         lib.kk3_status.argtypes = [vp]
         lib.kk3_phase_count.argtypes = [vp]
         lib.kk3_error_string.argtypes = [i32]
@@ -219,10 +220,13 @@ class StepContext:
         if rc != 0:
             raise KK3Error(rc, "decode-step kernel")
 
-    def launch(self, stream: int | None = None, stop_phase: int = -1) -> None:
+    def launch(self, stream: int | None = None, stop_phase: int = -1, start_phase: int = 0) -> None:
         if stream is None:
             stream = torch.cuda.current_stream(self.device).cuda_stream
-        if stop_phase >= 0:
+        if start_phase > 0:
+            rc = self.lib.kk3_debug_phases(self.handle, self.table, self.nslots, ctypes.c_void_p(stream), start_phase,
+                                           stop_phase)
+        elif stop_phase >= 0:
             rc = self.lib.kk3_debug_step(self.handle, self.table, self.nslots, ctypes.c_void_p(stream), stop_phase)
         else:
             rc = self.lib.kk3_step(self.handle, self.table, self.nslots, ctypes.c_void_p(stream))

@@ -8,7 +8,8 @@ import copy
 import torch
 
 from kimi_k3_goalbox_b200 import cases
-from kimi_k3_goalbox_b200.cases import is_mla
+from kimi_k3_goalbox_b200.cases import is_mla  # noqa: F401
+from kimi_k3_goalbox_b200.phase_profile import phase_program
 
 # The smallest geometry the kernels accept: Kimi's fixed head dims, small everything else.
 SMALL = {"layers": 5, "hidden": 256, "latent_hidden": 128, "intermediate": 128, "dense_intermediate": 256,
@@ -37,29 +38,6 @@ def rank_equivalent(case_id: str, **over) -> dict:
     p.update(over)
     p.pop("checkpoint", None)
     return dict(copy.deepcopy(c), id=c["id"] + "-rank-equivalent", gpus=1, tp=1, params=p)
-
-
-def phase_program(params: dict) -> list[tuple[str, int]]:
-    """Host mirror of the kernel's grid-phase sequence (kk3_kernel.cuh): index i ends at stop_phase i+1."""
-    L, fd = params["layers"], params["first_dense"]
-    prog = [("embed", -1)]
-    for l in range(L):
-        prog.append(("attn_prologue", l))
-        if is_mla(params, l):
-            prog += [("mla_proj", l), ("mla_rows", l), ("mla_qb", l), ("mla_absorb", l), ("mla_attend", l),
-                     ("mla_combine", l)]
-        else:
-            prog += [("kda_proj", l), ("kda", l)]
-        prog += [("o_proj", l), ("mlp_prologue", l)]
-        if l < fd:
-            prog += [("dense_gate_up", l), ("dense_down", l)]
-        else:
-            prog += [("moe_in", l), ("route", l), ("experts_gate_up", l), ("experts_down", l), ("moe_combine", l),
-                     ("latent_up", l)]
-    if L <= fd:
-        prog.append(("fold", -1))
-    prog += [("head_prologue", -1), ("lm_head", -1), ("argmax", -1)]
-    return prog
 
 
 def rel_l2(got: torch.Tensor, want: torch.Tensor) -> float:
