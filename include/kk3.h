@@ -143,6 +143,8 @@ enum kk3_debug_buffer_id {
     KK3_BUF_SHARED_ACT, KK3_BUF_X3, KK3_BUF_ROUTE_W, KK3_BUF_QKV, KK3_BUF_MLA_Q, KK3_BUF_ABSORBED,
     KK3_BUF_ATTN_LAT, KK3_BUF_EXPERT_SUM, KK3_BUF_BLOCKS, KK3_BUF_EXCHANGE,
     KK3_BUF_PHASE_TS, /* u64 globaltimer (ns) at kernel start and at the end of every grid phase */
+    KK3_BUF_ARRIVE_TS, /* u64 [256 phases][grid] barrier arrival time of every CTA */
+    KK3_BUF_SUB_TS,    /* u64 [256 phases][16] sub-phase stamps of one CTA or warp */
     KK3_BUF_COUNT
 };
 int kk3_debug_buffer(kk3_ctx* ctx, int id, void** ptr, size_t* bytes);
@@ -156,6 +158,11 @@ size_t kk3_exchange_bytes(kk3_ctx* ctx);
 /* Single-process testing aid: use an existing device allocation of kk3_exchange_bytes() bytes as rank r's
  * exchange buffer instead of an IPC mapping (no counterpart in the reference). */
 int kk3_debug_set_peer(kk3_ctx* ctx, int r, void* device_ptr);
+
+/* Fault localisation: enable (1) or disable (0) per-CTA progress publishing to mapped host memory, and copy
+ * the current words (2 x 1024 ints: [0][cta] = phase reached, [1][cta] = progress code) into `out` (may be
+ * NULL). Readable after a device fault, when the context can no longer be queried. */
+int kk3_debug_trace(kk3_ctx* ctx, int enable, int* out, int n);
 
 /* Launch shape of the step kernel: CTAs (one per SM), threads per CTA, dynamic shared memory bytes. */
 int kk3_launch_config(kk3_ctx* ctx, int* grid, int* threads, size_t* smem);

@@ -8,6 +8,9 @@
 #include "../../include/kk3.h"
 
 #define KK3_DEV __device__ __forceinline__
+// Phase engines are real functions: one shared copy stays hot in the instruction cache across phases and
+// layers (inlining a copy per call site made every phase run cold code).
+#define KK3_FN static __device__ __noinline__
 
 namespace kk3 {
 
@@ -22,6 +25,8 @@ constexpr int kMaxExperts = 1024;
 constexpr int kMaxPtrs = KK3_GLOBAL_SLOTS + 96 * KK3_LAYER_SLOTS;   // 3104 slots: up to 96 layers
 constexpr int kMlaPos = 32;            // cache positions per attention sub-tile
 constexpr int kMaxPhases = 2048;       // phase timestamp capacity (a 96-layer step has ~1500 phases)
+constexpr int kArrivePhases = 256;     // phases with per-CTA barrier arrival stamps
+constexpr int kTraceWords = 2 * 1024 + 4096;   // mapped trace: phase and progress per CTA, marker per warp
 
 // device error word values (also the host-visible status)
 constexpr int kErrTimeout = 1;
@@ -77,11 +82,14 @@ struct Scratch {
   float* fix_part;    // [2 * warps_total, 16 * 64 * 2] stream-K partial tiles
   int* fix_cnt;       // [max tiles] stream-K arrival counters
   unsigned long long* argmax_key; // [B]
-  unsigned* bar;      // [2] grid barrier: count, generation
+  unsigned* bar;      // grid barrier word (see grid_sync)
   int* err;           // device error word, polled by every wait (device memory: cheap to poll)
   int* err_host;      // host-visible copy in mapped host memory, written only when an error is raised
   int* phase_count;   // number of grid phases of the last complete step
   unsigned long long* phase_ts;  // [kMaxPhases + 1] globaltimer at kernel start and at the end of each phase
+  unsigned long long* arrive_ts; // [kArrivePhases][grid] barrier arrival time of every CTA (profiling)
+  unsigned long long* sub_ts;    // [kArrivePhases][16] sub-phase stamps of one CTA / warp (profiling)
+  int* trace_host;    // mapped host memory [2][1024]: per-CTA phase and progress, readable after a fault
 };
 
 // One-shot exchange buffers, symmetric across ranks (this rank's and peers' mapped copies).
@@ -101,6 +109,7 @@ struct StepArgs {
   unsigned epoch;       // step counter (1, 2, ...), orders the peer flags
   int stop_phase;       // debug: return after this many grid phases (-1: run everything)
   int start_phase;      // debug: skip the work (and barriers) of phases before this one (0: run everything)
+  int trace;            // debug: publish per-CTA progress to mapped host memory (fault localisation)
   int nptr;
   const void* ptr[kMaxPtrs];
 };
@@ -142,6 +151,11 @@ KK3_DEV uint4 ldg_stream16(const void* p) {
 KK3_DEV unsigned ldg_nc32(const void* p) {
   unsigned v;
   asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+KK3_DEV unsigned ldg_nc16(const void* p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
   return v;
 }
 KK3_DEV unsigned ldg_nc8(const void* p) {
@@ -213,6 +227,29 @@ KK3_DEV float block_sum(float v, float* red) {
   return warp_sum(t);
 }
 
+// profiling stamp `k` (< 16) of the current phase, written by the calling thread
+KK3_DEV void sub_stamp(const StepArgs& a, int phase, int k, unsigned long long v = 0) {
+  if (phase >= 0 && phase < kArrivePhases) a.s.sub_ts[phase * 16 + k] = v ? v : globaltimer();
+}
+
+// fault localisation: thread 0 of each CTA publishes (slot 0) its phase and (slot 1) a progress code
+KK3_DEV void trace_progress(const StepArgs& a, int which, int value) {
+  if (a.trace && threadIdx.x == 0) {
+    reinterpret_cast<volatile int*>(a.s.trace_host)[which * 1024 + blockIdx.x] = value;
+    __threadfence_system();
+  }
+}
+// per-warp marker (lane 0), for locating a fault inside an engine; only when tracing is enabled
+KK3_DEV void trace_warp(const StepArgs& a, int value) {
+  if (a.trace && (threadIdx.x & 31) == 0) {
+    const int w = blockIdx.x * kWarps + (threadIdx.x >> 5);
+    if (w < 4096) {
+      reinterpret_cast<volatile int*>(a.s.trace_host)[2 * 1024 + w] = value;
+      __threadfence_system();
+    }
+  }
+}
+
 // pointer-table access
 template <typename T>
 KK3_DEV const T* gptr(const StepArgs& a, int slot) { return reinterpret_cast<const T*>(a.ptr[slot]); }
@@ -231,35 +268,38 @@ KK3_DEV void set_error(const StepArgs& a, int code) {
 }
 KK3_DEV bool failed(const StepArgs& a) { return ld_volatile_int(a.s.err) != 0; }
 
-// Bounded grid-wide barrier (sense reversal on a generation counter). Returns false when the wait ran
-// past the timeout or another CTA already reported an error; the kernel then unwinds.
-KK3_DEV bool grid_sync(const StepArgs& a) {
+// Bounded grid-wide barrier on one 32-bit word. Every CTA adds 1, except CTA 0 which adds 2^31 - (G - 1), so
+// the word advances by exactly 2^31 per barrier and its top bit flips once all G CTAs have arrived: one
+// atomic per CTA, no reset. Waiters poll the word (acquire); the error word is checked only every 64 polls
+// and the wait gives up after timeout_ns. Returns false on timeout or a reported error; the kernel unwinds.
+// When `arrive_ts` is set, each CTA stamps its arrival time (phase profiling).
+KK3_DEV bool grid_sync(const StepArgs& a, int phase = -1) {
   __shared__ int ok_flag;
   __syncthreads();
   if (threadIdx.x == 0) {
-    unsigned* count = a.s.bar;
-    unsigned* gen = a.s.bar + 1;
+    unsigned* word = a.s.bar;
     int ok = 1;
-    unsigned my_gen = ld_acquire_gpu(gen);
+    if (a.s.arrive_ts && phase >= 0 && phase < kArrivePhases)
+      a.s.arrive_ts[(size_t)phase * gridDim.x + blockIdx.x] = globaltimer();
+    const unsigned add = blockIdx.x == 0 ? 0x80000000u - (gridDim.x - 1) : 1u;
     __threadfence();
-    unsigned arrived = atomicAdd(count, 1u);
-    if (arrived == gridDim.x - 1) {
-      atomicExch(count, 0u);
-      __threadfence();
-      atomicAdd(gen, 1u);
-    } else {
-      const unsigned long long t0 = globaltimer();
-      while (ld_acquire_gpu(gen) == my_gen) {
-        if (failed(a) || globaltimer() - t0 > (unsigned long long)a.g.timeout_ns) {
+    const unsigned old = atomicAdd(word, add);
+    unsigned long long t0 = 0;
+    for (unsigned spin = 0;; ++spin) {
+      if (((old ^ ld_acquire_gpu(word)) & 0x80000000u) != 0) break;
+      // back off so that ~150 polling CTAs do not congest the L2 slice the working CTAs also use
+      if (spin >= 2) __nanosleep(spin < 16 ? 100 : 400);
+      if ((spin & 63) == 63) {
+        const unsigned long long t = globaltimer();
+        if (t0 == 0) t0 = t;
+        if (failed(a) || t - t0 > (unsigned long long)a.g.timeout_ns) {
           set_error(a, kErrTimeout);
           ok = 0;
           break;
         }
-        __nanosleep(64);
       }
     }
     __threadfence();
-    if (failed(a)) ok = 0;
     ok_flag = ok;
   }
   __syncthreads();

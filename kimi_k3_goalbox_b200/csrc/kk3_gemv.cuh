@@ -54,12 +54,24 @@ KK3_DEV void cp_async16_g(void* smem_dst, const void* src) {
   asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(smem_dst)),
                "l"(src) : "memory");
 }
+// streamed weights: L2 evict-first, so the stream does not push code, activations and partials out of L2
+KK3_DEV unsigned long long l2_evict_first_policy() {
+  unsigned long long pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+KK3_DEV void cp_async16_stream(void* smem_dst, const void* src, unsigned long long pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(
+                   (unsigned)__cvta_generic_to_shared(smem_dst)),
+               "l"(src), "l"(pol) : "memory");
+}
 KK3_DEV void cp_async_commit_g() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 KK3_DEV void cp_async_wait_g() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// One 64-wide k-step of a 16-row tile: A fragments from this lane's ring slot, activations from global.
-template <int NT, int MT>
+// One 64-wide k-step of a 16-row tile: A fragments from this lane's ring slot; activations from the slot
+// too when they were staged with it (XS), otherwise from global memory.
+template <int NT, int MT, bool XS>
 KK3_DEV void mma_step_bf16(const uint4* __restrict__ slot, const bf16* __restrict__ x, int ldx, int ncols, int ks,
                            float (&acc)[MT][NT][4]) {
   const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
@@ -76,9 +88,14 @@ KK3_DEV void mma_step_bf16(const uint4* __restrict__ slot, const bf16* __restric
     const int n = nt * 8 + r;
     uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
     if (n < ncols) {
-      const bf16* xr = x + (size_t)n * ldx + ks * 64 + 8 * c;
-      X0 = ld_act16(xr);
-      X1 = ld_act16(xr + 32);
+      if (XS) {
+        X0 = slot[(MT * 4 + nt * 2 + 0) * 32 + lane];
+        X1 = slot[(MT * 4 + nt * 2 + 1) * 32 + lane];
+      } else {
+        const bf16* xr = x + (size_t)n * ldx + ks * 64 + 8 * c;
+        X0 = ld_act16(xr);
+        X1 = ld_act16(xr + 32);
+      }
     }
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
@@ -192,14 +209,19 @@ KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const 
 // Deterministic combination of a tile split over warps first..lastw (see the file comment). `acc` is this
 // warp's partial; slot 0/1 of a warp holds its first/other partial tile. Returns true (with the complete
 // tile in `acc`) when this warp arrived last and must run the epilogue.
-template <int NV>
+template <int NT, int MT>
 KK3_DEV bool stream_k_fixup(const StepArgs& a, float* part_base, int* cnt, long long gw, bool first_seg,
                             long long tile_beg, long long first, long long lastw, long long U, long long GW,
-                            float (&acc)[NV]) {
+                            float (&acc)[MT][NT][4]) {
+  constexpr int NV = MT * NT * 4;
   const int lane = threadIdx.x & 31;
   float* slot = part_base + (size_t)(gw * 2 + (first_seg ? 0 : 1)) * (NV * 32);
 #pragma unroll
-  for (int i = 0; i < NV; ++i) slot[i * 32 + lane] = acc[i];
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) slot[((mt * NT + nt) * 4 + i) * 32 + lane] = acc[mt][nt][i];
   __threadfence();
   __syncwarp();
   int old = 0;
@@ -207,22 +229,31 @@ KK3_DEV bool stream_k_fixup(const StepArgs& a, float* part_base, int* cnt, long 
   old = __shfl_sync(0xffffffffu, old, 0);
   if (old != (int)(lastw - first)) return false;
   __threadfence();
-  float sum[NV];
+  float sum[MT][NT][4];
 #pragma unroll
-  for (int i = 0; i < NV; ++i) sum[i] = 0.0f;
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sum[mt][nt][i] = 0.0f;
   for (long long w = first; w <= lastw; ++w) {
-    if (w == gw) {
+    const bool mine = w == gw;
+    const long long wbeg = U * w / GW;
+    const float* ps = part_base + (size_t)(w * 2 + (wbeg >= tile_beg ? 0 : 1)) * (NV * 32);
 #pragma unroll
-      for (int i = 0; i < NV; ++i) sum[i] += acc[i];
-    } else {
-      const long long wbeg = U * w / GW;
-      const float* ps = part_base + (size_t)(w * 2 + (wbeg >= tile_beg ? 0 : 1)) * (NV * 32);
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int i = 0; i < NV; ++i) sum[i] += ld_cg_f32(ps + i * 32 + lane);
-    }
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          sum[mt][nt][i] += mine ? acc[mt][nt][i] : ld_cg_f32(ps + ((mt * NT + nt) * 4 + i) * 32 + lane);
   }
 #pragma unroll
-  for (int i = 0; i < NV; ++i) acc[i] = sum[i];
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[mt][nt][i] = sum[mt][nt][i];
   if (lane == 0) atomicExch(cnt, 0);
   return true;
 }
@@ -242,47 +273,22 @@ KK3_DEV Cursor locate(const GemvJob* jobs, long long u) {
   return c;
 }
 
-KK3_DEV void advance(Cursor& c, const GemvJob* jobs) {
-  if (++c.ks == jobs[c.ji].ksteps) {
-    c.ks = 0;
-    if (++c.tile == jobs[c.ji].tiles) {
-      c.tile = 0;
-      ++c.ji;
-    }
-  }
-}
-
-// stage this lane's 16-byte pieces of one unit (rows r, r+8; k = 64ks + 8c and +32) into its ring slot
-template <int MT>
-KK3_DEV void issue_bf16(const GemvJob& j, const Cursor& c, uint4* slot) {
-  const int lane = threadIdx.x & 31, r = lane >> 2, cc = lane & 3;
-  int ra = c.tile * 16 + r, rb = ra + 8;
-  ra = ra < j.rows ? ra : j.rows - 1;
-  rb = rb < j.rows ? rb : j.rows - 1;
-  const int k0 = c.ks * 64 + 8 * cc;
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
-    const bf16* base = (mt == 0) ? j.w : j.w2;
-    const bf16* pa = base + (size_t)ra * j.K + k0;
-    const bf16* pb = base + (size_t)rb * j.K + k0;
-    cp_async16_g(slot + (mt * 4 + 0) * 32 + lane, pa);
-    cp_async16_g(slot + (mt * 4 + 1) * 32 + lane, pa + 32);
-    cp_async16_g(slot + (mt * 4 + 2) * 32 + lane, pb);
-    cp_async16_g(slot + (mt * 4 + 3) * 32 + lane, pb + 32);
-  }
-}
-
-constexpr int kGemvSmemPerWarp = 12 * 1024;   // ring bytes per warp (6 stages x 2 KB, or 3 x 4 KB)
+constexpr int kGemvSmemPerWarp = 12 * 1024;   // ring bytes per warp (the ring depth follows from the slot size)
 
 // Run a list of dense BF16 jobs with warp-level stream-K over CTAs [cta_lo, cta_hi).
+// Producer and consumer walk the warp's unit range with separate cursors; per tile they set up row and
+// activation pointers once, per unit they only add the k offset (the per-unit instruction count bounds the
+// stream rate at the small batch sizes of decode).
 template <int NT, int MT>
-KK3_DEV void run_gemv(const StepArgs& a, const GemvJob* jobs, int njobs, int cta_lo, int cta_hi, int parity,
-                         int bank = 0) {
+KK3_FN void run_gemv(const StepArgs& a, const GemvJob* jobs, int njobs, int cta_lo, int cta_hi, int parity,
+                         int bank = 0, int ph = -1) {
   if ((int)blockIdx.x < cta_lo || (int)blockIdx.x >= cta_hi) return;
   extern __shared__ __align__(16) unsigned char kk3_dyn_smem[];
-  constexpr int S = (MT == 1) ? 6 : 3;   // ring depth in units
-  constexpr int kSlotVec = MT * 4 * 32;  // uint4 per unit slot
-  const int warp = threadIdx.x >> 5;
+  constexpr bool XS = NT <= 2;                                   // stage activations with the weights
+  constexpr int kSlotVec = (MT * 4 + (XS ? NT * 2 : 0)) * 32;    // uint4 per unit slot
+  constexpr int S = kGemvSmemPerWarp / (kSlotVec * 16);          // ring depth in units
+  static_assert(S >= 2, "ring too shallow");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
   const GemvJob& lastj = jobs[njobs - 1];
   const long long U = lastj.ubase + (long long)lastj.tiles * lastj.ksteps;
   long long GW = (long long)(cta_hi - cta_lo) * kWarps;
@@ -290,22 +296,82 @@ KK3_DEV void run_gemv(const StepArgs& a, const GemvJob* jobs, int njobs, int cta
   const long long gw = (long long)(blockIdx.x - cta_lo) * kWarps + warp;
   if (U == 0 || gw >= GW) return;
   const long long ubeg = U * gw / GW, uend = U * (gw + 1) / GW;
+  const int nunits = (int)(uend - ubeg);
   uint4* ring = reinterpret_cast<uint4*>(kk3_dyn_smem + (size_t)warp * kGemvSmemPerWarp);
   float* part_base = a.s.fix_part + bank * a.g.fix_bank;
   int* cnt_base = a.s.fix_cnt + bank * a.g.cnt_bank;
+  const unsigned long long pol = l2_evict_first_policy();
+  const bool stamp = ph >= 0 && blockIdx.x == 0 && threadIdx.x == 0;
+  if (stamp) sub_stamp(a, ph, 8);
 
-  Cursor pc = locate(jobs, ubeg);
-  Cursor cc = pc;
-  long long pu = ubeg;
+  // ---- producer: cursor + per-tile pointers
+  const Cursor start = locate(jobs, ubeg);
+  int p_ji = start.ji, p_tile = start.tile, p_ks = start.ks, p_ksteps = 0, p_tiles = 0;
+  const bf16* p_wa[MT];
+  const bf16* p_wb[MT];
+  const bf16* p_x[NT];
+  auto p_setup = [&]() {
+    const GemvJob& j = jobs[p_ji];
+    p_ksteps = j.ksteps;
+    p_tiles = j.tiles;
+    int ra = p_tile * 16 + r, rb = ra + 8;
+    ra = ra < j.rows ? ra : j.rows - 1;
+    rb = rb < j.rows ? rb : j.rows - 1;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const bf16* base = (mt == 0) ? j.w : j.w2;
+      p_wa[mt] = base + (size_t)ra * j.K + 8 * c;
+      p_wb[mt] = base + (size_t)rb * j.K + 8 * c;
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int n = nt * 8 + r;
+      p_x[nt] = (XS && n < j.ncols) ? j.x + (size_t)n * j.ldx + 8 * c : nullptr;
+    }
+  };
+  int p_left = nunits, p_slot = 0;
+  auto p_issue = [&]() {
+    uint4* slot = ring + p_slot * kSlotVec;
+    const int off = p_ks * 64;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      cp_async16_stream(slot + (mt * 4 + 0) * 32 + lane, p_wa[mt] + off, pol);
+      cp_async16_stream(slot + (mt * 4 + 1) * 32 + lane, p_wa[mt] + off + 32, pol);
+      cp_async16_stream(slot + (mt * 4 + 2) * 32 + lane, p_wb[mt] + off, pol);
+      cp_async16_stream(slot + (mt * 4 + 3) * 32 + lane, p_wb[mt] + off + 32, pol);
+    }
+    if (XS) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        if (p_x[nt]) {
+          cp_async16_g(slot + (MT * 4 + nt * 2 + 0) * 32 + lane, p_x[nt] + off);
+          cp_async16_g(slot + (MT * 4 + nt * 2 + 1) * 32 + lane, p_x[nt] + off + 32);
+        }
+      }
+    }
+    p_slot = p_slot + 1 == S ? 0 : p_slot + 1;
+    --p_left;
+    if (++p_ks == p_ksteps) {
+      p_ks = 0;
+      if (++p_tile == p_tiles) {
+        p_tile = 0;
+        ++p_ji;
+      }
+      if (p_left > 0) p_setup();
+    }
+  };
+  p_setup();
 #pragma unroll
   for (int i = 0; i < S - 1; ++i) {
-    if (pu < uend) {
-      issue_bf16<MT>(jobs[pc.ji], pc, ring + (int)((pu - ubeg) % S) * kSlotVec);
-      advance(pc, jobs);
-      ++pu;
-    }
+    if (p_left > 0) p_issue();
     cp_async_commit_g();
   }
+
+  // ---- consumer
+  int c_ji = start.ji, c_tile = start.tile, c_ks = start.ks, c_slot = 0;
+  int c_ksteps = jobs[c_ji].ksteps, c_tiles = jobs[c_ji].tiles;
+  const bf16* c_x = jobs[c_ji].x;
+  int c_ldx = jobs[c_ji].ldx, c_ncols = jobs[c_ji].ncols;
   float acc[MT][NT][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
@@ -313,38 +379,88 @@ KK3_DEV void run_gemv(const StepArgs& a, const GemvJob* jobs, int njobs, int cta
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[mt][nt][i] = 0.0f;
-  long long seg_start = ubeg;
-  for (long long u = ubeg; u < uend; ++u) {
-    if (pu < uend) {
-      issue_bf16<MT>(jobs[pc.ji], pc, ring + (int)((pu - ubeg) % S) * kSlotVec);
-      advance(pc, jobs);
-      ++pu;
-    }
+  bool first_seg = true;
+  for (int n = 0; n < nunits; ++n) {
+    if (p_left > 0) p_issue();
     cp_async_commit_g();
     cp_async_wait_g<S - 1>();
-    const GemvJob& j = jobs[cc.ji];
-    mma_step_bf16<NT, MT>(ring + (int)((u - ubeg) % S) * kSlotVec, j.x, j.ldx, j.ncols, cc.ks, acc);
-    if (cc.ks == j.ksteps - 1 || u == uend - 1) {
-      const long long tile_beg = j.ubase + (long long)cc.tile * j.ksteps;
-      const long long first = owner_of(tile_beg, U, GW), lastw = owner_of(tile_beg + j.ksteps - 1, U, GW);
-      bool done = first == lastw;
-      if (!done) {
-        done = stream_k_fixup<MT * NT * 4>(a, part_base, cnt_base + j.tile0 + cc.tile, gw, seg_start == ubeg,
-                                           tile_beg, first, lastw, U, GW,
-                                           *reinterpret_cast<float(*)[MT * NT * 4]>(&acc[0][0][0]));
+    if (stamp && n == 0) sub_stamp(a, ph, 9);
+    if (a.trace && warp == 0 && (n & 63) == 0) trace_progress(a, 1, 0x100000 | n);
+    mma_step_bf16<NT, MT, XS>(ring + c_slot * kSlotVec, c_x, c_ldx, c_ncols, c_ks, acc);
+    c_slot = c_slot + 1 == S ? 0 : c_slot + 1;
+    if (c_ks == c_ksteps - 1 || n == nunits - 1) {
+      const GemvJob& j = jobs[c_ji];
+      const long long tile_beg = j.ubase + (long long)c_tile * c_ksteps;
+      const bool inside = tile_beg >= ubeg && tile_beg + c_ksteps <= uend;   // the whole tile is this warp's
+      bool done = inside;
+      if (!inside) {
+        const long long first = owner_of(tile_beg, U, GW), lastw = owner_of(tile_beg + c_ksteps - 1, U, GW);
+        done = first == lastw ||
+               stream_k_fixup<NT, MT>(a, part_base, cnt_base + j.tile0 + c_tile, gw, first_seg, tile_beg, first,
+                                      lastw, U, GW, acc);
       }
-      if (done) gemv_epilogue<NT, MT>(a, j, cc.tile, acc, parity);
+      if (done) gemv_epilogue<NT, MT>(a, j, c_tile, acc, parity);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
           for (int i = 0; i < 4; ++i) acc[mt][nt][i] = 0.0f;
-      seg_start = u + 1;
+      first_seg = false;
     }
-    advance(cc, jobs);
+    if (++c_ks == c_ksteps) {
+      c_ks = 0;
+      if (++c_tile == c_tiles) {
+        c_tile = 0;
+        if (++c_ji < njobs) {
+          c_ksteps = jobs[c_ji].ksteps;
+          c_tiles = jobs[c_ji].tiles;
+          c_x = jobs[c_ji].x;
+          c_ldx = jobs[c_ji].ldx;
+          c_ncols = jobs[c_ji].ncols;
+        }
+      }
+    }
   }
   cp_async_wait_g<0>();
+  if (stamp) {
+    sub_stamp(a, ph, 10);
+    sub_stamp(a, ph, 11, (unsigned long long)nunits);
+  }
+}
+
+// L2 lookahead: weights never depend on activations, so while a latency-bound phase runs, CTAs that are done
+// with it prefetch the next GEMV phase's weight matrices into L2 (cp.async.bulk.prefetch). The set is split
+// evenly over all CTAs in 64 KB pieces and capped so it fits comfortably in the 126 MB L2.
+constexpr long long kPrefetchCap = 96ll << 20;
+constexpr unsigned kPrefetchPiece = 64u << 10;
+
+KK3_DEV void prefetch_l2(const void* p, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+KK3_FN void prefetch_jobs(const GemvJob* jobs, int njobs) {
+  long long total = 0;
+  for (int i = 0; i < njobs; ++i) total += (long long)jobs[i].rows * jobs[i].K * 2 * (jobs[i].w2 ? 2 : 1);
+  if (total <= 0 || total > kPrefetchCap) return;
+  const long long pieces = (total + kPrefetchPiece - 1) / kPrefetchPiece;
+  const long long nthreads = (long long)gridDim.x * 32;
+  if (threadIdx.x >= 32) return;
+  for (long long piece = (long long)blockIdx.x * 32 + threadIdx.x; piece < pieces; piece += nthreads) {
+    long long off = piece * kPrefetchPiece;
+    for (int i = 0; i < njobs; ++i) {
+      for (int m = 0; m < (jobs[i].w2 ? 2 : 1); ++m) {
+        const long long bytes = (long long)jobs[i].rows * jobs[i].K * 2;
+        if (off < bytes) {
+          const long long n = bytes - off < kPrefetchPiece ? bytes - off : kPrefetchPiece;
+          prefetch_l2(reinterpret_cast<const unsigned char*>(m ? jobs[i].w2 : jobs[i].w) + off, (unsigned)n);
+          i = njobs;
+          break;
+        }
+        off -= bytes;
+      }
+    }
+  }
 }
 
 // Finalise job unit bases / tile counts (all threads compute identical values).
@@ -376,24 +492,24 @@ struct ExpertPhase {
 };
 
 template <int MT>
-KK3_DEV void expert_epilogue(const StepArgs& a, const ExpertPhase& ph, int first_pair, int npairs, int tile,
-                             const float (&acc)[MT][4]) {
+KK3_DEV void expert_epilogue(const StepArgs& a, int rows, int first_pair, int npairs, int tile,
+                             const float (&acc)[MT][1][4]) {
   const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int row = tile * 16 + r + 8 * (i >> 1);
     const int col = 2 * c + (i & 1);
-    if (col >= npairs || row >= ph.rows) continue;
+    if (col >= npairs || row >= rows) continue;
     const int p = first_pair + col;
     if (MT == 2) {
-      const float g = round_bf(acc[0][i]), u = round_bf(acc[MT - 1][i]);
+      const float g = round_bf(acc[0][0][i]), u = round_bf(acc[MT - 1][0][i]);
       const float act = round_bf(situ_f(g, u));
       a.s.act_p[(size_t)p * a.g.inter + row] = __float2half_rn(act);
     } else {
       int b = a.s.pair_row[p], slot = a.s.pair_slot[p];
       b = b < 0 ? 0 : (b >= a.g.B ? a.g.B - 1 : b);
       slot = slot < 0 ? 0 : (slot >= a.g.K ? a.g.K - 1 : slot);
-      a.s.out_slot[((size_t)b * a.g.K + slot) * a.g.lh + row] = f2bf(acc[0][i]);
+      a.s.out_slot[((size_t)b * a.g.K + slot) * a.g.lh + row] = f2bf(acc[0][0][i]);
     }
   }
 }
@@ -409,22 +525,26 @@ KK3_DEV void e2m1x8_cvt(unsigned w, unsigned (&r)[4]) {
 
 KK3_DEV unsigned lds32(const unsigned char* p) { return *reinterpret_cast<const unsigned*>(p); }
 
-constexpr int kFp4Row = 48;                 // staged bytes per row and unit (32 used; 48 keeps LDS conflict-free)
-constexpr int kFp4Slot = 16 * kFp4Row;      // one matrix, one unit
-
 struct ExpertCursor {
   int chunk, tile, ks;
 };
 
+constexpr int kFp4Row = 48;                 // staged bytes per row and unit (32 used; 48 keeps LDS conflict-free)
+constexpr int kFp4Slot = 16 * kFp4Row;      // one matrix, one unit
+
 // Stream-K over (expert chunk, tile, k-step) units. Chunks come from the routing phase. A unit is a
-// 16-row tile x 64 k (two E2M1 groups); the warp's 32 lanes stage its 16 rows x 32 bytes per matrix with
-// one 16-byte cp.async each into a ring (8 deep for gate+up, 16 for down), then every quad reads its
-// rows' 4-byte quarters, converts E2M1 -> FP16 in hardware, and applies the E8M0 scale per group in FP32.
+// 16-row tile x 64 k (two E2M1 groups). Each unit is staged into a per-warp cp.async ring: the 16 rows x 32
+// code bytes of every matrix (one 16-byte copy per lane and matrix) plus the FP16 activation pieces each lane
+// multiplies (lane-private). The E8M0 scales travel a register ring filled with the codes. Each quad reads
+// its rows' 4-byte code quarters, converts E2M1 -> FP16 in hardware and applies the scale per 32-wide group
+// to the FP32 accumulator.
 template <int MT>
-KK3_DEV void run_experts(const StepArgs& a, const ExpertPhase& ph) {
+KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
   extern __shared__ __align__(16) unsigned char kk3_dyn_smem[];
-  constexpr int S = (MT == 2) ? 8 : 16;
-  constexpr int kSlot = MT * kFp4Slot;
+  constexpr int kXOff = MT * kFp4Slot;                 // activation pieces after the code rows
+  constexpr int kSlot = kXOff + 2 * 32 * 16;
+  constexpr int S = kGemvSmemPerWarp / kSlot;
+  static_assert(S >= 2, "ring too shallow");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
   const int npk = a.g.B * a.g.K;
   int nchunks = ld_volatile_int(a.s.chunk_info);
@@ -441,9 +561,29 @@ KK3_DEV void run_experts(const StepArgs& a, const ExpertPhase& ph) {
   float* part_base = a.s.fix_part;
   const int rowbytes = ph.K / 2, sbytes = ph.K / 32;
 
-  auto chunk_expert = [&](int chunk) {
+  // routing-table values are clamped so that a routing fault can never address outside the buffers
+  struct ChunkInfo {
+    int chunk, expert, first_pair, npairs;
+    const __half* xrow;   // activation row this lane multiplies (lane r < npairs), else null
+  };
+  auto load_chunk = [&](int chunk, ChunkInfo& ci) {
+    ci.chunk = chunk;
     int e = a.s.chunk_info[1 + chunk * 3];
-    return e < 0 ? 0 : (e >= a.g.E ? a.g.E - 1 : e);
+    int fp = a.s.chunk_info[2 + chunk * 3];
+    int np = a.s.chunk_info[3 + chunk * 3];
+    ci.expert = e < 0 ? 0 : (e >= a.g.E ? a.g.E - 1 : e);
+    fp = fp < 0 ? 0 : (fp >= npk ? npk - 1 : fp);
+    np = np < 0 ? 0 : (np > 8 ? 8 : np);
+    np = fp + np > npk ? npk - fp : np;
+    ci.first_pair = fp;
+    ci.npairs = np;
+    ci.xrow = nullptr;
+    if (r < np) {
+      const int p = fp + r;
+      int prow = a.s.pair_row[p];
+      prow = prow < 0 ? 0 : (prow >= a.g.B ? a.g.B - 1 : prow);
+      ci.xrow = (MT == 2) ? a.s.latent_p + (size_t)prow * a.g.lh : a.s.act_p + (size_t)p * a.g.inter;
+    }
   };
   auto at = [&](long long u) {
     ExpertCursor q;
@@ -462,78 +602,87 @@ KK3_DEV void run_experts(const StepArgs& a, const ExpertPhase& ph) {
       }
     }
   };
-  // staging: lane -> (row = lane/2, 16-byte half = lane%2) of every matrix
   const int srow = lane >> 1, shalf = lane & 1;
-  auto issue = [&](const ExpertCursor& q, unsigned char* slot) {
-    const int e = chunk_expert(q.chunk);
+  auto issue = [&](const ExpertCursor& q, const ChunkInfo& ci, unsigned char* slot) {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-      const uint8_t* src = ph.codes[mt] + (size_t)e * ph.expert_codes + (size_t)(q.tile * 16 + srow) * rowbytes +
-                           q.ks * 32 + shalf * 16;
+      const uint8_t* src = ph.codes[mt] + (size_t)ci.expert * ph.expert_codes +
+                           (size_t)(q.tile * 16 + srow) * rowbytes + q.ks * 32 + shalf * 16;
       cp_async16_g(slot + mt * kFp4Slot + srow * kFp4Row + shalf * 16, src);
+    }
+    if (ci.xrow) {
+      cp_async16_g(slot + kXOff + lane * 16, ci.xrow + q.ks * 64 + 8 * c);
+      cp_async16_g(slot + kXOff + 512 + lane * 16, ci.xrow + q.ks * 64 + 32 + 8 * c);
+    }
+  };
+  // E8M0 scales of rows r, r+8 for a unit's two groups, packed as (row r+8 << 16 | row r) per matrix; loaded by
+  // the producer when it stages the unit and shifted through a register ring, so they arrive with the codes
+  auto load_scales = [&](const ExpertCursor& q, const ChunkInfo& ci, unsigned (&sc)[MT]) {
+    const int rowa = q.tile * 16 + r;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const uint8_t* sbase = ph.scales[mt] + (size_t)ci.expert * ph.expert_scales + q.ks * 2;
+      const unsigned lo = ldg_nc16(sbase + (size_t)rowa * sbytes);
+      const unsigned hi = ldg_nc16(sbase + (size_t)(rowa + 8) * sbytes);
+      sc[mt] = lo | (hi << 16);
     }
   };
 
   ExpertCursor pc = at(ubeg), cc = pc;
+  ChunkInfo pci, cci;
+  load_chunk(pc.chunk, pci);
+  cci = pci;
   long long pu = ubeg;
+  unsigned sring[S][MT];   // scales of the units in the ring, oldest first (compile-time indices only)
+#pragma unroll
+  for (int i = 0; i < S; ++i)
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) sring[i][mt] = 0x7f7f7f7fu;
 #pragma unroll
   for (int i = 0; i < S - 1; ++i) {
     if (pu < uend) {
-      issue(pc, ring + (int)((pu - ubeg) % S) * kSlot);
+      if (pc.chunk != pci.chunk) load_chunk(pc.chunk, pci);
+      issue(pc, pci, ring + (int)((pu - ubeg) % S) * kSlot);
+      load_scales(pc, pci, sring[i]);
       step(pc);
       ++pu;
     }
     cp_async_commit_g();
   }
-  float acc[MT][4];
+  float acc[MT][1][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[mt][i] = 0.0f;
+    for (int i = 0; i < 4; ++i) acc[mt][0][i] = 0.0f;
   long long seg_start = ubeg;
-  int cur_chunk = -1, expert = 0, first_pair = 0, npairs = 0;
-  const __half* xrow = nullptr;
   for (long long u = ubeg; u < uend; ++u) {
     __syncwarp();   // every lane is done with the slot the next issue overwrites
     if (pu < uend) {
-      issue(pc, ring + (int)((pu - ubeg) % S) * kSlot);
+      if (pc.chunk != pci.chunk) load_chunk(pc.chunk, pci);
+      issue(pc, pci, ring + (int)((pu - ubeg) % S) * kSlot);
+      load_scales(pc, pci, sring[S - 1]);
       step(pc);
       ++pu;
     }
     cp_async_commit_g();
-    if (cc.chunk != cur_chunk) {
-      cur_chunk = cc.chunk;
-      expert = chunk_expert(cur_chunk);
-      first_pair = a.s.chunk_info[2 + cur_chunk * 3];
-      npairs = a.s.chunk_info[3 + cur_chunk * 3];
-      first_pair = first_pair < 0 ? 0 : (first_pair >= npk ? npk - 1 : first_pair);
-      npairs = npairs < 0 ? 0 : (npairs > 8 ? 8 : npairs);
-      npairs = first_pair + npairs > npk ? npk - first_pair : npairs;
-      xrow = nullptr;
-      if (r < npairs) {
-        const int p = first_pair + r;
-        int prow = a.s.pair_row[p];
-        prow = prow < 0 ? 0 : (prow >= a.g.B ? a.g.B - 1 : prow);
-        xrow = (MT == 2) ? a.s.latent_p + (size_t)prow * a.g.lh : a.s.act_p + (size_t)p * a.g.inter;
-      }
-    }
-    // scales of rows r, r+8 for the unit's two groups, and the activations
-    const int rowa = cc.tile * 16 + r;
+    cp_async_wait_g<S - 1>();
+    __syncwarp();
     unsigned sa[MT], sb[MT];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-      const uint8_t* sbase = ph.scales[mt] + (size_t)expert * ph.expert_scales + cc.ks * 2;
-      sa[mt] = *reinterpret_cast<const unsigned short*>(sbase + (size_t)rowa * sbytes);
-      sb[mt] = *reinterpret_cast<const unsigned short*>(sbase + (size_t)(rowa + 8) * sbytes);
+      sa[mt] = sring[0][mt] & 0xffffu;
+      sb[mt] = sring[0][mt] >> 16;
     }
-    uint4 X[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-    if (xrow) {
-      X[0] = ld_act16(xrow + cc.ks * 64 + 8 * c);
-      X[1] = ld_act16(xrow + cc.ks * 64 + 32 + 8 * c);
-    }
-    cp_async_wait_g<S - 1>();
-    __syncwarp();
+#pragma unroll
+    for (int i = 0; i + 1 < S; ++i)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) sring[i][mt] = sring[i + 1][mt];
     const unsigned char* slot = ring + (int)((u - ubeg) % S) * kSlot;
+    uint4 X[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+    if (cci.xrow) {
+      X[0] = *reinterpret_cast<const uint4*>(slot + kXOff + lane * 16);
+      X[1] = *reinterpret_cast<const uint4*>(slot + kXOff + 512 + lane * 16);
+    }
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
@@ -548,27 +697,30 @@ KK3_DEV void run_experts(const StepArgs& a, const ExpertPhase& ph) {
         mma_f16(t, ra[2], rb[2], ra[3], rb[3], X[g].z, X[g].w);
         const float fa = e8m0_to_f32((sa[mt] >> (8 * g)) & 0xffu);
         const float fb = e8m0_to_f32((sb[mt] >> (8 * g)) & 0xffu);
-        acc[mt][0] = fmaf(t[0], fa, acc[mt][0]);
-        acc[mt][1] = fmaf(t[1], fa, acc[mt][1]);
-        acc[mt][2] = fmaf(t[2], fb, acc[mt][2]);
-        acc[mt][3] = fmaf(t[3], fb, acc[mt][3]);
+        acc[mt][0][0] = fmaf(t[0], fa, acc[mt][0][0]);
+        acc[mt][0][1] = fmaf(t[1], fa, acc[mt][0][1]);
+        acc[mt][0][2] = fmaf(t[2], fb, acc[mt][0][2]);
+        acc[mt][0][3] = fmaf(t[3], fb, acc[mt][0][3]);
       }
     }
     if (cc.ks == ph.ksteps - 1 || u == uend - 1) {
       const long long tile_beg = (long long)cc.chunk * per_chunk + (long long)cc.tile * ph.ksteps;
-      const long long first = owner_of(tile_beg, U, GW), lastw = owner_of(tile_beg + ph.ksteps - 1, U, GW);
+      const bool inside = tile_beg >= ubeg && tile_beg + ph.ksteps <= uend;   // the whole tile is this warp's
+      const long long first = inside ? gw : owner_of(tile_beg, U, GW);
+      const long long lastw = inside ? gw : owner_of(tile_beg + ph.ksteps - 1, U, GW);
       bool done = first == lastw;
       if (!done)
-        done = stream_k_fixup<MT * 4>(a, part_base, a.s.fix_cnt + cc.chunk * ph.tiles + cc.tile, gw, seg_start == ubeg,
-                                      tile_beg, first, lastw, U, GW, *reinterpret_cast<float(*)[MT * 4]>(&acc[0][0]));
-      if (done) expert_epilogue<MT>(a, ph, first_pair, npairs, cc.tile, acc);
+        done = stream_k_fixup<1, MT>(a, part_base, a.s.fix_cnt + cc.chunk * ph.tiles + cc.tile, gw, seg_start == ubeg,
+                                     tile_beg, first, lastw, U, GW, acc);
+      if (done) expert_epilogue<MT>(a, ph.rows, cci.first_pair, cci.npairs, cc.tile, acc);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[mt][i] = 0.0f;
+        for (int i = 0; i < 4; ++i) acc[mt][0][i] = 0.0f;
       seg_start = u + 1;
     }
     step(cc);
+    if (u + 1 < uend && cc.chunk != cci.chunk) load_chunk(cc.chunk, cci);
   }
   cp_async_wait_g<0>();
 }

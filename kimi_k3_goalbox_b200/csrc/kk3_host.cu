@@ -53,6 +53,9 @@ struct kk3_ctx {
   void* peer_open[kMaxTp] = {};
   int* err_host = nullptr;
   int* err_dev = nullptr;
+  int* trace_host = nullptr;   // mapped progress words (fault localisation): [2][1024] per CTA, [4096] per warp
+  int* trace_dev = nullptr;
+  int trace = 0;
   unsigned epoch = 0;
   int failed = 0;
   int peers_open = 0;
@@ -185,7 +188,8 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
       {(void**)&s.shared_red, B * g.h * 2}, {(void**)&s.expert_sum, B * g.lh * 4},
       {(void**)&s.fix_part, (size_t)g.fix_bank * 2 * 4}, {(void**)&s.fix_cnt, (size_t)g.cnt_bank * 2 * 4},
       {(void**)&s.argmax_key, B * 8}, {(void**)&bar, 64}, {(void**)&phase_count, 64}, {(void**)&s.err, 64},
-      {(void**)&s.phase_ts, (kMaxPhases + 1) * 8},
+      {(void**)&s.phase_ts, (kMaxPhases + 1) * 8}, {(void**)&s.arrive_ts, (size_t)kArrivePhases * 1024 * 8},
+      {(void**)&s.sub_ts, (size_t)kArrivePhases * 16 * 8},
   };
   size_t total = 0;
   for (auto& it : items) total += align_up(it.bytes, 256);
@@ -210,6 +214,12 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
     cudaFreeHost(x->err_host); cudaFree(x->scratch); delete x; return KK3_ERR_CUDA;
   }
   s.err_host = x->err_dev;
+  if (cudaHostAlloc((void**)&x->trace_host, kTraceWords * sizeof(int), cudaHostAllocMapped) != cudaSuccess ||
+      cudaHostGetDevicePointer((void**)&x->trace_dev, x->trace_host, 0) != cudaSuccess) {
+    cudaFreeHost(x->err_host); cudaFree(x->scratch); delete x; return KK3_ERR_CUDA;
+  }
+  memset(x->trace_host, 0xff, kTraceWords * sizeof(int));
+  s.trace_host = x->trace_dev;
   // exchange buffer: flags [B][tp] u32, then two parity regions {att bf16 [tp][B][h], exp f32 [tp][B][lh],
   // shd bf16 [tp][B][h], key u64 [tp][B]}
   Comm& c = x->comm;
@@ -263,12 +273,13 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   // diagnostics table
   void* bp[KK3_BUF_COUNT] = {s.prefix, s.xa, s.xm, s.attn_in, s.scores, s.latent, s.shared_act, s.x3, s.route_w,
                              s.qkv, s.mla_q, s.absorbed, s.absorbed, s.expert_sum, s.blocks, x->comm_local,
-                             s.phase_ts};
+                             s.phase_ts, s.arrive_ts, s.sub_ts};
   size_t bb[KK3_BUF_COUNT] = {B * g.h * 2, B * g.h * 2, B * g.h * 2, B * (size_t)g.hr * g.vd * 2, B * g.E * 4,
                               B * g.lh * 2, B * (size_t)g.sinter * 2, B * g.lh * 2, B * g.K * 4, B * qkv_w * 2,
                               B * (size_t)g.hr * (g.nr + g.rd) * 2, B * (size_t)g.hr * g.kr * 2,
                               B * (size_t)g.hr * g.kr * 2, B * g.lh * 4, (size_t)g.nblk * B * g.h * 2, x->comm_bytes,
-                              (size_t)(kMaxPhases + 1) * 8};
+                              (size_t)(kMaxPhases + 1) * 8, (size_t)kArrivePhases * 1024 * 8,
+                              (size_t)kArrivePhases * 16 * 8};
   for (int i = 0; i < KK3_BUF_COUNT; ++i) { x->buf_ptr[i] = bp[i]; x->buf_bytes[i] = bb[i]; }
   *out = x;
   return KK3_OK;
@@ -329,6 +340,7 @@ static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int
   a->epoch = ++x->epoch;
   a->stop_phase = stop_phase;
   a->start_phase = start_phase < 0 ? 0 : start_phase;
+  a->trace = x->trace;
   a->nptr = n;
   memcpy(a->ptr, table, sizeof(void*) * n);
   cudaError_t e = launch_kernel(x->nt, a, x->grid, x->smem, (cudaStream_t)stream);
@@ -377,6 +389,16 @@ extern "C" int kk3_debug_copy(kk3_ctx* x, int id, void* dst, size_t bytes) {
   return KK3_OK;
 }
 
+extern "C" int kk3_debug_trace(kk3_ctx* x, int enable, int* out, int n) {
+  if (!x) return KK3_ERR_ARG;
+  if (enable >= 0) x->trace = enable;
+  if (out) {
+    const int m = n < kTraceWords ? n : kTraceWords;
+    for (int i = 0; i < m; ++i) out[i] = ((volatile int*)x->trace_host)[i];
+  }
+  return KK3_OK;
+}
+
 extern "C" void kk3_free(kk3_ctx* x) {
   if (!x) return;
   cudaSetDevice(x->cfg.device);
@@ -385,6 +407,7 @@ extern "C" void kk3_free(kk3_ctx* x) {
   if (x->comm_local) cudaFree(x->comm_local);
   if (x->scratch) cudaFree(x->scratch);
   if (x->err_host) cudaFreeHost(x->err_host);
+  if (x->trace_host) cudaFreeHost(x->trace_host);
   delete x->args;
   delete x;
 }

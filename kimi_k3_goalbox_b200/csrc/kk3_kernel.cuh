@@ -19,7 +19,7 @@ enum Pending : int { PEND_NONE = 0, PEND_EMBED, PEND_DENSE };
 
 // ---- row phases ------------------------------------------------------------------------------------
 
-KK3_DEV void phase_embed(const StepArgs& a, unsigned seq, int parity, float* fsm) {
+KK3_FN void phase_embed(const StepArgs& a, unsigned seq, int parity, float* fsm) {
   const Geo& g = a.g;
   const long long* tok = gptr<long long>(a, KK3_TOKEN);
   const bf16* emb = gptr<bf16>(a, KK3_EMBED);
@@ -46,87 +46,99 @@ KK3_DEV void phase_embed(const StepArgs& a, unsigned seq, int parity, float* fsm
   (void)fsm;
 }
 
-// finish a pending exchange into prefix (embedding: assign; dense FFN: add), then the attention prologue
-KK3_DEV bool phase_attn_prologue(const StepArgs& a, int layer, int nb, int pending, bool need_signal, unsigned seq,
-                                 int parity, float* fsm) {
+// load this thread's chunks of prefix row b, folding a pending exchange in first (embedding: assign;
+// dense FFN / attention: add, or assign right after a block push), and write the result back
+KK3_DEV void load_prefix(const StepArgs& a, int b, int fold, bool assign, int parity, uint4 (&pre)[kRowChunks]) {
   const Geo& g = a.g;
-  float* red = fsm;
-  float* hbuf = fsm + 512;
+  const int nvec = g.h / 8;
+  bf16* row = a.s.prefix + (size_t)b * g.h;
+#pragma unroll
+  for (int q = 0; q < kRowChunks; ++q) {
+    const int c = threadIdx.x + q * kThreads;
+    pre[q] = make_uint4(0, 0, 0, 0);
+    if (c >= nvec) continue;
+    if (!fold) {
+      pre[q] = ld_act16(row + c * 8);
+      continue;
+    }
+    float x[8], old[8];
+    xch_sum8(a, parity, a.comm.att_off, b, g.h, c, x);
+    if (!assign) {
+      unpack8(ld_act16(row + c * 8), old);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = round_bf(old[e] + x[e]);
+    }
+    pre[q] = pack8(x);
+    *reinterpret_cast<uint4*>(row + c * 8) = pre[q];
+  }
+}
+
+KK3_DEV void store_row(bf16* dst, const uint4 (&v)[kRowChunks], int nvec) {
+#pragma unroll
+  for (int q = 0; q < kRowChunks; ++q) {
+    const int c = threadIdx.x + q * kThreads;
+    if (c < nvec) *reinterpret_cast<uint4*>(dst + c * 8) = v[q];
+  }
+}
+
+// finish a pending exchange into prefix (embedding: assign; dense FFN: add), then the attention prologue
+KK3_FN bool phase_attn_prologue(const StepArgs& a, int layer, int nb, int pending, bool need_signal, unsigned seq,
+                                 int parity, float* fsm, int ph = -1) {
+  const Geo& g = a.g;
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
-    if (pending != PEND_NONE) {
-      if (g.tp > 1) {
-        if (need_signal) xch_signal_row(a, b, seq);
-        if (!xch_wait_row(a, b, seq)) return false;
-      }
-      bf16* pre = a.s.prefix + (size_t)b * g.h;
-      for (int e = threadIdx.x; e < g.h; e += kThreads) {
-        float v;
-        if (g.tp == 1 && pending == PEND_EMBED) {
-          v = bf2f(pre[e]);
-        } else {
-          v = xch_sum_bf16(a, parity, a.comm.att_off, b, g.h, e);
-          if (pending == PEND_DENSE) v = round_bf(bf2f(pre[e]) + v);
-        }
-        pre[e] = f2bf(v);
-      }
-      __syncthreads();
+    if (b == 0 && threadIdx.x == 0) sub_stamp(a, ph, 0);
+    const bool fold = pending != PEND_NONE && !(g.tp == 1 && pending == PEND_EMBED);
+    if (pending != PEND_NONE && g.tp > 1) {
+      if (need_signal) xch_signal_row(a, b, seq);
+      if (!xch_wait_row(a, b, seq)) return false;
     }
-    mix_and_norm(a, b, nb, gptr<bf16>(a, KK3_ATTENTION_RES_NORM) + (size_t)layer * g.h,
-                 gptr<bf16>(a, KK3_ATTENTION_RES_PROJ) + (size_t)layer * g.h, gptr<bf16>(a, KK3_LN1) + (size_t)layer * g.h,
-                 1e-5f, a.s.xa + (size_t)b * g.h, hbuf, red);
-    if (layer % g.bs == 0) {
-      bf16* dst = a.s.blocks + ((size_t)nb * g.B + b) * g.h;
-      for (int e = threadIdx.x; e < g.h; e += kThreads) dst[e] = a.s.prefix[(size_t)b * g.h + e];
-    }
+    uint4 pre[kRowChunks];
+    load_prefix(a, b, fold, pending == PEND_EMBED, parity, pre);
+    mix_and_norm_regs(a, b, nb, pre, gptr<bf16>(a, KK3_ATTENTION_RES_NORM) + (size_t)layer * g.h,
+                      gptr<bf16>(a, KK3_ATTENTION_RES_PROJ) + (size_t)layer * g.h,
+                      gptr<bf16>(a, KK3_LN1) + (size_t)layer * g.h, 1e-5f, a.s.xa + (size_t)b * g.h, fsm, ph);
+    if (b == 0 && threadIdx.x == 0) sub_stamp(a, ph, 6);
+    if (layer % g.bs == 0) store_row(a.s.blocks + ((size_t)nb * g.B + b) * g.h, pre, g.h / 8);
     __syncthreads();
   }
   return true;
 }
 
 // fold a pending exchange into prefix without a following norm (only when the last layer is dense)
-KK3_DEV bool phase_fold_pending(const StepArgs& a, int pending, bool need_signal, unsigned seq, int parity) {
+KK3_FN bool phase_fold_pending(const StepArgs& a, int pending, bool need_signal, unsigned seq, int parity) {
   const Geo& g = a.g;
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
     if (g.tp > 1) {
       if (need_signal) xch_signal_row(a, b, seq);
       if (!xch_wait_row(a, b, seq)) return false;
     }
-    bf16* pre = a.s.prefix + (size_t)b * g.h;
-    for (int e = threadIdx.x; e < g.h; e += kThreads) {
-      const float v = xch_sum_bf16(a, parity, a.comm.att_off, b, g.h, e);
-      pre[e] = f2bf(pending == PEND_DENSE ? round_bf(bf2f(pre[e]) + v) : v);
-    }
+    uint4 pre[kRowChunks];
+    load_prefix(a, b, 1, pending == PEND_EMBED, parity, pre);
     __syncthreads();
   }
   return true;
 }
 
 // attention exchange -> prefix (assign right after a block push, else add), then the MLP prologue
-KK3_DEV bool phase_mlp_prologue(const StepArgs& a, int layer, int nb_after, unsigned seq, int parity, float* fsm) {
+KK3_FN bool phase_mlp_prologue(const StepArgs& a, int layer, int nb_after, unsigned seq, int parity, float* fsm) {
   const Geo& g = a.g;
-  float* red = fsm;
-  float* hbuf = fsm + 512;
-  const bool assign = (layer % g.bs) == 0;
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
     if (g.tp > 1) {
       xch_signal_row(a, b, seq);
       if (!xch_wait_row(a, b, seq)) return false;
     }
-    bf16* pre = a.s.prefix + (size_t)b * g.h;
-    for (int e = threadIdx.x; e < g.h; e += kThreads) {
-      const float att = xch_sum_bf16(a, parity, a.comm.att_off, b, g.h, e);
-      pre[e] = f2bf(assign ? att : round_bf(bf2f(pre[e]) + att));
-    }
+    uint4 pre[kRowChunks];
+    load_prefix(a, b, 1, (layer % g.bs) == 0, parity, pre);
+    mix_and_norm_regs(a, b, nb_after, pre, gptr<bf16>(a, KK3_MLP_RES_NORM) + (size_t)layer * g.h,
+                      gptr<bf16>(a, KK3_MLP_RES_PROJ) + (size_t)layer * g.h, gptr<bf16>(a, KK3_LN2) + (size_t)layer * g.h,
+                      1e-5f, a.s.xm + (size_t)b * g.h, fsm);
     __syncthreads();
-    mix_and_norm(a, b, nb_after, gptr<bf16>(a, KK3_MLP_RES_NORM) + (size_t)layer * g.h,
-                 gptr<bf16>(a, KK3_MLP_RES_PROJ) + (size_t)layer * g.h, gptr<bf16>(a, KK3_LN2) + (size_t)layer * g.h, 1e-5f,
-                 a.s.xm + (size_t)b * g.h, hbuf, red);
   }
   return true;
 }
 
 // MLA row prologue: q_a norm, latent norm (-> kv_write), rope part (-> pe_write)  (kimi.py:265-270)
-KK3_DEV void phase_mla_rows(const StepArgs& a, int layer, int midx, float* fsm) {
+KK3_FN void phase_mla_rows(const StepArgs& a, int layer, int midx, float* fsm) {
   const Geo& g = a.g;
   const bf16* qa = a.s.qkv;
   const bf16* ka = a.s.qkv + (size_t)g.B * g.qr;
@@ -142,63 +154,107 @@ KK3_DEV void phase_mla_rows(const StepArgs& a, int layer, int midx, float* fsm) 
 
 // MoE combine: expert_sum (slot order = ascending expert id, kimi.py:319-323), TP sum (:324),
 // latent_norm (:325) -> x3; shared-expert TP sum (:326) -> shared_red
-KK3_DEV bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int parity, float* fsm) {
+KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int parity, float* fsm) {
   const Geo& g = a.g;
   float* red = fsm;
-  float* tot = fsm + 512;   // [lh]
+  const int nvec = g.lh / 8, hvec = g.h / 8;
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
     const float* w = a.s.route_w + (size_t)b * g.K;
-    for (int e = threadIdx.x; e < g.lh; e += kThreads) {
-      float acc = 0.0f;
-      for (int j = 0; j < g.K; ++j) acc += bf2f(a.s.out_slot[((size_t)b * g.K + j) * g.lh + e]) * w[j];
-      tot[e] = acc;
-      a.s.expert_sum[(size_t)b * g.lh + e] = acc;
+    float tot[kRowChunks][8];
+#pragma unroll
+    for (int q = 0; q < kRowChunks; ++q) {
+      const int c = threadIdx.x + q * kThreads;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) tot[q][e] = 0.0f;
+      if (c >= nvec) continue;
+      for (int j = 0; j < g.K; ++j) {
+        float f[8];
+        unpack8(ld_act16(a.s.out_slot + ((size_t)b * g.K + j) * g.lh + c * 8), f);
+        const float wj = w[j];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) tot[q][e] += f[e] * wj;
+      }
+      float* es = a.s.expert_sum + (size_t)b * g.lh + c * 8;
+      *reinterpret_cast<float4*>(es) = make_float4(tot[q][0], tot[q][1], tot[q][2], tot[q][3]);
+      *reinterpret_cast<float4*>(es + 4) = make_float4(tot[q][4], tot[q][5], tot[q][6], tot[q][7]);
     }
     if (g.tp > 1) {
       const size_t off = ((size_t)g.rank * g.B + b) * g.lh;
       for (int dst = 0; dst < g.tp; ++dst) {
-        float* reg = reinterpret_cast<float*>(a.comm.base[dst] + a.comm.data_off[parity] + a.comm.exp_off);
-        for (int e = threadIdx.x; e < g.lh; e += kThreads) reg[off + e] = tot[e];
+        float* reg = reinterpret_cast<float*>(a.comm.base[dst] + a.comm.data_off[parity] + a.comm.exp_off) + off;
+#pragma unroll
+        for (int q = 0; q < kRowChunks; ++q) {
+          const int c = threadIdx.x + q * kThreads;
+          if (c >= nvec) continue;
+          *reinterpret_cast<float4*>(reg + c * 8) = make_float4(tot[q][0], tot[q][1], tot[q][2], tot[q][3]);
+          *reinterpret_cast<float4*>(reg + c * 8 + 4) = make_float4(tot[q][4], tot[q][5], tot[q][6], tot[q][7]);
+        }
       }
       xch_signal_row(a, b, seq);
       if (!xch_wait_row(a, b, seq)) return false;
       const float* reg = xlocal<float>(a, parity, a.comm.exp_off);
-      for (int e = threadIdx.x; e < g.lh; e += kThreads) {
-        float acc = 0.0f;
-        for (int src = 0; src < g.tp; ++src) acc += reg[((size_t)src * g.B + b) * g.lh + e];
-        tot[e] = acc;
+#pragma unroll
+      for (int q = 0; q < kRowChunks; ++q) {
+        const int c = threadIdx.x + q * kThreads;
+        if (c >= nvec) continue;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) tot[q][e] = 0.0f;
+        for (int src = 0; src < g.tp; ++src) {
+          const float* r = reg + ((size_t)src * g.B + b) * g.lh + c * 8;
+          const float4 v0 = *reinterpret_cast<const float4*>(r), v1 = *reinterpret_cast<const float4*>(r + 4);
+          tot[q][0] += v0.x; tot[q][1] += v0.y; tot[q][2] += v0.z; tot[q][3] += v0.w;
+          tot[q][4] += v1.x; tot[q][5] += v1.y; tot[q][6] += v1.z; tot[q][7] += v1.w;
+        }
       }
     }
-    __syncthreads();
     // x3 = rms(bf16(total), latent_norm)
-    float ss = 0.0f;
-    for (int e = threadIdx.x; e < g.lh; e += kThreads) {
-      const float v = round_bf(tot[e]);
-      tot[e] = v;
-      ss += v * v;
-    }
-    const float s = block_sum(ss, red);
-    const float rs = rsqrtf(s / (float)g.lh + 1e-5f);
+    float ss[1] = {0.0f};
+#pragma unroll
+    for (int q = 0; q < kRowChunks; ++q)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        tot[q][e] = round_bf(tot[q][e]);
+        ss[0] += tot[q][e] * tot[q][e];
+      }
+    block_sums<1>(ss, red);
+    const float rs = rsqrtf(ss[0] / (float)g.lh + 1e-5f);
     const bf16* ln = lptr<bf16>(a, layer, KK3_MOE_LATENT_NORM);
-    for (int e = threadIdx.x; e < g.lh; e += kThreads)
-      a.s.x3[(size_t)b * g.lh + e] = f2bf(round_bf(tot[e] * rs) * bf2f(ln[e]));
-    for (int e = threadIdx.x; e < g.h; e += kThreads)
-      a.s.shared_red[(size_t)b * g.h + e] = f2bf(xch_sum_bf16(a, parity, a.comm.shd_off, b, g.h, e));
+#pragma unroll
+    for (int q = 0; q < kRowChunks; ++q) {
+      const int c = threadIdx.x + q * kThreads;
+      if (c >= nvec) continue;
+      float wf[8], o[8];
+      unpack8(ld_act16(ln + c * 8), wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = round_bf(round_bf(tot[q][e] * rs) * wf[e]);
+      *reinterpret_cast<uint4*>(a.s.x3 + (size_t)b * g.lh + c * 8) = pack8(o);
+    }
+#pragma unroll
+    for (int q = 0; q < kRowChunks; ++q) {
+      const int c = threadIdx.x + q * kThreads;
+      if (c >= hvec) continue;
+      float x[8];
+      xch_sum8(a, parity, a.comm.shd_off, b, g.h, c, x);
+      *reinterpret_cast<uint4*>(a.s.shared_red + (size_t)b * g.h + c * 8) = pack8(x);
+    }
     __syncthreads();
   }
   return true;
 }
 
-KK3_DEV void phase_head_prologue(const StepArgs& a, int nb, float* fsm) {
+KK3_FN void phase_head_prologue(const StepArgs& a, int nb, float* fsm) {
   const Geo& g = a.g;
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
-    mix_and_norm(a, b, nb, gptr<bf16>(a, KK3_OUTPUT_RES_NORM), gptr<bf16>(a, KK3_OUTPUT_RES_PROJ),
-                 gptr<bf16>(a, KK3_FNORM), 1e-5f, a.s.xa + (size_t)b * g.h, fsm + 512, fsm);
+    uint4 pre[kRowChunks];
+    load_prefix(a, b, 0, false, 0, pre);
+    mix_and_norm_regs(a, b, nb, pre, gptr<bf16>(a, KK3_OUTPUT_RES_NORM), gptr<bf16>(a, KK3_OUTPUT_RES_PROJ),
+                      gptr<bf16>(a, KK3_FNORM), 1e-5f, a.s.xa + (size_t)b * g.h, fsm);
     if (threadIdx.x == 0) a.s.argmax_key[b] = 0ull;
+    __syncthreads();
   }
 }
 
-KK3_DEV bool phase_argmax(const StepArgs& a, unsigned seq, int parity) {
+KK3_FN bool phase_argmax(const StepArgs& a, unsigned seq, int parity) {
   const Geo& g = a.g;
   long long* next = gout<long long>(a, KK3_OUT_NEXT_TOKEN);
   long long* len = gout<long long>(a, KK3_OUT_CACHE_LENGTH);
@@ -236,26 +292,117 @@ KK3_DEV bool phase_argmax(const StepArgs& a, unsigned seq, int parity) {
   return true;
 }
 
+// ---- job lists of the GEMV phases (built identically by every thread) ---------------------------------
+
+KK3_DEV void job_init(GemvJob& j, const bf16* w, int rows, int K, const bf16* x, int ldx, int ncols, int epi, void* out,
+                      int ldo) {
+  j = GemvJob{};
+  j.w = w; j.rows = rows; j.K = K; j.x = x; j.ldx = ldx; j.ncols = ncols; j.epi = epi; j.out = out; j.ldo = ldo;
+}
+
+// L2 lookahead (prefetch_jobs) is issued only from phases that stream HBM themselves (KDA, MLA combine):
+// in the latency-bound row phases the bulk prefetch traffic queued ahead of their few dependent loads.
+
+// attention input projections: KDA q,k,v,g,f_a,beta (kimi.py:285, :290-291, :298) or MLA q_a, kv_a, g (:265-266, :282)
+KK3_DEV int attn_proj_jobs(const StepArgs& a, int l, bool mla, GemvJob* jobs) {
+  const Geo& g = a.g;
+  if (!mla) {
+    const int slots[4] = {KK3_KDA_Q, KK3_KDA_K, KK3_KDA_V, KK3_KDA_OUTPUT_GATE};
+    for (int i = 0; i < 3; ++i)
+      job_init(jobs[i], lptr<bf16>(a, l, slots[i]), g.qdim, g.h, a.s.xa, g.h, g.B, EPI_STORE_BF16,
+               a.s.qkv + (size_t)i * g.qdim, 3 * g.qdim);
+    job_init(jobs[3], lptr<bf16>(a, l, slots[3]), g.qdim, g.h, a.s.xa, g.h, g.B, EPI_STORE_BF16, a.s.og, g.qdim);
+    job_init(jobs[4], lptr<bf16>(a, l, KK3_KDA_FA), g.d, g.h, a.s.xa, g.h, g.B, EPI_STORE_BF16, a.s.fa, g.d);
+    job_init(jobs[5], lptr<bf16>(a, l, KK3_KDA_BETA), g.hr, g.h, a.s.xa, g.h, g.B, EPI_STORE_BF16, a.s.beta, g.hr);
+    prepare_jobs(jobs, 6);
+    return 6;
+  }
+  job_init(jobs[0], lptr<bf16>(a, l, KK3_MLA_QA), g.qr, g.h, a.s.xa, g.h, g.B, EPI_STORE_BF16, a.s.qkv, g.qr);
+  job_init(jobs[1], lptr<bf16>(a, l, KK3_MLA_KA), g.kr + g.rd, g.h, a.s.xa, g.h, g.B, EPI_STORE_BF16,
+           a.s.qkv + (size_t)g.B * g.qr, g.kr + g.rd);
+  job_init(jobs[2], lptr<bf16>(a, l, KK3_MLA_OUTPUT_GATE), g.hr * g.vd, g.h, a.s.xa, g.h, g.B, EPI_STORE_BF16, a.s.og,
+           g.hr * g.vd);
+  prepare_jobs(jobs, 3);
+  return 3;
+}
+
+// o projection -> exchange (kimi.py:283 / :299)
+KK3_DEV void o_job(const StepArgs& a, int l, GemvJob& j) {
+  const Geo& g = a.g;
+  job_init(j, lptr<bf16>(a, l, KK3_KDA_O), g.h, g.hr * g.vd, a.s.attn_in, g.hr * g.vd, g.B, EPI_EXCHANGE, nullptr, g.h);
+  j.aux_off = a.comm.att_off;
+  prepare_jobs(&j, 1);
+}
+
+// MLP input: dense gate/up (kimi.py:304), or router + latent down (pass 0) and shared gate/up (pass 1) (:308, :317, :326)
+KK3_DEV int mlp_in_jobs(const StepArgs& a, int l, GemvJob* j0, GemvJob& j1) {
+  const Geo& g = a.g;
+  if (l < g.first_dense) {
+    job_init(j1, lptr<bf16>(a, l, KK3_DENSE_GATE), g.dinter, g.h, a.s.xm, g.h, g.B, EPI_SITU, a.s.dense_act, g.dinter);
+    j1.w2 = lptr<bf16>(a, l, KK3_DENSE_UP);
+    prepare_jobs(&j1, 1);
+    return 0;
+  }
+  job_init(j0[0], lptr<bf16>(a, l, KK3_MOE_ROUTER), g.E, g.h, a.s.xm, g.h, g.B, EPI_SIGMOID_F32, a.s.scores, g.E);
+  job_init(j0[1], lptr<bf16>(a, l, KK3_MOE_LATENT_DOWN), g.lh, g.h, a.s.xm, g.h, g.B, EPI_LATENT, a.s.latent, g.lh);
+  j0[1].out2 = a.s.latent_p;
+  prepare_jobs(j0, 2);
+  job_init(j1, lptr<bf16>(a, l, KK3_MOE_SHARED_GATE), g.sinter, g.h, a.s.xm, g.h, g.B, EPI_SITU, a.s.shared_act,
+           g.sinter);
+  j1.w2 = lptr<bf16>(a, l, KK3_MOE_SHARED_UP);
+  prepare_jobs(&j1, 1);
+  return 2;
+}
+
+KK3_DEV void latent_up_job(const StepArgs& a, int l, GemvJob& j) {
+  const Geo& g = a.g;
+  job_init(j, lptr<bf16>(a, l, KK3_MOE_LATENT_UP), g.h, g.lh, a.s.x3, g.lh, g.B, EPI_ROUTED, a.s.prefix, g.h);
+  j.aux = a.s.shared_red;
+  prepare_jobs(&j, 1);
+}
+
+KK3_DEV void lm_head_job(const StepArgs& a, GemvJob& j) {
+  const Geo& g = a.g;
+  job_init(j, gptr<bf16>(a, KK3_LM_HEAD), g.V, g.h, a.s.xa, g.h, g.B, EPI_LOGITS, gout<float>(a, KK3_OUT_LOGITS), g.V);
+  j.aux = a.s.argmax_key;
+  j.aux_off = (long long)g.rank * g.V;
+  prepare_jobs(&j, 1);
+}
+
 // ---- the kernel -------------------------------------------------------------------------------------
 
 template <int NT>
 __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_constant__ StepArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
+  // GEMV job descriptors live in shared memory: built once per CTA by thread 0 from the parameter block,
+  // then read by every warp (indexing a per-thread array would put it in local memory)
+  __shared__ GemvJob sj[kMaxJobs];
+  __shared__ GemvJob sj2[2];
+  __shared__ ExpertPhase sph;
+  __shared__ int sjn;
   const Geo& g = a.g;
   float* fsm = reinterpret_cast<float*>(smem);
   int phase = 0;
   unsigned xi = 0;
   const unsigned seq0 = a.epoch * 1024u;
+  const bool lead = threadIdx.x == 0;
 #define KK3_RUN (phase >= a.start_phase)
 #define KK3_PHASE_END()                                                                      \
   do {                                                                                       \
-    if (KK3_RUN && !grid_sync(a)) return;                                                    \
+    if (KK3_RUN && !grid_sync(a, phase)) return;                                             \
     ++phase;                                                                                 \
+    trace_progress(a, 0, phase);                                                             \
     if (blockIdx.x == 0 && threadIdx.x == 0 && phase <= kMaxPhases) a.s.phase_ts[phase] = globaltimer(); \
     if (phase == a.stop_phase) return;                                                       \
   } while (0)
+#define KK3_BUILD(stmt)   \
+  do {                    \
+    if (lead) { stmt; }   \
+    __syncthreads();      \
+  } while (0)
 
   if (blockIdx.x == 0 && threadIdx.x == 0) a.s.phase_ts[0] = globaltimer();
+  trace_progress(a, 0, 0);
   // embedding (kimi.py:249-252)
   if (KK3_RUN) phase_embed(a, seq0 + xi, xi & 1, fsm);
   int pending = PEND_EMBED;
@@ -267,54 +414,36 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   for (int l = 0; l < g.L; ++l) {
     const bool mla = layer_is_mla(g, l);
     // attention prologue (kimi.py:257-262)
-    if (KK3_RUN && !phase_attn_prologue(a, l, nb, pending, pend_signal, seq0 + pend_x, pend_x & 1, fsm)) return;
+    if (KK3_RUN && !phase_attn_prologue(a, l, nb, pending, pend_signal, seq0 + pend_x, pend_x & 1, fsm, phase)) return;
     pending = PEND_NONE;
     if (l % g.bs == 0) ++nb;
     KK3_PHASE_END();
+    if (KK3_RUN) {
+      KK3_BUILD(sjn = attn_proj_jobs(a, l, mla, sj));
+      run_gemv<NT, 1>(a, sj, sjn, 0, gridDim.x, 0, 0, phase);
+    }
+    KK3_PHASE_END();
     if (!mla) {
-      // KDA projections (kimi.py:285, :290-291, :298)
-      GemvJob jobs[6] = {};
-      const bf16* wq[4] = {lptr<bf16>(a, l, KK3_KDA_Q), lptr<bf16>(a, l, KK3_KDA_K), lptr<bf16>(a, l, KK3_KDA_V),
-                           lptr<bf16>(a, l, KK3_KDA_OUTPUT_GATE)};
-      for (int i = 0; i < 3; ++i) {
-        jobs[i].w = wq[i]; jobs[i].rows = g.qdim; jobs[i].out = a.s.qkv + (size_t)i * g.qdim; jobs[i].ldo = 3 * g.qdim;
-      }
-      jobs[3].w = wq[3]; jobs[3].rows = g.qdim; jobs[3].out = a.s.og; jobs[3].ldo = g.qdim;
-      jobs[4].w = lptr<bf16>(a, l, KK3_KDA_FA); jobs[4].rows = g.d; jobs[4].out = a.s.fa; jobs[4].ldo = g.d;
-      jobs[5].w = lptr<bf16>(a, l, KK3_KDA_BETA); jobs[5].rows = g.hr; jobs[5].out = a.s.beta; jobs[5].ldo = g.hr;
-      for (int i = 0; i < 6; ++i) {
-        jobs[i].K = g.h; jobs[i].x = a.s.xa; jobs[i].ldx = g.h; jobs[i].ncols = g.B; jobs[i].epi = EPI_STORE_BF16;
-      }
-      prepare_jobs(jobs, 6);
-      if (KK3_RUN) run_gemv<NT, 1>(a, jobs, 6, 0, gridDim.x, 0);
-      KK3_PHASE_END();
-      // short conv + gated delta rule (kimi.py:286-299)
-      if (KK3_RUN)
+      // short conv + gated delta rule (kimi.py:286-299); then prefetch the o projection into L2
+      if (KK3_RUN) {
+        KK3_BUILD(o_job(a, l, sj2[0]));
         for (int it = blockIdx.x; it < g.B * g.hr; it += gridDim.x) kda_item(a, l, kidx, it / g.hr, it % g.hr, fsm);
+        prefetch_jobs(sj2, 1);
+      }
       ++kidx;
       KK3_PHASE_END();
     } else {
-      // MLA projections q_a, kv_a, output gate (kimi.py:265-266, :282)
-      GemvJob jobs[3] = {};
-      jobs[0].w = lptr<bf16>(a, l, KK3_MLA_QA); jobs[0].rows = g.qr; jobs[0].out = a.s.qkv; jobs[0].ldo = g.qr;
-      jobs[1].w = lptr<bf16>(a, l, KK3_MLA_KA); jobs[1].rows = g.kr + g.rd;
-      jobs[1].out = a.s.qkv + (size_t)g.B * g.qr; jobs[1].ldo = g.kr + g.rd;
-      jobs[2].w = lptr<bf16>(a, l, KK3_MLA_OUTPUT_GATE); jobs[2].rows = g.hr * g.vd; jobs[2].out = a.s.og;
-      jobs[2].ldo = g.hr * g.vd;
-      for (int i = 0; i < 3; ++i) {
-        jobs[i].K = g.h; jobs[i].x = a.s.xa; jobs[i].ldx = g.h; jobs[i].ncols = g.B; jobs[i].epi = EPI_STORE_BF16;
-      }
-      prepare_jobs(jobs, 3);
-      if (KK3_RUN) run_gemv<NT, 1>(a, jobs, 3, 0, gridDim.x, 0);
-      KK3_PHASE_END();
       if (KK3_RUN) phase_mla_rows(a, l, midx, fsm);
       KK3_PHASE_END();
       // q_b (kimi.py:265)
-      GemvJob qb = {};
-      qb.w = lptr<bf16>(a, l, KK3_MLA_QB); qb.rows = g.hr * (g.nr + g.rd); qb.K = g.qr; qb.x = a.s.mla_qan;
-      qb.ldx = g.qr; qb.ncols = g.B; qb.epi = EPI_STORE_BF16; qb.out = a.s.mla_q; qb.ldo = g.hr * (g.nr + g.rd);
-      prepare_jobs(&qb, 1);
-      if (KK3_RUN) run_gemv<NT, 1>(a, &qb, 1, 0, gridDim.x, 0);
+      if (KK3_RUN) {
+        KK3_BUILD({
+          job_init(sj[0], lptr<bf16>(a, l, KK3_MLA_QB), g.hr * (g.nr + g.rd), g.qr, a.s.mla_qan, g.qr, g.B,
+                   EPI_STORE_BF16, a.s.mla_q, g.hr * (g.nr + g.rd));
+          prepare_jobs(sj, 1);
+        });
+        run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, 0);
+      }
       KK3_PHASE_END();
       // absorbed query (kimi.py:271-272)
       if (KK3_RUN)
@@ -340,104 +469,100 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         }
       }
       KK3_PHASE_END();
-      if (KK3_RUN)
+      if (KK3_RUN) {
+        KK3_BUILD(o_job(a, l, sj2[0]));
         for (int it = blockIdx.x; it < g.B * g.hr; it += gridDim.x) mla_combine_item(a, l, it / g.hr, it % g.hr, fsm);
+        prefetch_jobs(sj2, 1);
+      }
       ++midx;
       KK3_PHASE_END();
     }
-    // o projection -> exchange (kimi.py:283 / :299)
-    {
-      GemvJob o = {};
-      o.w = lptr<bf16>(a, l, KK3_KDA_O); o.rows = g.h; o.K = g.hr * g.vd; o.x = a.s.attn_in; o.ldx = g.hr * g.vd;
-      o.ncols = g.B; o.epi = EPI_EXCHANGE; o.ldo = g.h; o.aux_off = a.comm.att_off;
-      prepare_jobs(&o, 1);
-      if (KK3_RUN) run_gemv<NT, 1>(a, &o, 1, 0, gridDim.x, xi & 1);
+    // o projection -> exchange
+    if (KK3_RUN) {
+      KK3_BUILD(o_job(a, l, sj[0]));
+      run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, xi & 1);
       if (g.tp > 1) __threadfence_system();
     }
     const unsigned x_att = xi++;
     KK3_PHASE_END();
-    const int nb_after = nb;
-    if (KK3_RUN && !phase_mlp_prologue(a, l, nb_after, seq0 + x_att, x_att & 1, fsm)) return;
+    if (KK3_RUN && !phase_mlp_prologue(a, l, nb, seq0 + x_att, x_att & 1, fsm)) return;
     KK3_PHASE_END();
     if (l < g.first_dense) {
       // dense FFN (kimi.py:304)
-      GemvJob gu = {};
-      gu.w = lptr<bf16>(a, l, KK3_DENSE_GATE); gu.w2 = lptr<bf16>(a, l, KK3_DENSE_UP); gu.rows = g.dinter; gu.K = g.h;
-      gu.x = a.s.xm; gu.ldx = g.h; gu.ncols = g.B; gu.epi = EPI_SITU; gu.out = a.s.dense_act; gu.ldo = g.dinter;
-      prepare_jobs(&gu, 1);
-      if (KK3_RUN) run_gemv<NT, 2>(a, &gu, 1, 0, gridDim.x, 0);
+      if (KK3_RUN) {
+        KK3_BUILD(mlp_in_jobs(a, l, sj, sj2[0]));
+        run_gemv<NT, 2>(a, sj2, 1, 0, gridDim.x, 0);
+      }
       KK3_PHASE_END();
-      GemvJob dn = {};
-      dn.w = lptr<bf16>(a, l, KK3_DENSE_DOWN); dn.rows = g.h; dn.K = g.dinter; dn.x = a.s.dense_act; dn.ldx = g.dinter;
-      dn.ncols = g.B; dn.epi = EPI_EXCHANGE; dn.ldo = g.h; dn.aux_off = a.comm.att_off;
-      prepare_jobs(&dn, 1);
-      if (KK3_RUN) run_gemv<NT, 1>(a, &dn, 1, 0, gridDim.x, xi & 1);
-      if (g.tp > 1) __threadfence_system();
+      if (KK3_RUN) {
+        KK3_BUILD({
+          job_init(sj[0], lptr<bf16>(a, l, KK3_DENSE_DOWN), g.h, g.dinter, a.s.dense_act, g.dinter, g.B, EPI_EXCHANGE,
+                   nullptr, g.h);
+          sj[0].aux_off = a.comm.att_off;
+          prepare_jobs(sj, 1);
+        });
+        run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, xi & 1);
+        if (g.tp > 1) __threadfence_system();
+      }
       pending = PEND_DENSE;
       pend_signal = true;
       pend_x = xi++;
       KK3_PHASE_END();
     } else {
-      // router, latent down (pass 0) and shared gate/up (pass 1) (kimi.py:308, :317, :326)
-      GemvJob j0[2] = {};
-      j0[0].w = lptr<bf16>(a, l, KK3_MOE_ROUTER); j0[0].rows = g.E; j0[0].epi = EPI_SIGMOID_F32; j0[0].out = a.s.scores;
-      j0[0].ldo = g.E;
-      j0[1].w = lptr<bf16>(a, l, KK3_MOE_LATENT_DOWN); j0[1].rows = g.lh; j0[1].epi = EPI_LATENT; j0[1].out = a.s.latent;
-      j0[1].out2 = a.s.latent_p; j0[1].ldo = g.lh;
-      for (int i = 0; i < 2; ++i) {
-        j0[i].K = g.h; j0[i].x = a.s.xm; j0[i].ldx = g.h; j0[i].ncols = g.B;
+      // router + latent down (pass 0), shared gate/up (pass 1) (kimi.py:308, :317, :326)
+      if (KK3_RUN) {
+        KK3_BUILD(mlp_in_jobs(a, l, sj, sj2[0]));
+        run_gemv<NT, 1>(a, sj, 2, 0, gridDim.x, 0, 0, phase);
+        run_gemv<NT, 2>(a, sj2, 1, 0, gridDim.x, 0, 1);
       }
-      prepare_jobs(j0, 2);
-      if (KK3_RUN) run_gemv<NT, 1>(a, j0, 2, 0, gridDim.x, 0, 0);
-      GemvJob j1 = {};
-      j1.w = lptr<bf16>(a, l, KK3_MOE_SHARED_GATE); j1.w2 = lptr<bf16>(a, l, KK3_MOE_SHARED_UP); j1.rows = g.sinter;
-      j1.K = g.h; j1.x = a.s.xm; j1.ldx = g.h; j1.ncols = g.B; j1.epi = EPI_SITU; j1.out = a.s.shared_act; j1.ldo = g.sinter;
-      prepare_jobs(&j1, 1);
-      if (KK3_RUN) run_gemv<NT, 2>(a, &j1, 1, 0, gridDim.x, 0, 1);
       KK3_PHASE_END();
       // routing on CTA 0 while the other CTAs run the shared-expert down projection (kimi.py:309-316, :326)
       const unsigned x_moe = xi++;
-      if (!KK3_RUN) {
-      } else if (blockIdx.x == 0) {
-        route_all(a, l, l - g.first_dense, smem);
-      } else {
-        GemvJob sd = {};
-        sd.w = lptr<bf16>(a, l, KK3_MOE_SHARED_DOWN); sd.rows = g.h; sd.K = g.sinter; sd.x = a.s.shared_act;
-        sd.ldx = g.sinter; sd.ncols = g.B; sd.epi = EPI_EXCHANGE; sd.ldo = g.h; sd.aux_off = a.comm.shd_off;
-        prepare_jobs(&sd, 1);
-        run_gemv<NT, 1>(a, &sd, 1, 1, gridDim.x, x_moe & 1);
-        if (g.tp > 1) __threadfence_system();
+      if (KK3_RUN) {
+        KK3_BUILD({
+          job_init(sj[0], lptr<bf16>(a, l, KK3_MOE_SHARED_DOWN), g.h, g.sinter, a.s.shared_act, g.sinter, g.B,
+                   EPI_EXCHANGE, nullptr, g.h);
+          sj[0].aux_off = a.comm.shd_off;
+          prepare_jobs(sj, 1);
+        });
+        if (blockIdx.x == 0) {
+          route_all(a, l, l - g.first_dense, smem);
+        } else {
+          run_gemv<NT, 1>(a, sj, 1, 1, gridDim.x, x_moe & 1);
+          if (g.tp > 1) __threadfence_system();
+        }
       }
       KK3_PHASE_END();
-      // routed experts (kimi.py:317-323)
-      {
-        ExpertPhase ph;
-        ph.codes[0] = lptr<uint8_t>(a, l, KK3_MOE_GATE_BLOCKS);
-        ph.codes[1] = lptr<uint8_t>(a, l, KK3_MOE_UP_BLOCKS);
-        ph.scales[0] = lptr<uint8_t>(a, l, KK3_MOE_GATE_SCALES);
-        ph.scales[1] = lptr<uint8_t>(a, l, KK3_MOE_UP_SCALES);
-        ph.rows = g.inter; ph.K = g.lh; ph.tiles = g.inter / 16; ph.ksteps = g.lh / 64;
-        ph.expert_codes = (long long)g.inter * g.lh / 2; ph.expert_scales = (long long)g.inter * g.lh / 32;
-        if (KK3_RUN) run_experts<2>(a, ph);
+      // routed experts (kimi.py:317-323); descriptor built once per CTA in shared memory
+      if (KK3_RUN) {
+        KK3_BUILD({
+          sph.codes[0] = lptr<uint8_t>(a, l, KK3_MOE_GATE_BLOCKS);
+          sph.codes[1] = lptr<uint8_t>(a, l, KK3_MOE_UP_BLOCKS);
+          sph.scales[0] = lptr<uint8_t>(a, l, KK3_MOE_GATE_SCALES);
+          sph.scales[1] = lptr<uint8_t>(a, l, KK3_MOE_UP_SCALES);
+          sph.rows = g.inter; sph.K = g.lh; sph.tiles = g.inter / 16; sph.ksteps = g.lh / 64;
+          sph.expert_codes = (long long)g.inter * g.lh / 2; sph.expert_scales = (long long)g.inter * g.lh / 32;
+        });
+        run_experts<2>(a, sph);
       }
       KK3_PHASE_END();
-      {
-        ExpertPhase ph;
-        ph.codes[0] = ph.codes[1] = lptr<uint8_t>(a, l, KK3_MOE_DOWN_BLOCKS);
-        ph.scales[0] = ph.scales[1] = lptr<uint8_t>(a, l, KK3_MOE_DOWN_SCALES);
-        ph.rows = g.lh; ph.K = g.inter; ph.tiles = g.lh / 16; ph.ksteps = g.inter / 64;
-        ph.expert_codes = (long long)g.lh * g.inter / 2; ph.expert_scales = (long long)g.lh * g.inter / 32;
-        if (KK3_RUN) run_experts<1>(a, ph);
+      if (KK3_RUN) {
+        KK3_BUILD({
+          sph.codes[0] = sph.codes[1] = lptr<uint8_t>(a, l, KK3_MOE_DOWN_BLOCKS);
+          sph.scales[0] = sph.scales[1] = lptr<uint8_t>(a, l, KK3_MOE_DOWN_SCALES);
+          sph.rows = g.lh; sph.K = g.inter; sph.tiles = g.lh / 16; sph.ksteps = g.inter / 64;
+          sph.expert_codes = (long long)g.lh * g.inter / 2; sph.expert_scales = (long long)g.lh * g.inter / 32;
+        });
+        run_experts<1>(a, sph);
       }
       KK3_PHASE_END();
       if (KK3_RUN && !phase_moe_combine(a, l, seq0 + x_moe, x_moe & 1, fsm)) return;
       KK3_PHASE_END();
       // latent up + shared + residual (kimi.py:325-329)
-      GemvJob up = {};
-      up.w = lptr<bf16>(a, l, KK3_MOE_LATENT_UP); up.rows = g.h; up.K = g.lh; up.x = a.s.x3; up.ldx = g.lh;
-      up.ncols = g.B; up.epi = EPI_ROUTED; up.out = a.s.prefix; up.aux = a.s.shared_red; up.ldo = g.h;
-      prepare_jobs(&up, 1);
-      if (KK3_RUN) run_gemv<NT, 1>(a, &up, 1, 0, gridDim.x, 0);
+      if (KK3_RUN) {
+        KK3_BUILD(latent_up_job(a, l, sj[0]));
+        run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, 0);
+      }
       KK3_PHASE_END();
     }
   }
@@ -449,13 +574,9 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   }
   if (KK3_RUN) phase_head_prologue(a, nb, fsm);
   KK3_PHASE_END();
-  {
-    GemvJob hd = {};
-    hd.w = gptr<bf16>(a, KK3_LM_HEAD); hd.rows = g.V; hd.K = g.h; hd.x = a.s.xa; hd.ldx = g.h; hd.ncols = g.B;
-    hd.epi = EPI_LOGITS; hd.out = gout<float>(a, KK3_OUT_LOGITS); hd.ldo = g.V; hd.aux = a.s.argmax_key;
-    hd.aux_off = (long long)g.rank * g.V;
-    prepare_jobs(&hd, 1);
-    if (KK3_RUN) run_gemv<NT, 1>(a, &hd, 1, 0, gridDim.x, 0);
+  if (KK3_RUN) {
+    KK3_BUILD(lm_head_job(a, sj[0]));
+    run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, 0);
   }
   KK3_PHASE_END();
   const unsigned x_key = xi++;
@@ -464,6 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
     if (phase + 1 <= kMaxPhases) a.s.phase_ts[phase + 1] = globaltimer();
     *a.s.phase_count = phase + 1;
   }
+#undef KK3_BUILD
 #undef KK3_PHASE_END
 #undef KK3_RUN
 }

@@ -43,122 +43,227 @@ KK3_DEV const T* xlocal(const StepArgs& a, int parity, long long off) {
 }
 
 // ------------------------------------------------------------------------------------------------
-// Row phase: block attention residual (kimi.py:199-204) followed by RMSNorm (common.py:13-21).
-// hidden = softmax_i(rms(v_i) . (norm*proj)) mixing of [blocks..., prefix] in FP32, cast to BF16;
-// out = bf16(bf16(hidden * rsqrt(mean(hidden^2) + eps)) * ln).
+// Row phases: one CTA per batch row, vectorised (16-byte loads of 8 BF16), each input read once into
+// registers, all row statistics reduced in one CTA-wide pass.
 
-constexpr int kMaxBlocks = 9;
+constexpr int kMaxBlocks = 9;        // block vectors + prefix mixed by one attention residual (<= 8 + 1)
+constexpr int kRowChunks = 2;        // 16-byte chunks per thread: rows up to 2 * 512 * 8 = 8192 elements
 
-KK3_DEV void mix_and_norm(const StepArgs& a, int b, int nb, const bf16* norm, const bf16* proj, const bf16* ln,
-                          float eps, bf16* out_row, float* hbuf, float* red) {
+KK3_DEV void unpack8(const uint4& v, float (&f)[8]) {
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(p[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+KK3_DEV uint4 pack8(const float (&f)[8]) {
+  uint4 v;
+  __nv_bfloat162* p = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return v;
+}
+
+// CTA-wide sums of the first `live` of N per-thread values (all threads receive the totals).
+// `red`: (kWarps + 1) * N floats. Warp partials go to shared memory, warp 0 adds them, one broadcast back.
+template <int N>
+KK3_DEV void block_sums(float (&v)[N], float* red, int live = N) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    if (i < live) v[i] = warp_sum(v[i]);
+  __syncthreads();
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      if (i < live) red[warp * N + i] = v[i];
+  }
+  __syncthreads();
+  if (warp == 0 && lane < live) {
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) t += red[w * N + lane];
+    red[kWarps * N + lane] = t;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    if (i < live) v[i] = red[kWarps * N + i];
+}
+
+// Block attention residual (kimi.py:199-204) then RMSNorm (common.py:13-21), for batch row b:
+// hidden = bf16(sum_i softmax_i(rms(v_i) . (norm*proj)) v_i) over v = [blocks[0..nb), prefix];
+// out = bf16(bf16(hidden * rsqrt(mean(hidden^2) + eps)) * ln). `pre` holds this thread's prefix chunks.
+KK3_FN void mix_and_norm_regs(const StepArgs& a, int b, int nb, const uint4 (&pre)[kRowChunks], const bf16* norm,
+                               const bf16* proj, const bf16* ln, float eps, bf16* out_row, float* red, int ph = -1) {
   const Geo& g = a.g;
-  const int tid = threadIdx.x;
-  const bf16* prefix = a.s.prefix + (size_t)b * g.h;
+  const int tid = threadIdx.x, nvec = g.h / 8;
+  const bool stamp = ph >= 0 && b == 0 && tid == 0;
+  float hidden[kRowChunks][8];
   if (nb > 0) {
-    const int n = nb + 1;
-    float ss[kMaxBlocks + 1], dt[kMaxBlocks + 1];
+    // the first kCached block vectors stay in registers between the two passes, later ones are re-read
+    constexpr int kCached = 2;
+    uint4 vals[kCached][kRowChunks];
+    float np[kRowChunks][8];
+    auto block_chunk = [&](int i, int q) -> uint4 {
+      const int c = tid + q * kThreads;
+      return c < nvec ? ld_act16(a.s.blocks + ((size_t)i * g.B + b) * g.h + c * 8) : make_uint4(0, 0, 0, 0);
+    };
 #pragma unroll
-    for (int i = 0; i <= kMaxBlocks; ++i) ss[i] = dt[i] = 0.0f;
-    for (int e = tid; e < g.h; e += kThreads) {
-      const float np = bf2f(norm[e]) * bf2f(proj[e]);
-#pragma unroll
-      for (int i = 0; i <= kMaxBlocks; ++i) {
-        if (i < n) {
-          const bf16* vec = (i < nb) ? a.s.blocks + ((size_t)i * g.B + b) * g.h : prefix;
-          const float v = bf2f(vec[e]);
-          ss[i] += v * v;
-          dt[i] += v * np;
-        }
+    for (int q = 0; q < kRowChunks; ++q) {
+      const int c = tid + q * kThreads;
+      float fn[8], fp[8];
+      uint4 un = make_uint4(0, 0, 0, 0), up = make_uint4(0, 0, 0, 0);
+      if (c < nvec) {
+        un = ld_act16(norm + c * 8);
+        up = ld_act16(proj + c * 8);
       }
+      unpack8(un, fn);
+      unpack8(up, fp);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) np[q][e] = fn[e] * fp[e];
+#pragma unroll
+      for (int i = 0; i < kCached; ++i) vals[i][q] = i < nb ? block_chunk(i, q) : make_uint4(0, 0, 0, 0);
     }
-    // reduce 2n values over the CTA: warp sums, then per-warp partials in shared memory
-    float* part = red;   // [kWarps][2 * (kMaxBlocks+1)]
-    const int warp = tid >> 5, lane = tid & 31;
+    auto vec_chunk = [&](int i, int q) -> uint4 {
+      if (i == nb) return pre[q];
+      if (i == 0) return vals[0][q];
+      if (i == 1) return vals[1][q];
+      return block_chunk(i, q);
+    };
+    // statistics: sum of squares and dot with norm*proj, for every block vector and the prefix
+    float st[2 * (kMaxBlocks + 1)];
+#pragma unroll
+    for (int i = 0; i < 2 * (kMaxBlocks + 1); ++i) st[i] = 0.0f;
 #pragma unroll
     for (int i = 0; i <= kMaxBlocks; ++i) {
-      if (i < n) {
-        const float s1 = warp_sum(ss[i]), s2 = warp_sum(dt[i]);
-        if (lane == 0) {
-          part[warp * 2 * (kMaxBlocks + 1) + 2 * i] = s1;
-          part[warp * 2 * (kMaxBlocks + 1) + 2 * i + 1] = s2;
+      if (i <= nb) {
+#pragma unroll
+        for (int q = 0; q < kRowChunks; ++q) {
+          float f[8];
+          unpack8(vec_chunk(i, q), f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            st[2 * i] += f[e] * f[e];
+            st[2 * i + 1] += f[e] * np[q][e];
+          }
         }
       }
     }
-    __syncthreads();
-    float* prob = red + kWarps * 2 * (kMaxBlocks + 1);   // [kMaxBlocks+1]
-    if (tid == 0) {
-      float logit[kMaxBlocks + 1];
-      float mx = -INFINITY;
-      for (int i = 0; i < n; ++i) {
-        float s1 = 0.0f, s2 = 0.0f;
-        for (int w = 0; w < kWarps; ++w) {
-          s1 += part[w * 2 * (kMaxBlocks + 1) + 2 * i];
-          s2 += part[w * 2 * (kMaxBlocks + 1) + 2 * i + 1];
+    if (stamp) sub_stamp(a, ph, 1);
+    block_sums<2 * (kMaxBlocks + 1)>(st, red, 2 * (nb + 1));
+    if (stamp) sub_stamp(a, ph, 2);
+    float prob[kMaxBlocks + 1];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i <= kMaxBlocks; ++i) {
+      prob[i] = (i <= nb) ? st[2 * i + 1] * rsqrtf(st[2 * i] / (float)g.h + 1e-5f) : -INFINITY;
+      mx = fmaxf(mx, prob[i]);
+    }
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i <= kMaxBlocks; ++i) {
+      prob[i] = (i <= nb) ? expf(prob[i] - mx) : 0.0f;
+      tot += prob[i];
+    }
+#pragma unroll
+    for (int q = 0; q < kRowChunks; ++q) {
+      float accv[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) accv[e] = 0.0f;
+#pragma unroll
+      for (int i = 0; i <= kMaxBlocks; ++i) {
+        if (i <= nb) {
+          float f[8];
+          unpack8(vec_chunk(i, q), f);
+          const float pi = prob[i] / tot;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) accv[e] += pi * f[e];
         }
-        logit[i] = s2 * rsqrtf(s1 / (float)g.h + 1e-5f);
-        mx = fmaxf(mx, logit[i]);
       }
-      float tot = 0.0f;
-      for (int i = 0; i < n; ++i) {
-        logit[i] = expf(logit[i] - mx);
-        tot += logit[i];
-      }
-      for (int i = 0; i < n; ++i) prob[i] = logit[i] / tot;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) hidden[q][e] = round_bf(accv[e]);
     }
-    __syncthreads();
-    float ssh = 0.0f;
-    for (int e = tid; e < g.h; e += kThreads) {
-      float acc = 0.0f;
-      for (int i = 0; i < n; ++i) {
-        const bf16* vec = (i < nb) ? a.s.blocks + ((size_t)i * g.B + b) * g.h : prefix;
-        acc += prob[i] * bf2f(vec[e]);
-      }
-      const float hv = round_bf(acc);
-      hbuf[e] = hv;
-      ssh += hv * hv;
-    }
-    const float tot = block_sum(ssh, red + kWarps * 2 * (kMaxBlocks + 1) + kMaxBlocks + 1);
-    const float rs = rsqrtf(tot / (float)g.h + eps);
-    for (int e = tid; e < g.h; e += kThreads) out_row[e] = f2bf(round_bf(hbuf[e] * rs) * bf2f(ln[e]));
   } else {
-    float ssh = 0.0f;
-    for (int e = tid; e < g.h; e += kThreads) {
-      const float hv = bf2f(prefix[e]);
-      ssh += hv * hv;
+#pragma unroll
+    for (int q = 0; q < kRowChunks; ++q) unpack8(pre[q], hidden[q]);
+  }
+  float ss[1] = {0.0f};
+#pragma unroll
+  for (int q = 0; q < kRowChunks; ++q)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss[0] += hidden[q][e] * hidden[q][e];
+  if (stamp) sub_stamp(a, ph, 3);
+  block_sums<1>(ss, red + (kWarps + 1) * 2 * (kMaxBlocks + 1));
+  if (stamp) sub_stamp(a, ph, 4);
+  const float rs = rsqrtf(ss[0] / (float)g.h + eps);
+#pragma unroll
+  for (int q = 0; q < kRowChunks; ++q) {
+    const int c = tid + q * kThreads;
+    if (c < nvec) {
+      float w[8], o[8];
+      unpack8(ld_act16(ln + c * 8), w);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = round_bf(round_bf(hidden[q][e] * rs) * w[e]);
+      *reinterpret_cast<uint4*>(out_row + c * 8) = pack8(o);
     }
-    const float tot = block_sum(ssh, red);
-    const float rs = rsqrtf(tot / (float)g.h + eps);
-    for (int e = tid; e < g.h; e += kThreads) out_row[e] = f2bf(round_bf(bf2f(prefix[e]) * rs) * bf2f(ln[e]));
+  }
+  if (stamp) sub_stamp(a, ph, 5);
+}
+
+// RMSNorm of one BF16 row of width n <= 8192 (common.py:13-21), vectorised
+KK3_FN void rms_row(const bf16* in, const bf16* w, int n, float eps, bf16* out, float* red) {
+  const int nvec = n / 8;
+  float x[kRowChunks][8];
+  float ss[1] = {0.0f};
+#pragma unroll
+  for (int q = 0; q < kRowChunks; ++q) {
+    const int c = threadIdx.x + q * kThreads;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (c < nvec) v = ld_act16(in + c * 8);
+    unpack8(v, x[q]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss[0] += x[q][e] * x[q][e];
+  }
+  block_sums<1>(ss, red);
+  const float rs = rsqrtf(ss[0] / (float)n + eps);
+#pragma unroll
+  for (int q = 0; q < kRowChunks; ++q) {
+    const int c = threadIdx.x + q * kThreads;
+    if (c < nvec) {
+      float wf[8], o[8];
+      unpack8(ld_act16(w + c * 8), wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = round_bf(round_bf(x[q][e] * rs) * wf[e]);
+      *reinterpret_cast<uint4*>(out + c * 8) = pack8(o);
+    }
   }
   __syncthreads();
 }
 
-// RMSNorm of one BF16 row of width n (common.py:13-21)
-KK3_DEV void rms_row(const bf16* in, const bf16* w, int n, float eps, bf16* out, float* red) {
-  float ss = 0.0f;
-  for (int e = threadIdx.x; e < n; e += kThreads) {
-    const float v = bf2f(in[e]);
-    ss += v * v;
-  }
-  const float tot = block_sum(ss, red);
-  const float rs = rsqrtf(tot / (float)n + eps);
-  for (int e = threadIdx.x; e < n; e += kThreads) out[e] = f2bf(round_bf(bf2f(in[e]) * rs) * bf2f(w[e]));
-  __syncthreads();
-}
-
-// Sum the tp BF16 partials of row b in an exchange sub-region (FP32, rank order) and round to BF16.
-KK3_DEV float xch_sum_bf16(const StepArgs& a, int parity, long long off, int b, int width, int e) {
+// Sum the tp BF16 partials of row b, 16-byte chunk c, of an exchange sub-region (FP32, rank order), rounded
+// to BF16 (kimi.py:343-347).
+KK3_DEV void xch_sum8(const StepArgs& a, int parity, long long off, int b, int width, int c, float (&out)[8]) {
   const bf16* base = xlocal<bf16>(a, parity, off);
-  float acc = 0.0f;
-  for (int src = 0; src < a.g.tp; ++src) acc += bf2f(base[((size_t)src * a.g.B + b) * width + e]);
-  return round_bf(acc);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) out[e] = 0.0f;
+  for (int src = 0; src < a.g.tp; ++src) {
+    float f[8];
+    unpack8(ld_act16(base + ((size_t)src * a.g.B + b) * width + c * 8), f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) out[e] += f[e];
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) out[e] = round_bf(out[e]);
 }
 
 // ------------------------------------------------------------------------------------------------
 // KDA: one CTA per (batch row, head). Short convolution (kimi.py:286-289), f_a/f_b gate (:290),
 // beta (:291), gated delta rule on the V-first FP32 state (:207-215), gated per-head RMSNorm (:296-298).
 
-KK3_DEV void kda_item(const StepArgs& a, int layer, int kidx, int b, int hh, float* sm) {
+KK3_FN void kda_item(const StepArgs& a, int layer, int kidx, int b, int hh, float* sm) {
   const Geo& g = a.g;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int D = g.qdim, dh = 128;
@@ -237,9 +342,16 @@ KK3_DEV void kda_item(const StepArgs& a, int layer, int kidx, int b, int hh, flo
   const float4 qq = *reinterpret_cast<const float4*>(qn + lane * 4);
   const float* st_in = lptr<float>(a, layer, KK3_KDA_RECURRENT_STATE) + (((size_t)b * g.hr + hh) * dh) * dh;
   float* st_out = gout<float>(a, KK3_OUT_RECURRENT_STATE) + ((((size_t)kidx * g.B + b) * g.hr + hh) * dh) * dh;
-  for (int v = warp * 8; v < warp * 8 + 8; ++v) {
-    float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (keep) s = *reinterpret_cast<const float4*>(st_in + (size_t)v * dh + lane * 4);
+  float4 rows[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    rows[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (keep) rows[i] = *reinterpret_cast<const float4*>(st_in + (size_t)(warp * 8 + i) * dh + lane * 4);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int v = warp * 8 + i;
+    float4 s = rows[i];
     s.x *= dk.x; s.y *= dk.y; s.z *= dk.z; s.w *= dk.w;
     const float pred = warp_sum(s.x * kk.x + s.y * kk.y + s.z * kk.z + s.w * kk.w);
     const float err = (sv[v] - pred) * sb;
@@ -273,7 +385,7 @@ KK3_DEV void kda_item(const StepArgs& a, int layer, int kidx, int b, int hh, flo
 // MLA (kimi.py:263-283), absorbed latent form.
 
 // absorbed[b, h, c] = bf16(sum_d q[b, h, d] * kb[h*256 + d, c]), d < nr   (kimi.py:271-272)
-KK3_DEV void mla_absorb_item(const StepArgs& a, int layer, int hh, int cq, float* sm) {
+KK3_FN void mla_absorb_item(const StepArgs& a, int layer, int hh, int cq, float* sm) {
   const Geo& g = a.g;
   const int tid = threadIdx.x;
   const int c = cq * 128 + (tid & 127), dq = tid >> 7;   // 4 quarters of the 128 nope dims
@@ -363,7 +475,7 @@ KK3_DEV void mla_stage(const StepArgs& a, int layer, int midx, int b, int t0, in
 
 // One split-K item: batch row b, positions [p0, p1) of its attended sequence (T = ctx+1 or 1).
 // Writes (m, l, O[kr]) per head for the combine phase (flash-decoding with online softmax).
-KK3_DEV void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int chunk, int p0, int p1, int T,
+KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int chunk, int p0, int p1, int T,
                              unsigned char* smem) {
   const Geo& g = a.g;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, r = lane >> 2, c = lane & 3;
@@ -500,7 +612,7 @@ KK3_DEV void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int 
 
 // Combine the split-K partials of (b, h), apply kb's value half and the sigmoid output gate
 // (kimi.py:280-282): out[d] = bf16(bf16(sum_c lat[c] * kb[h*256+128+d, c]) * bf16(sigmoid(og))).
-KK3_DEV void mla_combine_item(const StepArgs& a, int layer, int b, int hh, float* sm) {
+KK3_FN void mla_combine_item(const StepArgs& a, int layer, int b, int hh, float* sm) {
   const Geo& g = a.g;
   const int tid = threadIdx.x;
   const bool keep = !reinterpret_cast<const bool*>(a.ptr[KK3_RESET])[b];
@@ -560,7 +672,7 @@ KK3_DEV void mla_combine_item(const StepArgs& a, int layer, int b, int hh, float
 // Routing (kimi.py:308-316) for all rows, by one CTA: FP32 sigmoid scores + bias, top-k (lowest index
 // wins ties), weights renormalised over the unbiased scores, ids sorted ascending. Then group the
 // (row, slot) pairs by expert into chunks of <= 8 pairs for the MXFP4 phases.
-KK3_DEV void route_all(const StepArgs& a, int layer, int moe_idx, unsigned char* smem) {
+KK3_FN void route_all(const StepArgs& a, int layer, int moe_idx, unsigned char* smem) {
   const Geo& g = a.g;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int* ids = reinterpret_cast<int*>(smem);            // [B*K]

@@ -135,17 +135,49 @@ def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[d
             torch.cuda.synchronize()
             ts = ctx.debug_buffer(16, torch.int64, (len(prog) + 1,)).cpu().tolist()
             instep = [(ts[i + 1] - ts[i]) / 1000.0 for i in range(len(prog))]
+            grid = ctx.launch_config()[0]
+            sub = ctx.debug_buffer(18, torch.int64, (256, 16)).cpu()
+            narr = min(len(prog) - 1, 256)
+            arr = ctx.debug_buffer(17, torch.int64, (narr, grid)).cpu()
+            # per phase: slowest CTA's arrival after the phase began, and barrier latency after it
+            work, barrier, last_cta = [], [], []
+            for i in range(len(prog)):
+                if i < narr:
+                    row = arr[i]
+                    last = int(row.max())
+                    work.append((last - ts[i]) / 1000.0)
+                    barrier.append((ts[i + 1] - last) / 1000.0)
+                    last_cta.append(int(row.argmax()))
+                else:
+                    work.append(None)
+                    barrier.append(None)
+                    last_cta.append(None)
             empty = timed(len(prog) + 1, -1)      # walks the program, runs no phase: launch cost
             alone = [max(timed(i, i + 1 if i + 1 < len(prog) else -1) - empty, 1e-3) for i in range(len(prog))]
             ctx.check()
         finally:
             ctx.close()
     nbytes = phase_bytes(case)
-    rows = [{"phase": -1, "name": "full_step", "layer": -1, "us": round(full, 2), "bytes": 0, "GBps": None},
+    subinfo = {}
+    for i, (name, layer) in enumerate(prog[:256]):
+        st = sub[i].tolist()
+        base = ts[i]
+        if name == "attn_prologue" and st[0]:
+            subinfo[f"{name}:{layer}"] = {"after_wait": (st[0] - base) / 1e3, "stats": (st[1] - base) / 1e3,
+                                          "red1": (st[2] - base) / 1e3, "mix": (st[3] - base) / 1e3,
+                                          "red2": (st[4] - base) / 1e3, "store": (st[5] - base) / 1e3,
+                                          "done": (st[6] - base) / 1e3, "phase_end": (ts[i + 1] - base) / 1e3}
+        if name in ("kda_proj", "mla_proj", "moe_in") and st[8]:
+            subinfo[f"{name}:{layer}"] = {"warp0_start": (st[8] - base) / 1e3, "first_data": (st[9] - base) / 1e3,
+                                          "warp0_end": (st[10] - base) / 1e3, "units": st[11],
+                                          "phase_end": (ts[i + 1] - base) / 1e3}
+    rows = [{"phase": -2, "name": "sub_stamps", "layer": -1, "us": 0.0, "bytes": 0, "GBps": None, "info": subinfo},{"phase": -1, "name": "full_step", "layer": -1, "us": round(full, 2), "bytes": 0, "GBps": None},
             {"phase": -1, "name": "empty_launch", "layer": -1, "us": round(empty, 2), "bytes": 0, "GBps": None}]
     for i, (name, layer) in enumerate(prog):
         dt = instep[i]
         rows.append({"phase": i, "name": name, "layer": layer, "us": round(dt, 2), "alone_us": round(alone[i], 2),
+                     "work_us": None if work[i] is None else round(work[i], 2),
+                     "barrier_us": None if barrier[i] is None else round(barrier[i], 2), "last_cta": last_cta[i],
                      "bytes": nbytes[i], "GBps": round(nbytes[i] / (dt * 1e-6) / 1e9, 1) if nbytes[i] and dt > 0 else None})
     return rows
 
@@ -170,18 +202,26 @@ def main(argv=None) -> int:
     if args.batch:
         case = cases.variant(case, batch=args.batch)
     rows = profile(case, args.reps)
-    head, rows = rows[:2], rows[2:]
+    subrow, head, rows = rows[0], rows[1:3], rows[3:]
+    for k, v in list(subrow["info"].items())[:6]:
+        print("  sub-phase", k, {kk: (round(vv, 2) if isinstance(vv, float) else vv) for kk, vv in v.items()})
     total = sum(r["us"] for r in rows)
     print(f"{case['id']}: full step {head[0]['us']:.1f} us (events), empty launch {head[1]['us']:.1f} us, "
           f"in-step phases sum to {total:.1f} us (globaltimer), alone-sum {sum(r['alone_us'] for r in rows):.1f} us")
     agg: dict[str, list] = {}
     for r in rows:
-        a = agg.setdefault(r["name"], [0.0, 0])
+        a = agg.setdefault(r["name"], [0.0, 0, 0.0, 0.0, 0])
         a[0] += r["us"]
         a[1] += r["bytes"]
-    for name, (us, b) in sorted(agg.items(), key=lambda kv: -kv[1][0]):
+        if r["work_us"] is not None:
+            a[2] += r["work_us"]
+            a[3] += r["barrier_us"]
+            a[4] += 1
+    print(f"  {'phase':18s} {'in-step':>9s}  {'share':>5s}  {'GB/s':>13s}  {'slowest-CTA work':>16s}  {'barrier':>8s}")
+    for name, (us, b, wk, br, n) in sorted(agg.items(), key=lambda kv: -kv[1][0]):
         gbps = f"{b / (us * 1e-6) / 1e9:8.1f} GB/s" if b and us > 0 else "        -     "
-        print(f"  {name:18s} {us:9.1f} us  {100 * us / total:5.1f}%  {gbps}")
+        extra = f"  {wk / n:12.2f} us  {br / n:6.2f} us (mean of {n})" if n else ""
+        print(f"  {name:18s} {us:9.1f} us  {100 * us / total:5.1f}%  {gbps}{extra}")
     if args.json:
         with open(args.json, "w") as f:
             json.dump({"case": case["id"], "full_us": head[0]["us"], "empty_launch_us": head[1]["us"],

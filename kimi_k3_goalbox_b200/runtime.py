@@ -80,6 +80,7 @@ def load_library() -> ctypes.CDLL:
         lib.kk3_exchange_bytes.restype = ctypes.c_size_t
         lib.kk3_debug_set_peer.argtypes = [vp, i32, vp]
         lib.kk3_debug_copy.argtypes = [vp, i32, vp, ctypes.c_size_t]
+        lib.kk3_debug_trace.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_int), i32]
         lib.kk3_launch_config.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(ctypes.c_size_t)]
         _LIB = lib
     return _LIB
@@ -259,6 +260,13 @@ class StepContext:
         if rc != 0:
             raise KK3Error(rc, "kk3_debug_copy")
         return out
+
+    def trace(self, enable: bool | None = None) -> list[int]:
+        """Trace words: phase reached per CTA [1024], progress code per CTA [1024], marker per warp [4096];
+        optionally switch publishing on/off."""
+        buf = (ctypes.c_int * (2 * 1024 + 4096))()
+        self.lib.kk3_debug_trace(self.handle, -1 if enable is None else int(enable), buf, len(buf))
+        return list(buf)
 
     def launch_config(self) -> tuple[int, int, int]:
         g, t, s = ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
