@@ -61,6 +61,7 @@ typedef struct kk3_ctx kk3_ctx;
 #define KK3_ERR_DEVICE      (-5)  /* an in-kernel consistency check failed */
 #define KK3_ERR_PEERS       (-6)  /* tp > 1 and the peer buffers are not open yet */
 #define KK3_ERR_FAILED      (-7)  /* an earlier step failed; the context must be freed and rebuilt */
+#define KK3_ERR_TOO_LARGE   (-8)  /* kk3_step_noalloc: the geometry's scratch exceeds its static buffer */
 
 /* Pointer table. kk3_step takes one device pointer per slot, in this order:
  *   slots [0, KK3_GLOBAL_SLOTS): the global inputs and the outputs (enum below);
@@ -116,6 +117,20 @@ int kk3_step(kk3_ctx* ctx, const void* const* table, int table_size, void* strea
 /* Device-side status of the most recent steps, read from mapped host memory without synchronising:
  * KK3_OK, KK3_ERR_TIMEOUT or KK3_ERR_DEVICE. Call after the stream has been synchronised. */
 int kk3_status(kk3_ctx* ctx);
+
+/* Allocation-free variant of kk3_init + kk3_step + kk3_free for one TP1 step (no counterpart in the
+ * reference). For callers that cannot allocate device memory when they run a step: serving engines that have
+ * already handed nearly all of HBM to their own caches and pool, and latency-bound loops that must not call
+ * cudaMalloc/cudaFree, which synchronise the device. The step's scratch is a file-scope device array of
+ * 32 MiB per device; nothing is allocated. Geometries whose scratch does not fit get KK3_ERR_TOO_LARGE,
+ * tp > 1 gets KK3_ERR_UNSUPPORTED (a static device symbol cannot be exported to peers over CUDA IPC).
+ * The first call on a device does set-up (symbol address, kernel attributes); make it before any stream
+ * capture containing this call. Each call clears the scratch words that must start at zero on `stream`,
+ * then launches the step. `error_word` (optional, device-accessible int the caller zeroed) is set to a
+ * nonzero device code if an in-kernel wait times out. Calls whose steps overlap on one device share the
+ * scratch and race: serialise them. Same table, outputs and arithmetic as kk3_step. */
+int kk3_step_noalloc(const kk3_config* cfg, const void* const* table, int table_size, void* stream,
+                     int* error_word);
 
 /* Human-readable text for a return code. */
 const char* kk3_error_string(int code);

@@ -4,6 +4,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 #include "kk3_phases.cuh"
@@ -90,6 +91,7 @@ extern "C" const char* kk3_error_string(int code) {
     case KK3_ERR_DEVICE: return "in-kernel consistency check failed";
     case KK3_ERR_PEERS: return "tensor-parallel peers are not open";
     case KK3_ERR_FAILED: return "context failed earlier; rebuild it";
+    case KK3_ERR_TOO_LARGE: return "geometry needs more scratch than kk3_step_noalloc's static 32 MiB; use kk3_init";
     default: return "unknown kk3 error";
   }
 }
@@ -418,4 +420,241 @@ extern "C" int kk3_launch_config(kk3_ctx* x, int* grid, int* threads, size_t* sm
   if (threads) *threads = kThreads;
   if (smem) *smem = x->smem;
   return KK3_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// kk3_step_noalloc: the decode step with its scratch in one file-scope device array instead of memory that
+// kk3_init allocates. No counterpart in the reference.
+//
+// Who needs it: callers that cannot allocate device memory when they run a step. A serving engine hands
+// nearly all of HBM to its own caches and memory pool before the first request, so a later cudaMalloc of
+// tens of MB fails or fragments that pool; and a latency-bound loop must not call cudaMalloc or cudaFree,
+// because both synchronise the whole device and stall every other stream on it.
+//
+// What it does not do: allocate. No cudaMalloc, cudaHostAlloc, cudaFree or allocating library routine (torch
+// included) runs on this path; only cudaGetSymbolAddress, kernel attribute and occupancy queries (first call
+// per device), cudaMemsetAsync of the scratch and the cooperative launch.
+//
+// Limits: tp == 1 only, because CUDA IPC cannot export a static device symbol, so tensor-parallel peers
+// would have no exchange buffer to map. The scratch the geometry needs must fit kNoAllocScratchBytes
+// (32 MiB), which holds one TP8 rank's shapes at batch <= 8 and every small test geometry; larger
+// geometries get KK3_ERR_TOO_LARGE and should use kk3_init + kk3_step.
+//
+// Concurrency: there is one scratch array per device. Two calls whose steps overlap on one device (other
+// streams, other host threads) race on it and corrupt each other; serialise them.
+namespace kk3 {
+
+cudaError_t raise_smem_nt1(size_t smem);
+cudaError_t raise_smem_nt2(size_t smem);
+cudaError_t raise_smem_nt4(size_t smem);
+cudaError_t raise_smem_nt8(size_t smem);
+
+constexpr size_t kNoAllocScratchBytes = 32ull << 20;
+static __device__ __align__(256) unsigned char kk3_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+struct NoAllocDevice {
+  int ready = 0;
+  unsigned char* base = nullptr;   // device address of kk3_noalloc_scratch on this device
+  int sms = 0;
+  size_t smem_optin = 0;
+  unsigned epoch = 0;
+  kk3_config last = {};            // geometry of the previous call on this device
+  int has_last = 0;
+};
+static NoAllocDevice noalloc_dev[kNoAllocMaxDevices];
+static std::mutex noalloc_mu;
+
+// Geometry, scratch layout and launch shape of a TP1 step whose scratch starts at `base` (same formulas as
+// kk3_init). The layout starts with the words that must be zero when a step begins (see kk3_step_noalloc);
+// `zero_bytes` covers them.
+static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, StepArgs* a, size_t* total_bytes,
+                        size_t* zero_bytes, int* nt, size_t* smem) {
+  Geo& g = a->g;
+  memset(&g, 0, sizeof(g));
+  g.L = cfg->layers; g.B = cfg->batch; g.h = cfg->hidden; g.lh = cfg->latent_hidden; g.inter = cfg->inter_shard;
+  g.dinter = cfg->dense_inter_shard; g.sinter = cfg->shared_inter_shard; g.hr = cfg->heads; g.d = cfg->head_dim;
+  g.qr = cfg->q_lora_rank; g.kr = cfg->kv_lora_rank; g.nr = cfg->qk_nope_dim; g.rd = cfg->qk_rope_dim;
+  g.vd = cfg->v_head_dim; g.V = cfg->vocab_shard; g.E = cfg->experts; g.K = cfg->topk; g.ctx = cfg->context;
+  g.conv = cfg->conv_kernel; g.bs = cfg->attn_res_block_size; g.first_dense = cfg->first_dense; g.tp = 1;
+  g.rank = 0; g.qdim = g.hr * g.d;
+  for (int l = 0; l < g.L; ++l) {
+    if (((l + 1) % 4 == 0) || l == g.L - 1) ++g.nmla; else ++g.nkda;
+  }
+  g.nblk = (g.L + g.bs - 1) / g.bs;
+  g.timeout_ns = cfg->timeout_ns > 0 ? cfg->timeout_ns : 10000000000ll;
+  g.mla_mt = (g.hr + 15) / 16;
+  *nt = g.B <= 8 ? 1 : (g.B <= 16 ? 2 : (g.B <= 32 ? 4 : 8));
+  {
+    int chunks = sms / g.B;
+    chunks = chunks < 1 ? 1 : (chunks > 64 ? 64 : chunks);
+    int len = (g.ctx + 1 + chunks - 1) / chunks;
+    len = (len + kMlaPos - 1) / kMlaPos * kMlaPos;
+    g.mla_chunk_len = len;
+    g.mla_chunks = (g.ctx + 1 + len - 1) / len;
+  }
+  const long long gw = (long long)sms * kWarps;
+  g.fix_bank = 2ll * gw * (2 * *nt * 128);
+  {
+    long long tiles = 0;
+    auto mx = [&](long long v) { tiles = v > tiles ? v : tiles; };
+    mx((3ll * g.qdim + g.qdim + g.d + g.hr + 15 * 6) / 16 + 6);
+    mx((long long)(g.qr + g.kr + g.rd + g.hr * g.vd) / 16 + 3);
+    mx((long long)g.hr * (g.nr + g.rd) / 16 + 1);
+    mx(g.h / 16 + 1);
+    mx((long long)(g.dinter + 15) / 16 + 1);
+    mx((long long)(g.E + g.lh + 30) / 16 + 2);
+    mx((long long)(g.sinter + 15) / 16 + 1);
+    mx((long long)(g.V + 15) / 16 + 1);
+    mx((long long)g.B * g.K * ((g.inter > g.lh ? g.inter : g.lh) / 16));
+    g.cnt_bank = (int)tiles;
+  }
+  const size_t B = g.B;
+  const size_t qkv_w =
+      (size_t)3 * g.qdim > (size_t)(g.qr + g.kr + g.rd) ? (size_t)3 * g.qdim : (size_t)(g.qr + g.kr + g.rd);
+  Scratch& s = a->s;
+  memset(&s, 0, sizeof(s));
+  Comm& c = a->comm;
+  memset(&c, 0, sizeof(c));
+  // exchange buffer of a single rank: flags [B][1] u32, then two parity regions {att, exp, shd, key}
+  const size_t flag_bytes = align_up(B * 4, 256);
+  c.flag_off = 0;
+  c.att_off = 0;
+  size_t r = align_up(B * g.h * 2, 256);
+  c.exp_off = r;
+  r += align_up(B * g.lh * 4, 256);
+  c.shd_off = r;
+  r += align_up(B * g.h * 2, 256);
+  c.key_off = r;
+  r += align_up(B * 8, 256);
+  c.region_bytes = r;
+  c.data_off[0] = flag_bytes;
+  c.data_off[1] = flag_bytes + r;
+  const size_t comm_bytes = flag_bytes + 2 * r;
+  unsigned char* comm = nullptr;
+  int* err_mirror = nullptr;
+  struct Item { void** p; size_t bytes; };
+  Item items[] = {
+      // must be zero when a step begins: barrier word, phase count, error word and its mirror, stream-K
+      // tile counters, exchange flags (the exchange buffer's flag array comes first; its data regions
+      // after it are written before they are read)
+      {(void**)&s.bar, 64}, {(void**)&s.phase_count, 64}, {(void**)&s.err, 64}, {(void**)&err_mirror, 64},
+      {(void**)&s.fix_cnt, (size_t)g.cnt_bank * 2 * 4}, {(void**)&comm, comm_bytes},
+      // written before they are read within every step
+      {(void**)&s.prefix, B * g.h * 2}, {(void**)&s.blocks, (size_t)g.nblk * B * g.h * 2},
+      {(void**)&s.xa, B * g.h * 2}, {(void**)&s.xm, B * g.h * 2}, {(void**)&s.qkv, B * qkv_w * 2},
+      {(void**)&s.og, B * (size_t)g.qdim * 2}, {(void**)&s.fa, B * g.d * 2}, {(void**)&s.beta, B * g.hr * 2},
+      {(void**)&s.attn_in, B * (size_t)g.hr * g.vd * 2}, {(void**)&s.mla_qan, B * g.qr * 2},
+      {(void**)&s.mla_q, B * (size_t)g.hr * (g.nr + g.rd) * 2}, {(void**)&s.absorbed, B * (size_t)g.hr * g.kr * 2},
+      {(void**)&s.mla_part, B * (size_t)g.mla_chunks * g.hr * (g.kr + 2) * 4},
+      {(void**)&s.dense_act, B * (size_t)(g.dinter > 0 ? g.dinter : 64) * 2}, {(void**)&s.scores, B * g.E * 4},
+      {(void**)&s.latent, B * g.lh * 2}, {(void**)&s.latent_p, B * g.lh * 2},
+      {(void**)&s.shared_act, B * (size_t)(g.sinter > 0 ? g.sinter : 64) * 2}, {(void**)&s.route_ids, B * g.K * 4},
+      {(void**)&s.route_w, B * g.K * 4}, {(void**)&s.pair_row, B * g.K * 4}, {(void**)&s.pair_slot, B * g.K * 4},
+      {(void**)&s.chunk_info, (1 + B * g.K * 3) * 4}, {(void**)&s.act_p, B * g.K * (size_t)g.inter * 2},
+      {(void**)&s.out_slot, B * g.K * (size_t)g.lh * 2}, {(void**)&s.x3, B * g.lh * 2},
+      {(void**)&s.shared_red, B * g.h * 2}, {(void**)&s.expert_sum, B * g.lh * 4},
+      {(void**)&s.fix_part, (size_t)g.fix_bank * 2 * 4}, {(void**)&s.argmax_key, B * 8},
+      {(void**)&s.phase_ts, (kMaxPhases + 1) * 8}, {(void**)&s.sub_ts, (size_t)kArrivePhases * 16 * 8},
+  };
+  size_t off = 0;
+  for (auto& it : items) {
+    *it.p = base ? base + off : nullptr;
+    off += align_up(it.bytes, 256);
+    if (it.p == (void**)&comm) *zero_bytes = off - align_up(it.bytes, 256) + flag_bytes;
+  }
+  *total_bytes = off;
+  s.arrive_ts = nullptr;   // per-CTA barrier stamps are a profiling aid of the context path
+  s.trace_host = nullptr;
+  s.err_host = err_mirror;
+  c.base[0] = comm;
+  const int HR = g.mla_mt * 16;
+  size_t sm = (size_t)(HR + 2 * kMlaPos) * kRowK * 2 + (size_t)HR * kRowS * 4 + (size_t)HR * kRowP * 2 + 3 * HR * 4 + 64;
+  const size_t sm_row = (512 + (size_t)(g.h > g.lh ? g.h : g.lh)) * 4 + 64;
+  const size_t sm_abs = ((size_t)g.B * 128 + 4 * 16 * 128) * 4;
+  const size_t sm_route = ((size_t)g.B * g.K + 4 * kMaxExperts) * 4;
+  const size_t sm_gemv = (size_t)kWarps * kGemvSmemPerWarp;
+  sm = sm_gemv > sm ? sm_gemv : sm;
+  sm = sm_row > sm ? sm_row : sm;
+  sm = sm_abs > sm ? sm_abs : sm;
+  sm = sm_route > sm ? sm_route : sm;
+  *smem = align_up(sm, 128);
+  return KK3_OK;
+}
+
+// First call on a device, with that device current: find the scratch array's device address and the SM
+// count. The first call therefore does CUDA set-up work; make it before any stream capture that contains
+// this entry point and before latency-sensitive use.
+static int noalloc_setup(int device, NoAllocDevice* d) {
+  if (d->ready) return KK3_OK;
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, kk3_noalloc_scratch);
+  if (e != cudaSuccess || !p) return cuda_fail(e == cudaSuccess ? cudaErrorInvalidSymbol : e,
+                                               "cudaGetSymbolAddress(kk3_noalloc_scratch)");
+  cudaDeviceProp prop;
+  e = cudaGetDeviceProperties(&prop, device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+  d->base = (unsigned char*)p;
+  d->sms = prop.multiProcessorCount;
+  d->smem_optin = prop.sharedMemPerBlockOptin;
+  d->ready = 1;
+  return KK3_OK;
+}
+
+}  // namespace kk3
+
+extern "C" int kk3_step_noalloc(const kk3_config* cfg, const void* const* table, int table_size, void* stream,
+                                int* error_word) {
+  int rc = validate(cfg);
+  if (rc != KK3_OK) return rc;
+  if (cfg->tp != 1 || cfg->rank != 0) return KK3_ERR_UNSUPPORTED;
+  if (!table || table_size != KK3_GLOBAL_SLOTS + cfg->layers * KK3_LAYER_SLOTS || table_size > kMaxPtrs)
+    return KK3_ERR_ARG;
+  if (cfg->device < 0 || cfg->device >= kNoAllocMaxDevices) return KK3_ERR_ARG;
+  std::lock_guard<std::mutex> lock(noalloc_mu);   // host-side state only; see the concurrency note above
+  int prev = -1;
+  KK3_CUDA(cudaGetDevice(&prev));
+  if (prev != cfg->device) KK3_CUDA(cudaSetDevice(cfg->device));
+  struct Restore {
+    int dev;
+    bool on;
+    ~Restore() { if (on) cudaSetDevice(dev); }
+  } restore{prev, prev != cfg->device};
+  NoAllocDevice* d = &noalloc_dev[cfg->device];
+  rc = noalloc_setup(cfg->device, d);
+  if (rc != KK3_OK) return rc;
+  // the argument block is ~25 KB (one pointer per table slot); it lives on this host stack until the launch
+  // has copied it
+  StepArgs a;
+  size_t total = 0, zero = 0, smem = 0;
+  int nt = 1;
+  plan_noalloc(cfg, d->sms, d->base, &a, &total, &zero, &nt, &smem);
+  if (total > kNoAllocScratchBytes) return KK3_ERR_TOO_LARGE;
+  if (smem > d->smem_optin) return KK3_ERR_UNSUPPORTED;
+  // The kernel's dynamic shared memory limit is per-function state shared with kk3_init, which sets it to its
+  // own geometry's need. It is raised here when below this launch's need and never lowered, so a live context
+  // keeps working and a lower value a later kk3_init left is undone.
+  {
+    cudaError_t e = nt == 1 ? raise_smem_nt1(smem) : nt == 2 ? raise_smem_nt2(smem)
+                  : nt == 4 ? raise_smem_nt4(smem) : raise_smem_nt8(smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(kk3_step_kernel)");
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  // Zero state. The barrier word, phase count, error words, stream-K tile counters and exchange flags must
+  // be zero when a step begins; a completed step leaves them so, a failed one may not, so they are cleared
+  // before every launch. When the geometry differs from the previous call's, the whole planned scratch is
+  // cleared once, so nothing a previous geometry left behind is seen.
+  const bool same = d->has_last && memcmp(&d->last, cfg, sizeof(kk3_config)) == 0;
+  KK3_CUDA(cudaMemsetAsync(d->base, 0, same ? zero : total, st));
+  d->last = *cfg;
+  d->has_last = 1;
+  if (error_word) a.s.err_host = error_word;
+  a.epoch = ++d->epoch;
+  a.stop_phase = -1;
+  a.start_phase = 0;
+  a.trace = 0;
+  a.nptr = table_size;
+  memcpy(a.ptr, table, sizeof(void*) * table_size);
+  cudaError_t e = launch_kernel(nt, &a, d->sms, smem, st);
+  return cuda_fail(e, "cudaLaunchCooperativeKernel(kk3_step_kernel)");
 }

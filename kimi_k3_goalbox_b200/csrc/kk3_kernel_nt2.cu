@@ -12,6 +12,16 @@ cudaError_t prepare_nt2(size_t smem, int* occupancy) {
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occupancy, kk3_step_kernel<2>, kThreads, smem);
 }
 
+// Raise (never lower) the kernel's dynamic shared memory limit to at least `smem`; used by the allocation-free
+// entry point, which shares this per-function setting with contexts made by kk3_init.
+cudaError_t raise_smem_nt2(size_t smem) {
+  cudaFuncAttributes attr;
+  cudaError_t e = cudaFuncGetAttributes(&attr, kk3_step_kernel<2>);
+  if (e != cudaSuccess) return e;
+  if ((size_t)attr.maxDynamicSharedSizeBytes >= smem) return cudaSuccess;
+  return cudaFuncSetAttribute(kk3_step_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
 cudaError_t launch_nt2(const StepArgs* args, int grid, size_t smem, cudaStream_t stream) {
   void* params[] = {const_cast<StepArgs*>(args)};
   return cudaLaunchCooperativeKernel((const void*)kk3_step_kernel<2>, dim3(grid), dim3(kThreads), params, smem, stream);
