@@ -44,12 +44,20 @@ FALLBACK_HBM_GBS = 6650.0
 def pick_case(args, n: int) -> dict:
     if args.case:
         case = cases.get_case(args.case)
-        if case["tp"] != n:
-            case = cases.variant(case, tp=n)
     else:
         case = cases.get_case(DEFAULT_CASE)
         if n != 1:
             case = cases.variant(case, tp=n)
+    if getattr(args, "rank_equivalent", False) and case["tp"] > 1 and n == 1:
+        # one TP rank's shard shapes as a TP1 geometry: the same arithmetic and bytes as one rank of the case,
+        # with identity reductions
+        tp = case["tp"]
+        params = dict(case["params"])
+        for key in ("q_heads", "vocab", "intermediate", "dense_intermediate"):
+            params[key] //= tp
+        case = dict(case, id=case["id"] + "-rank-equivalent", gpus=1, tp=1, params=params)
+    elif args.case and case["tp"] != n:
+        case = cases.variant(case, tp=n)
     if args.batch:
         case = cases.variant(case, batch=args.batch)
     case["params"].pop("checkpoint", None)
@@ -77,27 +85,38 @@ def traffic_for(case_id: str):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks and throttle reasons, sampled every 50 ms with timestamps. The sampler starts before
+    the warm-up (nvidia-smi needs a moment to start); only samples inside [mark_start, mark_end], the timed
+    region, enter the summary."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_index: int):
         self.device_index = device_index
         self.proc = None
+        self.t0 = self.t1 = None
+        self.lines: list[str] = []
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
         return self
 
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
     def __exit__(self, *exc):
         if self.proc is not None:
+            time.sleep(0.1)   # let the sample that covers the end of the timed region arrive
             self.proc.terminate()
             try:
                 out, _ = self.proc.communicate(timeout=5)
@@ -105,26 +124,34 @@ class ClockSampler:
                 self.proc.kill()
                 out = ""
             self.lines = [l for l in out.splitlines() if l.strip()]
-        else:
-            self.lines = []
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
+        from datetime import datetime
+        sm, mx, reasons, power = [], None, set(), []
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in getattr(self, "lines", []):
+        for line in self.lines:
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                clk, mxv = float(parts[2]), float(parts[3])
             except ValueError:
                 continue
-            for name, val in zip(names, parts[5:9]):
+            # a sample reports the state just before its timestamp: keep those inside the timed window
+            if self.t0 is None or self.t1 is None or not (self.t0 <= ts <= self.t1 + 0.05):
+                continue
+            sm.append(clk)
+            mx = mxv
+            try:
+                power.append(float(parts[4]))
+            except ValueError:
+                pass
+            for name, val in zip(names, parts[6:10]):
                 if val.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "power_w_max": max(power) if power else None}
 
 
 def init_dist(n: int):
@@ -175,15 +202,17 @@ def run_b200(args, n: int, rank: int, local: int) -> dict | None:
         ctx._bind_inputs(values)
         ctx.bind_outputs(outputs)
         stream = torch.cuda.current_stream(device)
-        for _ in range(args.warmup):
-            ctx.launch(stream.cuda_stream)
-        barrier(n)
-        ctx.check()
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         t_all0, t_all1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier(n)
         with ClockSampler(local) as clocks:
+            for _ in range(args.warmup):
+                ctx.launch(stream.cuda_stream)
+            torch.cuda.synchronize()
+            barrier(n)
+            ctx.check()
+            barrier(n)
+            clocks.mark_start()
             t_all0.record(stream)
             for i in range(args.steps):
                 starts[i].record(stream)
@@ -191,6 +220,7 @@ def run_b200(args, n: int, rank: int, local: int) -> dict | None:
                 ends[i].record(stream)
             t_all1.record(stream)
             torch.cuda.synchronize()
+            clocks.mark_end()
         barrier(n)
         ctx.check()
         per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
@@ -317,20 +347,27 @@ def fast_cpu_inputs(case: dict) -> dict:
     from oracle import kimi_oracle as ko
     g = torch.Generator().manual_seed(0)
     block = torch.randn(1 << 22, generator=g)
+    codes = torch.randint(0, 256, (1 << 22,), generator=g, dtype=torch.uint8)
+    converted: dict = {}
+
+    def tile(t, src):
+        flat = t.view(-1)
+        for s in range(0, flat.numel(), src.numel()):
+            n = min(src.numel(), flat.numel() - s)
+            flat[s:s + n].copy_(src[:n])
+        return t
 
     def fill(shape, std, mean, dtype):
-        t = torch.empty(shape, dtype=dtype)
-        flat = t.view(-1)
-        for s in range(0, flat.numel(), block.numel()):
-            n = min(block.numel(), flat.numel() - s)
-            flat[s:s + n] = (block[:n] * std + mean).to(dtype)
-        return t
+        key = (std, mean, dtype)
+        if key not in converted:
+            converted[key] = (block * std + mean).to(dtype)
+        return tile(torch.empty(shape, dtype=dtype), converted[key])
 
     vals = {}
     p = case["params"]
     for name, (shape, dtype, fan_in, _) in ko.tensor_specs(case).items():
         if name.endswith("_blocks"):
-            vals[name] = torch.randint(0, 256, shape, generator=g, dtype=torch.uint8)
+            vals[name] = tile(torch.empty(shape, dtype=torch.uint8), codes)
         elif name.endswith("_scales"):
             e = round(-torch.log2(torch.tensor(2.93 * (p["latent_hidden"] if "down" not in name else p["intermediate"]) ** 0.5)).item())
             vals[name] = (126 + e + torch.randint(0, 3, shape, generator=g)).to(torch.uint8)
@@ -376,6 +413,8 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--case", default=None)
     ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--rank-equivalent", action="store_true",
+                    help="N=1 only: time one TP rank of --case (its shard shapes as a TP1 geometry)")
     ap.add_argument("--seed", type=int, default=20261201)
     ap.add_argument("--cpu-steps", type=int, default=5, help="samples of the attached cpu_baseline (N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -1,4 +1,4 @@
-"""Run selected phases of the decode-step kernel in isolation inside a profiler capture window.
+"""Run selected phases of the decode-step kernel (or whole steps) in isolation inside a profiler capture window.
 
     ncu --profile-from-start off --clock-control none -k regex:kk3_step_kernel ... \
         python -m kimi_k3_goalbox_b200.ncu_phase --case ID [--rank-equivalent] [--layers L] --phase NAME[:LAYER] ...
@@ -26,7 +26,8 @@ def main(argv=None) -> int:
     ap.add_argument("--rank-equivalent", action="store_true")
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--batch", type=int, default=None)
-    ap.add_argument("--phase", action="append", required=True, help="NAME or NAME:LAYER (first match if no layer)")
+    ap.add_argument("--phase", action="append", required=True,
+                    help="NAME or NAME:LAYER (first match if no layer), or 'step' for one whole step")
     args = ap.parse_args(argv)
     case = cases.get_case(args.case)
     case["params"].pop("checkpoint", None)
@@ -41,6 +42,9 @@ def main(argv=None) -> int:
     prog = phase_program(case["params"])
     picks = []
     for spec in args.phase:
+        if spec == "step":
+            picks.append(-1)
+            continue
         name, _, layer = spec.partition(":")
         idx = [i for i, (n, l) in enumerate(prog) if n == name and (not layer or l == int(layer))]
         if not idx:
@@ -62,12 +66,15 @@ def main(argv=None) -> int:
         torch.cuda.cudart().cudaProfilerStart()
         for i in picks:
             flush.zero_()
-            ctx.launch(stream, stop_phase=i + 1 if i + 1 < len(prog) else -1, start_phase=i)
+            if i < 0:
+                ctx.launch(stream)
+            else:
+                ctx.launch(stream, stop_phase=i + 1 if i + 1 < len(prog) else -1, start_phase=i)
         torch.cuda.synchronize()
         torch.cuda.cudart().cudaProfilerStop()
         ctx.check()
         ctx.close()
-    print("captured phases:", [f"{prog[i][0]}:{prog[i][1]} (#{i})" for i in picks])
+    print("captured:", [f"{prog[i][0]}:{prog[i][1]} (#{i})" if i >= 0 else "whole step" for i in picks])
     return 0
 
 

@@ -479,6 +479,8 @@ def timed_sample(case, values, part):
         t0 = time.perf_counter()
         _embed(st)
         st.blocks = [st.prefix]
+        # no layer ran, so the per-layer route list the outputs stack is empty: one placeholder row set
+        st.chosen = [torch.full((st.p["batch"], st.p["topk"]), -1, dtype=torch.int64, device=st.device)]
         _head(st)
         return time.perf_counter() - t0
     layer = int(part)
