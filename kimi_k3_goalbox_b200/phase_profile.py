@@ -140,7 +140,7 @@ def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[d
             narr = min(len(prog) - 1, 256)
             arr = ctx.debug_buffer(17, torch.int64, (narr, grid)).cpu()
             # per phase: slowest CTA's arrival after the phase began, and barrier latency after it
-            work, barrier, last_cta = [], [], []
+            work, barrier, last_cta, spread = [], [], [], []
             for i in range(len(prog)):
                 if i < narr:
                     row = arr[i]
@@ -148,10 +148,14 @@ def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[d
                     work.append((last - ts[i]) / 1000.0)
                     barrier.append((ts[i + 1] - last) / 1000.0)
                     last_cta.append(int(row.argmax()))
+                    rel = ((row - ts[i]).double() / 1000.0).sort().values
+                    q = lambda f: round(float(rel[min(len(rel) - 1, int(f * (len(rel) - 1)))]), 2)
+                    spread.append({"p10": q(0.1), "p50": q(0.5), "p90": q(0.9), "max": q(1.0)})
                 else:
                     work.append(None)
                     barrier.append(None)
                     last_cta.append(None)
+                    spread.append(None)
             empty = timed(len(prog) + 1, -1)      # walks the program, runs no phase: launch cost
             alone = [max(timed(i, i + 1 if i + 1 < len(prog) else -1) - empty, 1e-3) for i in range(len(prog))]
             ctx.check()
@@ -178,6 +182,7 @@ def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[d
         rows.append({"phase": i, "name": name, "layer": layer, "us": round(dt, 2), "alone_us": round(alone[i], 2),
                      "work_us": None if work[i] is None else round(work[i], 2),
                      "barrier_us": None if barrier[i] is None else round(barrier[i], 2), "last_cta": last_cta[i],
+                     "cta_done_us": spread[i],
                      "bytes": nbytes[i], "GBps": round(nbytes[i] / (dt * 1e-6) / 1e9, 1) if nbytes[i] and dt > 0 else None})
     return rows
 
@@ -210,17 +215,19 @@ def main(argv=None) -> int:
           f"in-step phases sum to {total:.1f} us (globaltimer), alone-sum {sum(r['alone_us'] for r in rows):.1f} us")
     agg: dict[str, list] = {}
     for r in rows:
-        a = agg.setdefault(r["name"], [0.0, 0, 0.0, 0.0, 0])
+        a = agg.setdefault(r["name"], [0.0, 0, 0.0, 0.0, 0, 0.0, 0.0])
         a[0] += r["us"]
         a[1] += r["bytes"]
         if r["work_us"] is not None:
             a[2] += r["work_us"]
             a[3] += r["barrier_us"]
             a[4] += 1
-    print(f"  {'phase':18s} {'in-step':>9s}  {'share':>5s}  {'GB/s':>13s}  {'slowest-CTA work':>16s}  {'barrier':>8s}")
-    for name, (us, b, wk, br, n) in sorted(agg.items(), key=lambda kv: -kv[1][0]):
+            a[5] += r["cta_done_us"]["p10"]
+            a[6] += r["cta_done_us"]["p50"]
+    print(f"  {'phase':18s} {'in-step':>9s}  {'share':>5s}  {'GB/s':>13s}  {'CTA done p10/p50/max':>22s}  {'barrier':>8s}")
+    for name, (us, b, wk, br, n, p10, p50) in sorted(agg.items(), key=lambda kv: -kv[1][0]):
         gbps = f"{b / (us * 1e-6) / 1e9:8.1f} GB/s" if b and us > 0 else "        -     "
-        extra = f"  {wk / n:12.2f} us  {br / n:6.2f} us (mean of {n})" if n else ""
+        extra = f"  {p10 / n:6.1f} /{p50 / n:6.1f} /{wk / n:6.1f} us  {br / n:6.2f} us (mean of {n})" if n else ""
         print(f"  {name:18s} {us:9.1f} us  {100 * us / total:5.1f}%  {gbps}{extra}")
     if args.json:
         with open(args.json, "w") as f:
