@@ -82,6 +82,7 @@ struct Scratch {
   float* fix_part;    // [2 * warps_total, 16 * 64 * 2] stream-K partial tiles
   int* fix_cnt;       // [max tiles] stream-K arrival counters
   unsigned long long* argmax_key; // [B]
+  int* route_done;    // routing CTAs finished in this layer (the last one groups the pairs; it resets the count)
   unsigned* bar;      // grid barrier word (see grid_sync)
   int* err;           // device error word, polled by every wait (device memory: cheap to poll)
   int* err_host;      // host-visible copy in mapped host memory, written only when an error is raised

@@ -302,6 +302,9 @@ KK3_FN void run_gemv(const StepArgs& a, const GemvJob* jobs, int njobs, int cta_
   int* cnt_base = a.s.fix_cnt + bank * a.g.cnt_bank;
   const unsigned long long pol = l2_evict_first_policy();
   const bool stamp = ph >= 0 && blockIdx.x == 0 && threadIdx.x == 0;
+  // read once: a field of the argument block read inside the loop is reloaded after every asynchronous copy
+  // (their asm carries a memory clobber), and the branch on it waits for that load
+  const bool trace = a.trace && warp == 0;
   if (stamp) sub_stamp(a, ph, 8);
 
   // ---- producer: cursor + per-tile pointers
@@ -385,7 +388,7 @@ KK3_FN void run_gemv(const StepArgs& a, const GemvJob* jobs, int njobs, int cta_
     cp_async_commit_g();
     cp_async_wait_g<S - 1>();
     if (stamp && n == 0) sub_stamp(a, ph, 9);
-    if (a.trace && warp == 0 && (n & 63) == 0) trace_progress(a, 1, 0x100000 | n);
+    if (trace && (n & 63) == 0) trace_progress(a, 1, 0x100000 | n);
     mma_step_bf16<NT, MT, XS>(ring + c_slot * kSlotVec, c_x, c_ldx, c_ncols, c_ks, acc);
     c_slot = c_slot + 1 == S ? 0 : c_slot + 1;
     if (c_ks == c_ksteps - 1 || n == nunits - 1) {

@@ -190,6 +190,7 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
       {(void**)&s.shared_red, B * g.h * 2}, {(void**)&s.expert_sum, B * g.lh * 4},
       {(void**)&s.fix_part, (size_t)g.fix_bank * 2 * 4}, {(void**)&s.fix_cnt, (size_t)g.cnt_bank * 2 * 4},
       {(void**)&s.argmax_key, B * 8}, {(void**)&bar, 64}, {(void**)&phase_count, 64}, {(void**)&s.err, 64},
+      {(void**)&s.route_done, 64},
       {(void**)&s.phase_ts, (kMaxPhases + 1) * 8}, {(void**)&s.arrive_ts, (size_t)kArrivePhases * 1024 * 8},
       {(void**)&s.sub_ts, (size_t)kArrivePhases * 16 * 8},
   };
@@ -535,10 +536,11 @@ static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, Ste
   int* err_mirror = nullptr;
   struct Item { void** p; size_t bytes; };
   Item items[] = {
-      // must be zero when a step begins: barrier word, phase count, error word and its mirror, stream-K
-      // tile counters, exchange flags (the exchange buffer's flag array comes first; its data regions
+      // must be zero when a step begins: barrier word, phase count, error word and its mirror, routing
+      // counter, stream-K tile counters, exchange flags (the exchange buffer's flag array comes first; its data regions
       // after it are written before they are read)
       {(void**)&s.bar, 64}, {(void**)&s.phase_count, 64}, {(void**)&s.err, 64}, {(void**)&err_mirror, 64},
+      {(void**)&s.route_done, 64},
       {(void**)&s.fix_cnt, (size_t)g.cnt_bank * 2 * 4}, {(void**)&comm, comm_bytes},
       // written before they are read within every step
       {(void**)&s.prefix, B * g.h * 2}, {(void**)&s.blocks, (size_t)g.nblk * B * g.h * 2},

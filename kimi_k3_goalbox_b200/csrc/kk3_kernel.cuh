@@ -167,12 +167,25 @@ KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int pa
 #pragma unroll
       for (int e = 0; e < 8; ++e) tot[q][e] = 0.0f;
       if (c >= nvec) continue;
-      for (int j = 0; j < g.K; ++j) {
-        float f[8];
-        unpack8(ld_act16(a.s.out_slot + ((size_t)b * g.K + j) * g.lh + c * 8), f);
-        const float wj = w[j];
+      // 8 slots' loads in flight at a time (L2), summed in slot order
+      const uint4* slot0 = reinterpret_cast<const uint4*>(a.s.out_slot + (size_t)b * g.K * g.lh) + c;
+      for (int j0 = 0; j0 < g.K; j0 += 8) {
+        uint4 v[8];
+        float wj[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) tot[q][e] += f[e] * wj;
+        for (int u = 0; u < 8; ++u) {
+          const bool live = j0 + u < g.K;
+          v[u] = live ? __ldcg(slot0 + (size_t)(j0 + u) * nvec) : make_uint4(0, 0, 0, 0);
+          wj[u] = live ? __ldcg(w + j0 + u) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (j0 + u >= g.K) break;
+          float f[8];
+          unpack8(v[u], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) tot[q][e] += f[e] * wj[u];
+        }
       }
       float* es = a.s.expert_sum + (size_t)b * g.lh + c * 8;
       *reinterpret_cast<float4*>(es) = make_float4(tot[q][0], tot[q][1], tot[q][2], tot[q][3]);
@@ -224,7 +237,7 @@ KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int pa
       const int c = threadIdx.x + q * kThreads;
       if (c >= nvec) continue;
       float wf[8], o[8];
-      unpack8(ld_act16(ln + c * 8), wf);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(ln) + c), wf);
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = round_bf(round_bf(tot[q][e] * rs) * wf[e]);
       *reinterpret_cast<uint4*>(a.s.x3 + (size_t)b * g.lh + c * 8) = pack8(o);
@@ -516,7 +529,8 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         run_gemv<NT, 2>(a, sj2, 1, 0, gridDim.x, 0, 1);
       }
       KK3_PHASE_END();
-      // routing on CTA 0 while the other CTAs run the shared-expert down projection (kimi.py:309-316, :326)
+      // routing of row b on CTA b while the other CTAs run the shared-expert down projection (kimi.py:309-316,
+      // :326)
       const unsigned x_moe = xi++;
       if (KK3_RUN) {
         KK3_BUILD({
@@ -525,10 +539,10 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
           sj[0].aux_off = a.comm.shd_off;
           prepare_jobs(sj, 1);
         });
-        if (blockIdx.x == 0) {
-          route_all(a, l, l - g.first_dense, smem);
+        if ((int)blockIdx.x < g.B) {
+          route_row(a, l, blockIdx.x, smem, phase);
         } else {
-          run_gemv<NT, 1>(a, sj, 1, 1, gridDim.x, x_moe & 1);
+          run_gemv<NT, 1>(a, sj, 1, g.B, gridDim.x, x_moe & 1);
           if (g.tp > 1) __threadfence_system();
         }
       }

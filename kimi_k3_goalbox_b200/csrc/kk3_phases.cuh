@@ -66,6 +66,15 @@ KK3_DEV uint4 pack8(const float (&f)[8]) {
   return v;
 }
 
+// Row-phase staging: block vectors go to dynamic shared memory after the reduction scratch.
+constexpr int kRowStageOff = 2048;   // bytes; the block_sums scratch (red) uses < 1.5 KB
+KK3_DEV void cp_async16_row(void* smem_dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(smem_dst)),
+               "l"(src) : "memory");
+}
+KK3_DEV void cp_async_commit_row() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+KK3_DEV void cp_async_wait_row() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // CTA-wide sums of the first `live` of N per-thread values (all threads receive the totals).
 // `red`: (kWarps + 1) * N floats. Warp partials go to shared memory, warp 0 adds them, one broadcast back.
 template <int N>
@@ -102,90 +111,106 @@ KK3_FN void mix_and_norm_regs(const StepArgs& a, int b, int nb, const uint4 (&pr
   const int tid = threadIdx.x, nvec = g.h / 8;
   const bool stamp = ph >= 0 && b == 0 && tid == 0;
   float hidden[kRowChunks][8];
+  // the final norm's weights are needed last; their load is issued first
+  uint4 lnw[kRowChunks];
+#pragma unroll
+  for (int q = 0; q < kRowChunks; ++q) {
+    const int c = tid + q * kThreads;
+    lnw[q] = c < nvec ? __ldg(reinterpret_cast<const uint4*>(ln) + c) : make_uint4(0, 0, 0, 0);
+  }
   if (nb > 0) {
-    // the first kCached block vectors stay in registers between the two passes, later ones are re-read
-    constexpr int kCached = 2;
-    uint4 vals[kCached][kRowChunks];
+    // every block vector this thread needs is staged into shared memory with one round of cp.async (each
+    // thread reads back only its own chunks, so no CTA barrier is needed); the statistics and the mix then
+    // read shared memory instead of issuing dependent L2 loads block after block
+    uint4* stage = reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(red) + kRowStageOff);
+    for (int i = 0; i < nb; ++i) {
+#pragma unroll
+      for (int q = 0; q < kRowChunks; ++q) {
+        const int c = tid + q * kThreads;
+        if (c < nvec) cp_async16_row(stage + (i * kRowChunks + q) * kThreads + tid,
+                                     a.s.blocks + ((size_t)i * g.B + b) * g.h + c * 8);
+      }
+    }
+    cp_async_commit_row();
     float np[kRowChunks][8];
-    auto block_chunk = [&](int i, int q) -> uint4 {
-      const int c = tid + q * kThreads;
-      return c < nvec ? ld_act16(a.s.blocks + ((size_t)i * g.B + b) * g.h + c * 8) : make_uint4(0, 0, 0, 0);
-    };
 #pragma unroll
     for (int q = 0; q < kRowChunks; ++q) {
       const int c = tid + q * kThreads;
       float fn[8], fp[8];
       uint4 un = make_uint4(0, 0, 0, 0), up = make_uint4(0, 0, 0, 0);
       if (c < nvec) {
-        un = ld_act16(norm + c * 8);
-        up = ld_act16(proj + c * 8);
+        un = __ldg(reinterpret_cast<const uint4*>(norm) + c);
+        up = __ldg(reinterpret_cast<const uint4*>(proj) + c);
       }
       unpack8(un, fn);
       unpack8(up, fp);
 #pragma unroll
       for (int e = 0; e < 8; ++e) np[q][e] = fn[e] * fp[e];
-#pragma unroll
-      for (int i = 0; i < kCached; ++i) vals[i][q] = i < nb ? block_chunk(i, q) : make_uint4(0, 0, 0, 0);
     }
-    auto vec_chunk = [&](int i, int q) -> uint4 {
-      if (i == nb) return pre[q];
-      if (i == 0) return vals[0][q];
-      if (i == 1) return vals[1][q];
-      return block_chunk(i, q);
-    };
-    // statistics: sum of squares and dot with norm*proj, for every block vector and the prefix
-    float st[2 * (kMaxBlocks + 1)];
+    cp_async_wait_row();
+    // Compact loops over the block vectors (not unrolled): this code runs once per layer with a cold
+    // instruction cache, so its size, not its arithmetic, sets its time. Summation orders are those of the
+    // CTA reduction used elsewhere: per thread over (chunk, element), warp shuffle tree, warps in order.
+    constexpr int kSt = 2 * (kMaxBlocks + 1);
+    const int warp = tid >> 5, lane = tid & 31;
+    float* wred = red;                    // [kWarps][kSt] warp partials
+    float* tot = red + kWarps * kSt;      // [kSt] statistics of every vector
+#pragma unroll 1
+    for (int i = 0; i <= nb; ++i) {
+      float ss = 0.0f, dt = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 2 * (kMaxBlocks + 1); ++i) st[i] = 0.0f;
+      for (int q = 0; q < kRowChunks; ++q) {
+        const int c = tid + q * kThreads;
+        float f[8];
+        unpack8(i == nb ? pre[q] : (c < nvec ? stage[(i * kRowChunks + q) * kThreads + tid] : make_uint4(0, 0, 0, 0)), f);
 #pragma unroll
-    for (int i = 0; i <= kMaxBlocks; ++i) {
-      if (i <= nb) {
-#pragma unroll
-        for (int q = 0; q < kRowChunks; ++q) {
-          float f[8];
-          unpack8(vec_chunk(i, q), f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            st[2 * i] += f[e] * f[e];
-            st[2 * i + 1] += f[e] * np[q][e];
-          }
+        for (int e = 0; e < 8; ++e) {
+          ss += f[e] * f[e];
+          dt += f[e] * np[q][e];
         }
+      }
+      ss = warp_sum(ss);
+      dt = warp_sum(dt);
+      if (lane == 0) {
+        wred[warp * kSt + 2 * i] = ss;
+        wred[warp * kSt + 2 * i + 1] = dt;
       }
     }
     if (stamp) sub_stamp(a, ph, 1);
-    block_sums<2 * (kMaxBlocks + 1)>(st, red, 2 * (nb + 1));
+    __syncthreads();
+    if (tid < 2 * (nb + 1)) {
+      float t = 0.0f;
+      for (int w = 0; w < kWarps; ++w) t += wred[w * kSt + tid];
+      tot[tid] = t;
+    }
+    __syncthreads();
     if (stamp) sub_stamp(a, ph, 2);
-    float prob[kMaxBlocks + 1];
+    // softmax over the nb + 1 logits rms(v_i) . (norm * proj), then the weighted sum
     float mx = -INFINITY;
+    for (int i = 0; i <= nb; ++i) mx = fmaxf(mx, tot[2 * i + 1] * rsqrtf(tot[2 * i] / (float)g.h + 1e-5f));
+    float den = 0.0f;
+    for (int i = 0; i <= nb; ++i) den += expf(tot[2 * i + 1] * rsqrtf(tot[2 * i] / (float)g.h + 1e-5f) - mx);
+    float accv[kRowChunks][8];
 #pragma unroll
-    for (int i = 0; i <= kMaxBlocks; ++i) {
-      prob[i] = (i <= nb) ? st[2 * i + 1] * rsqrtf(st[2 * i] / (float)g.h + 1e-5f) : -INFINITY;
-      mx = fmaxf(mx, prob[i]);
-    }
-    float tot = 0.0f;
+    for (int q = 0; q < kRowChunks; ++q)
 #pragma unroll
-    for (int i = 0; i <= kMaxBlocks; ++i) {
-      prob[i] = (i <= nb) ? expf(prob[i] - mx) : 0.0f;
-      tot += prob[i];
-    }
+      for (int e = 0; e < 8; ++e) accv[q][e] = 0.0f;
+#pragma unroll 1
+    for (int i = 0; i <= nb; ++i) {
+      const float pi = expf(tot[2 * i + 1] * rsqrtf(tot[2 * i] / (float)g.h + 1e-5f) - mx) / den;
 #pragma unroll
-    for (int q = 0; q < kRowChunks; ++q) {
-      float accv[8];
+      for (int q = 0; q < kRowChunks; ++q) {
+        const int c = tid + q * kThreads;
+        float f[8];
+        unpack8(i == nb ? pre[q] : (c < nvec ? stage[(i * kRowChunks + q) * kThreads + tid] : make_uint4(0, 0, 0, 0)), f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) accv[e] = 0.0f;
-#pragma unroll
-      for (int i = 0; i <= kMaxBlocks; ++i) {
-        if (i <= nb) {
-          float f[8];
-          unpack8(vec_chunk(i, q), f);
-          const float pi = prob[i] / tot;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) accv[e] += pi * f[e];
-        }
+        for (int e = 0; e < 8; ++e) accv[q][e] += pi * f[e];
       }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) hidden[q][e] = round_bf(accv[e]);
     }
+#pragma unroll
+    for (int q = 0; q < kRowChunks; ++q)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) hidden[q][e] = round_bf(accv[q][e]);
   } else {
 #pragma unroll
     for (int q = 0; q < kRowChunks; ++q) unpack8(pre[q], hidden[q]);
@@ -204,7 +229,7 @@ KK3_FN void mix_and_norm_regs(const StepArgs& a, int b, int nb, const uint4 (&pr
     const int c = tid + q * kThreads;
     if (c < nvec) {
       float w[8], o[8];
-      unpack8(ld_act16(ln + c * 8), w);
+      unpack8(lnw[q], w);
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = round_bf(round_bf(hidden[q][e] * rs) * w[e]);
       *reinterpret_cast<uint4*>(out_row + c * 8) = pack8(o);
@@ -669,103 +694,78 @@ KK3_FN void mla_combine_item(const StepArgs& a, int layer, int b, int hh, float*
 }
 
 // ------------------------------------------------------------------------------------------------
-// Routing (kimi.py:308-316) for all rows, by one CTA: FP32 sigmoid scores + bias, top-k (lowest index
-// wins ties), weights renormalised over the unbiased scores, ids sorted ascending. Then group the
-// (row, slot) pairs by expert into chunks of <= 8 pairs for the MXFP4 phases.
-KK3_FN void route_all(const StepArgs& a, int layer, int moe_idx, unsigned char* smem) {
+// Routing (kimi.py:308-316). Batch row b is routed by CTA b: FP32 sigmoid scores + bias, top-k with the
+// lowest index winning ties, weights renormalised over the unbiased scores, ids sorted ascending. Each of
+// the 16 warps selects the top-k of its 64 experts; warp 0 then selects the top-k of those 16*k candidates.
+// Exact: an expert dropped inside its warp has k better experts (under the order value desc, index asc) in
+// that warp alone. The last routing CTA to finish groups every row's (row, slot) pairs by expert into chunks
+// of <= 8 pairs for the MXFP4 phases, so no extra grid barrier is needed.
+
+// better(v, e) than (bv, bi): larger value, equal value and lower index. NaN never wins.
+KK3_DEV bool route_better(float v, int e, float bv, int bi) { return v > bv || (v == bv && e < bi); }
+
+KK3_DEV void route_group_pairs(const StepArgs& a, unsigned char* smem) {
   const Geo& g = a.g;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int npairs = g.B * g.K;
   int* ids = reinterpret_cast<int*>(smem);            // [B*K]
-  int* cnt = ids + g.B * g.K;                          // [E]
+  int* cnt = ids + kMaxBatch * kMaxTopk;               // [E]
   int* off = cnt + kMaxExperts;                        // [E]
   int* fill = off + kMaxExperts;                       // [E]
   int* coff = fill + kMaxExperts;                      // [E] chunk offsets
-  const float* bias = lptr<float>(a, layer, KK3_MOE_ROUTER_BIAS);
-  long long* out_ids = gout<long long>(a, KK3_OUT_EXPERT_IDS) + (size_t)layer * g.B * g.K;
   for (int e = tid; e < g.E; e += kThreads) {
     cnt[e] = 0;
     fill[e] = 0;
   }
-  for (int b = warp; b < g.B; b += kWarps) {
-    const float* sc = a.s.scores + (size_t)b * g.E;
-    // candidates: biased score (NaN scores count as -inf); taken or padded entries are NaN, which never wins
-    float v[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int e = lane + 32 * i;
-      const float x = e < g.E ? sc[e] + bias[e] : __int_as_float(0x7fc00000);
-      v[i] = (e < g.E && x != x) ? -INFINITY : x;
-    }
-    int mine = -1;   // lane j < K keeps the j-th selected expert
-    for (int j = 0; j < g.K; ++j) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int e = lane + 32 * i;
-        if (v[i] > bv || (v[i] == bv && e < bi)) {
-          bv = v[i];
-          bi = e;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      if (lane == j) mine = bi;
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (i == (bi >> 5) && (bi & 31) == lane) v[i] = __int_as_float(0x7fc00000);
-    }
-    // sort the K ids ascending: rank of each
-    int rank = 0;
-    for (int j = 0; j < g.K; ++j) {
-      const int other = __shfl_sync(0xffffffffu, mine, j);
-      if (lane < g.K && other < mine) ++rank;
-    }
-    const float w = lane < g.K ? sc[mine] : 0.0f;
-    const float wsum = warp_sum(w);
-    if (lane < g.K) {
-      a.s.route_ids[b * g.K + rank] = mine;
-      a.s.route_w[b * g.K + rank] = w / (wsum + 1e-20f);
-      out_ids[(size_t)b * g.K + rank] = (long long)mine;
-      ids[b * g.K + rank] = mine;
-    }
+  // other CTAs wrote these ids: read through L2
+  for (int i = tid; i < npairs; i += kThreads) {
+    int e = __ldcg(a.s.route_ids + i);
+    ids[i] = e < 0 ? 0 : (e >= g.E ? g.E - 1 : e);
   }
   __syncthreads();
-  const int npairs = g.B * g.K;
   for (int i = tid; i < npairs; i += kThreads) atomicAdd(&cnt[ids[i]], 1);
   __syncthreads();
-  if (warp == 0) {
-    // exclusive scans over experts of pair counts and chunk counts (one warp, 32 experts per step)
-    int run = 0, crun = 0;
-    for (int e0 = 0; e0 < g.E; e0 += 32) {
-      const int e = e0 + lane;
-      const int n = e < g.E ? cnt[e] : 0;
-      const int nc = (n + 7) / 8;
-      int incl = n, cincl = nc;
+  // exclusive scans over experts of pair counts and chunk counts: warp w scans experts [64w, 64w + 64)
+  // (two per lane), then the warp totals are scanned (E <= 1024 = kWarps * 64)
+  {
+    int* wtot = coff + kMaxExperts;   // [2][kWarps]
+    const int ea = warp * 64 + 2 * lane, eb = ea + 1;
+    const int na = ea < g.E ? cnt[ea] : 0, nb = eb < g.E ? cnt[eb] : 0;
+    const int ca = (na + 7) / 8, cb = (nb + 7) / 8;
+    int incl = na + nb, cincl = ca + cb;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t1 = __shfl_up_sync(0xffffffffu, incl, o);
-        const int t2 = __shfl_up_sync(0xffffffffu, cincl, o);
-        if (lane >= o) {
-          incl += t1;
-          cincl += t2;
-        }
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t1 = __shfl_up_sync(0xffffffffu, incl, o);
+      const int t2 = __shfl_up_sync(0xffffffffu, cincl, o);
+      if (lane >= o) {
+        incl += t1;
+        cincl += t2;
       }
-      if (e < g.E) {
-        off[e] = run + incl - n;
-        coff[e] = crun + cincl - nc;
-      }
-      run += __shfl_sync(0xffffffffu, incl, 31);
-      crun += __shfl_sync(0xffffffffu, cincl, 31);
     }
-    if (lane == 0) a.s.chunk_info[0] = crun;
+    if (lane == 31) {
+      wtot[warp] = incl;
+      wtot[kWarps + warp] = cincl;
+    }
+    __syncthreads();
+    int base = 0, cbase = 0;
+    for (int w = 0; w < warp; ++w) {
+      base += wtot[w];
+      cbase += wtot[kWarps + w];
+    }
+    const int exa = base + incl - (na + nb), cxa = cbase + cincl - (ca + cb);
+    if (ea < g.E) {
+      off[ea] = exa;
+      coff[ea] = cxa;
+    }
+    if (eb < g.E) {
+      off[eb] = exa + na;
+      coff[eb] = cxa + ca;
+    }
+    if (tid == 0) {
+      int t = 0;
+      for (int w = 0; w < kWarps; ++w) t += wtot[kWarps + w];
+      a.s.chunk_info[0] = t;
+    }
   }
   __syncthreads();
   for (int i = tid; i < npairs; i += kThreads) {
@@ -783,9 +783,107 @@ KK3_FN void route_all(const StepArgs& a, int layer, int moe_idx, unsigned char* 
       a.s.chunk_info[3 + ci * 3] = (n - q * 8) < 8 ? (n - q * 8) : 8;
     }
   }
-  (void)moe_idx;
+}
+
+KK3_FN void route_row(const StepArgs& a, int layer, int b, unsigned char* smem, int ph = -1) {
+  const Geo& g = a.g;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = g.K;
+  float* cval = reinterpret_cast<float*>(smem);                    // [kWarps][kMaxTopk]
+  int* cidx = reinterpret_cast<int*>(cval + kWarps * kMaxTopk);   // [kWarps][kMaxTopk]
+  __shared__ int s_last;
+  const float* sc = a.s.scores + (size_t)b * g.E;
+  const float* bias = lptr<float>(a, layer, KK3_MOE_ROUTER_BIAS);
+  const float kNaN = __int_as_float(0x7fc00000);
+  // this warp's experts: NaN scores count as -inf; missing or taken entries are NaN (never win)
+  const int e0 = warp * 64 + lane, e1 = e0 + 32;
+  float v0 = kNaN, v1 = kNaN;
+  if (e0 < g.E) {
+    const float x = __ldcg(sc + e0) + bias[e0];
+    v0 = x != x ? -INFINITY : x;
+  }
+  if (e1 < g.E) {
+    const float x = __ldcg(sc + e1) + bias[e1];
+    v1 = x != x ? -INFINITY : x;
+  }
+  for (int j = 0; j < K; ++j) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    if (route_better(v0, e0, bv, bi)) { bv = v0; bi = e0; }
+    if (route_better(v1, e1, bv, bi)) { bv = v1; bi = e1; }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (route_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    if (bi == e0) v0 = kNaN;
+    if (bi == e1) v1 = kNaN;
+    if (lane == 0) {
+      cval[warp * kMaxTopk + j] = bi == 0x7fffffff ? kNaN : bv;
+      cidx[warp * kMaxTopk + j] = bi;
+    }
+  }
+  __syncthreads();
+  if (b == 0 && tid == 0) sub_stamp(a, ph, 12);
+  if (warp == 0) {
+    // each warp's candidates are already in selection order: merge the kWarps sorted lists head to head;
+    // lane w < kWarps holds the head of list w, lane j < K keeps the j-th selected expert
+    int head = 0;
+    float hv = kNaN;
+    int hi = 0x7fffffff;
+    if (lane < kWarps) {
+      hv = cval[lane * kMaxTopk];
+      hi = cidx[lane * kMaxTopk];
+    }
+    int mine = -1;
+    for (int j = 0; j < K; ++j) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      if (route_better(hv, hi, bv, bi)) { bv = hv; bi = hi; }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (route_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+      }
+      if (lane == j) mine = bi;
+      if (lane < kWarps && hi == bi) {
+        ++head;
+        hv = head < K ? cval[lane * kMaxTopk + head] : kNaN;
+        hi = head < K ? cidx[lane * kMaxTopk + head] : 0x7fffffff;
+      }
+    }
+    // sort the K ids ascending: rank of each
+    int rank = 0;
+    for (int j = 0; j < K; ++j) {
+      const int other = __shfl_sync(0xffffffffu, mine, j);
+      if (lane < K && other < mine) ++rank;
+    }
+    const int safe = mine < 0 ? 0 : (mine >= g.E ? g.E - 1 : mine);
+    const float w = lane < K ? __ldcg(sc + safe) : 0.0f;
+    const float wsum = warp_sum(w);
+    if (lane < K) {
+      long long* out_ids = gout<long long>(a, KK3_OUT_EXPERT_IDS) + (size_t)layer * g.B * K;
+      a.s.route_ids[b * K + rank] = safe;
+      a.s.route_w[b * K + rank] = w / (wsum + 1e-20f);
+      out_ids[(size_t)b * K + rank] = (long long)safe;
+    }
+  }
+  // the last routing CTA to finish groups the pairs of every row
   __threadfence();
   __syncthreads();
+  if (tid == 0) s_last = atomicAdd(a.s.route_done, 1) == g.B - 1;
+  __syncthreads();
+  if (b == 0 && tid == 0) sub_stamp(a, ph, 13);
+  if (!s_last) return;
+  __threadfence();
+  if (tid == 0) sub_stamp(a, ph, 14);
+  route_group_pairs(a, smem);
+  if (tid == 0) sub_stamp(a, ph, 15);
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) atomicExch(a.s.route_done, 0);
 }
 
 }  // namespace kk3

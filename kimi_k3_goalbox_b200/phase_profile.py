@@ -171,6 +171,10 @@ def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[d
                                           "red1": (st[2] - base) / 1e3, "mix": (st[3] - base) / 1e3,
                                           "red2": (st[4] - base) / 1e3, "store": (st[5] - base) / 1e3,
                                           "done": (st[6] - base) / 1e3, "phase_end": (ts[i + 1] - base) / 1e3}
+        if name == "route" and st[12]:
+            subinfo[f"{name}:{layer}"] = {"cta0_candidates": (st[12] - base) / 1e3, "cta0_done": (st[13] - base) / 1e3,
+                                          "group_start": (st[14] - base) / 1e3, "group_end": (st[15] - base) / 1e3,
+                                          "phase_end": (ts[i + 1] - base) / 1e3}
         if name in ("kda_proj", "mla_proj", "moe_in") and st[8]:
             subinfo[f"{name}:{layer}"] = {"warp0_start": (st[8] - base) / 1e3, "first_data": (st[9] - base) / 1e3,
                                           "warp0_end": (st[10] - base) / 1e3, "units": st[11],
@@ -208,7 +212,7 @@ def main(argv=None) -> int:
         case = cases.variant(case, batch=args.batch)
     rows = profile(case, args.reps)
     subrow, head, rows = rows[0], rows[1:3], rows[3:]
-    for k, v in list(subrow["info"].items())[:6]:
+    for k, v in list(subrow["info"].items())[:9]:
         print("  sub-phase", k, {kk: (round(vv, 2) if isinstance(vv, float) else vv) for kk, vv in v.items()})
     total = sum(r["us"] for r in rows)
     print(f"{case['id']}: full step {head[0]['us']:.1f} us (events), empty launch {head[1]['us']:.1f} us, "

@@ -166,6 +166,19 @@ class StepContext:
             raise KK3Error(rc, "kk3_ipc_handle")
         return buf.raw
 
+    def exchange_bytes(self) -> int:
+        """Bytes of this rank's exchange buffer (flags + two parity regions)."""
+        return int(self.lib.kk3_exchange_bytes(self.handle))
+
+    def debug_set_peer(self, r: int, buf: torch.Tensor) -> None:
+        """Single-process testing aid: use a device tensor of exchange_bytes() bytes as rank r's buffer."""
+        if buf.numel() * buf.element_size() < self.exchange_bytes() or not buf.is_cuda:
+            raise ValueError("peer buffer must be a device tensor of at least exchange_bytes() bytes")
+        self._peer_keepalive = buf
+        rc = self.lib.kk3_debug_set_peer(self.handle, r, ctypes.c_void_p(buf.data_ptr()))
+        if rc != 0:
+            raise KK3Error(rc, "kk3_debug_set_peer")
+
     def open_peers(self, handles: list[bytes]) -> None:
         blob = b"".join(handles)
         rc = self.lib.kk3_open_peers(self.handle, blob)

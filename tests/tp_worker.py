@@ -1,0 +1,74 @@
+"""One rank of the tensor-parallel GPU parity test (launched by tests/test_gpu_tp.py through torchrun).
+
+Each rank builds the submission with the reference's execution context (rank, tp_rank, device, tp_group;
+megabench/harness/distributed.py:67-69), runs the step twice, and grades its outputs with the oracle's band
+rule against the BF16 and FP32 oracle computed with real all-reduces over the same process group
+(megabench/tasks/kimi.py:343-347). The second step must reproduce the first bit for bit: the in-kernel
+exchange alternates parity regions and sequence numbers between steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+from kimi_k3_goalbox_b200 import cases  # noqa: E402
+from kimi_k3_goalbox_b200.submission import build  # noqa: E402
+from oracle import kimi_oracle as ko  # noqa: E402
+from tests import gpu_helpers as gh  # noqa: E402
+
+
+def make_case(spec: dict) -> dict:
+    if spec["kind"] == "small":
+        return cases.variant(gh.small_case(spec["batch"]), tp=spec["tp"])
+    base = cases.get_case(spec["case"])
+    return cases.variant(base, **spec.get("params", {}))
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--spec", required=True, help="JSON case spec")
+    ap.add_argument("--seed", type=int, default=11)
+    args = ap.parse_args()
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    device = torch.device("cuda", rank)
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    case = make_case(json.loads(args.spec))
+    case["params"].pop("checkpoint", None)
+    assert case["tp"] == world, (case["tp"], world)
+    group = dist.group.WORLD
+    try:
+        with torch.inference_mode():
+            values = ko.make_inputs(case, args.seed, device, rank)
+            execution = {"rank": rank, "world_size": world, "tp_rank": rank, "ep_rank": 0, "backend": "nccl",
+                         "device": str(device), "tp_group": group, "ep_group": None}
+            run = build(dict(case, execution=execution))
+            first = {k: v.clone() for k, v in run(values).items()}
+            second = run(values)
+            torch.cuda.synchronize()
+            run.ctx.check()
+            expected = ko.reference(case, values, serial=False, tp_rank=rank, group=group)
+            details = ko.compare(case, values, expected, first, serial=False, tp_rank=rank, group=group)
+            for key, t in first.items():
+                assert torch.equal(t, second[key]), f"rank {rank}: second step differs in {key}"
+            run.close()
+        print(f"rank {rank} ok:", {k: (v.get("worst_ratio", v) if isinstance(v, dict) else v) for k, v in details.items()},
+              flush=True)
+    finally:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
