@@ -528,204 +528,248 @@ KK3_DEV void e2m1x8_cvt(unsigned w, unsigned (&r)[4]) {
 
 KK3_DEV unsigned lds32(const unsigned char* p) { return *reinterpret_cast<const unsigned*>(p); }
 
-struct ExpertCursor {
-  int chunk, tile, ks;
-};
-
-constexpr int kFp4Row = 48;                 // staged bytes per row and unit (32 used; 48 keeps LDS conflict-free)
-constexpr int kFp4Slot = 16 * kFp4Row;      // one matrix, one unit
 
 // Stream-K over (expert chunk, tile, k-step) units. Chunks come from the routing phase. A unit is a
-// 16-row tile x 64 k (two E2M1 groups). Each unit is staged into a per-warp cp.async ring: the 16 rows x 32
-// code bytes of every matrix (one 16-byte copy per lane and matrix) plus the FP16 activation pieces each lane
-// multiplies (lane-private). The E8M0 scales travel a register ring filled with the codes. Each quad reads
-// its rows' 4-byte code quarters, converts E2M1 -> FP16 in hardware and applies the scale per 32-wide group
-// to the FP32 accumulator.
+// 16-row tile x 64 k (two E2M1 groups of 32) of MT matrices. The per-warp cp.async ring carries only
+// weight bytes: the 16 x 32 code bytes of each matrix (row halves XOR-swizzled so the consumer's 4-byte
+// reads are bank-conflict free) and a 4-byte word of E8M0 scales per row (the aligned word holding this
+// unit's two groups). The FP16 activation pieces of the unit's (<= 8) pairs come from L2 into registers two
+// units ahead. Each quad converts its rows' E2M1 codes to FP16 in hardware (cvt.rn.f16x2.e2m1x2), runs
+// mma.sync per 32-wide group and applies the group scale to the FP32 partial. Everything the loop needs is
+// held in registers: nothing is reloaded from the argument block or the phase descriptor inside it.
+KK3_DEV void cp_async4_ca(void* smem_dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((unsigned)__cvta_generic_to_shared(smem_dst)),
+               "l"(src) : "memory");
+}
+
+KK3_DEV uint4 ld_cg16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
 template <int MT>
-KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
+KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* __restrict__ e8m0_lut) {
   extern __shared__ __align__(16) unsigned char kk3_dyn_smem[];
-  constexpr int kXOff = MT * kFp4Slot;                 // activation pieces after the code rows
-  constexpr int kSlot = kXOff + 2 * 32 * 16;
-  constexpr int S = kGemvSmemPerWarp / kSlot;
-  static_assert(S >= 2, "ring too shallow");
+  constexpr int kCode = 16 * 32;                  // code bytes per matrix and unit
+  constexpr int kScale = 16 * 4;                  // scale bytes per matrix and unit
+  constexpr int kSlot = MT * (kCode + kScale);
+  constexpr int S = (kGemvSmemPerWarp / kSlot) > 12 ? 12 : (kGemvSmemPerWarp / kSlot);
+  static_assert(S >= 3, "ring too shallow");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
+
+  // values of the unit loop live in registers; values used only when a tile or chunk changes are re-read
+  // from the descriptor there (once per ksteps units)
+  const int tiles = ph.tiles, ksteps = ph.ksteps;
   const int npk = a.g.B * a.g.K;
-  int nchunks = ld_volatile_int(a.s.chunk_info);
+  const bool trace = a.trace != 0;
+  int nchunks = __ldcg(a.s.chunk_info);
   nchunks = nchunks < 0 ? 0 : (nchunks > npk ? npk : nchunks);
-  const long long per_chunk = (long long)ph.tiles * ph.ksteps;
-  const long long U = (long long)nchunks * per_chunk;
+  const int per_chunk = tiles * ksteps;      // <= 512 tiles x 128 k-steps
+  const int U = nchunks * per_chunk;         // <= 2048 chunks: fits 32 bits
   if (U == 0) return;
-  long long GW = (long long)gridDim.x * kWarps;
+  int GW = gridDim.x * kWarps;
   GW = GW < U ? GW : U;
-  const long long gw = (long long)blockIdx.x * kWarps + warp;
+  const int gw = blockIdx.x * kWarps + warp;
   if (gw >= GW) return;
-  const long long ubeg = U * gw / GW, uend = U * (gw + 1) / GW;
+  const int ubeg = (int)((long long)U * gw / GW), uend = (int)((long long)U * (gw + 1) / GW);
+  const int nunits = uend - ubeg;
   unsigned char* ring = kk3_dyn_smem + (size_t)warp * kGemvSmemPerWarp;
-  float* part_base = a.s.fix_part;
-  const int rowbytes = ph.K / 2, sbytes = ph.K / 32;
+  if (trace) trace_warp(a, 1);
 
   // routing-table values are clamped so that a routing fault can never address outside the buffers
-  struct ChunkInfo {
-    int chunk, expert, first_pair, npairs;
-    const __half* xrow;   // activation row this lane multiplies (lane r < npairs), else null
+  auto chunk_expert = [&](int chunk) {
+    const int e = __ldcg(a.s.chunk_info + 1 + chunk * 3);
+    return e < 0 ? 0 : (e >= a.g.E ? a.g.E - 1 : e);
   };
-  auto load_chunk = [&](int chunk, ChunkInfo& ci) {
-    ci.chunk = chunk;
-    int e = a.s.chunk_info[1 + chunk * 3];
-    int fp = a.s.chunk_info[2 + chunk * 3];
-    int np = a.s.chunk_info[3 + chunk * 3];
-    ci.expert = e < 0 ? 0 : (e >= a.g.E ? a.g.E - 1 : e);
+  auto chunk_pairs = [&](int chunk, int& fp, int& np) {
+    fp = __ldcg(a.s.chunk_info + 2 + chunk * 3);
+    np = __ldcg(a.s.chunk_info + 3 + chunk * 3);
     fp = fp < 0 ? 0 : (fp >= npk ? npk - 1 : fp);
     np = np < 0 ? 0 : (np > 8 ? 8 : np);
     np = fp + np > npk ? npk - fp : np;
-    ci.first_pair = fp;
-    ci.npairs = np;
-    ci.xrow = nullptr;
-    if (r < np) {
-      const int p = fp + r;
-      int prow = a.s.pair_row[p];
+  };
+  // this lane's activation row for a chunk (pair r), or null when the chunk has fewer pairs
+  auto chunk_xrow = [&](int chunk) -> const __half* {
+    int fp, np;
+    chunk_pairs(chunk, fp, np);
+    if (r >= np) return nullptr;
+    const int p = fp + r;
+    if (MT == 2) {
+      int prow = __ldcg(a.s.pair_row + p);
       prow = prow < 0 ? 0 : (prow >= a.g.B ? a.g.B - 1 : prow);
-      ci.xrow = (MT == 2) ? a.s.latent_p + (size_t)prow * a.g.lh : a.s.act_p + (size_t)p * a.g.inter;
+      return a.s.latent_p + (size_t)prow * a.g.lh;
     }
-  };
-  auto at = [&](long long u) {
-    ExpertCursor q;
-    q.chunk = (int)(u / per_chunk);
-    const long long local = u - (long long)q.chunk * per_chunk;
-    q.tile = (int)(local / ph.ksteps);
-    q.ks = (int)(local % ph.ksteps);
-    return q;
-  };
-  auto step = [&](ExpertCursor& q) {
-    if (++q.ks == ph.ksteps) {
-      q.ks = 0;
-      if (++q.tile == ph.tiles) {
-        q.tile = 0;
-        ++q.chunk;
-      }
-    }
-  };
-  const int srow = lane >> 1, shalf = lane & 1;
-  auto issue = [&](const ExpertCursor& q, const ChunkInfo& ci, unsigned char* slot) {
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      const uint8_t* src = ph.codes[mt] + (size_t)ci.expert * ph.expert_codes +
-                           (size_t)(q.tile * 16 + srow) * rowbytes + q.ks * 32 + shalf * 16;
-      cp_async16_g(slot + mt * kFp4Slot + srow * kFp4Row + shalf * 16, src);
-    }
-    if (ci.xrow) {
-      cp_async16_g(slot + kXOff + lane * 16, ci.xrow + q.ks * 64 + 8 * c);
-      cp_async16_g(slot + kXOff + 512 + lane * 16, ci.xrow + q.ks * 64 + 32 + 8 * c);
-    }
-  };
-  // E8M0 scales of rows r, r+8 for a unit's two groups, packed as (row r+8 << 16 | row r) per matrix; loaded by
-  // the producer when it stages the unit and shifted through a register ring, so they arrive with the codes
-  auto load_scales = [&](const ExpertCursor& q, const ChunkInfo& ci, unsigned (&sc)[MT]) {
-    const int rowa = q.tile * 16 + r;
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      const uint8_t* sbase = ph.scales[mt] + (size_t)ci.expert * ph.expert_scales + q.ks * 2;
-      const unsigned lo = ldg_nc16(sbase + (size_t)rowa * sbytes);
-      const unsigned hi = ldg_nc16(sbase + (size_t)(rowa + 8) * sbytes);
-      sc[mt] = lo | (hi << 16);
-    }
+    return a.s.act_p + (size_t)p * a.g.inter;
   };
 
-  ExpertCursor pc = at(ubeg), cc = pc;
-  ChunkInfo pci, cci;
-  load_chunk(pc.chunk, pci);
-  cci = pci;
-  long long pu = ubeg;
-  unsigned sring[S][MT];   // scales of the units in the ring, oldest first (compile-time indices only)
+  const int c0 = ubeg / per_chunk;
+  const int rem0 = ubeg - c0 * per_chunk;
+
+  // ---- producer (weights into the ring, S - 1 units ahead); per-lane slot offsets are fixed
+  int p_chunk = c0, p_tile = rem0 / ksteps, p_ks = rem0 % ksteps;
+  const int srow = lane >> 1;
+  const int p_dst_code = srow * 32 + (((lane & 1) ^ ((srow >> 2) & 1)) * 16);   // swizzled half of the row
+  const int scl_mt = lane >> 4, scl_row = lane & 15;                             // scale row this lane stages
+  const bool scl_lane = scl_mt < MT;
+  const int p_dst_scl = MT * kCode + scl_mt * kScale + scl_row * 4;
+  const uint8_t* p_code[MT];   // this lane's 16 code bytes of the current unit, per matrix
+  const uint8_t* p_scl = ph.scales[0];   // this lane's scale row (word of the current unit pair)
+  auto p_setup = [&]() {
+    const size_t e = (size_t)chunk_expert(p_chunk);
+    const int rowbytes = ph.K / 2, sbytes = ph.K / 32;
 #pragma unroll
-  for (int i = 0; i < S; ++i)
+    for (int mt = 0; mt < MT; ++mt)
+      p_code[mt] = ph.codes[mt] + e * ph.expert_codes + (size_t)(p_tile * 16 + srow) * rowbytes + (lane & 1) * 16 +
+                   p_ks * 32;
+    if (scl_lane)
+      p_scl = ph.scales[scl_mt] + e * ph.expert_scales + (size_t)(p_tile * 16 + scl_row) * sbytes + (p_ks >> 1) * 4;
+  };
+  int p_left = nunits, p_slot = 0;
+  auto p_issue = [&]() {
+    unsigned char* slot = ring + p_slot * kSlot;
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt) sring[i][mt] = 0x7f7f7f7fu;
-#pragma unroll
-  for (int i = 0; i < S - 1; ++i) {
-    if (pu < uend) {
-      if (pc.chunk != pci.chunk) load_chunk(pc.chunk, pci);
-      issue(pc, pci, ring + (int)((pu - ubeg) % S) * kSlot);
-      load_scales(pc, pci, sring[i]);
-      step(pc);
-      ++pu;
+    for (int mt = 0; mt < MT; ++mt) {
+      cp_async16_g(slot + mt * kCode + p_dst_code, p_code[mt]);
+      p_code[mt] += 32;
     }
+    if (scl_lane) cp_async4_ca(slot + p_dst_scl, p_scl);
+    p_scl += (p_ks & 1) * 4;
+    p_slot = p_slot + 1 == S ? 0 : p_slot + 1;
+    --p_left;
+    if (++p_ks == ksteps) {
+      p_ks = 0;
+      if (++p_tile == tiles) {
+        p_tile = 0;
+        ++p_chunk;
+      }
+      if (p_left > 0) p_setup();
+    }
+  };
+  p_setup();
+#pragma unroll 1
+  for (int i = 0; i < S - 1; ++i) {
+    if (p_left > 0) p_issue();
     cp_async_commit_g();
   }
+
+  // ---- activations (registers, two units ahead)
+  int x_chunk = c0, x_ks = rem0 % ksteps, x_tile = rem0 / ksteps;
+  const __half* xrow = chunk_xrow(x_chunk);
+  const __half* xp = xrow ? xrow + x_ks * 64 + 8 * c : nullptr;
+  uint4 X[2][2];
+  auto x_load = [&](uint4 (&dst)[2]) {
+    dst[0] = make_uint4(0, 0, 0, 0);
+    dst[1] = make_uint4(0, 0, 0, 0);
+    if (xp) {
+      dst[0] = ld_cg16(xp);
+      dst[1] = ld_cg16(xp + 32);
+      xp += 64;
+    }
+    if (++x_ks == ksteps) {
+      x_ks = 0;
+      if (++x_tile == tiles) {
+        x_tile = 0;
+        ++x_chunk;
+        xrow = x_chunk < nchunks ? chunk_xrow(x_chunk) : nullptr;
+      }
+      xp = xrow ? xrow + 8 * c : nullptr;
+    }
+  };
+  x_load(X[0]);
+  if (trace) trace_warp(a, 4);
+
+  // ---- consumer; per-lane read offsets inside a slot are fixed
+  int c_chunk = c0, c_tile = rem0 / ksteps, c_ks = rem0 % ksteps;
+  int c_fp = 0, c_np = 0;
+  chunk_pairs(c_chunk, c_fp, c_np);
+  int c_slot = 0;
+  const int rsw = ((r >> 2) & 1) * 16;                                   // swizzle of rows r and r + 8
+  const int c_off0 = r * 32 + (0 ^ rsw) + 4 * c, c_off1 = r * 32 + (16 ^ rsw) + 4 * c;
+  const int c_scl = MT * kCode + r * 4;
   float acc[MT][1][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[mt][0][i] = 0.0f;
-  long long seg_start = ubeg;
-  for (long long u = ubeg; u < uend; ++u) {
-    __syncwarp();   // every lane is done with the slot the next issue overwrites
-    if (pu < uend) {
-      if (pc.chunk != pci.chunk) load_chunk(pc.chunk, pci);
-      issue(pc, pci, ring + (int)((pu - ubeg) % S) * kSlot);
-      load_scales(pc, pci, sring[S - 1]);
-      step(pc);
-      ++pu;
-    }
-    cp_async_commit_g();
-    cp_async_wait_g<S - 1>();
-    __syncwarp();
-    unsigned sa[MT], sb[MT];
+  for (int n0 = 0; n0 < nunits; n0 += 2) {
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      sa[mt] = sring[0][mt] & 0xffffu;
-      sb[mt] = sring[0][mt] >> 16;
-    }
+    for (int j = 0; j < 2; ++j) {
+      const int n = n0 + j;
+      if (n >= nunits) break;
+      __syncwarp();   // every lane is done with the slot the next issue overwrites
+      if (p_left > 0) p_issue();
+      cp_async_commit_g();
+      if (n + 1 < nunits) x_load(X[j ^ 1]);
+      cp_async_wait_g<S - 1>();
+      __syncwarp();
+      if (trace && n < 2) trace_warp(a, 5 | (n << 8));
+      const unsigned char* slot = ring + c_slot * kSlot;
+      c_slot = c_slot + 1 == S ? 0 : c_slot + 1;
+      const int pos = (c_ks & 1) << 4;   // bit offset of this unit's two scale bytes in a row's word
+      unsigned swa[MT], swb[MT], wa[MT][2], wb[MT][2];
 #pragma unroll
-    for (int i = 0; i + 1 < S; ++i)
+      for (int mt = 0; mt < MT; ++mt) {
+        swa[mt] = *reinterpret_cast<const unsigned*>(slot + c_scl + mt * kScale) >> pos;
+        swb[mt] = *reinterpret_cast<const unsigned*>(slot + c_scl + mt * kScale + 32) >> pos;
+        wa[mt][0] = lds32(slot + mt * kCode + c_off0);
+        wa[mt][1] = lds32(slot + mt * kCode + c_off1);
+        wb[mt][0] = lds32(slot + mt * kCode + c_off0 + 256);
+        wb[mt][1] = lds32(slot + mt * kCode + c_off1 + 256);
+      }
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) sring[i][mt] = sring[i + 1][mt];
-    const unsigned char* slot = ring + (int)((u - ubeg) % S) * kSlot;
-    uint4 X[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-    if (cci.xrow) {
-      X[0] = *reinterpret_cast<const uint4*>(slot + kXOff + lane * 16);
-      X[1] = *reinterpret_cast<const uint4*>(slot + kXOff + 512 + lane * 16);
-    }
+      for (int mt = 0; mt < MT; ++mt) {
+        // both groups' conversions first, then their MMAs interleaved so each dependent pair has an
+        // independent MMA between its halves
+        unsigned ra[2][4], rb[2][4];
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
+        for (int g = 0; g < 2; ++g) {
+          e2m1x8_cvt(wa[mt][g], ra[g]);
+          e2m1x8_cvt(wb[mt][g], rb[g]);
+        }
+        float t[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+        mma_f16(t[0], ra[0][0], rb[0][0], ra[0][1], rb[0][1], X[j][0].x, X[j][0].y);
+        mma_f16(t[1], ra[1][0], rb[1][0], ra[1][1], rb[1][1], X[j][1].x, X[j][1].y);
+        mma_f16(t[0], ra[0][2], rb[0][2], ra[0][3], rb[0][3], X[j][0].z, X[j][0].w);
+        mma_f16(t[1], ra[1][2], rb[1][2], ra[1][3], rb[1][3], X[j][1].z, X[j][1].w);
 #pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        const unsigned wa = lds32(slot + mt * kFp4Slot + r * kFp4Row + g * 16 + 4 * c);
-        const unsigned wb = lds32(slot + mt * kFp4Slot + (r + 8) * kFp4Row + g * 16 + 4 * c);
-        unsigned ra[4], rb[4];
-        e2m1x8_cvt(wa, ra);
-        e2m1x8_cvt(wb, rb);
-        float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        mma_f16(t, ra[0], rb[0], ra[1], rb[1], X[g].x, X[g].y);
-        mma_f16(t, ra[2], rb[2], ra[3], rb[3], X[g].z, X[g].w);
-        const float fa = e8m0_to_f32((sa[mt] >> (8 * g)) & 0xffu);
-        const float fb = e8m0_to_f32((sb[mt] >> (8 * g)) & 0xffu);
-        acc[mt][0][0] = fmaf(t[0], fa, acc[mt][0][0]);
-        acc[mt][0][1] = fmaf(t[1], fa, acc[mt][0][1]);
-        acc[mt][0][2] = fmaf(t[2], fb, acc[mt][0][2]);
-        acc[mt][0][3] = fmaf(t[3], fb, acc[mt][0][3]);
+        for (int g = 0; g < 2; ++g) {
+          // 2^(s - 127) from a 256-entry table (s = 0 and s = 255 exactly as the reference decodes them)
+          const float fa = e8m0_lut[(swa[mt] >> (8 * g)) & 0xffu];
+          const float fb = e8m0_lut[(swb[mt] >> (8 * g)) & 0xffu];
+          acc[mt][0][0] = fmaf(t[g][0], fa, acc[mt][0][0]);
+          acc[mt][0][1] = fmaf(t[g][1], fa, acc[mt][0][1]);
+          acc[mt][0][2] = fmaf(t[g][2], fb, acc[mt][0][2]);
+          acc[mt][0][3] = fmaf(t[g][3], fb, acc[mt][0][3]);
+        }
+      }
+      if (c_ks == ksteps - 1 || n == nunits - 1) {
+        const int tile_beg = c_chunk * per_chunk + c_tile * ksteps;
+        const bool inside = tile_beg >= ubeg && tile_beg + ksteps <= uend;   // the whole tile is this warp's
+        const long long first = inside ? gw : owner_of(tile_beg, U, GW);
+        const long long lastw = inside ? gw : owner_of(tile_beg + ksteps - 1, U, GW);
+        bool done = first == lastw;
+        if (!done)
+          done = stream_k_fixup<1, MT>(a, a.s.fix_part, a.s.fix_cnt + c_chunk * tiles + c_tile, gw,
+                                       tile_beg <= ubeg, tile_beg, first, lastw, U, GW, acc);
+        if (done) expert_epilogue<MT>(a, ph.rows, c_fp, c_np, c_tile, acc);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[mt][0][i] = 0.0f;
+      }
+      if (++c_ks == ksteps) {
+        c_ks = 0;
+        if (++c_tile == tiles) {
+          c_tile = 0;
+          ++c_chunk;
+          if (n + 1 < nunits) chunk_pairs(c_chunk, c_fp, c_np);
+        }
       }
     }
-    if (cc.ks == ph.ksteps - 1 || u == uend - 1) {
-      const long long tile_beg = (long long)cc.chunk * per_chunk + (long long)cc.tile * ph.ksteps;
-      const bool inside = tile_beg >= ubeg && tile_beg + ph.ksteps <= uend;   // the whole tile is this warp's
-      const long long first = inside ? gw : owner_of(tile_beg, U, GW);
-      const long long lastw = inside ? gw : owner_of(tile_beg + ph.ksteps - 1, U, GW);
-      bool done = first == lastw;
-      if (!done)
-        done = stream_k_fixup<1, MT>(a, part_base, a.s.fix_cnt + cc.chunk * ph.tiles + cc.tile, gw, seg_start == ubeg,
-                                     tile_beg, first, lastw, U, GW, acc);
-      if (done) expert_epilogue<MT>(a, ph.rows, cci.first_pair, cci.npairs, cc.tile, acc);
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[mt][0][i] = 0.0f;
-      seg_start = u + 1;
-    }
-    step(cc);
-    if (u + 1 < uend && cc.chunk != cci.chunk) load_chunk(cc.chunk, cci);
   }
   cp_async_wait_g<0>();
+  if (trace) trace_warp(a, 11);
 }
 
 }  // namespace kk3

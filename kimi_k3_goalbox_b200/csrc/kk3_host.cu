@@ -108,7 +108,9 @@ static int validate(const kk3_config* c) {
       c->dense_inter_shard % 64 == 0 && c->shared_inter_shard % 64 == 0 && c->vocab_shard >= 1 &&
       c->context >= 1 && c->attn_res_block_size >= 1 && c->first_dense >= 0 &&
       (c->layers + c->attn_res_block_size - 1) / c->attn_res_block_size <= kMaxBlocks - 1 &&
-      (long long)c->heads * 128 % 64 == 0 && (long long)c->vocab_shard * c->batch < (1ll << 31);
+      (long long)c->heads * 128 % 64 == 0 && (long long)c->vocab_shard * c->batch < (1ll << 31) &&
+      // MoE layers: the expert engine stages each row's scales for two 64-k steps as one aligned 4-byte word
+      (c->layers <= c->first_dense || (c->latent_hidden % 128 == 0 && c->inter_shard % 128 == 0));
   return ok ? KK3_OK : KK3_ERR_UNSUPPORTED;
 }
 

@@ -392,7 +392,10 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   __shared__ GemvJob sj[kMaxJobs];
   __shared__ GemvJob sj2[2];
   __shared__ ExpertPhase sph;
+  __shared__ float e8m0_lut[256];   // E8M0 scale byte -> FP32 factor, read by the MXFP4 expert engine
   __shared__ int sjn;
+  for (int i = threadIdx.x; i < 256; i += kThreads) e8m0_lut[i] = e8m0_to_f32((unsigned)i);
+  __syncthreads();
   const Geo& g = a.g;
   float* fsm = reinterpret_cast<float*>(smem);
   int phase = 0;
@@ -557,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
           sph.rows = g.inter; sph.K = g.lh; sph.tiles = g.inter / 16; sph.ksteps = g.lh / 64;
           sph.expert_codes = (long long)g.inter * g.lh / 2; sph.expert_scales = (long long)g.inter * g.lh / 32;
         });
-        run_experts<2>(a, sph);
+        run_experts<2>(a, sph, e8m0_lut);
       }
       KK3_PHASE_END();
       if (KK3_RUN) {
@@ -567,7 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
           sph.rows = g.lh; sph.K = g.inter; sph.tiles = g.lh / 16; sph.ksteps = g.inter / 64;
           sph.expert_codes = (long long)g.lh * g.inter / 2; sph.expert_scales = (long long)g.lh * g.inter / 32;
         });
-        run_experts<1>(a, sph);
+        run_experts<1>(a, sph, e8m0_lut);
       }
       KK3_PHASE_END();
       if (KK3_RUN && !phase_moe_combine(a, l, seq0 + x_moe, x_moe & 1, fsm)) return;

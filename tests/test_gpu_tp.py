@@ -57,7 +57,7 @@ def test_tp2_band_two_gpus(spec):
 @pytest.mark.gpu
 def test_exchange_wait_times_out():
     torch.cuda.set_device(0)
-    case = cases.variant(gh.small_case(2), tp=2)
+    case = cases.variant(gh.small_case(2, intermediate=256), tp=2)
     with torch.inference_mode():
         values = ko.make_inputs(case, 3, "cuda:0", 0)
         ctx = runtime.StepContext(case, rank=0, device=0, timeout_ns=50_000_000)

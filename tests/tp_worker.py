@@ -30,7 +30,8 @@ from tests import gpu_helpers as gh  # noqa: E402
 
 def make_case(spec: dict) -> dict:
     if spec["kind"] == "small":
-        return cases.variant(gh.small_case(spec["batch"]), tp=spec["tp"])
+        # expert intermediate 256: 128 rows per rank (the expert engine needs shards of 128)
+        return cases.variant(gh.small_case(spec["batch"], intermediate=128 * spec["tp"]), tp=spec["tp"])
     base = cases.get_case(spec["case"])
     return cases.variant(base, **spec.get("params", {}))
 
