@@ -83,6 +83,8 @@ struct Scratch {
   int* fix_cnt;       // [max tiles] stream-K arrival counters
   unsigned long long* argmax_key; // [B]
   int* route_done;    // routing CTAs finished in this layer (the last one groups the pairs; it resets the count)
+  float* situ_buf;    // [2 halves][tiles][32 lanes][4 * NT] bf16-rounded gate / up tiles of a situ pair
+  int* situ_cnt;      // [tiles] halves of a situ pair published (the second resets it)
   unsigned* bar;      // grid barrier word (see grid_sync)
   int* err;           // device error word, polled by every wait (device memory: cheap to poll)
   int* err_host;      // host-visible copy in mapped host memory, written only when an error is raised

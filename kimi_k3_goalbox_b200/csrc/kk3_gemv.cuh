@@ -28,6 +28,8 @@ enum Epi : int {
   EPI_STORE_BF16 = 0,   // out bf16 [col, ldo]
   EPI_SIGMOID_F32,      // out f32 [col, ldo] = sigmoid(acc)         (router scores, kimi.py:308)
   EPI_SITU,             // dual job: out bf16 = situ(bf16 gate, bf16 up) (kimi.py:194-196, :304, :326)
+  EPI_SITU_GATE,        // single-matrix halves of a situ pair: gate and up tiles are separate jobs of one pass;
+  EPI_SITU_UP,          // each publishes its tile, the second to finish a tile forms situ (kimi.py:194-196)
   EPI_LATENT,           // out bf16 [col, ldo] and out2 an FP16 copy for the MXFP4 path
   EPI_LOGITS,           // out f32 [col, ldo] = bf16-rounded logits, argmax keys (kimi.py:331, :218-227)
   EPI_ROUTED,           // prefix[col, row] += bf16(bf16(acc) + shared_red[col, row]) (kimi.py:325-329)
@@ -46,7 +48,7 @@ struct GemvJob {
   long long aux_off;    // epilogue extra (exchange sub-region offset, vocab offset, ...)
 };
 
-constexpr int kMaxJobs = 8;
+constexpr int kMaxJobs = 8;   // jobs of one GEMV pass (the MoE input pass has four)
 
 KK3_DEV long long owner_of(long long u, long long U, long long GW) { return ((u + 1) * GW - 1) / U; }
 
@@ -155,6 +157,41 @@ KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const 
           atomicMax(reinterpret_cast<unsigned long long*>(const_cast<void*>(j.aux)) + col, best);
       }
     }
+    return;
+  }
+  if (j.epi == EPI_SITU_GATE || j.epi == EPI_SITU_UP) {
+    // publish this half's bf16-rounded tile (lane-major: each lane's 4*NT values contiguous), then count the
+    // halves of the tile; the second half to arrive forms situ(gate, up) from the same lane positions
+    const int half = j.epi == EPI_SITU_UP ? 1 : 0;
+    float* buf = reinterpret_cast<float*>(const_cast<void*>(j.aux));
+    const size_t tile_floats = (size_t)32 * 4 * NT;
+    float* mine = buf + ((size_t)half * j.tiles + tile) * tile_floats + (size_t)lane * 4 * NT;
+    const float* other = buf + ((size_t)(1 - half) * j.tiles + tile) * tile_floats + (size_t)lane * 4 * NT;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+      *reinterpret_cast<float4*>(mine + nt * 4) =
+          make_float4(round_bf(acc[0][nt][0]), round_bf(acc[0][nt][1]), round_bf(acc[0][nt][2]), round_bf(acc[0][nt][3]));
+    __threadfence();
+    __syncwarp();
+    int* cnt = reinterpret_cast<int*>(j.out2) + tile;
+    int old = 0;
+    if (lane == 0) old = atomicAdd(cnt, 1);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old != 1) return;
+    __threadfence();
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = row0 + r + 8 * (i >> 1);
+        const int col = nt * 8 + 2 * c + (i & 1);
+        if (row >= j.rows || col >= j.ncols) continue;
+        const float mv = round_bf(acc[0][nt][i]), ov = ld_cg_f32(other + nt * 4 + i);
+        const float g = half ? ov : mv, u = half ? mv : ov;
+        reinterpret_cast<bf16*>(j.out)[(size_t)col * j.ldo + row] = f2bf(situ_f(g, u));
+      }
+    }
+    if (lane == 0) atomicExch(cnt, 0);
     return;
   }
 #pragma unroll

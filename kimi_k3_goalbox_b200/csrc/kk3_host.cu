@@ -161,9 +161,8 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
     mx((long long)(g.qr + g.kr + g.rd + g.hr * g.vd) / 16 + 3);
     mx((long long)g.hr * (g.nr + g.rd) / 16 + 1);
     mx(g.h / 16 + 1);
-    mx((long long)(g.dinter + 15) / 16 + 1);
-    mx((long long)(g.E + g.lh + 30) / 16 + 2);
-    mx((long long)(g.sinter + 15) / 16 + 1);
+    mx(2ll * ((g.dinter + 15) / 16) + 2);                                        // dense gate | up
+    mx((long long)(g.E + 15) / 16 + (g.lh + 15) / 16 + 2ll * ((g.sinter + 15) / 16) + 4);   // MoE input pass
     mx((long long)(g.V + 15) / 16 + 1);
     t = (long long)g.B * g.K * ((g.inter > g.lh ? g.inter : g.lh) / 16);
     mx(t);
@@ -174,6 +173,9 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   const size_t B = g.B;
   size_t qkv_w = (size_t)3 * g.qdim > (size_t)(g.qr + g.kr + g.rd) ? (size_t)3 * g.qdim : (size_t)(g.qr + g.kr + g.rd);
   Scratch& s = x->s;
+  // situ pairs: tiles of the larger of the dense and shared-expert intermediates, 4 * NT floats per lane
+  const size_t situ_tiles = (size_t)((g.dinter > g.sinter ? g.dinter : g.sinter) + 15) / 16 + 1;
+  const size_t situ_floats = 2 * situ_tiles * 32 * 4 * (size_t)x->nt;
   unsigned* bar = nullptr;
   int* phase_count = nullptr;
   Item items[] = {
@@ -191,8 +193,9 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
       {(void**)&s.out_slot, B * g.K * (size_t)g.lh * 2}, {(void**)&s.x3, B * g.lh * 2},
       {(void**)&s.shared_red, B * g.h * 2}, {(void**)&s.expert_sum, B * g.lh * 4},
       {(void**)&s.fix_part, (size_t)g.fix_bank * 2 * 4}, {(void**)&s.fix_cnt, (size_t)g.cnt_bank * 2 * 4},
+      {(void**)&s.situ_buf, situ_floats * 4},
       {(void**)&s.argmax_key, B * 8}, {(void**)&bar, 64}, {(void**)&phase_count, 64}, {(void**)&s.err, 64},
-      {(void**)&s.route_done, 64},
+      {(void**)&s.route_done, 64}, {(void**)&s.situ_cnt, situ_tiles * 4},
       {(void**)&s.phase_ts, (kMaxPhases + 1) * 8}, {(void**)&s.arrive_ts, (size_t)kArrivePhases * 1024 * 8},
       {(void**)&s.sub_ts, (size_t)kArrivePhases * 16 * 8},
   };
@@ -505,9 +508,8 @@ static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, Ste
     mx((long long)(g.qr + g.kr + g.rd + g.hr * g.vd) / 16 + 3);
     mx((long long)g.hr * (g.nr + g.rd) / 16 + 1);
     mx(g.h / 16 + 1);
-    mx((long long)(g.dinter + 15) / 16 + 1);
-    mx((long long)(g.E + g.lh + 30) / 16 + 2);
-    mx((long long)(g.sinter + 15) / 16 + 1);
+    mx(2ll * ((g.dinter + 15) / 16) + 2);                                        // dense gate | up
+    mx((long long)(g.E + 15) / 16 + (g.lh + 15) / 16 + 2ll * ((g.sinter + 15) / 16) + 4);   // MoE input pass
     mx((long long)(g.V + 15) / 16 + 1);
     mx((long long)g.B * g.K * ((g.inter > g.lh ? g.inter : g.lh) / 16));
     g.cnt_bank = (int)tiles;
@@ -517,6 +519,8 @@ static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, Ste
       (size_t)3 * g.qdim > (size_t)(g.qr + g.kr + g.rd) ? (size_t)3 * g.qdim : (size_t)(g.qr + g.kr + g.rd);
   Scratch& s = a->s;
   memset(&s, 0, sizeof(s));
+  const size_t situ_tiles = (size_t)((g.dinter > g.sinter ? g.dinter : g.sinter) + 15) / 16 + 1;
+  const size_t situ_floats = 2 * situ_tiles * 32 * 4 * (size_t)*nt;
   Comm& c = a->comm;
   memset(&c, 0, sizeof(c));
   // exchange buffer of a single rank: flags [B][1] u32, then two parity regions {att, exp, shd, key}
@@ -539,10 +543,10 @@ static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, Ste
   struct Item { void** p; size_t bytes; };
   Item items[] = {
       // must be zero when a step begins: barrier word, phase count, error word and its mirror, routing
-      // counter, stream-K tile counters, exchange flags (the exchange buffer's flag array comes first; its data regions
-      // after it are written before they are read)
+      // counter, situ pair counters, stream-K tile counters, exchange flags (the exchange buffer's flag
+      // array comes first; its data regions after it are written before they are read)
       {(void**)&s.bar, 64}, {(void**)&s.phase_count, 64}, {(void**)&s.err, 64}, {(void**)&err_mirror, 64},
-      {(void**)&s.route_done, 64},
+      {(void**)&s.route_done, 64}, {(void**)&s.situ_cnt, situ_tiles * 4},
       {(void**)&s.fix_cnt, (size_t)g.cnt_bank * 2 * 4}, {(void**)&comm, comm_bytes},
       // written before they are read within every step
       {(void**)&s.prefix, B * g.h * 2}, {(void**)&s.blocks, (size_t)g.nblk * B * g.h * 2},
@@ -559,6 +563,7 @@ static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, Ste
       {(void**)&s.out_slot, B * g.K * (size_t)g.lh * 2}, {(void**)&s.x3, B * g.lh * 2},
       {(void**)&s.shared_red, B * g.h * 2}, {(void**)&s.expert_sum, B * g.lh * 4},
       {(void**)&s.fix_part, (size_t)g.fix_bank * 2 * 4}, {(void**)&s.argmax_key, B * 8},
+      {(void**)&s.situ_buf, situ_floats * 4},
       {(void**)&s.phase_ts, (kMaxPhases + 1) * 8}, {(void**)&s.sub_ts, (size_t)kArrivePhases * 16 * 8},
   };
   size_t off = 0;

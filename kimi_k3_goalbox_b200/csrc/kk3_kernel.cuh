@@ -347,24 +347,32 @@ KK3_DEV void o_job(const StepArgs& a, int l, GemvJob& j) {
   prepare_jobs(&j, 1);
 }
 
-// MLP input: dense gate/up (kimi.py:304), or router + latent down (pass 0) and shared gate/up (pass 1) (:308, :317, :326)
-KK3_DEV int mlp_in_jobs(const StepArgs& a, int l, GemvJob* j0, GemvJob& j1) {
+KK3_DEV void situ_pair(const StepArgs& a, GemvJob* jobs, const bf16* gate, const bf16* up, int rows, bf16* out) {
+  const Geo& g = a.g;
+  job_init(jobs[0], gate, rows, g.h, a.s.xm, g.h, g.B, EPI_SITU_GATE, out, rows);
+  job_init(jobs[1], up, rows, g.h, a.s.xm, g.h, g.B, EPI_SITU_UP, out, rows);
+  for (int i = 0; i < 2; ++i) {
+    jobs[i].aux = a.s.situ_buf;
+    jobs[i].out2 = a.s.situ_cnt;
+  }
+}
+
+// MLP input in one pass of single-matrix jobs: dense gate and up (kimi.py:304), or router, latent down and the
+// shared expert's gate and up (:308, :317, :326); gate/up tiles meet in the situ epilogue
+KK3_DEV int mlp_in_jobs(const StepArgs& a, int l, GemvJob* jobs) {
   const Geo& g = a.g;
   if (l < g.first_dense) {
-    job_init(j1, lptr<bf16>(a, l, KK3_DENSE_GATE), g.dinter, g.h, a.s.xm, g.h, g.B, EPI_SITU, a.s.dense_act, g.dinter);
-    j1.w2 = lptr<bf16>(a, l, KK3_DENSE_UP);
-    prepare_jobs(&j1, 1);
-    return 0;
+    situ_pair(a, jobs, lptr<bf16>(a, l, KK3_DENSE_GATE), lptr<bf16>(a, l, KK3_DENSE_UP), g.dinter, a.s.dense_act);
+    prepare_jobs(jobs, 2);
+    return 2;
   }
-  job_init(j0[0], lptr<bf16>(a, l, KK3_MOE_ROUTER), g.E, g.h, a.s.xm, g.h, g.B, EPI_SIGMOID_F32, a.s.scores, g.E);
-  job_init(j0[1], lptr<bf16>(a, l, KK3_MOE_LATENT_DOWN), g.lh, g.h, a.s.xm, g.h, g.B, EPI_LATENT, a.s.latent, g.lh);
-  j0[1].out2 = a.s.latent_p;
-  prepare_jobs(j0, 2);
-  job_init(j1, lptr<bf16>(a, l, KK3_MOE_SHARED_GATE), g.sinter, g.h, a.s.xm, g.h, g.B, EPI_SITU, a.s.shared_act,
-           g.sinter);
-  j1.w2 = lptr<bf16>(a, l, KK3_MOE_SHARED_UP);
-  prepare_jobs(&j1, 1);
-  return 2;
+  job_init(jobs[0], lptr<bf16>(a, l, KK3_MOE_ROUTER), g.E, g.h, a.s.xm, g.h, g.B, EPI_SIGMOID_F32, a.s.scores, g.E);
+  job_init(jobs[1], lptr<bf16>(a, l, KK3_MOE_LATENT_DOWN), g.lh, g.h, a.s.xm, g.h, g.B, EPI_LATENT, a.s.latent, g.lh);
+  jobs[1].out2 = a.s.latent_p;
+  situ_pair(a, jobs + 2, lptr<bf16>(a, l, KK3_MOE_SHARED_GATE), lptr<bf16>(a, l, KK3_MOE_SHARED_UP), g.sinter,
+            a.s.shared_act);
+  prepare_jobs(jobs, 4);
+  return 4;
 }
 
 KK3_DEV void latent_up_job(const StepArgs& a, int l, GemvJob& j) {
@@ -506,8 +514,8 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
     if (l < g.first_dense) {
       // dense FFN (kimi.py:304)
       if (KK3_RUN) {
-        KK3_BUILD(mlp_in_jobs(a, l, sj, sj2[0]));
-        run_gemv<NT, 2>(a, sj2, 1, 0, gridDim.x, 0);
+        KK3_BUILD(sjn = mlp_in_jobs(a, l, sj));
+        run_gemv<NT, 1>(a, sj, sjn, 0, gridDim.x, 0);
       }
       KK3_PHASE_END();
       if (KK3_RUN) {
@@ -525,11 +533,10 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
       pend_x = xi++;
       KK3_PHASE_END();
     } else {
-      // router + latent down (pass 0), shared gate/up (pass 1) (kimi.py:308, :317, :326)
+      // router, latent down and the shared expert's gate/up in one pass (kimi.py:308, :317, :326)
       if (KK3_RUN) {
-        KK3_BUILD(mlp_in_jobs(a, l, sj, sj2[0]));
-        run_gemv<NT, 1>(a, sj, 2, 0, gridDim.x, 0, 0, phase);
-        run_gemv<NT, 2>(a, sj2, 1, 0, gridDim.x, 0, 1);
+        KK3_BUILD(sjn = mlp_in_jobs(a, l, sj));
+        run_gemv<NT, 1>(a, sj, sjn, 0, gridDim.x, 0, 0, phase);
       }
       KK3_PHASE_END();
       // routing of row b on CTA b while the other CTAs run the shared-expert down projection (kimi.py:309-316,
