@@ -570,10 +570,13 @@ KK3_DEV unsigned lds32(const unsigned char* p) { return *reinterpret_cast<const 
 // 16-row tile x 64 k (two E2M1 groups of 32) of MT matrices. The per-warp cp.async ring carries only
 // weight bytes: the 16 x 32 code bytes of each matrix (row halves XOR-swizzled so the consumer's 4-byte
 // reads are bank-conflict free) and a 4-byte word of E8M0 scales per row (the aligned word holding this
-// unit's two groups). The FP16 activation pieces of the unit's (<= 8) pairs come from L2 into registers two
-// units ahead. Each quad converts its rows' E2M1 codes to FP16 in hardware (cvt.rn.f16x2.e2m1x2), runs
-// mma.sync per 32-wide group and applies the group scale to the FP32 partial. Everything the loop needs is
-// held in registers: nothing is reloaded from the argument block or the phase descriptor inside it.
+// unit's two groups). The FP16 activation rows the CTA's chunks multiply are staged once per phase into a
+// shared-memory row cache (per-unit loads of the same few hot rows from L2 were the engine's bottleneck);
+// rows beyond its capacity are read from L2. Each quad converts its rows' E2M1 codes to FP16 in hardware
+// (cvt.rn.f16x2.e2m1x2), runs mma.sync per 32-wide group and applies the group scale to the FP32 partial.
+constexpr int kExpRing = 8 * 1024;        // per-warp ring bytes of the expert engine
+constexpr int kExpXCache = 64 * 1024;     // per-CTA activation row cache, after the rings
+
 KK3_DEV void cp_async4_ca(void* smem_dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((unsigned)__cvta_generic_to_shared(smem_dst)),
                "l"(src) : "memory");
@@ -588,10 +591,13 @@ KK3_DEV uint4 ld_cg16(const void* p) {
 template <int MT>
 KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* __restrict__ e8m0_lut) {
   extern __shared__ __align__(16) unsigned char kk3_dyn_smem[];
+  __shared__ unsigned long long s_mask;    // MT == 2: batch rows staged (bit b = latent row b)
+  __shared__ int s_first, s_count;        // MT == 1: pairs [s_first, s_first + s_count) staged
+  __shared__ int s_rowmap[kMaxBatch];     // MT == 2: cache slot i holds latent row s_rowmap[i]
   constexpr int kCode = 16 * 32;                  // code bytes per matrix and unit
   constexpr int kScale = 16 * 4;                  // scale bytes per matrix and unit
   constexpr int kSlot = MT * (kCode + kScale);
-  constexpr int S = (kGemvSmemPerWarp / kSlot) > 12 ? 12 : (kGemvSmemPerWarp / kSlot);
+  constexpr int S = (kExpRing / kSlot) > 12 ? 12 : (kExpRing / kSlot);
   static_assert(S >= 3, "ring too shallow");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
 
@@ -604,15 +610,9 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* _
   nchunks = nchunks < 0 ? 0 : (nchunks > npk ? npk : nchunks);
   const int per_chunk = tiles * ksteps;      // <= 512 tiles x 128 k-steps
   const int U = nchunks * per_chunk;         // <= 2048 chunks: fits 32 bits
-  if (U == 0) return;
+  if (U == 0) return;                        // the same for every thread of the grid
   int GW = gridDim.x * kWarps;
   GW = GW < U ? GW : U;
-  const int gw = blockIdx.x * kWarps + warp;
-  if (gw >= GW) return;
-  const int ubeg = (int)((long long)U * gw / GW), uend = (int)((long long)U * (gw + 1) / GW);
-  const int nunits = uend - ubeg;
-  unsigned char* ring = kk3_dyn_smem + (size_t)warp * kGemvSmemPerWarp;
-  if (trace) trace_warp(a, 1);
 
   // routing-table values are clamped so that a routing fault can never address outside the buffers
   auto chunk_expert = [&](int chunk) {
@@ -626,19 +626,70 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* _
     np = np < 0 ? 0 : (np > 8 ? 8 : np);
     np = fp + np > npk ? npk - fp : np;
   };
-  // this lane's activation row for a chunk (pair r), or null when the chunk has fewer pairs
-  auto chunk_xrow = [&](int chunk) -> const __half* {
-    int fp, np;
-    chunk_pairs(chunk, fp, np);
-    if (r >= np) return nullptr;
-    const int p = fp + r;
-    if (MT == 2) {
-      int prow = __ldcg(a.s.pair_row + p);
-      prow = prow < 0 ? 0 : (prow >= a.g.B ? a.g.B - 1 : prow);
-      return a.s.latent_p + (size_t)prow * a.g.lh;
-    }
-    return a.s.act_p + (size_t)p * a.g.inter;
+  auto pair_batch_row = [&](int p) {
+    const int b = __ldcg(a.s.pair_row + p);
+    return b < 0 ? 0 : (b >= a.g.B ? a.g.B - 1 : b);
   };
+
+  // ---- stage the activation rows of this CTA's chunks (all threads, before any warp leaves)
+  const int xrow_bytes = ph.K * 2, xstride = xrow_bytes + 64;   // +64 B: rows alternate bank halves
+  const int cap = kExpXCache / xstride;
+  unsigned char* xcache = kk3_dyn_smem + kWarps * kExpRing;
+  const int cw0 = blockIdx.x * kWarps;
+  if (threadIdx.x == 0) {
+    unsigned long long mask = 0ull;
+    int first = 0, count = 0;
+    if (cw0 < GW) {
+      const int cbeg = (int)((long long)U * cw0 / GW);
+      const int cend = (int)((long long)U * (cw0 + kWarps < GW ? cw0 + kWarps : GW) / GW);
+      int fp_lo, np_lo, fp_hi, np_hi;
+      chunk_pairs(cbeg / per_chunk, fp_lo, np_lo);
+      chunk_pairs((cend - 1) / per_chunk, fp_hi, np_hi);
+      const int p_lo = fp_lo, p_hi = fp_hi + np_hi > p_lo ? fp_hi + np_hi : p_lo;
+      if (MT == 2) {
+        for (int p = p_lo; p < p_hi; ++p) mask |= 1ull << pair_batch_row(p);
+        int n = 0;
+        for (int b = 0; b < a.g.B; ++b) {
+          if (!((mask >> b) & 1ull)) continue;
+          if (n == cap) {
+            mask &= ~(1ull << b);   // beyond capacity: read from L2
+            continue;
+          }
+          s_rowmap[n++] = b;
+        }
+        count = n;
+      } else {
+        first = p_lo;
+        count = p_hi - p_lo < cap ? p_hi - p_lo : cap;
+      }
+    }
+    s_mask = mask;
+    s_first = first;
+    s_count = count;
+  }
+  __syncthreads();
+  {
+    const int pieces_per_row = xrow_bytes / 16;
+    const int total = s_count * pieces_per_row;
+    for (int q = threadIdx.x; q < total; q += kThreads) {
+      const int i = q / pieces_per_row, col = q - i * pieces_per_row;
+      const __half* src = (MT == 2) ? a.s.latent_p + (size_t)s_rowmap[i] * a.g.lh
+                                    : a.s.act_p + (size_t)(s_first + i) * a.g.inter;
+      cp_async16_g(xcache + i * xstride + col * 16, src + col * 8);
+    }
+    cp_async_commit_g();
+    cp_async_wait_g<0>();
+    __syncthreads();
+  }
+  const unsigned long long xmask = s_mask;
+  const int xfirst = s_first, xcount = s_count;
+
+  const int gw = cw0 + warp;
+  if (gw >= GW) return;
+  const int ubeg = (int)((long long)U * gw / GW), uend = (int)((long long)U * (gw + 1) / GW);
+  const int nunits = uend - ubeg;
+  unsigned char* ring = kk3_dyn_smem + (size_t)warp * kExpRing;
+  if (trace) trace_warp(a, 1);
 
   const int c0 = ubeg / per_chunk;
   const int rem0 = ubeg - c0 * per_chunk;
@@ -689,37 +740,41 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* _
     if (p_left > 0) p_issue();
     cp_async_commit_g();
   }
-
-  // ---- activations (registers, two units ahead)
-  int x_chunk = c0, x_ks = rem0 % ksteps, x_tile = rem0 / ksteps;
-  const __half* xrow = chunk_xrow(x_chunk);
-  const __half* xp = xrow ? xrow + x_ks * 64 + 8 * c : nullptr;
-  uint4 X[2][2];
-  auto x_load = [&](uint4 (&dst)[2]) {
-    dst[0] = make_uint4(0, 0, 0, 0);
-    dst[1] = make_uint4(0, 0, 0, 0);
-    if (xp) {
-      dst[0] = ld_cg16(xp);
-      dst[1] = ld_cg16(xp + 32);
-      xp += 64;
-    }
-    if (++x_ks == ksteps) {
-      x_ks = 0;
-      if (++x_tile == tiles) {
-        x_tile = 0;
-        ++x_chunk;
-        xrow = x_chunk < nchunks ? chunk_xrow(x_chunk) : nullptr;
-      }
-      xp = xrow ? xrow + 8 * c : nullptr;
-    }
-  };
-  x_load(X[0]);
   if (trace) trace_warp(a, 4);
 
-  // ---- consumer; per-lane read offsets inside a slot are fixed
+  // ---- activations of the current chunk for this lane's pair r: a cached row (x_sm), an L2 row (x_gl)
+  // for a row beyond the cache, or none (zeros) when the chunk has fewer pairs
   int c_chunk = c0, c_tile = rem0 / ksteps, c_ks = rem0 % ksteps;
   int c_fp = 0, c_np = 0;
-  chunk_pairs(c_chunk, c_fp, c_np);
+  const unsigned char* x_sm = xcache;   // always a valid address; x_live masks lanes without a pair
+  const __half* x_gl = nullptr;
+  bool x_live = false;
+  auto x_setup = [&]() {
+    chunk_pairs(c_chunk, c_fp, c_np);
+    x_live = r < c_np;
+    x_sm = xcache;
+    x_gl = nullptr;
+    if (!x_live) return;
+    const int p = c_fp + r;
+    if (MT == 2) {
+      const int b = pair_batch_row(p);
+      if ((xmask >> b) & 1ull) {
+        x_sm = xcache + __popcll(xmask & ((1ull << b) - 1ull)) * xstride;
+      } else {
+        x_gl = a.s.latent_p + (size_t)b * a.g.lh;
+      }
+    } else {
+      const int i = p - xfirst;
+      if (i >= 0 && i < xcount) {
+        x_sm = xcache + i * xstride;
+      } else {
+        x_gl = a.s.act_p + (size_t)p * a.g.inter;
+      }
+    }
+  };
+  x_setup();
+
+  // ---- consumer; per-lane read offsets inside a slot are fixed
   int c_slot = 0;
   const int rsw = ((r >> 2) & 1) * 16;                                   // swizzle of rows r and r + 8
   const int c_off0 = r * 32 + (0 ^ rsw) + 4 * c, c_off1 = r * 32 + (16 ^ rsw) + 4 * c;
@@ -729,79 +784,86 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* _
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[mt][0][i] = 0.0f;
-  for (int n0 = 0; n0 < nunits; n0 += 2) {
+  for (int n = 0; n < nunits; ++n) {
+    __syncwarp();   // every lane is done with the slot the next issue overwrites
+    if (p_left > 0) p_issue();
+    cp_async_commit_g();
+    // this unit's activation pieces: k = 64 ks + 8c (+32), from the row cache (or L2 for an uncached row)
+    uint4 X[2];
+    if (x_gl) {
+      X[0] = ld_cg16(x_gl + c_ks * 64 + 8 * c);
+      X[1] = ld_cg16(x_gl + c_ks * 64 + 32 + 8 * c);
+    } else {
+      X[0] = *reinterpret_cast<const uint4*>(x_sm + c_ks * 128 + c * 16);
+      X[1] = *reinterpret_cast<const uint4*>(x_sm + c_ks * 128 + 64 + c * 16);
+    }
+    if (!x_live) {
+      X[0] = make_uint4(0, 0, 0, 0);
+      X[1] = make_uint4(0, 0, 0, 0);
+    }
+    cp_async_wait_g<S - 1>();
+    __syncwarp();
+    if (trace && n < 2) trace_warp(a, 5 | (n << 8));
+    const unsigned char* slot = ring + c_slot * kSlot;
+    c_slot = c_slot + 1 == S ? 0 : c_slot + 1;
+    const int pos = (c_ks & 1) << 4;   // bit offset of this unit's two scale bytes in a row's word
+    unsigned swa[MT], swb[MT], wa[MT][2], wb[MT][2];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int n = n0 + j;
-      if (n >= nunits) break;
-      __syncwarp();   // every lane is done with the slot the next issue overwrites
-      if (p_left > 0) p_issue();
-      cp_async_commit_g();
-      if (n + 1 < nunits) x_load(X[j ^ 1]);
-      cp_async_wait_g<S - 1>();
-      __syncwarp();
-      if (trace && n < 2) trace_warp(a, 5 | (n << 8));
-      const unsigned char* slot = ring + c_slot * kSlot;
-      c_slot = c_slot + 1 == S ? 0 : c_slot + 1;
-      const int pos = (c_ks & 1) << 4;   // bit offset of this unit's two scale bytes in a row's word
-      unsigned swa[MT], swb[MT], wa[MT][2], wb[MT][2];
+    for (int mt = 0; mt < MT; ++mt) {
+      swa[mt] = *reinterpret_cast<const unsigned*>(slot + c_scl + mt * kScale) >> pos;
+      swb[mt] = *reinterpret_cast<const unsigned*>(slot + c_scl + mt * kScale + 32) >> pos;
+      wa[mt][0] = lds32(slot + mt * kCode + c_off0);
+      wa[mt][1] = lds32(slot + mt * kCode + c_off1);
+      wb[mt][0] = lds32(slot + mt * kCode + c_off0 + 256);
+      wb[mt][1] = lds32(slot + mt * kCode + c_off1 + 256);
+    }
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        swa[mt] = *reinterpret_cast<const unsigned*>(slot + c_scl + mt * kScale) >> pos;
-        swb[mt] = *reinterpret_cast<const unsigned*>(slot + c_scl + mt * kScale + 32) >> pos;
-        wa[mt][0] = lds32(slot + mt * kCode + c_off0);
-        wa[mt][1] = lds32(slot + mt * kCode + c_off1);
-        wb[mt][0] = lds32(slot + mt * kCode + c_off0 + 256);
-        wb[mt][1] = lds32(slot + mt * kCode + c_off1 + 256);
+    for (int mt = 0; mt < MT; ++mt) {
+      // both groups' conversions first, then their MMAs interleaved so each dependent pair has an
+      // independent MMA between its halves
+      unsigned ra[2][4], rb[2][4];
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        e2m1x8_cvt(wa[mt][g], ra[g]);
+        e2m1x8_cvt(wb[mt][g], rb[g]);
       }
+      float t[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+      mma_f16(t[0], ra[0][0], rb[0][0], ra[0][1], rb[0][1], X[0].x, X[0].y);
+      mma_f16(t[1], ra[1][0], rb[1][0], ra[1][1], rb[1][1], X[1].x, X[1].y);
+      mma_f16(t[0], ra[0][2], rb[0][2], ra[0][3], rb[0][3], X[0].z, X[0].w);
+      mma_f16(t[1], ra[1][2], rb[1][2], ra[1][3], rb[1][3], X[1].z, X[1].w);
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        // both groups' conversions first, then their MMAs interleaved so each dependent pair has an
-        // independent MMA between its halves
-        unsigned ra[2][4], rb[2][4];
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          e2m1x8_cvt(wa[mt][g], ra[g]);
-          e2m1x8_cvt(wb[mt][g], rb[g]);
-        }
-        float t[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
-        mma_f16(t[0], ra[0][0], rb[0][0], ra[0][1], rb[0][1], X[j][0].x, X[j][0].y);
-        mma_f16(t[1], ra[1][0], rb[1][0], ra[1][1], rb[1][1], X[j][1].x, X[j][1].y);
-        mma_f16(t[0], ra[0][2], rb[0][2], ra[0][3], rb[0][3], X[j][0].z, X[j][0].w);
-        mma_f16(t[1], ra[1][2], rb[1][2], ra[1][3], rb[1][3], X[j][1].z, X[j][1].w);
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          // 2^(s - 127) from a 256-entry table (s = 0 and s = 255 exactly as the reference decodes them)
-          const float fa = e8m0_lut[(swa[mt] >> (8 * g)) & 0xffu];
-          const float fb = e8m0_lut[(swb[mt] >> (8 * g)) & 0xffu];
-          acc[mt][0][0] = fmaf(t[g][0], fa, acc[mt][0][0]);
-          acc[mt][0][1] = fmaf(t[g][1], fa, acc[mt][0][1]);
-          acc[mt][0][2] = fmaf(t[g][2], fb, acc[mt][0][2]);
-          acc[mt][0][3] = fmaf(t[g][3], fb, acc[mt][0][3]);
-        }
+      for (int g = 0; g < 2; ++g) {
+        // 2^(s - 127) from a 256-entry table (s = 0 and s = 255 exactly as the reference decodes them)
+        const float fa = e8m0_lut[(swa[mt] >> (8 * g)) & 0xffu];
+        const float fb = e8m0_lut[(swb[mt] >> (8 * g)) & 0xffu];
+        acc[mt][0][0] = fmaf(t[g][0], fa, acc[mt][0][0]);
+        acc[mt][0][1] = fmaf(t[g][1], fa, acc[mt][0][1]);
+        acc[mt][0][2] = fmaf(t[g][2], fb, acc[mt][0][2]);
+        acc[mt][0][3] = fmaf(t[g][3], fb, acc[mt][0][3]);
       }
-      if (c_ks == ksteps - 1 || n == nunits - 1) {
-        const int tile_beg = c_chunk * per_chunk + c_tile * ksteps;
-        const bool inside = tile_beg >= ubeg && tile_beg + ksteps <= uend;   // the whole tile is this warp's
-        const long long first = inside ? gw : owner_of(tile_beg, U, GW);
-        const long long lastw = inside ? gw : owner_of(tile_beg + ksteps - 1, U, GW);
-        bool done = first == lastw;
-        if (!done)
-          done = stream_k_fixup<1, MT>(a, a.s.fix_part, a.s.fix_cnt + c_chunk * tiles + c_tile, gw,
-                                       tile_beg <= ubeg, tile_beg, first, lastw, U, GW, acc);
-        if (done) expert_epilogue<MT>(a, ph.rows, c_fp, c_np, c_tile, acc);
+    }
+    if (c_ks == ksteps - 1 || n == nunits - 1) {
+      const int tile_beg = c_chunk * per_chunk + c_tile * ksteps;
+      const bool inside = tile_beg >= ubeg && tile_beg + ksteps <= uend;   // the whole tile is this warp's
+      const long long first = inside ? gw : owner_of(tile_beg, U, GW);
+      const long long lastw = inside ? gw : owner_of(tile_beg + ksteps - 1, U, GW);
+      bool done = first == lastw;
+      if (!done)
+        done = stream_k_fixup<1, MT>(a, a.s.fix_part, a.s.fix_cnt + c_chunk * tiles + c_tile, gw,
+                                     tile_beg <= ubeg, tile_beg, first, lastw, U, GW, acc);
+      if (done) expert_epilogue<MT>(a, ph.rows, c_fp, c_np, c_tile, acc);
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
+      for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) acc[mt][0][i] = 0.0f;
-      }
-      if (++c_ks == ksteps) {
-        c_ks = 0;
-        if (++c_tile == tiles) {
-          c_tile = 0;
-          ++c_chunk;
-          if (n + 1 < nunits) chunk_pairs(c_chunk, c_fp, c_np);
-        }
+        for (int i = 0; i < 4; ++i) acc[mt][0][i] = 0.0f;
+    }
+    if (++c_ks == ksteps) {
+      c_ks = 0;
+      if (++c_tile == tiles) {
+        c_tile = 0;
+        ++c_chunk;
+        if (n + 1 < nunits) x_setup();
       }
     }
   }
