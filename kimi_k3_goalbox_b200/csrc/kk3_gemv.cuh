@@ -531,25 +531,22 @@ struct ExpertPhase {
   long long expert_scales;   // bytes of scales per expert (rows * K / 32)
 };
 
+// Expert epilogue for one complete 16-row tile. `dst[e]` is the output row of this lane's column 2c + e in
+// the chunk (null when the chunk has fewer pairs): the FP16 activation row of the pair (MT == 2) or the
+// pair's bf16 slot-output row (MT == 1); it is resolved once per chunk, not per tile.
 template <int MT>
-KK3_DEV void expert_epilogue(const StepArgs& a, int rows, int first_pair, int npairs, int tile,
-                             const float (&acc)[MT][1][4]) {
-  const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
+KK3_DEV void expert_epilogue(int rows, int tile, void* const (&dst)[2], const float (&acc)[MT][1][4]) {
+  const int lane = threadIdx.x & 31, r = lane >> 2;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int row = tile * 16 + r + 8 * (i >> 1);
-    const int col = 2 * c + (i & 1);
-    if (col >= npairs || row >= rows) continue;
-    const int p = first_pair + col;
+    void* d = dst[i & 1];
+    if (d == nullptr || row >= rows) continue;
     if (MT == 2) {
       const float g = round_bf(acc[0][0][i]), u = round_bf(acc[MT - 1][0][i]);
-      const float act = round_bf(situ_f(g, u));
-      a.s.act_p[(size_t)p * a.g.inter + row] = __float2half_rn(act);
+      reinterpret_cast<__half*>(d)[row] = __float2half_rn(round_bf(situ_f(g, u)));
     } else {
-      int b = a.s.pair_row[p], slot = a.s.pair_slot[p];
-      b = b < 0 ? 0 : (b >= a.g.B ? a.g.B - 1 : b);
-      slot = slot < 0 ? 0 : (slot >= a.g.K ? a.g.K - 1 : slot);
-      a.s.out_slot[((size_t)b * a.g.K + slot) * a.g.lh + row] = f2bf(acc[0][0][i]);
+      reinterpret_cast<bf16*>(d)[row] = f2bf(acc[0][0][i]);
     }
   }
 }
@@ -749,8 +746,23 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* _
   const unsigned char* x_sm = xcache;   // always a valid address; x_live masks lanes without a pair
   const __half* x_gl = nullptr;
   bool x_live = false;
+  void* out_row[2] = {nullptr, nullptr};   // epilogue targets of this lane's columns 2c, 2c + 1
   auto x_setup = [&]() {
     chunk_pairs(c_chunk, c_fp, c_np);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int col = 2 * c + e;
+      out_row[e] = nullptr;
+      if (col >= c_np) continue;
+      const int pc = c_fp + col;
+      if (MT == 2) {
+        out_row[e] = a.s.act_p + (size_t)pc * a.g.inter;
+      } else {
+        int slot = __ldcg(a.s.pair_slot + pc);
+        slot = slot < 0 ? 0 : (slot >= a.g.K ? a.g.K - 1 : slot);
+        out_row[e] = a.s.out_slot + ((size_t)pair_batch_row(pc) * a.g.K + slot) * a.g.lh;
+      }
+    }
     x_live = r < c_np;
     x_sm = xcache;
     x_gl = nullptr;
@@ -852,7 +864,7 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* _
       if (!done)
         done = stream_k_fixup<1, MT>(a, a.s.fix_part, a.s.fix_cnt + c_chunk * tiles + c_tile, gw,
                                      tile_beg <= ubeg, tile_beg, first, lastw, U, GW, acc);
-      if (done) expert_epilogue<MT>(a, ph.rows, c_fp, c_np, c_tile, acc);
+      if (done) expert_epilogue<MT>(ph.rows, c_tile, out_row, acc);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll

@@ -139,6 +139,7 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   g.nblk = (g.L + g.bs - 1) / g.bs;
   g.timeout_ns = cfg->timeout_ns > 0 ? cfg->timeout_ns : 10000000000ll;
   g.mla_mt = (g.hr + 15) / 16;
+  if (g.mla_mt == 5) g.mla_mt = 6;   // the attention kernel is instantiated for 1-4 and 6 head tiles
   cudaDeviceProp prop;
   if (cudaGetDeviceProperties(&prop, cfg->device) != cudaSuccess) { delete x; return KK3_ERR_CUDA; }
   x->sms = prop.multiProcessorCount;
@@ -256,7 +257,7 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   x->peers_open = g.tp == 1;
   // shared memory: the largest phase (MLA attention with all head tiles, or row buffers)
   const int HR = g.mla_mt * 16;
-  size_t sm_mla = (size_t)(HR + 2 * kMlaPos) * kRowK * 2 + (size_t)HR * kRowS * 4 + (size_t)HR * kRowP * 2 + 3 * HR * 4 + 64;
+  size_t sm_mla = mla_smem_bytes(HR);
   size_t sm_row = (512 + (size_t)(g.h > g.lh ? g.h : g.lh)) * 4 + 64;
   size_t sm_abs = ((size_t)g.B * 128 + 4 * 16 * 128) * 4;
   size_t sm_route = ((size_t)g.B * g.K + 4 * kMaxExperts) * 4;
@@ -490,6 +491,7 @@ static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, Ste
   g.nblk = (g.L + g.bs - 1) / g.bs;
   g.timeout_ns = cfg->timeout_ns > 0 ? cfg->timeout_ns : 10000000000ll;
   g.mla_mt = (g.hr + 15) / 16;
+  if (g.mla_mt == 5) g.mla_mt = 6;   // the attention kernel is instantiated for 1-4 and 6 head tiles
   *nt = g.B <= 8 ? 1 : (g.B <= 16 ? 2 : (g.B <= 32 ? 4 : 8));
   {
     int chunks = sms / g.B;
@@ -578,7 +580,7 @@ static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, Ste
   s.err_host = err_mirror;
   c.base[0] = comm;
   const int HR = g.mla_mt * 16;
-  size_t sm = (size_t)(HR + 2 * kMlaPos) * kRowK * 2 + (size_t)HR * kRowS * 4 + (size_t)HR * kRowP * 2 + 3 * HR * 4 + 64;
+  size_t sm = mla_smem_bytes(HR);
   const size_t sm_row = (512 + (size_t)(g.h > g.lh ? g.h : g.lh)) * 4 + 64;
   const size_t sm_abs = ((size_t)g.B * 128 + 4 * 16 * 128) * 4;
   const size_t sm_route = ((size_t)g.B * g.K + 4 * kMaxExperts) * 4;

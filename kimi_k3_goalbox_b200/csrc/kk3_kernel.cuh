@@ -489,7 +489,14 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
           const int p0 = rem * g.mla_chunk_len;
           int p1 = p0 + g.mla_chunk_len;
           p1 = p1 < T ? p1 : T;
-          mla_attend_item(a, l, midx, b, rem, p0, p1, T, smem);
+          // one instantiation per head-tile count (hr <= 96): accumulators sized exactly, 3 stages up to 64 heads
+          switch (g.mla_mt) {
+            case 1: mla_attend_item<1, 3>(a, l, midx, b, rem, p0, p1, T, smem, phase); break;
+            case 2: mla_attend_item<2, 3>(a, l, midx, b, rem, p0, p1, T, smem, phase); break;
+            case 3: mla_attend_item<3, 3>(a, l, midx, b, rem, p0, p1, T, smem, phase); break;
+            case 4: mla_attend_item<4, 3>(a, l, midx, b, rem, p0, p1, T, smem, phase); break;
+            default: mla_attend_item<6, 2>(a, l, midx, b, rem, p0, p1, T, smem, phase); break;
+          }
         }
       }
       KK3_PHASE_END();

@@ -451,6 +451,19 @@ constexpr int kRowK = 584;   // padded row (elements) of a cached position: 512 
 constexpr int kRowP = 40;    // padded row of the BF16 probability tile (32 positions + 8)
 constexpr int kRowS = 33;    // padded row of the FP32 score tile
 
+// Pipeline depth (position sub-tiles in flight) and k-split of the score product for a head-tile count:
+// three stages while they fit next to the query tile, the 576-wide score dot products split over up to four
+// warps per (head tile, 8 positions) so that all 16 warps take part.
+__host__ __device__ inline int mla_stages(int HR) { return HR <= 64 ? 3 : 2; }
+__host__ __device__ inline int mla_kq(int MT) {
+  const int q = kWarps / (MT * 4);
+  return q < 1 ? 1 : (q > 4 ? 4 : q);
+}
+__host__ __device__ inline size_t mla_smem_bytes(int HR) {
+  return (size_t)(HR + mla_stages(HR) * kMlaPos) * kRowK * 2 + (size_t)mla_kq(HR / 16) * HR * kRowS * 4 +
+         (size_t)HR * kRowP * 2 + 3 * HR * 4 + 64;
+}
+
 KK3_DEV unsigned smem_u32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
 
 KK3_DEV void cp_async16(void* dst, const void* src) {
@@ -499,21 +512,33 @@ KK3_DEV void mla_stage(const StepArgs& a, int layer, int midx, int b, int t0, in
 }
 
 // One split-K item: batch row b, positions [p0, p1) of its attended sequence (T = ctx+1 or 1).
-// Writes (m, l, O[kr]) per head for the combine phase (flash-decoding with online softmax).
+// Writes (m, l, O[kr]) per head for the combine phase (flash-decoding with online softmax). Position
+// sub-tiles of 32 stream through an NS-deep cp.async ring; the score product S = Q K^T is split over
+// (head tile, 8 positions, k-quarter) so every warp works, and the k-partials are summed in a fixed order.
+template <int MT, int NS>
 KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int chunk, int p0, int p1, int T,
-                             unsigned char* smem) {
+                            unsigned char* smem, int ph = -1) {
   const Geo& g = a.g;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, r = lane >> 2, c = lane & 3;
-  const int MT = g.mla_mt, HR = MT * 16;
-  const int qk = g.kr + g.rd;   // 576
-  bf16* Qs = reinterpret_cast<bf16*>(smem);                   // [HR][kRowK]
-  bf16* Ks = Qs + HR * kRowK;                                 // [2][32][kRowK]
-  float* Ss = reinterpret_cast<float*>(Ks + 2 * kMlaPos * kRowK);   // [HR][kRowS]
-  bf16* Ps = reinterpret_cast<bf16*>(Ss + HR * kRowS);        // [HR][kRowP]
-  float* mrun = reinterpret_cast<float*>(Ps + HR * kRowP);    // [HR]
-  float* lrun = mrun + HR;                                    // [HR]
-  float* alpha = lrun + HR;                                   // [HR]
+  constexpr int HR = MT * 16;
+  const bool stamp = ph >= 0 && b == 0 && chunk == 0 && tid == 0;   // sub-phase stamps of one item
+  if (stamp) sub_stamp(a, ph, 0);
+  const int KQ = mla_kq(MT), kper = (g.kr + g.rd) / 16 / KQ;   // 36 k-steps of 16, split KQ ways
+  bf16* Qs = reinterpret_cast<bf16*>(smem);                         // [HR][kRowK]
+  bf16* Ks = Qs + HR * kRowK;                                       // [NS][32][kRowK]
+  float* Sp = reinterpret_cast<float*>(Ks + NS * kMlaPos * kRowK);   // [KQ][HR][kRowS] k-partial scores
+  bf16* Ps = reinterpret_cast<bf16*>(Sp + KQ * HR * kRowS);         // [HR][kRowP]
+  float* mrun = reinterpret_cast<float*>(Ps + HR * kRowP);          // [HR]
+  float* lrun = mrun + HR;                                          // [HR]
+  float* alpha = lrun + HR;                                         // [HR]
   const float scale = rsqrtf((float)(g.nr + g.rd));
+  const int Tend = p1 < T ? p1 : T;
+  const int nsub = (p1 - p0 + kMlaPos - 1) / kMlaPos;
+  // the first NS - 1 sub-tiles go out before the query tile is assembled
+  for (int s = 0; s < NS - 1; ++s) {
+    if (s < nsub) mla_stage(a, layer, midx, b, p0 + s * kMlaPos, Tend, Ks + s * kMlaPos * kRowK);
+    else cp_async_commit();
+  }
   // Q rows: absorbed (512) | q rope (64); zero for padded heads
   for (int i = tid; i < HR * 72; i += kThreads) {
     const int hh = i / 72, q = i % 72;
@@ -528,47 +553,52 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
     mrun[i] = -INFINITY;
     lrun[i] = 0.0f;
   }
+  if (stamp) sub_stamp(a, ph, 1);
   // O accumulators: warp w owns latent dims [32w, 32w+32) for every head tile
-  float O[6][4][4];
+  float O[MT][4][4];
 #pragma unroll
-  for (int mt = 0; mt < 6; ++mt)
+  for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) O[mt][nt][i] = 0.0f;
 
-  const int nsub = (p1 - p0 + kMlaPos - 1) / kMlaPos;
-  mla_stage(a, layer, midx, b, p0, p1 < T ? p1 : T, Ks);
   for (int s = 0; s < nsub; ++s) {
     const int t0 = p0 + s * kMlaPos;
-    bf16* Kc = Ks + (s & 1) * kMlaPos * kRowK;
-    if (s + 1 < nsub) {
-      mla_stage(a, layer, midx, b, t0 + kMlaPos, p1 < T ? p1 : T, Ks + ((s + 1) & 1) * kMlaPos * kRowK);
-      cp_async_wait_one();
-    } else {
-      cp_async_wait_all();
-    }
+    bf16* Kc = Ks + (s % NS) * kMlaPos * kRowK;
+    if (s + NS - 1 < nsub)
+      mla_stage(a, layer, midx, b, t0 + (NS - 1) * kMlaPos, Tend, Ks + ((s + NS - 1) % NS) * kMlaPos * kRowK);
+    else
+      cp_async_commit();
+    if (NS == 3) asm volatile("cp.async.wait_group 2;" ::: "memory");
+    else asm volatile("cp.async.wait_group 1;" ::: "memory");
     __syncthreads();
-    // S = Q K^T over 576 dims: items (head tile, 8-position n-tile)
-    for (int it = warp; it < MT * 4; it += kWarps) {
-      const int mt = it >> 2, nt = it & 3;
+    if (stamp && s < 2) sub_stamp(a, ph, 2 + 4 * s);
+    // k-partial scores: items (k-quarter, head tile, 8-position n-tile)
+    for (int it = warp; it < MT * 4 * KQ; it += kWarps) {
+      const int kq = it % KQ, mt = (it / KQ) >> 2, nt = (it / KQ) & 3;
       float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      for (int k0 = 0; k0 < qk; k0 += 16) {
+      for (int ks = kq * kper; ks < (kq + 1) * kper; ++ks) {
+        const int k0 = ks * 16;
         unsigned af[4], bfr[2];
         ldsm_x4(af, Qs + (mt * 16 + (lane & 15)) * kRowK + k0 + (lane >> 4) * 8);
         ldsm_x2(bfr, Kc + (nt * 8 + (lane & 7)) * kRowK + k0 + ((lane >> 3) & 1) * 8);
         mma_bf16(sacc, af[0], af[1], af[2], af[3], bfr[0], bfr[1]);
       }
-      Ss[(mt * 16 + r) * kRowS + nt * 8 + 2 * c] = sacc[0] * scale;
-      Ss[(mt * 16 + r) * kRowS + nt * 8 + 2 * c + 1] = sacc[1] * scale;
-      Ss[(mt * 16 + r + 8) * kRowS + nt * 8 + 2 * c] = sacc[2] * scale;
-      Ss[(mt * 16 + r + 8) * kRowS + nt * 8 + 2 * c + 1] = sacc[3] * scale;
+      float* sp = Sp + (size_t)kq * HR * kRowS;
+      sp[(mt * 16 + r) * kRowS + nt * 8 + 2 * c] = sacc[0];
+      sp[(mt * 16 + r) * kRowS + nt * 8 + 2 * c + 1] = sacc[1];
+      sp[(mt * 16 + r + 8) * kRowS + nt * 8 + 2 * c] = sacc[2];
+      sp[(mt * 16 + r + 8) * kRowS + nt * 8 + 2 * c + 1] = sacc[3];
     }
     __syncthreads();
-    // online softmax, one warp per head row, one lane per position
+    if (stamp && s < 2) sub_stamp(a, ph, 3 + 4 * s);
+    // online softmax, one warp per head row, one lane per position (k-partials summed in order)
     for (int hh = warp; hh < HR; hh += kWarps) {
       const bool valid = (t0 + lane) < p1 && (t0 + lane) < T && hh < g.hr;
-      const float sv = valid ? Ss[hh * kRowS + lane] : -INFINITY;
+      float sum = 0.0f;
+      for (int q = 0; q < KQ; ++q) sum += Sp[((size_t)q * HR + hh) * kRowS + lane];
+      const float sv = valid ? sum * scale : -INFINITY;
       const float mt_ = warp_max(sv);
       const float mold = mrun[hh];
       const float mnew = fmaxf(mold, mt_);
@@ -583,15 +613,14 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
       }
     }
     __syncthreads();
+    if (stamp && s < 2) sub_stamp(a, ph, 4 + 4 * s);
     // O = O * alpha + P V over this sub-tile: warp w owns dims [32w, 32w+32)
 #pragma unroll
-    for (int mt = 0; mt < 6; ++mt) {
-      if (mt < MT) {
-        const float a0 = alpha[mt * 16 + r], a1 = alpha[mt * 16 + r + 8];
+    for (int mt = 0; mt < MT; ++mt) {
+      const float a0 = alpha[mt * 16 + r], a1 = alpha[mt * 16 + r + 8];
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-          O[mt][nt][0] *= a0; O[mt][nt][1] *= a0; O[mt][nt][2] *= a1; O[mt][nt][3] *= a1;
-        }
+      for (int nt = 0; nt < 4; ++nt) {
+        O[mt][nt][0] *= a0; O[mt][nt][1] *= a0; O[mt][nt][2] *= a1; O[mt][nt][3] *= a1;
       }
     }
 #pragma unroll
@@ -600,17 +629,19 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) ldsm_x2_t(bfr[nt], Kc + (k0 + (lane & 15)) * kRowK + warp * 32 + nt * 8);
 #pragma unroll
-      for (int mt = 0; mt < 6; ++mt) {
-        if (mt < MT) {
-          unsigned af[4];
-          ldsm_x4(af, Ps + (mt * 16 + (lane & 15)) * kRowP + k0 + (lane >> 4) * 8);
+      for (int mt = 0; mt < MT; ++mt) {
+        unsigned af[4];
+        ldsm_x4(af, Ps + (mt * 16 + (lane & 15)) * kRowP + k0 + (lane >> 4) * 8);
 #pragma unroll
-          for (int nt = 0; nt < 4; ++nt) mma_bf16(O[mt][nt], af[0], af[1], af[2], af[3], bfr[nt][0], bfr[nt][1]);
-        }
+        for (int nt = 0; nt < 4; ++nt) mma_bf16(O[mt][nt], af[0], af[1], af[2], af[3], bfr[nt][0], bfr[nt][1]);
       }
     }
     __syncthreads();
+    if (stamp && s < 2) sub_stamp(a, ph, 5 + 4 * s);
   }
+  cp_async_wait_all();
+  if (stamp) sub_stamp(a, ph, 10);
+  if (stamp) sub_stamp(a, ph, 11, (unsigned long long)nsub);
   // write the partial: [b][chunk][h] x (m, l, O[512])
   const int stride = g.kr + 2;
   float* base = a.s.mla_part + (((size_t)b * g.mla_chunks + chunk) * g.hr) * stride;
@@ -619,16 +650,14 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
     base[(size_t)hh * stride + 1] = lrun[hh];
   }
 #pragma unroll
-  for (int mt = 0; mt < 6; ++mt) {
-    if (mt < MT) {
+  for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
+    for (int nt = 0; nt < 4; ++nt) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int hh = mt * 16 + r + 8 * (i >> 1);
-          const int col = warp * 32 + nt * 8 + 2 * c + (i & 1);
-          if (hh < g.hr) base[(size_t)hh * stride + 2 + col] = O[mt][nt][i];
-        }
+      for (int i = 0; i < 4; ++i) {
+        const int hh = mt * 16 + r + 8 * (i >> 1);
+        const int col = warp * 32 + nt * 8 + 2 * c + (i & 1);
+        if (hh < g.hr) base[(size_t)hh * stride + 2 + col] = O[mt][nt][i];
       }
     }
   }

@@ -171,6 +171,11 @@ def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[d
                                           "red1": (st[2] - base) / 1e3, "mix": (st[3] - base) / 1e3,
                                           "red2": (st[4] - base) / 1e3, "store": (st[5] - base) / 1e3,
                                           "done": (st[6] - base) / 1e3, "phase_end": (ts[i + 1] - base) / 1e3}
+        if name == "mla_attend" and st[0]:
+            subinfo[f"{name}:{layer}"] = {k: (st[i] - base) / 1e3 for i, k in enumerate(
+                ["start", "q_ready", "t0_data", "t0_scores", "t0_softmax", "t0_pv", "t1_data", "t1_scores",
+                 "t1_softmax", "t1_pv", "item_end"]) if st[i]} | {"subtiles": st[11],
+                                                                  "phase_end": (ts[i + 1] - base) / 1e3}
         if name == "route" and st[12]:
             subinfo[f"{name}:{layer}"] = {"cta0_candidates": (st[12] - base) / 1e3, "cta0_done": (st[13] - base) / 1e3,
                                           "group_start": (st[14] - base) / 1e3, "group_end": (st[15] - base) / 1e3,
@@ -212,7 +217,7 @@ def main(argv=None) -> int:
         case = cases.variant(case, batch=args.batch)
     rows = profile(case, args.reps)
     subrow, head, rows = rows[0], rows[1:3], rows[3:]
-    for k, v in list(subrow["info"].items())[:9]:
+    for k, v in list(subrow["info"].items())[:12]:
         print("  sub-phase", k, {kk: (round(vv, 2) if isinstance(vv, float) else vv) for kk, vv in v.items()})
     total = sum(r["us"] for r in rows)
     print(f"{case['id']}: full step {head[0]['us']:.1f} us (events), empty launch {head[1]['us']:.1f} us, "
