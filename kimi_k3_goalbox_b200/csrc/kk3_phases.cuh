@@ -486,26 +486,34 @@ KK3_DEV void ldsm_x2_t(unsigned (&r)[2], const void* p) {
 }
 
 // stage positions [t0, t0+32) of row b (cache rows, the new token at t == ctx, zero beyond T)
-KK3_DEV void mla_stage(const StepArgs& a, int layer, int midx, int b, int t0, int T, bf16* dst) {
-  const Geo& g = a.g;
-  const bf16* kv = lptr<bf16>(a, layer, KK3_MLA_KV_CACHE);
-  const bf16* pe = lptr<bf16>(a, layer, KK3_MLA_PE_CACHE);
-  const bf16* kvw = gout<bf16>(a, KK3_OUT_KV_WRITE) + ((size_t)midx * g.B + b) * g.kr;
-  const bf16* pew = gout<bf16>(a, KK3_OUT_PE_WRITE) + ((size_t)midx * g.B + b) * g.rd;
-  const bool keep = !reinterpret_cast<const bool*>(a.ptr[KK3_RESET])[b];
-  for (int i = threadIdx.x; i < kMlaPos * 72; i += kThreads) {
-    const int tl = i / 72, q = i % 72, t = t0 + tl;
+// Source rows of one batch row's attended sequence: cache positions first (kept rows only), then the new
+// token's latent and rope rows. Each thread stages the same (position, 16-byte piece) pattern for every
+// sub-tile, so its piece offsets are computed once per item.
+struct MlaSrc {
+  const bf16* kv;    // kv_cache row 0 of this batch row
+  const bf16* pe;    // pe_cache row 0
+  const bf16* kvw;   // new token's latent row (kv_write)
+  const bf16* pew;   // new token's rope row (pe_write)
+  int ncache;        // cached positions attended (ctx for a kept row, 0 after a reset)
+  int kr, rd;
+};
+
+constexpr int kMlaPieces = kMlaPos * 72;                       // 16-byte pieces of one 32-position sub-tile
+constexpr int kMlaPiecesPerThread = (kMlaPieces + kThreads - 1) / kThreads;
+
+KK3_DEV void mla_stage(const MlaSrc& src, int t0, int T, bf16* dst) {
+#pragma unroll
+  for (int j = 0; j < kMlaPiecesPerThread; ++j) {
+    const int i = threadIdx.x + j * kThreads;
+    if (i >= kMlaPieces) break;
+    const int tl = i / 72, q = i - (i / 72) * 72, t = t0 + tl;
     bf16* d = dst + tl * kRowK + q * 8;
-    // position index in the attended sequence: cache rows first (keep rows only), then the new token
-    const int ncache = keep ? g.ctx : 0;
-    if (t >= T) {
-      *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
-    } else if (t < ncache) {
-      const bf16* src = q < 64 ? kv + ((size_t)b * g.ctx + t) * g.kr + q * 8 : pe + ((size_t)b * g.ctx + t) * g.rd + (q - 64) * 8;
-      cp_async16(d, src);
+    if (t < src.ncache) {
+      cp_async16(d, q < 64 ? src.kv + (size_t)t * src.kr + q * 8 : src.pe + (size_t)t * src.rd + (q - 64) * 8);
+    } else if (t < T) {
+      *reinterpret_cast<uint4*>(d) = ld_act16(q < 64 ? src.kvw + q * 8 : src.pew + (q - 64) * 8);
     } else {
-      const bf16* src = q < 64 ? kvw + q * 8 : pew + (q - 64) * 8;
-      *reinterpret_cast<uint4*>(d) = ld_act16(src);
+      *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
     }
   }
   cp_async_commit();
@@ -534,20 +542,30 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
   const float scale = rsqrtf((float)(g.nr + g.rd));
   const int Tend = p1 < T ? p1 : T;
   const int nsub = (p1 - p0 + kMlaPos - 1) / kMlaPos;
-  // the first NS - 1 sub-tiles go out before the query tile is assembled
-  for (int s = 0; s < NS - 1; ++s) {
-    if (s < nsub) mla_stage(a, layer, midx, b, p0 + s * kMlaPos, Tend, Ks + s * kMlaPos * kRowK);
-    else cp_async_commit();
-  }
-  // Q rows: absorbed (512) | q rope (64); zero for padded heads
+  MlaSrc src;
+  src.kv = lptr<bf16>(a, layer, KK3_MLA_KV_CACHE) + (size_t)b * g.ctx * g.kr;
+  src.pe = lptr<bf16>(a, layer, KK3_MLA_PE_CACHE) + (size_t)b * g.ctx * g.rd;
+  src.kvw = gout<bf16>(a, KK3_OUT_KV_WRITE) + ((size_t)midx * g.B + b) * g.kr;
+  src.pew = gout<bf16>(a, KK3_OUT_PE_WRITE) + ((size_t)midx * g.B + b) * g.rd;
+  src.ncache = reinterpret_cast<const bool*>(a.ptr[KK3_RESET])[b] ? 0 : g.ctx;
+  src.kr = g.kr;
+  src.rd = g.rd;
+  // Q rows: absorbed (512) | q rope (64), copied asynchronously in the group of the first sub-tile; zero for
+  // padded heads
   for (int i = tid; i < HR * 72; i += kThreads) {
     const int hh = i / 72, q = i % 72;
-    uint4 v = make_uint4(0, 0, 0, 0);
+    bf16* d = Qs + hh * kRowK + q * 8;
     if (hh < g.hr) {
-      if (q < 64) v = ld_act16(a.s.absorbed + (((size_t)b * g.hr + hh) * g.kr) + q * 8);
-      else v = ld_act16(a.s.mla_q + ((size_t)b * g.hr + hh) * (g.nr + g.rd) + g.nr + (q - 64) * 8);
+      cp_async16(d, q < 64 ? a.s.absorbed + (((size_t)b * g.hr + hh) * g.kr) + q * 8
+                           : a.s.mla_q + ((size_t)b * g.hr + hh) * (g.nr + g.rd) + g.nr + (q - 64) * 8);
+    } else {
+      *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
     }
-    *reinterpret_cast<uint4*>(Qs + hh * kRowK + q * 8) = v;
+  }
+  // the first NS - 1 sub-tiles go out right behind it
+  for (int s = 0; s < NS - 1; ++s) {
+    if (s < nsub) mla_stage(src, p0 + s * kMlaPos, Tend, Ks + s * kMlaPos * kRowK);
+    else cp_async_commit();
   }
   for (int i = tid; i < HR; i += kThreads) {
     mrun[i] = -INFINITY;
@@ -567,7 +585,7 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
     const int t0 = p0 + s * kMlaPos;
     bf16* Kc = Ks + (s % NS) * kMlaPos * kRowK;
     if (s + NS - 1 < nsub)
-      mla_stage(a, layer, midx, b, t0 + (NS - 1) * kMlaPos, Tend, Ks + ((s + NS - 1) % NS) * kMlaPos * kRowK);
+      mla_stage(src, t0 + (NS - 1) * kMlaPos, Tend, Ks + ((s + NS - 1) % NS) * kMlaPos * kRowK);
     else
       cp_async_commit();
     if (NS == 3) asm volatile("cp.async.wait_group 2;" ::: "memory");
@@ -577,14 +595,21 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
     // k-partial scores: items (k-quarter, head tile, 8-position n-tile)
     for (int it = warp; it < MT * 4 * KQ; it += kWarps) {
       const int kq = it % KQ, mt = (it / KQ) >> 2, nt = (it / KQ) & 3;
-      float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      for (int ks = kq * kper; ks < (kq + 1) * kper; ++ks) {
-        const int k0 = ks * 16;
+      // two accumulators (even / odd k-steps) so consecutive MMAs do not wait on each other
+      float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sacc2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int ks = kq * kper; ks < (kq + 1) * kper; ks += 2) {
         unsigned af[4], bfr[2];
-        ldsm_x4(af, Qs + (mt * 16 + (lane & 15)) * kRowK + k0 + (lane >> 4) * 8);
-        ldsm_x2(bfr, Kc + (nt * 8 + (lane & 7)) * kRowK + k0 + ((lane >> 3) & 1) * 8);
+        ldsm_x4(af, Qs + (mt * 16 + (lane & 15)) * kRowK + ks * 16 + (lane >> 4) * 8);
+        ldsm_x2(bfr, Kc + (nt * 8 + (lane & 7)) * kRowK + ks * 16 + ((lane >> 3) & 1) * 8);
         mma_bf16(sacc, af[0], af[1], af[2], af[3], bfr[0], bfr[1]);
+        if (ks + 1 < (kq + 1) * kper) {
+          ldsm_x4(af, Qs + (mt * 16 + (lane & 15)) * kRowK + (ks + 1) * 16 + (lane >> 4) * 8);
+          ldsm_x2(bfr, Kc + (nt * 8 + (lane & 7)) * kRowK + (ks + 1) * 16 + ((lane >> 3) & 1) * 8);
+          mma_bf16(sacc2, af[0], af[1], af[2], af[3], bfr[0], bfr[1]);
+        }
       }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sacc[i] += sacc2[i];
       float* sp = Sp + (size_t)kq * HR * kRowS;
       sp[(mt * 16 + r) * kRowS + nt * 8 + 2 * c] = sacc[0];
       sp[(mt * 16 + r) * kRowS + nt * 8 + 2 * c + 1] = sacc[1];

@@ -217,7 +217,7 @@ def main(argv=None) -> int:
         case = cases.variant(case, batch=args.batch)
     rows = profile(case, args.reps)
     subrow, head, rows = rows[0], rows[1:3], rows[3:]
-    for k, v in list(subrow["info"].items())[:12]:
+    for k, v in [kv for kv in subrow["info"].items() if kv[0].startswith(("mla_attend", "route", "attn_prologue:2", "moe_in:1"))]:
         print("  sub-phase", k, {kk: (round(vv, 2) if isinstance(vv, float) else vv) for kk, vv in v.items()})
     total = sum(r["us"] for r in rows)
     print(f"{case['id']}: full step {head[0]['us']:.1f} us (events), empty launch {head[1]['us']:.1f} us, "
