@@ -273,6 +273,8 @@ KK3_DEV bool stream_k_fixup(const StepArgs& a, float* part_base, int* cnt, long 
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) sum[mt][nt][i] = 0.0f;
+  // plain (non-volatile) L2 loads: the compiler may issue later warps' loads before earlier sums complete
+#pragma unroll 4
   for (long long w = first; w <= lastw; ++w) {
     const bool mine = w == gw;
     const long long wbeg = U * w / GW;
@@ -283,7 +285,7 @@ KK3_DEV bool stream_k_fixup(const StepArgs& a, float* part_base, int* cnt, long 
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          sum[mt][nt][i] += mine ? acc[mt][nt][i] : ld_cg_f32(ps + ((mt * NT + nt) * 4 + i) * 32 + lane);
+          sum[mt][nt][i] += mine ? acc[mt][nt][i] : __ldcg(ps + ((mt * NT + nt) * 4 + i) * 32 + lane);
   }
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)

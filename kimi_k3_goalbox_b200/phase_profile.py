@@ -150,7 +150,8 @@ def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[d
                     last_cta.append(int(row.argmax()))
                     rel = ((row - ts[i]).double() / 1000.0).sort().values
                     q = lambda f: round(float(rel[min(len(rel) - 1, int(f * (len(rel) - 1)))]), 2)
-                    spread.append({"p10": q(0.1), "p50": q(0.5), "p90": q(0.9), "max": q(1.0)})
+                    order = ((row - ts[i]).double()).argsort(descending=True)[:8].tolist()
+                    spread.append({"p10": q(0.1), "p50": q(0.5), "p90": q(0.9), "max": q(1.0), "latest": order})
                 else:
                     work.append(None)
                     barrier.append(None)
