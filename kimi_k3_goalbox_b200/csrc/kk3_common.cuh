@@ -82,7 +82,6 @@ struct Scratch {
   float* fix_part;    // [2 * warps_total, 16 * 64 * 2] stream-K partial tiles
   int* fix_cnt;       // [max tiles] stream-K arrival counters
   unsigned long long* argmax_key; // [B]
-  int* route_done;    // routing CTAs finished in this layer (the last one groups the pairs; it resets the count)
   float* situ_buf;    // [2 halves][tiles][32 lanes][4 * NT] bf16-rounded gate / up tiles of a situ pair
   int* situ_cnt;      // [tiles] halves of a situ pair published (the second resets it)
   unsigned* bar;      // grid barrier word (see grid_sync)
@@ -273,10 +272,18 @@ KK3_DEV bool failed(const StepArgs& a) { return ld_volatile_int(a.s.err) != 0; }
 
 // Bounded grid-wide barrier on one 32-bit word. Every CTA adds 1, except CTA 0 which adds 2^31 - (G - 1), so
 // the word advances by exactly 2^31 per barrier and its top bit flips once all G CTAs have arrived: one
-// atomic per CTA, no reset. Waiters poll the word (acquire); the error word is checked only every 64 polls
-// and the wait gives up after timeout_ns. Returns false on timeout or a reported error; the kernel unwinds.
-// When `arrive_ts` is set, each CTA stamps its arrival time (phase profiling).
-KK3_DEV bool grid_sync(const StepArgs& a, int phase = -1) {
+// atomic per CTA, no reset. The arrival is a release RMW (the CTA's writes, ordered before it by the CTA
+// barrier, become visible with it) and the waiters poll with acquire loads, so no separate fences sit on the
+// critical path. The error word is checked every 64 polls and the wait gives up after timeout_ns. Returns
+// false on timeout or a reported error; the kernel unwinds. When `arrive_ts` is set, each CTA stamps its
+// arrival time (phase profiling).
+KK3_DEV unsigned atom_add_release_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.release.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+KK3_FN bool grid_sync(const StepArgs& a, int phase = -1) {
   __shared__ int ok_flag;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -285,13 +292,12 @@ KK3_DEV bool grid_sync(const StepArgs& a, int phase = -1) {
     if (a.s.arrive_ts && phase >= 0 && phase < kArrivePhases)
       a.s.arrive_ts[(size_t)phase * gridDim.x + blockIdx.x] = globaltimer();
     const unsigned add = blockIdx.x == 0 ? 0x80000000u - (gridDim.x - 1) : 1u;
-    __threadfence();
-    const unsigned old = atomicAdd(word, add);
+    const unsigned old = atom_add_release_gpu(word, add);
     unsigned long long t0 = 0;
     for (unsigned spin = 0;; ++spin) {
       if (((old ^ ld_acquire_gpu(word)) & 0x80000000u) != 0) break;
-      // back off so that ~150 polling CTAs do not congest the L2 slice the working CTAs also use
-      if (spin >= 2) __nanosleep(spin < 16 ? 100 : 400);
+      // after ~20 us of polling (long tails), back off so the waiters do not keep the word's L2 slice busy
+      if (spin >= 32) __nanosleep(64);
       if ((spin & 63) == 63) {
         const unsigned long long t = globaltimer();
         if (t0 == 0) t0 = t;
@@ -302,7 +308,6 @@ KK3_DEV bool grid_sync(const StepArgs& a, int phase = -1) {
         }
       }
     }
-    __threadfence();
     ok_flag = ok;
   }
   __syncthreads();

@@ -713,11 +713,14 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* _
       p_scl = ph.scales[scl_mt] + e * ph.expert_scales + (size_t)(p_tile * 16 + scl_row) * sbytes + (p_ks >> 1) * 4;
   };
   int p_left = nunits, p_slot = 0;
+  // weight codes are read once per step: evict them first, so that the activations, partial tiles and the
+  // next phases' small operands stay in L2
+  const unsigned long long pol = l2_evict_first_policy();
   auto p_issue = [&]() {
     unsigned char* slot = ring + p_slot * kSlot;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-      cp_async16_g(slot + mt * kCode + p_dst_code, p_code[mt]);
+      cp_async16_stream(slot + mt * kCode + p_dst_code, p_code[mt], pol);
       p_code[mt] += 32;
     }
     if (scl_lane) cp_async4_ca(slot + p_dst_scl, p_scl);

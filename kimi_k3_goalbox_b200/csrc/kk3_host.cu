@@ -196,7 +196,7 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
       {(void**)&s.fix_part, (size_t)g.fix_bank * 2 * 4}, {(void**)&s.fix_cnt, (size_t)g.cnt_bank * 2 * 4},
       {(void**)&s.situ_buf, situ_floats * 4},
       {(void**)&s.argmax_key, B * 8}, {(void**)&bar, 64}, {(void**)&phase_count, 64}, {(void**)&s.err, 64},
-      {(void**)&s.route_done, 64}, {(void**)&s.situ_cnt, situ_tiles * 4},
+      {(void**)&s.situ_cnt, situ_tiles * 4},
       {(void**)&s.phase_ts, (kMaxPhases + 1) * 8}, {(void**)&s.arrive_ts, (size_t)kArrivePhases * 1024 * 8},
       {(void**)&s.sub_ts, (size_t)kArrivePhases * 16 * 8},
   };
@@ -260,7 +260,7 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   size_t sm_mla = mla_smem_bytes(HR);
   size_t sm_row = (512 + (size_t)(g.h > g.lh ? g.h : g.lh)) * 4 + 64;
   size_t sm_abs = ((size_t)g.B * 128 + 4 * 16 * 128) * 4;
-  size_t sm_route = ((size_t)g.B * g.K + 4 * kMaxExperts) * 4;
+  size_t sm_route = kRouteSmem;
   size_t sm_gemv = (size_t)kWarps * kGemvSmemPerWarp;   // per-warp cp.async rings of the GEMV phases
   size_t sm = sm_mla;
   sm = sm_gemv > sm ? sm_gemv : sm;
@@ -544,11 +544,11 @@ static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, Ste
   int* err_mirror = nullptr;
   struct Item { void** p; size_t bytes; };
   Item items[] = {
-      // must be zero when a step begins: barrier word, phase count, error word and its mirror, routing
-      // counter, situ pair counters, stream-K tile counters, exchange flags (the exchange buffer's flag
+      // must be zero when a step begins: barrier word, phase count, error word and its mirror, situ pair
+      // counters, stream-K tile counters, exchange flags (the exchange buffer's flag
       // array comes first; its data regions after it are written before they are read)
       {(void**)&s.bar, 64}, {(void**)&s.phase_count, 64}, {(void**)&s.err, 64}, {(void**)&err_mirror, 64},
-      {(void**)&s.route_done, 64}, {(void**)&s.situ_cnt, situ_tiles * 4},
+      {(void**)&s.situ_cnt, situ_tiles * 4},
       {(void**)&s.fix_cnt, (size_t)g.cnt_bank * 2 * 4}, {(void**)&comm, comm_bytes},
       // written before they are read within every step
       {(void**)&s.prefix, B * g.h * 2}, {(void**)&s.blocks, (size_t)g.nblk * B * g.h * 2},
@@ -583,7 +583,7 @@ static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, Ste
   size_t sm = mla_smem_bytes(HR);
   const size_t sm_row = (512 + (size_t)(g.h > g.lh ? g.h : g.lh)) * 4 + 64;
   const size_t sm_abs = ((size_t)g.B * 128 + 4 * 16 * 128) * 4;
-  const size_t sm_route = ((size_t)g.B * g.K + 4 * kMaxExperts) * 4;
+  const size_t sm_route = kRouteSmem;
   const size_t sm_gemv = (size_t)kWarps * kGemvSmemPerWarp;
   sm = sm_gemv > sm ? sm_gemv : sm;
   sm = sm_row > sm ? sm_row : sm;

@@ -24,23 +24,29 @@ KK3_FN void phase_embed(const StepArgs& a, unsigned seq, int parity, float* fsm)
   const long long* tok = gptr<long long>(a, KK3_TOKEN);
   const bf16* emb = gptr<bf16>(a, KK3_EMBED);
   long long* out_ids = gout<long long>(a, KK3_OUT_EXPERT_IDS);
+  #pragma unroll 1
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
     const long long t = tok[b] - (long long)g.rank * g.V;
     const bool mine = t >= 0 && t < g.V;
     const bf16* row = emb + (size_t)(mine ? t : 0) * g.h;
     const bf16 zero = f2bf(0.0f);
     if (g.tp == 1) {
+      #pragma unroll 1
       for (int e = threadIdx.x; e < g.h; e += kThreads) a.s.prefix[(size_t)b * g.h + e] = mine ? row[e] : zero;
     } else {
       const size_t off = ((size_t)g.rank * g.B + b) * g.h;
+      #pragma unroll 1
       for (int dst = 0; dst < g.tp; ++dst) {
         bf16* reg = reinterpret_cast<bf16*>(a.comm.base[dst] + a.comm.data_off[parity] + a.comm.att_off);
+        #pragma unroll 1
         for (int e = threadIdx.x; e < g.h; e += kThreads) reg[off + e] = mine ? row[e] : zero;
       }
       xch_signal_row(a, b, seq);
     }
     // dense layers report -1 expert ids (kimi.py:305)
+    #pragma unroll 1
     for (int l = 0; l < g.first_dense && l < g.L; ++l)
+      #pragma unroll 1
       for (int j = threadIdx.x; j < g.K; j += kThreads) out_ids[((size_t)l * g.B + b) * g.K + j] = -1;
   }
   (void)fsm;
@@ -85,6 +91,7 @@ KK3_DEV void store_row(bf16* dst, const uint4 (&v)[kRowChunks], int nvec) {
 KK3_FN bool phase_attn_prologue(const StepArgs& a, int layer, int nb, int pending, bool need_signal, unsigned seq,
                                  int parity, float* fsm, int ph = -1) {
   const Geo& g = a.g;
+  #pragma unroll 1
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
     if (b == 0 && threadIdx.x == 0) sub_stamp(a, ph, 0);
     const bool fold = pending != PEND_NONE && !(g.tp == 1 && pending == PEND_EMBED);
@@ -107,6 +114,7 @@ KK3_FN bool phase_attn_prologue(const StepArgs& a, int layer, int nb, int pendin
 // fold a pending exchange into prefix without a following norm (only when the last layer is dense)
 KK3_FN bool phase_fold_pending(const StepArgs& a, int pending, bool need_signal, unsigned seq, int parity) {
   const Geo& g = a.g;
+  #pragma unroll 1
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
     if (g.tp > 1) {
       if (need_signal) xch_signal_row(a, b, seq);
@@ -122,6 +130,7 @@ KK3_FN bool phase_fold_pending(const StepArgs& a, int pending, bool need_signal,
 // attention exchange -> prefix (assign right after a block push, else add), then the MLP prologue
 KK3_FN bool phase_mlp_prologue(const StepArgs& a, int layer, int nb_after, unsigned seq, int parity, float* fsm) {
   const Geo& g = a.g;
+  #pragma unroll 1
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
     if (g.tp > 1) {
       xch_signal_row(a, b, seq);
@@ -144,9 +153,11 @@ KK3_FN void phase_mla_rows(const StepArgs& a, int layer, int midx, float* fsm) {
   const bf16* ka = a.s.qkv + (size_t)g.B * g.qr;
   bf16* kvw = gout<bf16>(a, KK3_OUT_KV_WRITE) + (size_t)midx * g.B * g.kr;
   bf16* pew = gout<bf16>(a, KK3_OUT_PE_WRITE) + (size_t)midx * g.B * g.rd;
+  #pragma unroll 1
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
     rms_row(qa + (size_t)b * g.qr, lptr<bf16>(a, layer, KK3_MLA_QN), g.qr, 1e-6f, a.s.mla_qan + (size_t)b * g.qr, fsm);
     rms_row(ka + (size_t)b * (g.kr + g.rd), lptr<bf16>(a, layer, KK3_MLA_KN), g.kr, 1e-6f, kvw + (size_t)b * g.kr, fsm);
+    #pragma unroll 1
     for (int e = threadIdx.x; e < g.rd; e += kThreads) pew[(size_t)b * g.rd + e] = ka[(size_t)b * (g.kr + g.rd) + g.kr + e];
     __syncthreads();
   }
@@ -158,6 +169,7 @@ KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int pa
   const Geo& g = a.g;
   float* red = fsm;
   const int nvec = g.lh / 8, hvec = g.h / 8;
+  #pragma unroll 1
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
     const float* w = a.s.route_w + (size_t)b * g.K;
     float tot[kRowChunks][8];
@@ -169,6 +181,7 @@ KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int pa
       if (c >= nvec) continue;
       // 8 slots' loads in flight at a time (L2), summed in slot order
       const uint4* slot0 = reinterpret_cast<const uint4*>(a.s.out_slot + (size_t)b * g.K * g.lh) + c;
+      #pragma unroll 1
       for (int j0 = 0; j0 < g.K; j0 += 8) {
         uint4 v[8];
         float wj[8];
@@ -193,6 +206,7 @@ KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int pa
     }
     if (g.tp > 1) {
       const size_t off = ((size_t)g.rank * g.B + b) * g.lh;
+      #pragma unroll 1
       for (int dst = 0; dst < g.tp; ++dst) {
         float* reg = reinterpret_cast<float*>(a.comm.base[dst] + a.comm.data_off[parity] + a.comm.exp_off) + off;
 #pragma unroll
@@ -212,6 +226,7 @@ KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int pa
         if (c >= nvec) continue;
 #pragma unroll
         for (int e = 0; e < 8; ++e) tot[q][e] = 0.0f;
+        #pragma unroll 1
         for (int src = 0; src < g.tp; ++src) {
           const float* r = reg + ((size_t)src * g.B + b) * g.lh + c * 8;
           const float4 v0 = *reinterpret_cast<const float4*>(r), v1 = *reinterpret_cast<const float4*>(r + 4);
@@ -257,6 +272,7 @@ KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int pa
 
 KK3_FN void phase_head_prologue(const StepArgs& a, int nb, float* fsm) {
   const Geo& g = a.g;
+  #pragma unroll 1
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
     uint4 pre[kRowChunks];
     load_prefix(a, b, 0, false, 0, pre);
@@ -273,6 +289,7 @@ KK3_FN bool phase_argmax(const StepArgs& a, unsigned seq, int parity) {
   long long* len = gout<long long>(a, KK3_OUT_CACHE_LENGTH);
   const bool* reset = gptr<bool>(a, KK3_RESET);
   __shared__ unsigned long long best;
+  #pragma unroll 1
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
     if (threadIdx.x == 0) best = *reinterpret_cast<volatile unsigned long long*>(a.s.argmax_key + b);
     __syncthreads();
@@ -288,6 +305,7 @@ KK3_FN bool phase_argmax(const StepArgs& a, unsigned seq, int parity) {
       if (threadIdx.x == 0) {
         const unsigned long long* reg = xlocal<unsigned long long>(a, parity, a.comm.key_off);
         unsigned long long m = 0ull;
+        #pragma unroll 1
         for (int src = 0; src < g.tp; ++src) {
           const unsigned long long k = reg[(size_t)src * g.B + b];
           m = k > m ? k : m;
@@ -435,6 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   KK3_PHASE_END();
 
   int nb = 0, kidx = 0, midx = 0;
+  #pragma unroll 1
   for (int l = 0; l < g.L; ++l) {
     const bool mla = layer_is_mla(g, l);
     // attention prologue (kimi.py:257-262)
@@ -451,6 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
       // short conv + gated delta rule (kimi.py:286-299); then prefetch the o projection into L2
       if (KK3_RUN) {
         KK3_BUILD(o_job(a, l, sj2[0]));
+        #pragma unroll 1
         for (int it = blockIdx.x; it < g.B * g.hr; it += gridDim.x) kda_item(a, l, kidx, it / g.hr, it % g.hr, fsm);
         prefetch_jobs(sj2, 1);
       }
@@ -471,13 +491,16 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
       KK3_PHASE_END();
       // absorbed query (kimi.py:271-272)
       if (KK3_RUN)
+        #pragma unroll 1
         for (int it = blockIdx.x; it < g.hr * 4; it += gridDim.x) mla_absorb_item(a, l, it / 4, it % 4, fsm);
       KK3_PHASE_END();
       // split-K attention over [cache, new token] (kimi.py:274-280)
       if (KK3_RUN) {
         const bool* reset = gptr<bool>(a, KK3_RESET);
         int total = 0;
+        #pragma unroll 1
         for (int b = 0; b < g.B; ++b) total += reset[b] ? 1 : g.mla_chunks;
+        #pragma unroll 1
         for (int it = blockIdx.x; it < total; it += gridDim.x) {
           int b = 0, rem = it;
           for (; b < g.B; ++b) {
@@ -502,6 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
       KK3_PHASE_END();
       if (KK3_RUN) {
         KK3_BUILD(o_job(a, l, sj2[0]));
+        #pragma unroll 1
         for (int it = blockIdx.x; it < g.B * g.hr; it += gridDim.x) mla_combine_item(a, l, it / g.hr, it % g.hr, fsm);
         prefetch_jobs(sj2, 1);
       }
@@ -546,24 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         run_gemv<NT, 1>(a, sj, sjn, 0, gridDim.x, 0, 0, phase);
       }
       KK3_PHASE_END();
-      // routing of row b on CTA b while the other CTAs run the shared-expert down projection (kimi.py:309-316,
-      // :326)
       const unsigned x_moe = xi++;
-      if (KK3_RUN) {
-        KK3_BUILD({
-          job_init(sj[0], lptr<bf16>(a, l, KK3_MOE_SHARED_DOWN), g.h, g.sinter, a.s.shared_act, g.sinter, g.B,
-                   EPI_EXCHANGE, nullptr, g.h);
-          sj[0].aux_off = a.comm.shd_off;
-          prepare_jobs(sj, 1);
-        });
-        if ((int)blockIdx.x < g.B) {
-          route_row(a, l, blockIdx.x, smem, phase);
-        } else {
-          run_gemv<NT, 1>(a, sj, 1, g.B, gridDim.x, x_moe & 1);
-          if (g.tp > 1) __threadfence_system();
-        }
-      }
-      KK3_PHASE_END();
       // routed experts (kimi.py:317-323); descriptor built once per CTA in shared memory
       if (KK3_RUN) {
         KK3_BUILD({
@@ -574,6 +581,8 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
           sph.rows = g.inter; sph.K = g.lh; sph.tiles = g.inter / 16; sph.ksteps = g.lh / 64;
           sph.expert_codes = (long long)g.inter * g.lh / 2; sph.expert_scales = (long long)g.inter * g.lh / 32;
         });
+        // every CTA routes all rows (identical tables), then the experts start (kimi.py:309-316)
+        route_cta(a, l, smem, phase);
         run_experts<2>(a, sph, e8m0_lut);
       }
       KK3_PHASE_END();
@@ -583,7 +592,15 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
           sph.scales[0] = sph.scales[1] = lptr<uint8_t>(a, l, KK3_MOE_DOWN_SCALES);
           sph.rows = g.lh; sph.K = g.inter; sph.tiles = g.lh / 16; sph.ksteps = g.inter / 64;
           sph.expert_codes = (long long)g.lh * g.inter / 2; sph.expert_scales = (long long)g.lh * g.inter / 32;
+          job_init(sj[0], lptr<bf16>(a, l, KK3_MOE_SHARED_DOWN), g.h, g.sinter, a.s.shared_act, g.sinter, g.B,
+                   EPI_EXCHANGE, nullptr, g.h);
+          sj[0].aux_off = a.comm.shd_off;
+          prepare_jobs(sj, 1);
         });
+        // the shared expert's down projection first (kimi.py:326), then the routed experts' (:320-323); the
+        // routed experts' fix-up uses counter bank 0, so this one takes bank 1
+        run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, x_moe & 1, 1);
+        if (g.tp > 1) __threadfence_system();
         run_experts<1>(a, sph, e8m0_lut);
       }
       KK3_PHASE_END();

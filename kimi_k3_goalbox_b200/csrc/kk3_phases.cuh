@@ -123,6 +123,7 @@ KK3_FN void mix_and_norm_regs(const StepArgs& a, int b, int nb, const uint4 (&pr
     // thread reads back only its own chunks, so no CTA barrier is needed); the statistics and the mix then
     // read shared memory instead of issuing dependent L2 loads block after block
     uint4* stage = reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(red) + kRowStageOff);
+#pragma unroll 1
     for (int i = 0; i < nb; ++i) {
 #pragma unroll
       for (int q = 0; q < kRowChunks; ++q) {
@@ -180,6 +181,7 @@ KK3_FN void mix_and_norm_regs(const StepArgs& a, int b, int nb, const uint4 (&pr
     __syncthreads();
     if (tid < 2 * (nb + 1)) {
       float t = 0.0f;
+#pragma unroll 1
       for (int w = 0; w < kWarps; ++w) t += wred[w * kSt + tid];
       tot[tid] = t;
     }
@@ -187,8 +189,10 @@ KK3_FN void mix_and_norm_regs(const StepArgs& a, int b, int nb, const uint4 (&pr
     if (stamp) sub_stamp(a, ph, 2);
     // softmax over the nb + 1 logits rms(v_i) . (norm * proj), then the weighted sum
     float mx = -INFINITY;
+#pragma unroll 1
     for (int i = 0; i <= nb; ++i) mx = fmaxf(mx, tot[2 * i + 1] * rsqrtf(tot[2 * i] / (float)g.h + 1e-5f));
     float den = 0.0f;
+#pragma unroll 1
     for (int i = 0; i <= nb; ++i) den += expf(tot[2 * i + 1] * rsqrtf(tot[2 * i] / (float)g.h + 1e-5f) - mx);
     float accv[kRowChunks][8];
 #pragma unroll
@@ -496,6 +500,7 @@ struct MlaSrc {
   const bf16* pew;   // new token's rope row (pe_write)
   int ncache;        // cached positions attended (ctx for a kept row, 0 after a reset)
   int kr, rd;
+  unsigned long long pol;   // L2 evict_first: the cache is read once per step
 };
 
 constexpr int kMlaPieces = kMlaPos * 72;                       // 16-byte pieces of one 32-position sub-tile
@@ -509,7 +514,8 @@ KK3_DEV void mla_stage(const MlaSrc& src, int t0, int T, bf16* dst) {
     const int tl = i / 72, q = i - (i / 72) * 72, t = t0 + tl;
     bf16* d = dst + tl * kRowK + q * 8;
     if (t < src.ncache) {
-      cp_async16(d, q < 64 ? src.kv + (size_t)t * src.kr + q * 8 : src.pe + (size_t)t * src.rd + (q - 64) * 8);
+      cp_async16_stream(d, q < 64 ? src.kv + (size_t)t * src.kr + q * 8 : src.pe + (size_t)t * src.rd + (q - 64) * 8,
+                        src.pol);
     } else if (t < T) {
       *reinterpret_cast<uint4*>(d) = ld_act16(q < 64 ? src.kvw + q * 8 : src.pew + (q - 64) * 8);
     } else {
@@ -548,6 +554,7 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
   src.kvw = gout<bf16>(a, KK3_OUT_KV_WRITE) + ((size_t)midx * g.B + b) * g.kr;
   src.pew = gout<bf16>(a, KK3_OUT_PE_WRITE) + ((size_t)midx * g.B + b) * g.rd;
   src.ncache = reinterpret_cast<const bool*>(a.ptr[KK3_RESET])[b] ? 0 : g.ctx;
+  src.pol = l2_evict_first_policy();
   src.kr = g.kr;
   src.rd = g.rd;
   // Q rows: absorbed (512) | q rope (64), copied asynchronously in the group of the first sub-tile; zero for
@@ -748,196 +755,223 @@ KK3_FN void mla_combine_item(const StepArgs& a, int layer, int b, int hh, float*
 }
 
 // ------------------------------------------------------------------------------------------------
-// Routing (kimi.py:308-316). Batch row b is routed by CTA b: FP32 sigmoid scores + bias, top-k with the
-// lowest index winning ties, weights renormalised over the unbiased scores, ids sorted ascending. Each of
-// the 16 warps selects the top-k of its 64 experts; warp 0 then selects the top-k of those 16*k candidates.
-// Exact: an expert dropped inside its warp has k better experts (under the order value desc, index asc) in
-// that warp alone. The last routing CTA to finish groups every row's (row, slot) pairs by expert into chunks
-// of <= 8 pairs for the MXFP4 phases, so no extra grid barrier is needed.
+// Routing (kimi.py:308-316), done by every CTA at the start of the expert gate/up phase: warp w routes batch
+// rows w, w + 16, ... (sigmoid scores + bias held 32 per lane, top-k with the lowest index winning ties,
+// weights renormalised over the unbiased scores, ids sorted ascending), then the CTA groups the (row, slot)
+// pairs by expert into chunks of <= 8 pairs for the MXFP4 phases. Every CTA computes the same tables and
+// writes them (identical values), so the experts start without a grid barrier of their own.
 
-// better(v, e) than (bv, bi): larger value, equal value and lower index. NaN never wins.
-KK3_DEV bool route_better(float v, int e, float bv, int bi) { return v > bv || (v == bv && e < bi); }
+// shared memory of the routing step: the selected ids [kMaxBatch * kMaxTopk] at 0; the grouping's per-expert
+// row masks and offsets and its scan totals after them (< 32 KB); then each warp's keys, lane-major with a
+// padded stride (conflict-free 16-byte reads), and the router bias
+constexpr int kRouteStride = 36;   // u32 words per lane: up to 32 keys (E <= 1024) plus padding
+constexpr size_t kRouteKeyOff = 32 * 1024;
+constexpr size_t kRouteBiasOff = kRouteKeyOff + (size_t)kWarps * 32 * kRouteStride * 4;
+constexpr size_t kRouteSmem = kRouteBiasOff + (size_t)kMaxExperts * 4;
+static_assert((size_t)kMaxBatch * kMaxTopk * 4 + (size_t)kMaxExperts * 16 + 2 * kWarps * 4 <= kRouteKeyOff,
+              "routing tables overlap the keys");
 
+KK3_DEV unsigned warp_excl_scan(unsigned v) {
+  const int lane = threadIdx.x & 31;
+  unsigned x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned t = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += t;
+  }
+  return x - v;
+}
+
+// group the pairs whose expert ids are in smem[0, B*K) by expert and write the pair and chunk tables. Every
+// CTA writes these tables, so the order must not depend on thread timing: a row holds an expert at most once,
+// so the pairs of expert e are placed in batch-row order through a 64-bit mask of the rows that chose e.
 KK3_DEV void route_group_pairs(const StepArgs& a, unsigned char* smem) {
   const Geo& g = a.g;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int npairs = g.B * g.K;
-  int* ids = reinterpret_cast<int*>(smem);            // [B*K]
-  int* cnt = ids + kMaxBatch * kMaxTopk;               // [E]
-  int* off = cnt + kMaxExperts;                        // [E]
-  int* fill = off + kMaxExperts;                       // [E]
-  int* coff = fill + kMaxExperts;                      // [E] chunk offsets
-  for (int e = tid; e < g.E; e += kThreads) {
-    cnt[e] = 0;
-    fill[e] = 0;
-  }
-  // other CTAs wrote these ids: read through L2
-  for (int i = tid; i < npairs; i += kThreads) {
-    int e = __ldcg(a.s.route_ids + i);
-    ids[i] = e < 0 ? 0 : (e >= g.E ? g.E - 1 : e);
-  }
+  const int K = g.K;   // <= 32: pair (b, j) is handled by lane j of a warp
+  const int* ids = reinterpret_cast<const int*>(smem);                                     // [B*K]
+  unsigned long long* rows = reinterpret_cast<unsigned long long*>(smem + kMaxBatch * kMaxTopk * 4);   // [E]
+  int* off = reinterpret_cast<int*>(rows + kMaxExperts);   // [E] first pair of each expert
+  int* coff = off + kMaxExperts;                           // [E] first chunk of each expert
+  int* wtot = coff + kMaxExperts;                          // [2][kWarps]
+  // cold code (once per layer): compact loops, no divisions
+#pragma unroll 1
+  for (int e = tid; e < g.E; e += kThreads) rows[e] = 0ull;
   __syncthreads();
-  for (int i = tid; i < npairs; i += kThreads) atomicAdd(&cnt[ids[i]], 1);
+#pragma unroll 1
+  for (int b = warp; b < g.B; b += kWarps)
+    if (lane < K) atomicOr(&rows[ids[b * K + lane]], 1ull << b);
   __syncthreads();
   // exclusive scans over experts of pair counts and chunk counts: warp w scans experts [64w, 64w + 64)
   // (two per lane), then the warp totals are scanned (E <= 1024 = kWarps * 64)
   {
-    int* wtot = coff + kMaxExperts;   // [2][kWarps]
     const int ea = warp * 64 + 2 * lane, eb = ea + 1;
-    const int na = ea < g.E ? cnt[ea] : 0, nb = eb < g.E ? cnt[eb] : 0;
-    const int ca = (na + 7) / 8, cb = (nb + 7) / 8;
-    int incl = na + nb, cincl = ca + cb;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t1 = __shfl_up_sync(0xffffffffu, incl, o);
-      const int t2 = __shfl_up_sync(0xffffffffu, cincl, o);
-      if (lane >= o) {
-        incl += t1;
-        cincl += t2;
-      }
-    }
+    const int na = ea < g.E ? __popcll(rows[ea]) : 0, nb = eb < g.E ? __popcll(rows[eb]) : 0;
+    const int ca = (na + 7) >> 3, cb = (nb + 7) >> 3;
+    const int pa = warp_excl_scan((unsigned)(na + nb)), pc = warp_excl_scan((unsigned)(ca + cb));
     if (lane == 31) {
-      wtot[warp] = incl;
-      wtot[kWarps + warp] = cincl;
+      wtot[warp] = pa + na + nb;
+      wtot[kWarps + warp] = pc + ca + cb;
     }
     __syncthreads();
-    int base = 0, cbase = 0;
-    for (int w = 0; w < warp; ++w) {
-      base += wtot[w];
-      cbase += wtot[kWarps + w];
+    int base = 0, cbase = 0, ctotal = 0;
+#pragma unroll 1
+    for (int w = 0; w < kWarps; ++w) {
+      base += w < warp ? wtot[w] : 0;
+      cbase += w < warp ? wtot[kWarps + w] : 0;
+      ctotal += wtot[kWarps + w];
     }
-    const int exa = base + incl - (na + nb), cxa = cbase + cincl - (ca + cb);
     if (ea < g.E) {
-      off[ea] = exa;
-      coff[ea] = cxa;
+      off[ea] = base + pa;
+      coff[ea] = cbase + pc;
     }
     if (eb < g.E) {
-      off[eb] = exa + na;
-      coff[eb] = cxa + ca;
+      off[eb] = base + pa + na;
+      coff[eb] = cbase + pc + ca;
     }
-    if (tid == 0) {
-      int t = 0;
-      for (int w = 0; w < kWarps; ++w) t += wtot[kWarps + w];
-      a.s.chunk_info[0] = t;
-    }
+    if (tid == 0) a.s.chunk_info[0] = ctotal;
   }
   __syncthreads();
-  for (int i = tid; i < npairs; i += kThreads) {
-    const int e = ids[i];
-    const int pos = off[e] + atomicAdd(&fill[e], 1);
-    a.s.pair_row[pos] = i / g.K;
-    a.s.pair_slot[pos] = i % g.K;
+#pragma unroll 1
+  for (int b = warp; b < g.B; b += kWarps) {
+    if (lane < K) {
+      const int e = ids[b * K + lane];
+      const int pos = off[e] + __popcll(rows[e] & ((1ull << b) - 1ull));
+      a.s.pair_row[pos] = b;
+      a.s.pair_slot[pos] = lane;
+    }
   }
+#pragma unroll 1
   for (int e = tid; e < g.E; e += kThreads) {
-    const int n = cnt[e];
+    const int n = __popcll(rows[e]);
+#pragma unroll 1
     for (int q = 0; q * 8 < n; ++q) {
-      const int ci = coff[e] + q;
-      a.s.chunk_info[1 + ci * 3] = e;
-      a.s.chunk_info[2 + ci * 3] = off[e] + q * 8;
-      a.s.chunk_info[3 + ci * 3] = (n - q * 8) < 8 ? (n - q * 8) : 8;
+      int* ci = a.s.chunk_info + 1 + (coff[e] + q) * 3;
+      ci[0] = e;
+      ci[1] = off[e] + q * 8;
+      ci[2] = n - q * 8 < 8 ? n - q * 8 : 8;
     }
   }
 }
 
-KK3_FN void route_row(const StepArgs& a, int layer, int b, unsigned char* smem, int ph = -1) {
+// order-preserving 32-bit key of a routing value (a larger value has a larger key). NaN counts as -inf and
+// -0 is keyed as +0, so values that compare equal have equal keys; absent entries get key 0, below them all.
+KK3_DEV unsigned route_key(float x) {
+  x = x != x ? -INFINITY : x;
+  x = x == 0.0f ? 0.0f : x;
+  const unsigned u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+
+// Warp w routes batch rows w, w + 16, ...; lane l holds the keys of experts [l * n, l * n + n) (n = E / 32
+// rounded up) in shared memory, staged with cp.async. The K-th largest key T is found by bisection from the
+// top bit with warp-wide counts (stopping as soon as exactly K keys are >= the probe). Every expert above T is
+// taken, and of those equal to T the lowest indices (torch.topk's order as the reference uses it: value
+// descending, then index ascending); lane-order prefix sums place the ids in ascending order. This code runs
+// once per layer from a cold instruction cache, so its loops are kept compact.
+KK3_FN void route_cta(const StepArgs& a, int layer, unsigned char* smem, int ph = -1) {
   const Geo& g = a.g;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int K = g.K;
-  float* cval = reinterpret_cast<float*>(smem);                    // [kWarps][kMaxTopk]
-  int* cidx = reinterpret_cast<int*>(cval + kWarps * kMaxTopk);   // [kWarps][kMaxTopk]
-  __shared__ int s_last;
-  const float* sc = a.s.scores + (size_t)b * g.E;
+  const int K = g.K, E = g.E;
+  constexpr unsigned kFull = 0xffffffffu;
+  const int nper = (E + 31) >> 5, nq = (nper + 3) >> 2, e0 = lane * nper;
+  int* ids = reinterpret_cast<int*>(smem);   // [B*K] sorted per row
+  float* bias_s = reinterpret_cast<float*>(smem + kRouteBiasOff);
+  unsigned* wk = reinterpret_cast<unsigned*>(smem + kRouteKeyOff) + ((size_t)warp * 32 + lane) * kRouteStride;
+  const uint4* wk4 = reinterpret_cast<const uint4*>(wk);
   const float* bias = lptr<float>(a, layer, KK3_MOE_ROUTER_BIAS);
-  const float kNaN = __int_as_float(0x7fc00000);
-  // this warp's experts: NaN scores count as -inf; missing or taken entries are NaN (never win)
-  const int e0 = warp * 64 + lane, e1 = e0 + 32;
-  float v0 = kNaN, v1 = kNaN;
-  if (e0 < g.E) {
-    const float x = __ldcg(sc + e0) + bias[e0];
-    v0 = x != x ? -INFINITY : x;
-  }
-  if (e1 < g.E) {
-    const float x = __ldcg(sc + e1) + bias[e1];
-    v1 = x != x ? -INFINITY : x;
-  }
-  for (int j = 0; j < K; ++j) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    if (route_better(v0, e0, bv, bi)) { bv = v0; bi = e0; }
-    if (route_better(v1, e1, bv, bi)) { bv = v1; bi = e1; }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (route_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
-    }
-    if (bi == e0) v0 = kNaN;
-    if (bi == e1) v1 = kNaN;
-    if (lane == 0) {
-      cval[warp * kMaxTopk + j] = bi == 0x7fffffff ? kNaN : bv;
-      cidx[warp * kMaxTopk + j] = bi;
-    }
-  }
+  long long* out_ids = gout<long long>(a, KK3_OUT_EXPERT_IDS) + (size_t)layer * g.B * K;
+  const bool stamp = ph >= 0 && blockIdx.x == 0 && tid == 0;
+  auto stage_row = [&](int b) {
+    const float* sc = a.s.scores + (size_t)b * E + e0;
+#pragma unroll 1
+    for (int i = 0; i < nper; ++i)
+      if (e0 + i < E) cp_async4_ca(wk + i, sc + i);
+  };
+#pragma unroll 1
+  for (int e = tid; e < E; e += kThreads) cp_async4_ca(bias_s + e, bias + e);
+  if (warp < g.B) stage_row(warp);
+  cp_async_commit();
+  cp_async_wait_all();
   __syncthreads();
-  if (b == 0 && tid == 0) sub_stamp(a, ph, 12);
-  if (warp == 0) {
-    // each warp's candidates are already in selection order: merge the kWarps sorted lists head to head;
-    // lane w < kWarps holds the head of list w, lane j < K keeps the j-th selected expert
-    int head = 0;
-    float hv = kNaN;
-    int hi = 0x7fffffff;
-    if (lane < kWarps) {
-      hv = cval[lane * kMaxTopk];
-      hi = cidx[lane * kMaxTopk];
+#pragma unroll 1
+  for (int b = warp; b < g.B; b += kWarps) {
+    if (b != warp) {
+      stage_row(b);
+      cp_async_commit();
+      cp_async_wait_all();
     }
-    int mine = -1;
-    for (int j = 0; j < K; ++j) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-      if (route_better(hv, hi, bv, bi)) { bv = hv; bi = hi; }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (route_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    // keys in place; absent experts and padding get key 0, below every real key
+#pragma unroll 1
+    for (int i = 0; i < nq * 4; ++i)
+      wk[i] = (i < nper && e0 + i < E) ? route_key(__uint_as_float(wk[i]) + bias_s[e0 + i]) : 0u;
+    unsigned T = 0u;
+#pragma unroll 1
+    for (int bit = 31; bit >= 0; --bit) {
+      const unsigned probe = T | (1u << bit);
+      unsigned n = 0;
+#pragma unroll 1
+      for (int q = 0; q < nq; ++q) {
+        {
+          const uint4 v = wk4[q];
+          n += (v.x >= probe ? 1u : 0u) + (v.y >= probe ? 1u : 0u) + (v.z >= probe ? 1u : 0u) + (v.w >= probe ? 1u : 0u);
+        }
       }
-      if (lane == j) mine = bi;
-      if (lane < kWarps && hi == bi) {
-        ++head;
-        hv = head < K ? cval[lane * kMaxTopk + head] : kNaN;
-        hi = head < K ? cidx[lane * kMaxTopk + head] : 0x7fffffff;
+      n = __reduce_add_sync(kFull, n);
+      if (n >= (unsigned)K) {
+        T = probe;
+        if (n == (unsigned)K) break;
       }
     }
-    // sort the K ids ascending: rank of each
-    int rank = 0;
-    for (int j = 0; j < K; ++j) {
-      const int other = __shfl_sync(0xffffffffu, mine, j);
-      if (lane < K && other < mine) ++rank;
+    if (stamp && b == 0) sub_stamp(a, ph, 12);
+    // take every key above T and, in index order, the first K - #(above) keys equal to T
+    unsigned gt = 0, eq = 0;
+#pragma unroll 1
+    for (int q = 0; q < nq; ++q) {
+      {
+        const uint4 v = wk4[q];
+        gt += (v.x > T ? 1u : 0u) + (v.y > T ? 1u : 0u) + (v.z > T ? 1u : 0u) + (v.w > T ? 1u : 0u);
+        eq += (v.x == T ? 1u : 0u) + (v.y == T ? 1u : 0u) + (v.z == T ? 1u : 0u) + (v.w == T ? 1u : 0u);
+      }
     }
-    const int safe = mine < 0 ? 0 : (mine >= g.E ? g.E - 1 : mine);
-    const float w = lane < K ? __ldcg(sc + safe) : 0.0f;
+    const unsigned need = (unsigned)K - __reduce_add_sync(kFull, gt);
+    const unsigned tie0 = warp_excl_scan(eq);
+    unsigned ties = tie0 < need ? (need - tie0 < eq ? need - tie0 : eq) : 0u;   // ties this lane takes
+    unsigned pos = warp_excl_scan(gt + ties);
+    int* row_ids = ids + b * K;
+#pragma unroll 1
+    for (int i = 0; i < nper; ++i) {
+      const unsigned k = wk[i];
+      bool take = k > T;
+      if (k == T && ties > 0) {
+        take = true;
+        --ties;
+      }
+      if (take) {
+        if (pos < (unsigned)K) row_ids[pos] = e0 + i;
+        ++pos;
+      }
+    }
+    __syncwarp();
+    if (stamp && b == 0) sub_stamp(a, ph, 13);
+    int e = lane < K ? row_ids[lane] : 0;
+    e = e < 0 ? 0 : (e >= E ? E - 1 : e);
+    const float w = lane < K ? __ldcg(a.s.scores + (size_t)b * E + e) : 0.0f;
     const float wsum = warp_sum(w);
     if (lane < K) {
-      long long* out_ids = gout<long long>(a, KK3_OUT_EXPERT_IDS) + (size_t)layer * g.B * K;
-      a.s.route_ids[b * K + rank] = safe;
-      a.s.route_w[b * K + rank] = w / (wsum + 1e-20f);
-      out_ids[(size_t)b * K + rank] = (long long)safe;
+      row_ids[lane] = e;
+      a.s.route_ids[b * K + lane] = e;
+      a.s.route_w[b * K + lane] = w / (wsum + 1e-20f);
+      out_ids[(size_t)b * K + lane] = (long long)e;
     }
+    __syncwarp();
   }
-  // the last routing CTA to finish groups the pairs of every row
-  __threadfence();
   __syncthreads();
-  if (tid == 0) s_last = atomicAdd(a.s.route_done, 1) == g.B - 1;
-  __syncthreads();
-  if (b == 0 && tid == 0) sub_stamp(a, ph, 13);
-  if (!s_last) return;
-  __threadfence();
-  if (tid == 0) sub_stamp(a, ph, 14);
+  if (stamp) sub_stamp(a, ph, 14);
   route_group_pairs(a, smem);
-  if (tid == 0) sub_stamp(a, ph, 15);
-  __threadfence();
   __syncthreads();
-  if (tid == 0) atomicExch(a.s.route_done, 0);
+  if (stamp) sub_stamp(a, ph, 15);
 }
 
 }  // namespace kk3

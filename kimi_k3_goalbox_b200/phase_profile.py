@@ -40,7 +40,7 @@ def phase_program(params: dict) -> list[tuple[str, int]]:
         if l < fd:
             prog += [("dense_gate_up", l), ("dense_down", l)]
         else:
-            prog += [("moe_in", l), ("route", l), ("experts_gate_up", l), ("experts_down", l), ("moe_combine", l),
+            prog += [("moe_in", l), ("experts_gate_up", l), ("experts_down", l), ("moe_combine", l),
                      ("latent_up", l)]
     if L <= fd:
         prog.append(("fold", -1))
@@ -85,12 +85,10 @@ def phase_bytes(case: dict, distinct_experts: float | None = None) -> list[int]:
             b = 2 * h * di
         elif name == "moe_in":
             b = 2 * h * (E + lh + 2 * sh)
-        elif name == "route":
-            b = 2 * h * sh
         elif name == "experts_gate_up":
             b = int(dist * 2 * fp4(inter, lh))
         elif name == "experts_down":
-            b = int(dist * fp4(lh, inter))
+            b = 2 * h * sh + int(dist * fp4(lh, inter))
         elif name == "latent_up":
             b = 2 * h * lh
         elif name == "lm_head":
@@ -177,9 +175,10 @@ def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[d
                 ["start", "q_ready", "t0_data", "t0_scores", "t0_softmax", "t0_pv", "t1_data", "t1_scores",
                  "t1_softmax", "t1_pv", "item_end"]) if st[i]} | {"subtiles": st[11],
                                                                   "phase_end": (ts[i + 1] - base) / 1e3}
-        if name == "route" and st[12]:
-            subinfo[f"{name}:{layer}"] = {"cta0_candidates": (st[12] - base) / 1e3, "cta0_done": (st[13] - base) / 1e3,
-                                          "group_start": (st[14] - base) / 1e3, "group_end": (st[15] - base) / 1e3,
+        if name == "experts_gate_up" and st[15]:
+            subinfo[f"{name}:{layer}"] = {"mark": (st[11] - base) / 1e3 if st[11] else None,
+                                          "warp0_threshold": (st[12] - base) / 1e3, "warp0_row": (st[13] - base) / 1e3,
+                                          "all_rows": (st[14] - base) / 1e3, "grouped": (st[15] - base) / 1e3,
                                           "phase_end": (ts[i + 1] - base) / 1e3}
         if name in ("kda_proj", "mla_proj", "moe_in") and st[8]:
             subinfo[f"{name}:{layer}"] = {"warp0_start": (st[8] - base) / 1e3, "first_data": (st[9] - base) / 1e3,
@@ -218,7 +217,7 @@ def main(argv=None) -> int:
         case = cases.variant(case, batch=args.batch)
     rows = profile(case, args.reps)
     subrow, head, rows = rows[0], rows[1:3], rows[3:]
-    for k, v in [kv for kv in subrow["info"].items() if kv[0].startswith(("mla_attend", "route", "attn_prologue:2", "moe_in:1"))]:
+    for k, v in [kv for kv in subrow["info"].items() if kv[0].startswith(("mla_attend", "experts_gate_up", "attn_prologue:2", "moe_in:1"))]:
         print("  sub-phase", k, {kk: (round(vv, 2) if isinstance(vv, float) else vv) for kk, vv in v.items()})
     total = sum(r["us"] for r in rows)
     print(f"{case['id']}: full step {head[0]['us']:.1f} us (events), empty launch {head[1]['us']:.1f} us, "

@@ -104,7 +104,7 @@ def test_phase_program_shape():
     prog = gh.phase_program(p)
     assert prog[0] == ("embed", -1) and prog[-1] == ("argmax", -1)
     # 5 layers: layer 0 KDA+dense, 1-2 KDA+MoE, 3-4 MLA+MoE
-    per_layer = {0: 1 + 2 + 2 + 2, 1: 1 + 2 + 2 + 6, 2: 1 + 2 + 2 + 6, 3: 1 + 6 + 2 + 6, 4: 1 + 6 + 2 + 6}
+    per_layer = {0: 1 + 2 + 2 + 2, 1: 1 + 2 + 2 + 5, 2: 1 + 2 + 2 + 5, 3: 1 + 6 + 2 + 5, 4: 1 + 6 + 2 + 5}
     assert len(prog) == 1 + sum(per_layer.values()) + 3
 
 
