@@ -160,6 +160,7 @@ enum kk3_debug_buffer_id {
     KK3_BUF_PHASE_TS, /* u64 globaltimer (ns) at kernel start and at the end of every grid phase */
     KK3_BUF_ARRIVE_TS, /* u64 [256 phases][grid] barrier arrival time of every CTA */
     KK3_BUF_SUB_TS,    /* u64 [256 phases][16] sub-phase stamps of one CTA or warp */
+    KK3_BUF_WARP_TS,   /* u64 [256 phases][grid][16 warps] time each GEMV / expert engine warp finished */
     KK3_BUF_COUNT
 };
 int kk3_debug_buffer(kk3_ctx* ctx, int id, void** ptr, size_t* bytes);

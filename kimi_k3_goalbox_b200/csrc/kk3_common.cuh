@@ -90,6 +90,7 @@ struct Scratch {
   int* phase_count;   // number of grid phases of the last complete step
   unsigned long long* phase_ts;  // [kMaxPhases + 1] globaltimer at kernel start and at the end of each phase
   unsigned long long* arrive_ts; // [kArrivePhases][grid] barrier arrival time of every CTA (profiling)
+  unsigned long long* warp_ts;   // [kArrivePhases][grid][kWarps] time each engine warp finished (profiling)
   unsigned long long* sub_ts;    // [kArrivePhases][16] sub-phase stamps of one CTA / warp (profiling)
   int* trace_host;    // mapped host memory [2][1024]: per-CTA phase and progress, readable after a fault
 };
@@ -241,6 +242,18 @@ KK3_DEV void trace_progress(const StepArgs& a, int which, int value) {
     __threadfence_system();
   }
 }
+// the grid phase this CTA is in, for the engines' profiling stamps (set at kernel start and by grid_sync)
+static __shared__ int kk3_cur_phase;
+
+// lane 0 of an engine warp records when the warp finished its share of the phase (profiling only)
+KK3_DEV void warp_end_stamp(const StepArgs& a) {
+  if (a.s.warp_ts && (threadIdx.x & 31) == 0) {
+    const int ph = kk3_cur_phase;
+    if (ph >= 0 && ph < kArrivePhases)
+      a.s.warp_ts[((size_t)ph * gridDim.x + blockIdx.x) * kWarps + (threadIdx.x >> 5)] = globaltimer();
+  }
+}
+
 // per-warp marker (lane 0), for locating a fault inside an engine; only when tracing is enabled
 KK3_DEV void trace_warp(const StepArgs& a, int value) {
   if (a.trace && (threadIdx.x & 31) == 0) {
@@ -283,6 +296,12 @@ KK3_DEV unsigned atom_add_release_gpu(unsigned* p, unsigned v) {
   return old;
 }
 
+KK3_DEV int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 KK3_FN bool grid_sync(const StepArgs& a, int phase = -1) {
   __shared__ int ok_flag;
   __syncthreads();
@@ -309,6 +328,7 @@ KK3_FN bool grid_sync(const StepArgs& a, int phase = -1) {
       }
     }
     ok_flag = ok;
+    kk3_cur_phase = phase + 1;
   }
   __syncthreads();
   return ok_flag != 0;

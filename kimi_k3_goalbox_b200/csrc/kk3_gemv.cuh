@@ -171,14 +171,13 @@ KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const 
     for (int nt = 0; nt < NT; ++nt)
       *reinterpret_cast<float4*>(mine + nt * 4) =
           make_float4(round_bf(acc[0][nt][0]), round_bf(acc[0][nt][1]), round_bf(acc[0][nt][2]), round_bf(acc[0][nt][3]));
-    __threadfence();
-    __syncwarp();
+    __syncwarp();   // every lane's stores before lane 0's release
     int* cnt = reinterpret_cast<int*>(j.out2) + tile;
     int old = 0;
-    if (lane == 0) old = atomicAdd(cnt, 1);
+    if (lane == 0) old = atom_add_acq_rel_gpu(cnt, 1);
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old != 1) return;
-    __threadfence();
+    __syncwarp();   // lane 0's acquire before every lane's loads of the other half
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -259,13 +258,14 @@ KK3_DEV bool stream_k_fixup(const StepArgs& a, float* part_base, int* cnt, long 
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) slot[((mt * NT + nt) * 4 + i) * 32 + lane] = acc[mt][nt][i];
-  __threadfence();
+  // one acquire-release RMW publishes this warp's partial (the warp barrier orders every lane's stores before
+  // lane 0's release) and, for the last arriver, acquires the others' partials: no separate fences
   __syncwarp();
   int old = 0;
-  if (lane == 0) old = atomicAdd(cnt, 1);
+  if (lane == 0) old = atom_add_acq_rel_gpu(cnt, 1);
   old = __shfl_sync(0xffffffffu, old, 0);
   if (old != (int)(lastw - first)) return false;
-  __threadfence();
+  __syncwarp();   // lane 0's acquire before every lane's partial loads
   float sum[MT][NT][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
@@ -274,7 +274,7 @@ KK3_DEV bool stream_k_fixup(const StepArgs& a, float* part_base, int* cnt, long 
 #pragma unroll
       for (int i = 0; i < 4; ++i) sum[mt][nt][i] = 0.0f;
   // plain (non-volatile) L2 loads: the compiler may issue later warps' loads before earlier sums complete
-#pragma unroll 4
+#pragma unroll 8
   for (long long w = first; w <= lastw; ++w) {
     const bool mine = w == gw;
     const long long wbeg = U * w / GW;
@@ -465,6 +465,7 @@ KK3_FN void run_gemv(const StepArgs& a, const GemvJob* jobs, int njobs, int cta_
     }
   }
   cp_async_wait_g<0>();
+  warp_end_stamp(a);
   if (stamp) {
     sub_stamp(a, ph, 10);
     sub_stamp(a, ph, 11, (unsigned long long)nunits);
@@ -885,6 +886,7 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* _
     }
   }
   cp_async_wait_g<0>();
+  warp_end_stamp(a);
   if (trace) trace_warp(a, 11);
 }
 

@@ -198,6 +198,7 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
       {(void**)&s.argmax_key, B * 8}, {(void**)&bar, 64}, {(void**)&phase_count, 64}, {(void**)&s.err, 64},
       {(void**)&s.situ_cnt, situ_tiles * 4},
       {(void**)&s.phase_ts, (kMaxPhases + 1) * 8}, {(void**)&s.arrive_ts, (size_t)kArrivePhases * 1024 * 8},
+      {(void**)&s.warp_ts, (size_t)kArrivePhases * x->grid * kWarps * 8},
       {(void**)&s.sub_ts, (size_t)kArrivePhases * 16 * 8},
   };
   size_t total = 0;
@@ -282,13 +283,13 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   // diagnostics table
   void* bp[KK3_BUF_COUNT] = {s.prefix, s.xa, s.xm, s.attn_in, s.scores, s.latent, s.shared_act, s.x3, s.route_w,
                              s.qkv, s.mla_q, s.absorbed, s.absorbed, s.expert_sum, s.blocks, x->comm_local,
-                             s.phase_ts, s.arrive_ts, s.sub_ts};
+                             s.phase_ts, s.arrive_ts, s.sub_ts, s.warp_ts};
   size_t bb[KK3_BUF_COUNT] = {B * g.h * 2, B * g.h * 2, B * g.h * 2, B * (size_t)g.hr * g.vd * 2, B * g.E * 4,
                               B * g.lh * 2, B * (size_t)g.sinter * 2, B * g.lh * 2, B * g.K * 4, B * qkv_w * 2,
                               B * (size_t)g.hr * (g.nr + g.rd) * 2, B * (size_t)g.hr * g.kr * 2,
                               B * (size_t)g.hr * g.kr * 2, B * g.lh * 4, (size_t)g.nblk * B * g.h * 2, x->comm_bytes,
                               (size_t)(kMaxPhases + 1) * 8, (size_t)kArrivePhases * 1024 * 8,
-                              (size_t)kArrivePhases * 16 * 8};
+                              (size_t)kArrivePhases * 16 * 8, (size_t)kArrivePhases * x->grid * kWarps * 8};
   for (int i = 0; i < KK3_BUF_COUNT; ++i) { x->buf_ptr[i] = bp[i]; x->buf_bytes[i] = bb[i]; }
   *out = x;
   return KK3_OK;
@@ -576,6 +577,7 @@ static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, Ste
   }
   *total_bytes = off;
   s.arrive_ts = nullptr;   // per-CTA barrier stamps are a profiling aid of the context path
+  s.warp_ts = nullptr;
   s.trace_host = nullptr;
   s.err_host = err_mirror;
   c.base[0] = comm;

@@ -421,6 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   __shared__ float e8m0_lut[256];   // E8M0 scale byte -> FP32 factor, read by the MXFP4 expert engine
   __shared__ int sjn;
   for (int i = threadIdx.x; i < 256; i += kThreads) e8m0_lut[i] = e8m0_to_f32((unsigned)i);
+  if (threadIdx.x == 0) kk3_cur_phase = 0;
   __syncthreads();
   const Geo& g = a.g;
   float* fsm = reinterpret_cast<float*>(smem);

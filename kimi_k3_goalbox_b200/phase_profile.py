@@ -137,6 +137,7 @@ def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[d
             sub = ctx.debug_buffer(18, torch.int64, (256, 16)).cpu()
             narr = min(len(prog) - 1, 256)
             arr = ctx.debug_buffer(17, torch.int64, (narr, grid)).cpu()
+            wts = ctx.debug_buffer(19, torch.int64, (narr, grid, 16)).cpu()
             # per phase: slowest CTA's arrival after the phase began, and barrier latency after it
             work, barrier, last_cta, spread = [], [], [], []
             for i in range(len(prog)):
@@ -184,6 +185,24 @@ def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[d
             subinfo[f"{name}:{layer}"] = {"warp0_start": (st[8] - base) / 1e3, "first_data": (st[9] - base) / 1e3,
                                           "warp0_end": (st[10] - base) / 1e3, "units": st[11],
                                           "phase_end": (ts[i + 1] - base) / 1e3}
+    # engine warps (GEMV / experts): when each warp finished, relative to the phase start; entries outside the
+    # phase's window are stale (warps without work in this phase)
+    for i, (name, layer) in enumerate(prog[:narr]):
+        lo, hi = ts[i], ts[i + 1]
+        wend = wts[i].double()
+        valid = (wend >= lo) & (wend <= hi)
+        if int(valid.sum()) < 64:
+            continue
+        wrel = torch.where(valid, (wend - lo) / 1e3, torch.full_like(wend, float("nan")))
+        wsorted = wrel[valid].sort().values
+        wq = lambda f: round(float(wsorted[min(len(wsorted) - 1, int(f * (len(wsorted) - 1)))]), 2)
+        wspread = (torch.nan_to_num(wrel, nan=-1e9).max(1).values - torch.nan_to_num(wrel, nan=1e9).min(1).values)
+        wspread = wspread[valid.any(1)]
+        by_warp = [round(float(wrel[:, k][valid[:, k]].mean()), 1) if bool(valid[:, k].any()) else None
+                   for k in range(16)]
+        subinfo[f"warps {name}:{layer}"] = {"end_p10": wq(0.1), "end_p50": wq(0.5), "end_p90": wq(0.9),
+                                            "end_max": wq(1.0), "cta_spread_mean": round(float(wspread.mean()), 2),
+                                            "mean_end_by_warp": by_warp}
     rows = [{"phase": -2, "name": "sub_stamps", "layer": -1, "us": 0.0, "bytes": 0, "GBps": None, "info": subinfo},{"phase": -1, "name": "full_step", "layer": -1, "us": round(full, 2), "bytes": 0, "GBps": None},
             {"phase": -1, "name": "empty_launch", "layer": -1, "us": round(empty, 2), "bytes": 0, "GBps": None}]
     for i, (name, layer) in enumerate(prog):
@@ -217,7 +236,7 @@ def main(argv=None) -> int:
         case = cases.variant(case, batch=args.batch)
     rows = profile(case, args.reps)
     subrow, head, rows = rows[0], rows[1:3], rows[3:]
-    for k, v in [kv for kv in subrow["info"].items() if kv[0].startswith(("mla_attend", "experts_gate_up", "attn_prologue:2", "moe_in:1"))]:
+    for k, v in [kv for kv in subrow["info"].items() if kv[0].startswith(("mla_attend", "experts_gate_up", "attn_prologue:2", "moe_in:1", "warps ")) and (not kv[0].startswith("warps ") or kv[0].endswith(":1"))]:
         print("  sub-phase", k, {kk: (round(vv, 2) if isinstance(vv, float) else vv) for kk, vv in v.items()})
     total = sum(r["us"] for r in rows)
     print(f"{case['id']}: full step {head[0]['us']:.1f} us (events), empty launch {head[1]['us']:.1f} us, "
