@@ -67,7 +67,9 @@ typedef struct kk3_ctx kk3_ctx;
  *   slots [0, KK3_GLOBAL_SLOTS): the global inputs and the outputs (enum below);
  *   then KK3_LAYER_SLOTS slots per layer l at KK3_GLOBAL_SLOTS + l*KK3_LAYER_SLOTS + slot.
  * Every tensor must be contiguous, on the context's device, with the reference's shape and dtype
- * (kimi.py:72-122 weights, :164-182 state, :332-340 outputs). Unused slots may be NULL. */
+ * (kimi.py:72-122 weights, :164-182 state, :332-340 outputs). Unused slots may be NULL. Every pointer except
+ * KK3_TOKEN and KK3_RESET must be 16-byte aligned (read with 16-byte vector loads); the step entry points
+ * return KK3_ERR_ARG otherwise, before launching anything. */
 enum kk3_global_slot {
     KK3_TOKEN = 0, KK3_RESET, KK3_EMBED, KK3_LM_HEAD, KK3_FNORM, KK3_OUTPUT_RES_NORM, KK3_OUTPUT_RES_PROJ,
     KK3_LN1, KK3_LN2, KK3_ATTENTION_RES_NORM, KK3_MLP_RES_NORM, KK3_ATTENTION_RES_PROJ, KK3_MLP_RES_PROJ,

@@ -333,12 +333,22 @@ extern "C" int kk3_debug_set_peer(kk3_ctx* x, int r, void* device_ptr) {
 
 extern "C" size_t kk3_exchange_bytes(kk3_ctx* x) { return x ? x->comm_bytes : 0; }
 
+// Every tensor except the token ids and reset flags is read with 16-byte vector or cp.async loads, so a
+// misaligned pointer would fault on the device: reject it here instead.
+static bool table_aligned(const void* const* table, int n) {
+  for (int i = 0; i < n; ++i) {
+    if (i == KK3_TOKEN || i == KK3_RESET) continue;
+    if (reinterpret_cast<uintptr_t>(table[i]) & 15u) return false;
+  }
+  return true;
+}
+
 static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int stop_phase, int start_phase) {
   if (!x || !table) return KK3_ERR_ARG;
   if (x->failed) return KK3_ERR_FAILED;
   if (!x->peers_open) return KK3_ERR_PEERS;
   const int need = KK3_GLOBAL_SLOTS + x->g.L * KK3_LAYER_SLOTS;
-  if (n != need || n > kMaxPtrs) return KK3_ERR_ARG;
+  if (n != need || n > kMaxPtrs || !table_aligned(table, n)) return KK3_ERR_ARG;
   if (*x->err_host != 0) {
     x->failed = 1;
     return KK3_ERR_FAILED;
@@ -621,7 +631,8 @@ extern "C" int kk3_step_noalloc(const kk3_config* cfg, const void* const* table,
   int rc = validate(cfg);
   if (rc != KK3_OK) return rc;
   if (cfg->tp != 1 || cfg->rank != 0) return KK3_ERR_UNSUPPORTED;
-  if (!table || table_size != KK3_GLOBAL_SLOTS + cfg->layers * KK3_LAYER_SLOTS || table_size > kMaxPtrs)
+  if (!table || table_size != KK3_GLOBAL_SLOTS + cfg->layers * KK3_LAYER_SLOTS || table_size > kMaxPtrs ||
+      !table_aligned(table, table_size))
     return KK3_ERR_ARG;
   if (cfg->device < 0 || cfg->device >= kNoAllocMaxDevices) return KK3_ERR_ARG;
   std::lock_guard<std::mutex> lock(noalloc_mu);   // host-side state only; see the concurrency note above

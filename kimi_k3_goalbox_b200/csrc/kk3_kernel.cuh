@@ -568,6 +568,11 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
       // router, latent down and the shared expert's gate/up in one pass (kimi.py:308, :317, :326)
       if (KK3_RUN) {
         KK3_BUILD(sjn = mlp_in_jobs(a, l, sj));
+        // the router bias is read by every CTA at the start of the next phase: bring it into L2 now
+        if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0 && g.E * 4 >= 16) {
+          const float* rb = lptr<float>(a, l, KK3_MOE_ROUTER_BIAS);
+          if ((reinterpret_cast<uintptr_t>(rb) & 15u) == 0) prefetch_l2(rb, (unsigned)(g.E * 4) & ~15u);
+        }
         run_gemv<NT, 1>(a, sj, sjn, 0, gridDim.x, 0, 0, phase);
       }
       KK3_PHASE_END();

@@ -762,12 +762,12 @@ KK3_FN void mla_combine_item(const StepArgs& a, int layer, int b, int hh, float*
 // writes them (identical values), so the experts start without a grid barrier of their own.
 
 // shared memory of the routing step: the selected ids [kMaxBatch * kMaxTopk] at 0; the grouping's per-expert
-// row masks and offsets and its scan totals after them (< 32 KB); then each warp's keys, lane-major with a
-// padded stride (conflict-free 16-byte reads), and the router bias
+// row masks and offsets and its scan totals after them (< 32 KB); then each warp's scores and the router
+// bias, lane-major [lane][kRouteStride] with a padded stride
 constexpr int kRouteStride = 36;   // u32 words per lane: up to 32 keys (E <= 1024) plus padding
 constexpr size_t kRouteKeyOff = 32 * 1024;
 constexpr size_t kRouteBiasOff = kRouteKeyOff + (size_t)kWarps * 32 * kRouteStride * 4;
-constexpr size_t kRouteSmem = kRouteBiasOff + (size_t)kMaxExperts * 4;
+constexpr size_t kRouteSmem = kRouteBiasOff + (size_t)32 * kRouteStride * 4;
 static_assert((size_t)kMaxBatch * kMaxTopk * 4 + (size_t)kMaxExperts * 16 + 2 * kWarps * 4 <= kRouteKeyOff,
               "routing tables overlap the keys");
 
@@ -864,37 +864,49 @@ KK3_DEV unsigned route_key(float x) {
 }
 
 
+KK3_DEV unsigned warp_sum_u32(unsigned v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
 // Warp w routes batch rows w, w + 16, ...; lane l holds the keys of experts [l * n, l * n + n) (n = E / 32
-// rounded up) in shared memory, staged with cp.async. The K-th largest key T is found by bisection from the
-// top bit with warp-wide counts (stopping as soon as exactly K keys are >= the probe). Every expert above T is
-// taken, and of those equal to T the lowest indices (torch.topk's order as the reference uses it: value
-// descending, then index ascending); lane-order prefix sums place the ids in ascending order. This code runs
-// once per layer from a cold instruction cache, so its loops are kept compact.
+// rounded up) in registers, computed from a shared-memory staging copy (cp.async) of the row's scores and of
+// the bias, read 16 bytes at a time. The K-th largest key T is found by bisection: the bits above the
+// highest bit in which the largest and the smallest key differ are common to all keys, and the remaining bits
+// are resolved two per round (three probes counted together) with warp-wide counts, stopping as soon as
+// exactly K keys are >= the chosen probe. Every expert above T is taken, and of those equal to T the lowest
+// indices (torch.topk's order as the reference uses it: value descending, then index ascending); lane-order
+// prefix sums place the ids in ascending order.
 KK3_FN void route_cta(const StepArgs& a, int layer, unsigned char* smem, int ph = -1) {
   const Geo& g = a.g;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = g.K, E = g.E;
-  constexpr unsigned kFull = 0xffffffffu;
-  const int nper = (E + 31) >> 5, nq = (nper + 3) >> 2, e0 = lane * nper;
+  constexpr int kPer = kRouteStride - 4;   // 32 keys per lane at most (E <= 1024)
+  const int nper = (E + 31) >> 5, e0 = lane * nper;
+  const int nlive = E - e0 < 0 ? 0 : (E - e0 < nper ? E - e0 : nper);   // this lane's real experts
   int* ids = reinterpret_cast<int*>(smem);   // [B*K] sorted per row
-  float* bias_s = reinterpret_cast<float*>(smem + kRouteBiasOff);
-  unsigned* wk = reinterpret_cast<unsigned*>(smem + kRouteKeyOff) + ((size_t)warp * 32 + lane) * kRouteStride;
-  const uint4* wk4 = reinterpret_cast<const uint4*>(wk);
+  // bias and each warp's scores in the same lane-major layout [lane][kRouteStride] (16-byte aligned rows)
+  float* bias_l = reinterpret_cast<float*>(smem + kRouteBiasOff) + lane * kRouteStride;
+  float* sc_w = reinterpret_cast<float*>(smem + kRouteKeyOff) + (size_t)warp * 32 * kRouteStride;
+  float* sc_l = sc_w + lane * kRouteStride;
   const float* bias = lptr<float>(a, layer, KK3_MOE_ROUTER_BIAS);
   long long* out_ids = gout<long long>(a, KK3_OUT_EXPERT_IDS) + (size_t)layer * g.B * K;
   const bool stamp = ph >= 0 && blockIdx.x == 0 && tid == 0;
   auto stage_row = [&](int b) {
     const float* sc = a.s.scores + (size_t)b * E + e0;
 #pragma unroll 1
-    for (int i = 0; i < nper; ++i)
-      if (e0 + i < E) cp_async4_ca(wk + i, sc + i);
+    for (int i = 0; i < nlive; ++i) cp_async4_ca(sc_l + i, sc + i);
   };
+  if (warp == 0) {
 #pragma unroll 1
-  for (int e = tid; e < E; e += kThreads) cp_async4_ca(bias_s + e, bias + e);
+    for (int i = 0; i < nlive; ++i) cp_async4_ca(bias_l + i, bias + e0 + i);
+  }
   if (warp < g.B) stage_row(warp);
   cp_async_commit();
   cp_async_wait_all();
   __syncthreads();
+  if (stamp) sub_stamp(a, ph, 9);
 #pragma unroll 1
   for (int b = warp; b < g.B; b += kWarps) {
     if (b != warp) {
@@ -902,49 +914,81 @@ KK3_FN void route_cta(const StepArgs& a, int layer, unsigned char* smem, int ph 
       cp_async_commit();
       cp_async_wait_all();
     }
-    // keys in place; absent experts and padding get key 0, below every real key
-#pragma unroll 1
-    for (int i = 0; i < nq * 4; ++i)
-      wk[i] = (i < nper && e0 + i < E) ? route_key(__uint_as_float(wk[i]) + bias_s[e0 + i]) : 0u;
-    unsigned T = 0u;
-#pragma unroll 1
-    for (int bit = 31; bit >= 0; --bit) {
-      const unsigned probe = T | (1u << bit);
-      unsigned n = 0;
-#pragma unroll 1
-      for (int q = 0; q < nq; ++q) {
-        {
-          const uint4 v = wk4[q];
-          n += (v.x >= probe ? 1u : 0u) + (v.y >= probe ? 1u : 0u) + (v.z >= probe ? 1u : 0u) + (v.w >= probe ? 1u : 0u);
+    // keys; absent experts and padding get key 0, below every real key
+    unsigned key[kPer];
+    unsigned kmax = 0u, kmin = 0xffffffffu;
+#pragma unroll
+    for (int q = 0; q < kPer / 4; ++q) {
+      const float4 sv = reinterpret_cast<const float4*>(sc_l)[q], bv = reinterpret_cast<const float4*>(bias_l)[q];
+      const float x[4] = {sv.x + bv.x, sv.y + bv.y, sv.z + bv.z, sv.w + bv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = 4 * q + j;
+        key[i] = i < nlive ? route_key(x[j]) : 0u;
+        if (i < nlive) {
+          kmax = key[i] > kmax ? key[i] : kmax;
+          kmin = key[i] < kmin ? key[i] : kmin;
         }
       }
-      n = __reduce_add_sync(kFull, n);
-      if (n >= (unsigned)K) {
-        T = probe;
-        if (n == (unsigned)K) break;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned x = __shfl_xor_sync(0xffffffffu, kmax, o), y = __shfl_xor_sync(0xffffffffu, kmin, o);
+      kmax = x > kmax ? x : kmax;
+      kmin = y < kmin ? y : kmin;
+    }
+    if (stamp && b == 0) sub_stamp(a, ph, 10);
+    int bit = 31 - __clz(kmax ^ kmin);   // -1 when every key is equal
+    unsigned T = bit < 0 ? kmax : (bit >= 31 ? 0u : (kmax & ~((2u << bit) - 1u)));
+    bool done = false;
+#pragma unroll 1
+    for (; bit >= 1 && !done; bit -= 2) {
+      // probes T|hi, T|lo|... : p1 = T + lo, p2 = T + hi, p3 = T + hi + lo (lo = bit - 1, hi = bit)
+      const unsigned hi = 1u << bit, lo = 1u << (bit - 1);
+      const unsigned p1 = T | lo, p2 = T | hi, p3 = T | hi | lo;
+      unsigned n1 = 0, n2 = 0, n3 = 0;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        n1 += key[i] >= p1 ? 1u : 0u;
+        n2 += key[i] >= p2 ? 1u : 0u;
+        n3 += key[i] >= p3 ? 1u : 0u;
       }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        n1 += __shfl_xor_sync(0xffffffffu, n1, o);
+        n2 += __shfl_xor_sync(0xffffffffu, n2, o);
+        n3 += __shfl_xor_sync(0xffffffffu, n3, o);
+      }
+      const unsigned k = (unsigned)K;
+      if (n3 >= k) { T = p3; done = n3 == k; }
+      else if (n2 >= k) { T = p2; done = n2 == k; }
+      else if (n1 >= k) { T = p1; done = n1 == k; }
+    }
+    if (!done && bit == 0) {   // an odd number of bits: the last one alone
+      const unsigned p = T | 1u;
+      unsigned n = 0;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) n += key[i] >= p ? 1u : 0u;
+      n = warp_sum_u32(n);
+      if (n >= (unsigned)K) T = p;
     }
     if (stamp && b == 0) sub_stamp(a, ph, 12);
     // take every key above T and, in index order, the first K - #(above) keys equal to T
     unsigned gt = 0, eq = 0;
-#pragma unroll 1
-    for (int q = 0; q < nq; ++q) {
-      {
-        const uint4 v = wk4[q];
-        gt += (v.x > T ? 1u : 0u) + (v.y > T ? 1u : 0u) + (v.z > T ? 1u : 0u) + (v.w > T ? 1u : 0u);
-        eq += (v.x == T ? 1u : 0u) + (v.y == T ? 1u : 0u) + (v.z == T ? 1u : 0u) + (v.w == T ? 1u : 0u);
-      }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      gt += key[i] > T ? 1u : 0u;
+      eq += key[i] == T ? 1u : 0u;
     }
-    const unsigned need = (unsigned)K - __reduce_add_sync(kFull, gt);
+    const unsigned need = (unsigned)K - warp_sum_u32(gt);
     const unsigned tie0 = warp_excl_scan(eq);
     unsigned ties = tie0 < need ? (need - tie0 < eq ? need - tie0 : eq) : 0u;   // ties this lane takes
     unsigned pos = warp_excl_scan(gt + ties);
     int* row_ids = ids + b * K;
-#pragma unroll 1
-    for (int i = 0; i < nper; ++i) {
-      const unsigned k = wk[i];
-      bool take = k > T;
-      if (k == T && ties > 0) {
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      bool take = key[i] > T;
+      if (key[i] == T && ties > 0) {
         take = true;
         --ties;
       }
@@ -955,9 +999,10 @@ KK3_FN void route_cta(const StepArgs& a, int layer, unsigned char* smem, int ph 
     }
     __syncwarp();
     if (stamp && b == 0) sub_stamp(a, ph, 13);
+    // weights: the unbiased scores of the chosen experts, from the staged row
     int e = lane < K ? row_ids[lane] : 0;
     e = e < 0 ? 0 : (e >= E ? E - 1 : e);
-    const float w = lane < K ? __ldcg(a.s.scores + (size_t)b * E + e) : 0.0f;
+    const float w = lane < K ? sc_w[(e / nper) * kRouteStride + e % nper] : 0.0f;
     const float wsum = warp_sum(w);
     if (lane < K) {
       row_ids[lane] = e;

@@ -177,7 +177,8 @@ def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[d
                  "t1_softmax", "t1_pv", "item_end"]) if st[i]} | {"subtiles": st[11],
                                                                   "phase_end": (ts[i + 1] - base) / 1e3}
         if name == "experts_gate_up" and st[15]:
-            subinfo[f"{name}:{layer}"] = {"mark": (st[11] - base) / 1e3 if st[11] else None,
+            subinfo[f"{name}:{layer}"] = {"raw5": st[5], "raw6": st[6], "raw7": st[7], "raw8": st[8],
+                                          "staged": (st[9] - base) / 1e3, "warp0_keys": (st[10] - base) / 1e3,
                                           "warp0_threshold": (st[12] - base) / 1e3, "warp0_row": (st[13] - base) / 1e3,
                                           "all_rows": (st[14] - base) / 1e3, "grouped": (st[15] - base) / 1e3,
                                           "phase_end": (ts[i + 1] - base) / 1e3}

@@ -17,7 +17,7 @@ import torch
 from kimi_k3_goalbox_b200 import cases, runtime, synthetic
 from tests import gpu_helpers as gh
 
-KK3_ERR_UNSUPPORTED, KK3_ERR_TOO_LARGE = -2, -8
+KK3_ERR_ARG, KK3_ERR_UNSUPPORTED, KK3_ERR_TOO_LARGE = -1, -2, -8
 FLOAT_TOL = 1e-6   # relative L2 distance allowed for float outputs (integer outputs must match exactly)
 
 
@@ -110,3 +110,19 @@ def test_noalloc_rejects_tensor_parallel_configs(lib):
     n = runtime.GLOBAL_SLOTS + case["params"]["layers"] * runtime.LAYER_SLOTS
     table = (ctypes.c_void_p * n)()
     assert lib.kk3_step_noalloc(ctypes.byref(cfg), table, n, None, None) == KK3_ERR_UNSUPPORTED
+
+
+def test_noalloc_rejects_misaligned_pointers(lib):
+    """A tensor pointer off a 16-byte boundary is refused before any CUDA call (runs without a GPU); token
+    ids and reset flags are read with scalar loads and may sit anywhere. The table holds placeholder
+    addresses that are never dereferenced."""
+    case = gh.small_case(3)
+    cfg = runtime.rank_config(case, 0, 0)
+    n = runtime.GLOBAL_SLOTS + case["params"]["layers"] * runtime.LAYER_SLOTS
+    table = (ctypes.c_void_p * n)()
+    table[2] = 0x10002   # KK3_EMBED, 2 bytes off
+    assert lib.kk3_step_noalloc(ctypes.byref(cfg), table, n, None, None) == KK3_ERR_ARG
+    lsl = runtime.GLOBAL_SLOTS + runtime.LAYER_SLOTS * 1 + 19   # layer 1, KK3_MOE_ROUTER
+    table[2] = None
+    table[lsl] = 0x10008
+    assert lib.kk3_step_noalloc(ctypes.byref(cfg), table, n, None, None) == KK3_ERR_ARG
