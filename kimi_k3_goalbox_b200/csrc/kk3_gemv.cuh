@@ -566,16 +566,39 @@ KK3_DEV void e2m1x8_cvt(unsigned w, unsigned (&r)[4]) {
 KK3_DEV unsigned lds32(const unsigned char* p) { return *reinterpret_cast<const unsigned*>(p); }
 
 
-// Stream-K over (expert chunk, tile, k-step) units. Chunks come from the routing phase. A unit is a
-// 16-row tile x 64 k (two E2M1 groups of 32) of MT matrices. The per-warp cp.async ring carries only
-// weight bytes: the 16 x 32 code bytes of each matrix (row halves XOR-swizzled so the consumer's 4-byte
-// reads are bank-conflict free) and a 4-byte word of E8M0 scales per row (the aligned word holding this
-// unit's two groups). The FP16 activation rows the CTA's chunks multiply are staged once per phase into a
-// shared-memory row cache (per-unit loads of the same few hot rows from L2 were the engine's bottleneck);
-// rows beyond its capacity are read from L2. Each quad converts its rows' E2M1 codes to FP16 in hardware
-// (cvt.rn.f16x2.e2m1x2), runs mma.sync per 32-wide group and applies the group scale to the FP32 partial.
-constexpr int kExpRing = 8 * 1024;        // per-warp ring bytes of the expert engine
+// Stream-K over (expert chunk, tile, k-step) units. Chunks come from the routing step. A unit is a 16-row
+// tile x 64 k (two E2M1 groups of 32) of MT matrices; the loop runs over unit pairs (128 k, four groups,
+// one 4-byte word of E8M0 scales per row), whose first or last unit may lie outside the warp's range (then
+// its groups are skipped). The per-warp cp.async ring carries only weight bytes: 16 rows x 64 code bytes
+// per matrix (16-byte chunks XOR-swizzled so that ldmatrix reads are bank-conflict free) and the scale
+// word of each row. The FP16 activation rows the CTA's chunks multiply are staged once per phase into a
+// shared-memory row cache; rows beyond its capacity are read from L2 through the same generic loads. One
+// ldmatrix.x4 gives a lane the four group words of its row; each quad converts them to FP16 in hardware
+// (cvt.rn.f16x2.e2m1x2), runs mma.sync per 32-wide group and applies the group scale to the FP32 partial,
+// in the same order as a unit at a time.
+// E8M0 scale byte -> FP32 factor (2^(s - 127); s = 0 and s = 255 exactly as the reference decodes them),
+// filled at kernel start; at namespace scope so the engine's reads compile to shared-memory loads
+static __shared__ float kk3_e8m0_lut[256];
+
+constexpr int kExpRing = 8704;            // per-warp ring bytes: four MT=2 pair slots (2176 B) or eight MT=1
 constexpr int kExpXCache = 64 * 1024;     // per-CTA activation row cache, after the rings
+constexpr int kExpSmem = kWarps * kExpRing + kExpXCache;
+
+KK3_DEV void ldsm4(unsigned (&r)[4], unsigned addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+KK3_DEV unsigned lds32_u(unsigned addr) {
+  unsigned v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+// f16 MMA without `volatile`, so the compiler may interleave independent groups
+KK3_DEV void mma_f16_nv(float (&d)[4], unsigned a0, unsigned a1, unsigned a2, unsigned a3, unsigned b0, unsigned b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
 KK3_DEV void cp_async4_ca(void* smem_dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((unsigned)__cvta_generic_to_shared(smem_dst)),
@@ -589,16 +612,16 @@ KK3_DEV uint4 ld_cg16(const void* p) {
 }
 
 template <int MT>
-KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* __restrict__ e8m0_lut) {
+KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
   extern __shared__ __align__(16) unsigned char kk3_dyn_smem[];
   __shared__ unsigned long long s_mask;    // MT == 2: batch rows staged (bit b = latent row b)
   __shared__ int s_first, s_count;        // MT == 1: pairs [s_first, s_first + s_count) staged
   __shared__ int s_rowmap[kMaxBatch];     // MT == 2: cache slot i holds latent row s_rowmap[i]
-  constexpr int kCode = 16 * 32;                  // code bytes per matrix and unit
-  constexpr int kScale = 16 * 4;                  // scale bytes per matrix and unit
+  constexpr int kCode = 16 * 64;                  // code bytes per matrix and unit pair
+  constexpr int kScale = 16 * 4;                  // scale bytes per matrix and unit pair (one word per row)
   constexpr int kSlot = MT * (kCode + kScale);
   constexpr int S = (kExpRing / kSlot) > 12 ? 12 : (kExpRing / kSlot);
-  static_assert(S >= 3, "ring too shallow");
+  static_assert(S >= 4, "ring too shallow");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
 
   // values of the unit loop live in registers; values used only when a tile or chunk changes are re-read
@@ -691,45 +714,51 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* _
   unsigned char* ring = kk3_dyn_smem + (size_t)warp * kExpRing;
   if (trace) trace_warp(a, 1);
 
-  const int c0 = ubeg / per_chunk;
-  const int rem0 = ubeg - c0 * per_chunk;
+  // ---- unit pairs: pair P holds units 2P, 2P + 1 (ksteps is even, so a pair never spans two tiles)
+  const int kpairs = ksteps >> 1;
+  const int pbeg = ubeg >> 1, npairs = ((uend + 1) >> 1) - pbeg;
+  const int c0 = (2 * pbeg) / per_chunk;
+  const int rem0 = 2 * pbeg - c0 * per_chunk;
+  const int t0 = rem0 / ksteps, kp0 = (rem0 - t0 * ksteps) >> 1;
 
-  // ---- producer (weights into the ring, S - 1 units ahead); per-lane slot offsets are fixed
-  int p_chunk = c0, p_tile = rem0 / ksteps, p_ks = rem0 % ksteps;
-  const int srow = lane >> 1;
-  const int p_dst_code = srow * 32 + (((lane & 1) ^ ((srow >> 2) & 1)) * 16);   // swizzled half of the row
-  const int scl_mt = lane >> 4, scl_row = lane & 15;                             // scale row this lane stages
+  // ---- producer (weights into the ring, S - 1 pairs ahead); per-lane slot offsets are fixed
+  const unsigned ring_s = (unsigned)__cvta_generic_to_shared(ring);
+  int p_chunk = c0, p_tile = t0, p_kp = kp0;
+  const int prow = lane >> 2, pq = lane & 3;                                   // row (and row + 8), 16-byte chunk
+  const unsigned p_dst_code = prow * 64 + ((pq ^ ((prow >> 1) & 3)) << 4);     // swizzled chunk of the row
+  const int scl_mt = lane >> 4, scl_row = lane & 15;                           // scale row this lane stages
   const bool scl_lane = scl_mt < MT;
-  const int p_dst_scl = MT * kCode + scl_mt * kScale + scl_row * 4;
-  const uint8_t* p_code[MT];   // this lane's 16 code bytes of the current unit, per matrix
-  const uint8_t* p_scl = ph.scales[0];   // this lane's scale row (word of the current unit pair)
+  const unsigned p_dst_scl = MT * kCode + scl_mt * kScale + scl_row * 4;
+  const uint8_t* p_code[MT];   // this lane's 16 code bytes of row prow of the current pair, per matrix
+  const uint8_t* p_scl = ph.scales[0];
+  const size_t rowbytes = (size_t)(ph.K >> 1), sbytes = (size_t)(ph.K >> 5);
+  const unsigned long long pol = l2_evict_first_policy();   // codes are read once per step
   auto p_setup = [&]() {
     const size_t e = (size_t)chunk_expert(p_chunk);
-    const int rowbytes = ph.K / 2, sbytes = ph.K / 32;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
-      p_code[mt] = ph.codes[mt] + e * ph.expert_codes + (size_t)(p_tile * 16 + srow) * rowbytes + (lane & 1) * 16 +
-                   p_ks * 32;
+      p_code[mt] = ph.codes[mt] + e * ph.expert_codes + (size_t)(p_tile * 16 + prow) * rowbytes + p_kp * 64 + pq * 16;
     if (scl_lane)
-      p_scl = ph.scales[scl_mt] + e * ph.expert_scales + (size_t)(p_tile * 16 + scl_row) * sbytes + (p_ks >> 1) * 4;
+      p_scl = ph.scales[scl_mt] + e * ph.expert_scales + (size_t)(p_tile * 16 + scl_row) * sbytes + p_kp * 4;
   };
-  int p_left = nunits, p_slot = 0;
-  // weight codes are read once per step: evict them first, so that the activations, partial tiles and the
-  // next phases' small operands stay in L2
-  const unsigned long long pol = l2_evict_first_policy();
+  int p_left = npairs, p_slot = 0;
   auto p_issue = [&]() {
-    unsigned char* slot = ring + p_slot * kSlot;
+    const unsigned slot = ring_s + p_slot * kSlot;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-      cp_async16_stream(slot + mt * kCode + p_dst_code, p_code[mt], pol);
-      p_code[mt] += 32;
+      asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;"
+                   ::"r"(slot + mt * kCode + p_dst_code), "l"(p_code[mt]), "l"(pol) : "memory");
+      asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;"
+                   ::"r"(slot + mt * kCode + 512 + p_dst_code), "l"(p_code[mt] + 8 * rowbytes), "l"(pol) : "memory");
+      p_code[mt] += 64;
     }
-    if (scl_lane) cp_async4_ca(slot + p_dst_scl, p_scl);
-    p_scl += (p_ks & 1) * 4;
+    if (scl_lane)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(slot + p_dst_scl), "l"(p_scl) : "memory");
+    p_scl += 4;
     p_slot = p_slot + 1 == S ? 0 : p_slot + 1;
     --p_left;
-    if (++p_ks == ksteps) {
-      p_ks = 0;
+    if (++p_kp == kpairs) {
+      p_kp = 0;
       if (++p_tile == tiles) {
         p_tile = 0;
         ++p_chunk;
@@ -745,13 +774,16 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* _
   }
   if (trace) trace_warp(a, 4);
 
-  // ---- activations of the current chunk for this lane's pair r: a cached row (x_sm), an L2 row (x_gl)
-  // for a row beyond the cache, or none (zeros) when the chunk has fewer pairs
-  int c_chunk = c0, c_tile = rem0 / ksteps, c_ks = rem0 % ksteps;
+  // ---- activations of the current chunk for this lane's pair r (generic pointer: a cached row in shared
+  // memory or an L2 row); lanes without a pair read any cached row, their MMA columns are never stored
+  int c_chunk = c0, c_tile = t0, c_kp = kp0;
   int c_fp = 0, c_np = 0;
-  const unsigned char* x_sm = xcache;   // always a valid address; x_live masks lanes without a pair
-  const __half* x_gl = nullptr;
-  bool x_live = false;
+  // lanes without a pair read a cached row (or a real global row when nothing fits the cache)
+  const unsigned char* xdead = cap > 0 ? xcache
+                                       : reinterpret_cast<const unsigned char*>(MT == 2 ? a.s.latent_p : a.s.act_p);
+  const unsigned char* xp = xdead;
+  int x_off = 0;             // byte offset of this lane's row in the cache (when cached)
+  bool x_shared = cap > 0;   // every lane's row of the current chunk is in the cache (shared-memory loads)
   void* out_row[2] = {nullptr, nullptr};   // epilogue targets of this lane's columns 2c, 2c + 1
   auto x_setup = [&]() {
     chunk_pairs(c_chunk, c_fp, c_np);
@@ -769,99 +801,86 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* _
         out_row[e] = a.s.out_slot + ((size_t)pair_batch_row(pc) * a.g.K + slot) * a.g.lh;
       }
     }
-    x_live = r < c_np;
-    x_sm = xcache;
-    x_gl = nullptr;
-    if (!x_live) return;
-    const int p = c_fp + r;
-    if (MT == 2) {
-      const int b = pair_batch_row(p);
-      if ((xmask >> b) & 1ull) {
-        x_sm = xcache + __popcll(xmask & ((1ull << b) - 1ull)) * xstride;
+    xp = xdead;
+    x_off = 0;
+    bool cached = cap > 0;
+    if (r < c_np) {
+      const int p = c_fp + r;
+      if (MT == 2) {
+        const int b = pair_batch_row(p);
+        cached = (xmask >> b) & 1ull;
+        x_off = cached ? __popcll(xmask & ((1ull << b) - 1ull)) * xstride : 0;
+        xp = cached ? xcache + x_off : reinterpret_cast<const unsigned char*>(a.s.latent_p + (size_t)b * a.g.lh);
       } else {
-        x_gl = a.s.latent_p + (size_t)b * a.g.lh;
-      }
-    } else {
-      const int i = p - xfirst;
-      if (i >= 0 && i < xcount) {
-        x_sm = xcache + i * xstride;
-      } else {
-        x_gl = a.s.act_p + (size_t)p * a.g.inter;
+        const int i = p - xfirst;
+        cached = i >= 0 && i < xcount;
+        x_off = cached ? i * xstride : 0;
+        xp = cached ? xcache + x_off : reinterpret_cast<const unsigned char*>(a.s.act_p + (size_t)p * a.g.inter);
       }
     }
+    x_shared = __all_sync(0xffffffffu, cached);
   };
   x_setup();
 
   // ---- consumer; per-lane read offsets inside a slot are fixed
   int c_slot = 0;
-  const int rsw = ((r >> 2) & 1) * 16;                                   // swizzle of rows r and r + 8
-  const int c_off0 = r * 32 + (0 ^ rsw) + 4 * c, c_off1 = r * 32 + (16 ^ rsw) + 4 * c;
-  const int c_scl = MT * kCode + r * 4;
+  const int lrow = lane & 7, lq = lane >> 3;   // ldmatrix: this lane addresses row lrow (+8) of chunk lq
+  const unsigned c_ldsm = lrow * 64 + ((lq ^ ((lrow >> 1) & 3)) << 4);
+  const unsigned c_scl = MT * kCode + r * 4;
   float acc[MT][1][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[mt][0][i] = 0.0f;
-  for (int n = 0; n < nunits; ++n) {
+  const bool lo_first = (ubeg & 1) == 0, hi_last = (uend & 1) == 0;
+  for (int n = 0; n < npairs; ++n) {
     __syncwarp();   // every lane is done with the slot the next issue overwrites
     if (p_left > 0) p_issue();
     cp_async_commit_g();
-    // this unit's activation pieces: k = 64 ks + 8c (+32), from the row cache (or L2 for an uncached row)
-    uint4 X[2];
-    if (x_gl) {
-      X[0] = ld_cg16(x_gl + c_ks * 64 + 8 * c);
-      X[1] = ld_cg16(x_gl + c_ks * 64 + 32 + 8 * c);
-    } else {
-      X[0] = *reinterpret_cast<const uint4*>(x_sm + c_ks * 128 + c * 16);
-      X[1] = *reinterpret_cast<const uint4*>(x_sm + c_ks * 128 + 64 + c * 16);
-    }
-    if (!x_live) {
-      X[0] = make_uint4(0, 0, 0, 0);
-      X[1] = make_uint4(0, 0, 0, 0);
-    }
+    // this pair's activation pieces: k = 128 kp + 64 u + 32 g + 8c, group j = 2u + g; the first is loaded
+    // before the ring wait, each next one while the previous group is being multiplied
+    const int xko = c_kp * 256 + c * 16;
+    auto ldx = [&](int j) -> uint4 {
+      if (x_shared) return *reinterpret_cast<const uint4*>(xcache + x_off + xko + j * 64);   // shared
+      return *reinterpret_cast<const uint4*>(xp + xko + j * 64);                              // generic
+    };
+    uint4 xn = ldx(0);
     cp_async_wait_g<S - 1>();
     __syncwarp();
     if (trace && n < 2) trace_warp(a, 5 | (n << 8));
-    const unsigned char* slot = ring + c_slot * kSlot;
+    const unsigned slot = ring_s + c_slot * kSlot;
     c_slot = c_slot + 1 == S ? 0 : c_slot + 1;
-    const int pos = (c_ks & 1) << 4;   // bit offset of this unit's two scale bytes in a row's word
-    unsigned swa[MT], swb[MT], wa[MT][2], wb[MT][2];
+    const bool lo = n > 0 || lo_first, hi = n < npairs - 1 || hi_last;
+    unsigned wa[MT][4], wb[MT][4], sa[MT], sb[MT];   // group words and scale words of rows r and r + 8
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-      swa[mt] = *reinterpret_cast<const unsigned*>(slot + c_scl + mt * kScale) >> pos;
-      swb[mt] = *reinterpret_cast<const unsigned*>(slot + c_scl + mt * kScale + 32) >> pos;
-      wa[mt][0] = lds32(slot + mt * kCode + c_off0);
-      wa[mt][1] = lds32(slot + mt * kCode + c_off1);
-      wb[mt][0] = lds32(slot + mt * kCode + c_off0 + 256);
-      wb[mt][1] = lds32(slot + mt * kCode + c_off1 + 256);
+      ldsm4(wa[mt], slot + mt * kCode + c_ldsm);
+      ldsm4(wb[mt], slot + mt * kCode + 512 + c_ldsm);
+      sa[mt] = *reinterpret_cast<const unsigned*>(ring + (slot - ring_s) + c_scl + mt * kScale);
+      sb[mt] = *reinterpret_cast<const unsigned*>(ring + (slot - ring_s) + c_scl + mt * kScale + 32);
     }
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      // both groups' conversions first, then their MMAs interleaved so each dependent pair has an
-      // independent MMA between its halves
-      unsigned ra[2][4], rb[2][4];
+    for (int j = 0; j < 4; ++j) {
+      const uint4 X = xn;
+      if (j < 3) xn = ldx(j + 1);
+      if (j < 2 ? !lo : !hi) continue;
 #pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        e2m1x8_cvt(wa[mt][g], ra[g]);
-        e2m1x8_cvt(wb[mt][g], rb[g]);
-      }
-      float t[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
-      mma_f16(t[0], ra[0][0], rb[0][0], ra[0][1], rb[0][1], X[0].x, X[0].y);
-      mma_f16(t[1], ra[1][0], rb[1][0], ra[1][1], rb[1][1], X[1].x, X[1].y);
-      mma_f16(t[0], ra[0][2], rb[0][2], ra[0][3], rb[0][3], X[0].z, X[0].w);
-      mma_f16(t[1], ra[1][2], rb[1][2], ra[1][3], rb[1][3], X[1].z, X[1].w);
-#pragma unroll
-      for (int g = 0; g < 2; ++g) {
+      for (int mt = 0; mt < MT; ++mt) {
+        unsigned ra[4], rb[4];
+        e2m1x8_cvt(wa[mt][j], ra);
+        e2m1x8_cvt(wb[mt][j], rb);
+        float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        mma_f16_nv(t, ra[0], rb[0], ra[1], rb[1], X.x, X.y);
+        mma_f16_nv(t, ra[2], rb[2], ra[3], rb[3], X.z, X.w);
         // 2^(s - 127) from a 256-entry table (s = 0 and s = 255 exactly as the reference decodes them)
-        const float fa = e8m0_lut[(swa[mt] >> (8 * g)) & 0xffu];
-        const float fb = e8m0_lut[(swb[mt] >> (8 * g)) & 0xffu];
-        acc[mt][0][0] = fmaf(t[g][0], fa, acc[mt][0][0]);
-        acc[mt][0][1] = fmaf(t[g][1], fa, acc[mt][0][1]);
-        acc[mt][0][2] = fmaf(t[g][2], fb, acc[mt][0][2]);
-        acc[mt][0][3] = fmaf(t[g][3], fb, acc[mt][0][3]);
+        const float fa = kk3_e8m0_lut[(sa[mt] >> (8 * j)) & 0xffu], fb = kk3_e8m0_lut[(sb[mt] >> (8 * j)) & 0xffu];
+        acc[mt][0][0] = fmaf(t[0], fa, acc[mt][0][0]);
+        acc[mt][0][1] = fmaf(t[1], fa, acc[mt][0][1]);
+        acc[mt][0][2] = fmaf(t[2], fb, acc[mt][0][2]);
+        acc[mt][0][3] = fmaf(t[3], fb, acc[mt][0][3]);
       }
     }
-    if (c_ks == ksteps - 1 || n == nunits - 1) {
+    if ((c_kp == kpairs - 1 && hi) || n == npairs - 1) {
       const int tile_beg = c_chunk * per_chunk + c_tile * ksteps;
       const bool inside = tile_beg >= ubeg && tile_beg + ksteps <= uend;   // the whole tile is this warp's
       const long long first = inside ? gw : owner_of(tile_beg, U, GW);
@@ -876,12 +895,12 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph, const float* _
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[mt][0][i] = 0.0f;
     }
-    if (++c_ks == ksteps) {
-      c_ks = 0;
+    if (++c_kp == kpairs) {
+      c_kp = 0;
       if (++c_tile == tiles) {
         c_tile = 0;
         ++c_chunk;
-        if (n + 1 < nunits) x_setup();
+        if (n + 1 < npairs) x_setup();
       }
     }
   }

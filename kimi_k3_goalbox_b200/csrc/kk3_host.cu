@@ -268,6 +268,7 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   sm = sm_row > sm ? sm_row : sm;
   sm = sm_abs > sm ? sm_abs : sm;
   sm = sm_route > sm ? sm_route : sm;
+  sm = (size_t)kExpSmem > sm ? (size_t)kExpSmem : sm;   // expert rings + activation row cache
   x->smem = align_up(sm, 128);
   if (x->smem > (size_t)prop.sharedMemPerBlockOptin) {
     kk3_free(x);
@@ -601,6 +602,7 @@ static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, Ste
   sm = sm_row > sm ? sm_row : sm;
   sm = sm_abs > sm ? sm_abs : sm;
   sm = sm_route > sm ? sm_route : sm;
+  sm = (size_t)kExpSmem > sm ? (size_t)kExpSmem : sm;   // expert rings + activation row cache
   *smem = align_up(sm, 128);
   return KK3_OK;
 }

@@ -418,9 +418,8 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   __shared__ GemvJob sj[kMaxJobs];
   __shared__ GemvJob sj2[2];
   __shared__ ExpertPhase sph;
-  __shared__ float e8m0_lut[256];   // E8M0 scale byte -> FP32 factor, read by the MXFP4 expert engine
   __shared__ int sjn;
-  for (int i = threadIdx.x; i < 256; i += kThreads) e8m0_lut[i] = e8m0_to_f32((unsigned)i);
+  for (int i = threadIdx.x; i < 256; i += kThreads) kk3_e8m0_lut[i] = e8m0_to_f32((unsigned)i);
   if (threadIdx.x == 0) kk3_cur_phase = 0;
   __syncthreads();
   const Geo& g = a.g;
@@ -589,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         });
         // every CTA routes all rows (identical tables), then the experts start (kimi.py:309-316)
         route_cta(a, l, smem, phase);
-        run_experts<2>(a, sph, e8m0_lut);
+        run_experts<2>(a, sph);
       }
       KK3_PHASE_END();
       if (KK3_RUN) {
@@ -607,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         // routed experts' fix-up uses counter bank 0, so this one takes bank 1
         run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, x_moe & 1, 1);
         if (g.tp > 1) __threadfence_system();
-        run_experts<1>(a, sph, e8m0_lut);
+        run_experts<1>(a, sph);
       }
       KK3_PHASE_END();
       if (KK3_RUN && !phase_moe_combine(a, l, seq0 + x_moe, x_moe & 1, fsm)) return;
