@@ -580,8 +580,8 @@ KK3_DEV unsigned lds32(const unsigned char* p) { return *reinterpret_cast<const 
 // filled at kernel start; at namespace scope so the engine's reads compile to shared-memory loads
 static __shared__ float kk3_e8m0_lut[256];
 
-constexpr int kExpRing = 8704;            // per-warp ring bytes: four MT=2 pair slots (2176 B) or eight MT=1
-constexpr int kExpXCache = 64 * 1024;     // per-CTA activation row cache, after the rings
+constexpr int kExpRing = 10240;           // per-warp ring bytes: four MT=2 pair slots (2560 B) or six MT=1
+constexpr int kExpXCache = 56 * 1024;     // per-CTA activation row cache, after the rings
 constexpr int kExpSmem = kWarps * kExpRing + kExpXCache;
 
 KK3_DEV void ldsm4(unsigned (&r)[4], unsigned addr) {
@@ -618,7 +618,9 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
   __shared__ int s_first, s_count;        // MT == 1: pairs [s_first, s_first + s_count) staged
   __shared__ int s_rowmap[kMaxBatch];     // MT == 2: cache slot i holds latent row s_rowmap[i]
   constexpr int kCode = 16 * 64;                  // code bytes per matrix and unit pair
-  constexpr int kScale = 16 * 4;                  // scale bytes per matrix and unit pair (one word per row)
+  // scale bytes per matrix and unit pair: the 16-byte window (four pairs) of every row, or, when a row's scales
+  // are not a multiple of 16 bytes, the tile's whole scale block (16 rows x K/32 bytes, contiguous)
+  constexpr int kScale = MT == 2 ? 256 : 512;
   constexpr int kSlot = MT * (kCode + kScale);
   constexpr int S = (kExpRing / kSlot) > 12 ? 12 : (kExpRing / kSlot);
   static_assert(S >= 4, "ring too shallow");
@@ -726,12 +728,17 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
   int p_chunk = c0, p_tile = t0, p_kp = kp0;
   const int prow = lane >> 2, pq = lane & 3;                                   // row (and row + 8), 16-byte chunk
   const unsigned p_dst_code = prow * 64 + ((pq ^ ((prow >> 1) & 3)) << 4);     // swizzled chunk of the row
-  const int scl_mt = lane >> 4, scl_row = lane & 15;                           // scale row this lane stages
-  const bool scl_lane = scl_mt < MT;
-  const unsigned p_dst_scl = MT * kCode + scl_mt * kScale + scl_row * 4;
   const uint8_t* p_code[MT];   // this lane's 16 code bytes of row prow of the current pair, per matrix
-  const uint8_t* p_scl = ph.scales[0];
   const size_t rowbytes = (size_t)(ph.K >> 1), sbytes = (size_t)(ph.K >> 5);
+  // scales with 16-byte copies (L1 bypassed): windowed (K % 512 == 0) - lane (mt, row) copies the 16-byte
+  // window of its row holding pairs 4w..4w+3 - or whole-tile (K <= 512, or K <= 1024 for MT = 1) - lane
+  // (mt, piece) copies one 16-byte piece of the tile's contiguous 16 x K/32-byte scale block
+  const bool swin = (sbytes & 15) == 0;
+  const int spm = MT == 2 ? 16 : 32;                                             // lanes per matrix
+  const int scl_mt = lane / spm, scl_i = lane % spm;                             // matrix, row or piece
+  const bool scl_lane = scl_mt < MT && (swin ? scl_i < 16 : scl_i < (int)sbytes);
+  const unsigned p_dst_scl = MT * kCode + scl_mt * kScale + scl_i * 16;
+  const uint8_t* p_scl = ph.scales[0];   // this lane's window row (plus 16 * window) or tile piece
   const unsigned long long pol = l2_evict_first_policy();   // codes are read once per step
   auto p_setup = [&]() {
     const size_t e = (size_t)chunk_expert(p_chunk);
@@ -739,7 +746,8 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
     for (int mt = 0; mt < MT; ++mt)
       p_code[mt] = ph.codes[mt] + e * ph.expert_codes + (size_t)(p_tile * 16 + prow) * rowbytes + p_kp * 64 + pq * 16;
     if (scl_lane)
-      p_scl = ph.scales[scl_mt] + e * ph.expert_scales + (size_t)(p_tile * 16 + scl_row) * sbytes + p_kp * 4;
+      p_scl = ph.scales[scl_mt] + e * ph.expert_scales +
+              (swin ? (size_t)(p_tile * 16 + scl_i) * sbytes : (size_t)p_tile * 16 * sbytes + scl_i * 16);
   };
   int p_left = npairs, p_slot = 0;
   auto p_issue = [&]() {
@@ -753,8 +761,8 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
       p_code[mt] += 64;
     }
     if (scl_lane)
-      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(slot + p_dst_scl), "l"(p_scl) : "memory");
-    p_scl += 4;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(slot + p_dst_scl),
+                   "l"(p_scl + (swin ? (p_kp >> 2) * 16 : 0)) : "memory");
     p_slot = p_slot + 1 == S ? 0 : p_slot + 1;
     --p_left;
     if (++p_kp == kpairs) {
@@ -826,7 +834,10 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
   int c_slot = 0;
   const int lrow = lane & 7, lq = lane >> 3;   // ldmatrix: this lane addresses row lrow (+8) of chunk lq
   const unsigned c_ldsm = lrow * 64 + ((lq ^ ((lrow >> 1) & 3)) << 4);
-  const unsigned c_scl = MT * kCode + r * 4;
+  // this lane's scale words (rows r, r + 8) of pair kp: + (kp & 3) * 4 (windowed) or + kp * 4 (whole tile)
+  const unsigned c_scl_a = MT * kCode + r * (swin ? 16u : (unsigned)sbytes);
+  const unsigned c_scl_b = MT * kCode + (r + 8) * (swin ? 16u : (unsigned)sbytes);
+  const int c_kmask = swin ? 3 : 0x7fffffff;
   float acc[MT][1][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
@@ -856,8 +867,9 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
     for (int mt = 0; mt < MT; ++mt) {
       ldsm4(wa[mt], slot + mt * kCode + c_ldsm);
       ldsm4(wb[mt], slot + mt * kCode + 512 + c_ldsm);
-      sa[mt] = *reinterpret_cast<const unsigned*>(ring + (slot - ring_s) + c_scl + mt * kScale);
-      sb[mt] = *reinterpret_cast<const unsigned*>(ring + (slot - ring_s) + c_scl + mt * kScale + 32);
+      const unsigned char* sl = ring + (slot - ring_s) + mt * kScale + (c_kp & c_kmask) * 4;
+      sa[mt] = *reinterpret_cast<const unsigned*>(sl + c_scl_a);
+      sb[mt] = *reinterpret_cast<const unsigned*>(sl + c_scl_b);
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {

@@ -109,8 +109,13 @@ static int validate(const kk3_config* c) {
       c->context >= 1 && c->attn_res_block_size >= 1 && c->first_dense >= 0 &&
       (c->layers + c->attn_res_block_size - 1) / c->attn_res_block_size <= kMaxBlocks - 1 &&
       (long long)c->heads * 128 % 64 == 0 && (long long)c->vocab_shard * c->batch < (1ll << 31) &&
-      // MoE layers: the expert engine stages each row's scales for two 64-k steps as one aligned 4-byte word
-      (c->layers <= c->first_dense || (c->latent_hidden % 128 == 0 && c->inter_shard % 128 == 0));
+      // MoE layers: the expert engine walks 128-k unit pairs and copies scales in 16-byte pieces, either a
+      // 16-byte window per row (K % 512 == 0) or the tile's whole scale block (gate/up: K = latent_hidden
+      // <= 512; down: K = inter_shard <= 1024)
+      (c->layers <= c->first_dense ||
+       (c->latent_hidden % 128 == 0 && c->inter_shard % 128 == 0 &&
+        (c->latent_hidden % 512 == 0 || c->latent_hidden <= 512) &&
+        (c->inter_shard % 512 == 0 || c->inter_shard <= 1024)));
   return ok ? KK3_OK : KK3_ERR_UNSUPPORTED;
 }
 
