@@ -708,6 +708,7 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
   }
   const unsigned long long xmask = s_mask;
   const int xfirst = s_first, xcount = s_count;
+  if (blockIdx.x == 0 && threadIdx.x == 0) sub_stamp(a, kk3_cur_phase, 1);   // activation rows staged
 
   const int gw = cw0 + warp;
   if (gw >= GW) return;
@@ -740,8 +741,14 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
   const unsigned p_dst_scl = MT * kCode + scl_mt * kScale + scl_i * 16;
   const uint8_t* p_scl = ph.scales[0];   // this lane's window row (plus 16 * window) or tile piece
   const unsigned long long pol = l2_evict_first_policy();   // codes are read once per step
+  int p_echunk = -1;   // chunk whose expert id is cached in p_e (tiles of a chunk share the expert)
+  size_t p_e = 0;
   auto p_setup = [&]() {
-    const size_t e = (size_t)chunk_expert(p_chunk);
+    if (p_chunk != p_echunk) {
+      p_e = (size_t)chunk_expert(p_chunk);
+      p_echunk = p_chunk;
+    }
+    const size_t e = p_e;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
       p_code[mt] = ph.codes[mt] + e * ph.expert_codes + (size_t)(p_tile * 16 + prow) * rowbytes + p_kp * 64 + pq * 16;

@@ -323,6 +323,31 @@ KK3_FN bool phase_argmax(const StepArgs& a, unsigned seq, int parity) {
   return true;
 }
 
+// The row phases read a few per-layer vectors once each, at the head of latency-bound chains. The phase
+// before each of them asks for those vectors in L2 (three bulk prefetches from the last CTA), so the row
+// phase finds them there instead of in HBM.
+KK3_DEV void prefetch_vectors(const void* v0, const void* v1, const void* v2, int bytes) {
+  if (blockIdx.x != gridDim.x - 1 || threadIdx.x >= 3) return;
+  const void* v = threadIdx.x == 0 ? v0 : (threadIdx.x == 1 ? v1 : v2);
+  const unsigned n = (unsigned)bytes & ~15u;
+  if (v && (reinterpret_cast<uintptr_t>(v) & 15u) == 0 && n >= 16) prefetch_l2(v, n);
+}
+// attention (which = 0) or MLP (1) prologue vectors of layer l, the head's (l = L), or the latent norm (2)
+KK3_DEV void prefetch_row_inputs(const StepArgs& a, int which, int l) {
+  const Geo& g = a.g;
+  if (which == 2) {
+    prefetch_vectors(lptr<bf16>(a, l, KK3_MOE_LATENT_NORM), nullptr, nullptr, g.lh * 2);
+  } else if (l >= g.L) {
+    prefetch_vectors(gptr<bf16>(a, KK3_FNORM), gptr<bf16>(a, KK3_OUTPUT_RES_NORM), gptr<bf16>(a, KK3_OUTPUT_RES_PROJ),
+                     g.h * 2);
+  } else {
+    const size_t o = (size_t)l * g.h;
+    prefetch_vectors(gptr<bf16>(a, which ? KK3_MLP_RES_NORM : KK3_ATTENTION_RES_NORM) + o,
+                     gptr<bf16>(a, which ? KK3_MLP_RES_PROJ : KK3_ATTENTION_RES_PROJ) + o,
+                     gptr<bf16>(a, which ? KK3_LN2 : KK3_LN1) + o, g.h * 2);
+  }
+}
+
 // ---- job lists of the GEMV phases (built identically by every thread) ---------------------------------
 
 KK3_DEV void job_init(GemvJob& j, const bf16* w, int rows, int K, const bf16* x, int ldx, int ncols, int epi, void* out,
@@ -446,7 +471,10 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   if (blockIdx.x == 0 && threadIdx.x == 0) a.s.phase_ts[0] = globaltimer();
   trace_progress(a, 0, 0);
   // embedding (kimi.py:249-252)
-  if (KK3_RUN) phase_embed(a, seq0 + xi, xi & 1, fsm);
+  if (KK3_RUN) {
+    prefetch_row_inputs(a, 0, 0);
+    phase_embed(a, seq0 + xi, xi & 1, fsm);
+  }
   int pending = PEND_EMBED;
   bool pend_signal = false;
   unsigned pend_x = xi++;
@@ -535,6 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
     // o projection -> exchange
     if (KK3_RUN) {
       KK3_BUILD(o_job(a, l, sj[0]));
+      prefetch_row_inputs(a, 1, l);
       run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, xi & 1);
       if (g.tp > 1) __threadfence_system();
     }
@@ -556,6 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
           sj[0].aux_off = a.comm.att_off;
           prepare_jobs(sj, 1);
         });
+        prefetch_row_inputs(a, 0, l + 1);
         run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, xi & 1);
         if (g.tp > 1) __threadfence_system();
       }
@@ -604,8 +634,10 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         });
         // the shared expert's down projection first (kimi.py:326), then the routed experts' (:320-323); the
         // routed experts' fix-up uses counter bank 0, so this one takes bank 1
+        prefetch_row_inputs(a, 2, l);
         run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, x_moe & 1, 1);
         if (g.tp > 1) __threadfence_system();
+        if (blockIdx.x == 0 && threadIdx.x == 0) sub_stamp(a, phase, 0);
         run_experts<1>(a, sph);
       }
       KK3_PHASE_END();
@@ -614,6 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
       // latent up + shared + residual (kimi.py:325-329)
       if (KK3_RUN) {
         KK3_BUILD(latent_up_job(a, l, sj[0]));
+        prefetch_row_inputs(a, 0, l + 1);
         run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, 0);
       }
       KK3_PHASE_END();
