@@ -855,20 +855,20 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
     __syncwarp();   // every lane is done with the slot the next issue overwrites
     if (p_left > 0) p_issue();
     cp_async_commit_g();
-    // this pair's activation pieces: k = 128 kp + 64 u + 32 g + 8c, group j = 2u + g; the first is loaded
-    // before the ring wait, each next one while the previous group is being multiplied
-    const int xko = c_kp * 256 + c * 16;
-    auto ldx = [&](int j) -> uint4 {
-      if (x_shared) return *reinterpret_cast<const uint4*>(xcache + x_off + xko + j * 64);   // shared
-      return *reinterpret_cast<const uint4*>(xp + xko + j * 64);                              // generic
-    };
-    uint4 xn = ldx(0);
     cp_async_wait_g<S - 1>();
     __syncwarp();
     if (trace && n < 2) trace_warp(a, 5 | (n << 8));
     const unsigned slot = ring_s + c_slot * kSlot;
     c_slot = c_slot + 1 == S ? 0 : c_slot + 1;
     const bool lo = n > 0 || lo_first, hi = n < npairs - 1 || hi_last;
+    // this pair's activation pieces: k = 128 kp + 64 u + 32 g + 8c, group j = 2u + g; each next one is
+    // loaded while the previous group is being multiplied
+    const int xko = c_kp * 256 + c * 16;
+    auto ldx = [&](int j) -> uint4 {
+      if (x_shared) return *reinterpret_cast<const uint4*>(xcache + x_off + xko + j * 64);   // shared
+      return *reinterpret_cast<const uint4*>(xp + xko + j * 64);                              // generic
+    };
+    uint4 xn = ldx(0);
     unsigned wa[MT][4], wb[MT][4], sa[MT], sb[MT];   // group words and scale words of rows r and r + 8
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
@@ -901,13 +901,14 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
     }
     if ((c_kp == kpairs - 1 && hi) || n == npairs - 1) {
       const int tile_beg = c_chunk * per_chunk + c_tile * ksteps;
-      const bool inside = tile_beg >= ubeg && tile_beg + ksteps <= uend;   // the whole tile is this warp's
-      const long long first = inside ? gw : owner_of(tile_beg, U, GW);
-      const long long lastw = inside ? gw : owner_of(tile_beg + ksteps - 1, U, GW);
-      bool done = first == lastw;
-      if (!done)
-        done = stream_k_fixup<1, MT>(a, a.s.fix_part, a.s.fix_cnt + c_chunk * tiles + c_tile, gw,
-                                     tile_beg <= ubeg, tile_beg, first, lastw, U, GW, acc);
+      // the whole tile is this warp's: no fix-up (owners are computed only for split tiles, a 64-bit division)
+      bool done = tile_beg >= ubeg && tile_beg + ksteps <= uend;
+      if (!done) {
+        const long long first = owner_of(tile_beg, U, GW), lastw = owner_of(tile_beg + ksteps - 1, U, GW);
+        done = first == lastw ||
+               stream_k_fixup<1, MT>(a, a.s.fix_part, a.s.fix_cnt + c_chunk * tiles + c_tile, gw, tile_beg <= ubeg,
+                                     tile_beg, first, lastw, U, GW, acc);
+      }
       if (done) expert_epilogue<MT>(ph.rows, c_tile, out_row, acc);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)

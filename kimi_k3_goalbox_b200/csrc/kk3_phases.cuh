@@ -814,13 +814,19 @@ KK3_DEV void route_group_pairs(const StepArgs& a, unsigned char* smem) {
       wtot[kWarps + warp] = pc + ca + cb;
     }
     __syncthreads();
-    int base = 0, cbase = 0, ctotal = 0;
-#pragma unroll 1
-    for (int w = 0; w < kWarps; ++w) {
-      base += w < warp ? wtot[w] : 0;
-      cbase += w < warp ? wtot[kWarps + w] : 0;
-      ctotal += wtot[kWarps + w];
+    // exclusive prefix of the warp totals: lane w < kWarps holds warp w's totals, scanned with shuffles
+    int tp = lane < kWarps ? wtot[lane] : 0, tc = lane < kWarps ? wtot[kWarps + lane] : 0;
+#pragma unroll
+    for (int o = 1; o < kWarps; o <<= 1) {
+      const int up = __shfl_up_sync(0xffffffffu, tp, o), uc = __shfl_up_sync(0xffffffffu, tc, o);
+      if (lane >= o) {
+        tp += up;
+        tc += uc;
+      }
     }
+    const int base = warp > 0 ? __shfl_sync(0xffffffffu, tp, warp - 1) : 0;
+    const int cbase = warp > 0 ? __shfl_sync(0xffffffffu, tc, warp - 1) : 0;
+    const int ctotal = __shfl_sync(0xffffffffu, tc, kWarps - 1);
     if (ea < g.E) {
       off[ea] = base + pa;
       coff[ea] = cbase + pc;
@@ -886,19 +892,34 @@ KK3_FN void route_cta(const StepArgs& a, int layer, unsigned char* smem, int ph 
   const int nper = (E + 31) >> 5, e0 = lane * nper;
   const int nlive = E - e0 < 0 ? 0 : (E - e0 < nper ? E - e0 : nper);   // this lane's real experts
   int* ids = reinterpret_cast<int*>(smem);   // [B*K] sorted per row
-  // bias and each warp's scores in the same lane-major layout [lane][kRouteStride] (16-byte aligned rows)
-  float* bias_l = reinterpret_cast<float*>(smem + kRouteBiasOff) + lane * kRouteStride;
+  // bias and each warp's scores: linear ([e], lane l's run at l * n) when n % 4 == 0 and E % 4 == 0, so that
+  // the staging copies are coalesced 16-byte pieces and each lane reads its run 16 bytes at a time (a lane
+  // stride of n words, a multiple of 4 but not of 8, is bank-conflict free); else lane-major rows
+  // [lane][kRouteStride] filled with 4-byte copies
+  const bool lin = (nper & 3) == 0 && (E & 3) == 0;
+  const int lstride = lin ? nper : kRouteStride;
+  float* bias_w = reinterpret_cast<float*>(smem + kRouteBiasOff);
+  float* bias_l = bias_w + lane * lstride;
   float* sc_w = reinterpret_cast<float*>(smem + kRouteKeyOff) + (size_t)warp * 32 * kRouteStride;
-  float* sc_l = sc_w + lane * kRouteStride;
+  float* sc_l = sc_w + lane * lstride;
   const float* bias = lptr<float>(a, layer, KK3_MOE_ROUTER_BIAS);
   long long* out_ids = gout<long long>(a, KK3_OUT_EXPERT_IDS) + (size_t)layer * g.B * K;
   const bool stamp = ph >= 0 && blockIdx.x == 0 && tid == 0;
   auto stage_row = [&](int b) {
-    const float* sc = a.s.scores + (size_t)b * E + e0;
+    if (lin) {
+      const float* sc = a.s.scores + (size_t)b * E;
 #pragma unroll 1
-    for (int i = 0; i < nlive; ++i) cp_async4_ca(sc_l + i, sc + i);
+      for (int q = lane; q < (E >> 2); q += 32) cp_async16(sc_w + 4 * q, sc + 4 * q);
+    } else {
+      const float* sc = a.s.scores + (size_t)b * E + e0;
+#pragma unroll 1
+      for (int i = 0; i < nlive; ++i) cp_async4_ca(sc_l + i, sc + i);
+    }
   };
-  if (warp == 0) {
+  if (lin) {
+#pragma unroll 1
+    for (int q = tid; q < (E >> 2); q += kThreads) cp_async16(bias_w + 4 * q, bias + 4 * q);
+  } else if (warp == 0) {
 #pragma unroll 1
     for (int i = 0; i < nlive; ++i) cp_async4_ca(bias_l + i, bias + e0 + i);
   }
@@ -910,9 +931,11 @@ KK3_FN void route_cta(const StepArgs& a, int layer, unsigned char* smem, int ph 
 #pragma unroll 1
   for (int b = warp; b < g.B; b += kWarps) {
     if (b != warp) {
+      __syncwarp();   // every lane is done with the previous row (linear layout: lanes read each other's copies)
       stage_row(b);
       cp_async_commit();
       cp_async_wait_all();
+      __syncwarp();
     }
     // keys; absent experts and padding get key 0, below every real key
     unsigned key[kPer];
@@ -1002,7 +1025,7 @@ KK3_FN void route_cta(const StepArgs& a, int layer, unsigned char* smem, int ph 
     // weights: the unbiased scores of the chosen experts, from the staged row
     int e = lane < K ? row_ids[lane] : 0;
     e = e < 0 ? 0 : (e >= E ? E - 1 : e);
-    const float w = lane < K ? sc_w[(e / nper) * kRouteStride + e % nper] : 0.0f;
+    const float w = lane < K ? sc_w[lin ? e : (e / nper) * kRouteStride + e % nper] : 0.0f;
     const float wsum = warp_sum(w);
     if (lane < K) {
       row_ids[lane] = e;
