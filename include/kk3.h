@@ -67,9 +67,11 @@ typedef struct kk3_ctx kk3_ctx;
  *   slots [0, KK3_GLOBAL_SLOTS): the global inputs and the outputs (enum below);
  *   then KK3_LAYER_SLOTS slots per layer l at KK3_GLOBAL_SLOTS + l*KK3_LAYER_SLOTS + slot.
  * Every tensor must be contiguous, on the context's device, with the reference's shape and dtype
- * (kimi.py:72-122 weights, :164-182 state, :332-340 outputs). Unused slots may be NULL. Every pointer except
- * KK3_TOKEN and KK3_RESET must be 16-byte aligned (read with 16-byte vector loads); the step entry points
- * return KK3_ERR_ARG otherwise, before launching anything. */
+ * (kimi.py:72-122 weights, :164-182 state, :332-340 outputs). Slots the geometry does not use may be NULL
+ * (per layer: the other attention kind's and the other FFN kind's slots; the MLA cache outputs without MLA
+ * layers, the KDA state outputs without KDA layers); every used slot must be non-NULL. Every pointer except
+ * KK3_TOKEN and KK3_RESET must be 16-byte aligned (read with 16-byte vector loads). The step entry points
+ * return KK3_ERR_ARG for a NULL used slot or a misaligned pointer, before launching anything. */
 enum kk3_global_slot {
     KK3_TOKEN = 0, KK3_RESET, KK3_EMBED, KK3_LM_HEAD, KK3_FNORM, KK3_OUTPUT_RES_NORM, KK3_OUTPUT_RES_PROJ,
     KK3_LN1, KK3_LN2, KK3_ATTENTION_RES_NORM, KK3_MLP_RES_NORM, KK3_ATTENTION_RES_PROJ, KK3_MLP_RES_PROJ,
@@ -96,6 +98,11 @@ enum kk3_layer_slot {
 
 /* Number of pointer-table slots for a geometry: KK3_GLOBAL_SLOTS + layers * KK3_LAYER_SLOTS. */
 int kk3_table_size(const kk3_config* cfg);
+
+/* Check a pointer table against a geometry on the host only (no CUDA call): KK3_OK, or KK3_ERR_ARG when its
+ * size is wrong, a used slot is NULL or a pointer is misaligned; the step entry points make the same checks
+ * before launching. */
+int kk3_check_table(const kk3_config* cfg, const void* const* table, int table_size);
 
 /* Create a context: validate the geometry, allocate device scratch and the symmetric exchange buffer.
  * Replaces the reference's per-rank set-up inside `build(case)` (megabench/harness/runner.py:53-69,

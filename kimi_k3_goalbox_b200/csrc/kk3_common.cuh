@@ -46,7 +46,8 @@ struct Geo {
   int mla_chunk_len; // positions per chunk (multiple of kMlaPos)
   long long fix_bank; // floats per stream-K partial bank (two banks: two GEMV passes may share a phase)
   int cnt_bank;       // counters per stream-K counter bank
-  int mla_mt;         // 16-row head tiles of the MLA attention (ceil(hr / 16))
+  int mla_mt;         // 16-row head tiles per head group of the MLA attention (<= 4)
+  int mla_groups;     // head groups: ceil(ceil(hr / 16) / mla_mt)
 };
 
 // scratch buffers (device pointers owned by the context)

@@ -65,6 +65,21 @@ struct kk3_ctx {
   void* buf_ptr[KK3_BUF_COUNT] = {};
 };
 
+// MLA attention work split: heads in groups of at most four 16-row tiles (the accumulators of a group stay
+// in registers), and each batch row's attended positions in chunks so that rows x chunks x groups items fill
+// one wave of the grid.
+static void plan_mla(Geo& g, int grid) {
+  const int tiles = (g.hr + 15) / 16;
+  g.mla_groups = (tiles + 3) / 4;
+  g.mla_mt = (tiles + g.mla_groups - 1) / g.mla_groups;
+  int chunks = grid / (g.B * g.mla_groups);
+  chunks = chunks < 1 ? 1 : (chunks > 64 ? 64 : chunks);
+  int len = (g.ctx + 1 + chunks - 1) / chunks;
+  len = (len + kMlaPos - 1) / kMlaPos * kMlaPos;
+  g.mla_chunk_len = len;
+  g.mla_chunks = (g.ctx + 1 + len - 1) / len;
+}
+
 static int cuda_fail(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return KK3_OK;
   fprintf(stderr, "kk3: %s failed: %s\n", what, cudaGetErrorString(e));
@@ -143,21 +158,12 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   }
   g.nblk = (g.L + g.bs - 1) / g.bs;
   g.timeout_ns = cfg->timeout_ns > 0 ? cfg->timeout_ns : 10000000000ll;
-  g.mla_mt = (g.hr + 15) / 16;
-  if (g.mla_mt == 5) g.mla_mt = 6;   // the attention kernel is instantiated for 1-4 and 6 head tiles
   cudaDeviceProp prop;
   if (cudaGetDeviceProperties(&prop, cfg->device) != cudaSuccess) { delete x; return KK3_ERR_CUDA; }
   x->sms = prop.multiProcessorCount;
   x->grid = x->sms;
   x->nt = g.B <= 8 ? 1 : (g.B <= 16 ? 2 : (g.B <= 32 ? 4 : 8));
-  {
-    int chunks = x->grid / g.B;
-    chunks = chunks < 1 ? 1 : (chunks > 64 ? 64 : chunks);
-    int len = (g.ctx + 1 + chunks - 1) / chunks;
-    len = (len + kMlaPos - 1) / kMlaPos * kMlaPos;
-    g.mla_chunk_len = len;
-    g.mla_chunks = (g.ctx + 1 + len - 1) / len;
-  }
+  plan_mla(g, x->grid);
   const long long gw = (long long)x->grid * kWarps;
   g.fix_bank = 2ll * gw * (2 * x->nt * 128);
   {
@@ -349,12 +355,48 @@ static bool table_aligned(const void* const* table, int n) {
   return true;
 }
 
+// Slots the geometry reads or writes (the runtime's table layout): the global inputs, the outputs (the MLA
+// cache rows only with MLA layers, the KDA states only with KDA layers), and per layer its attention block
+// (MLA or KDA) and its FFN block (dense or MoE). Every one of them must be non-NULL; the rest may be NULL.
+static bool slot_required(const Geo& g, int i) {
+  if (i < KK3_GLOBAL_SLOTS) {
+    if (i == KK3_OUT_KV_WRITE || i == KK3_OUT_PE_WRITE) return g.nmla > 0;
+    if (i == KK3_OUT_RECURRENT_STATE || i == KK3_OUT_CONV_STATE) return g.nkda > 0;
+    return i <= KK3_OUT_CACHE_LENGTH;
+  }
+  const int l = (i - KK3_GLOBAL_SLOTS) / KK3_LAYER_SLOTS, s = (i - KK3_GLOBAL_SLOTS) % KK3_LAYER_SLOTS;
+  const bool mla = ((l + 1) % 4 == 0) || l == g.L - 1;
+  if (s < KK3_DENSE_GATE) return s <= (mla ? (int)KK3_MLA_PE_CACHE : (int)KK3_KDA_RECURRENT_STATE);
+  return s <= (l < g.first_dense ? (int)KK3_DENSE_DOWN : (int)KK3_MOE_SHARED_DOWN);
+}
+
+static bool table_complete(const void* const* table, int n, const Geo& g) {
+  for (int i = 0; i < n; ++i)
+    if (table[i] == nullptr && slot_required(g, i)) return false;
+  return true;
+}
+
+extern "C" int kk3_check_table(const kk3_config* cfg, const void* const* table, int table_size) {
+  const int rc = validate(cfg);
+  if (rc != KK3_OK) return rc;
+  if (!table || table_size != KK3_GLOBAL_SLOTS + cfg->layers * KK3_LAYER_SLOTS || table_size > kMaxPtrs ||
+      !table_aligned(table, table_size))
+    return KK3_ERR_ARG;
+  Geo g{};
+  g.L = cfg->layers;
+  g.first_dense = cfg->first_dense;
+  for (int l = 0; l < g.L; ++l) {
+    if (((l + 1) % 4 == 0) || l == g.L - 1) ++g.nmla; else ++g.nkda;
+  }
+  return table_complete(table, table_size, g) ? KK3_OK : KK3_ERR_ARG;
+}
+
 static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int stop_phase, int start_phase) {
   if (!x || !table) return KK3_ERR_ARG;
   if (x->failed) return KK3_ERR_FAILED;
   if (!x->peers_open) return KK3_ERR_PEERS;
   const int need = KK3_GLOBAL_SLOTS + x->g.L * KK3_LAYER_SLOTS;
-  if (n != need || n > kMaxPtrs || !table_aligned(table, n)) return KK3_ERR_ARG;
+  if (n != need || n > kMaxPtrs || !table_aligned(table, n) || !table_complete(table, n, x->g)) return KK3_ERR_ARG;
   if (*x->err_host != 0) {
     x->failed = 1;
     return KK3_ERR_FAILED;
@@ -507,17 +549,8 @@ static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, Ste
   }
   g.nblk = (g.L + g.bs - 1) / g.bs;
   g.timeout_ns = cfg->timeout_ns > 0 ? cfg->timeout_ns : 10000000000ll;
-  g.mla_mt = (g.hr + 15) / 16;
-  if (g.mla_mt == 5) g.mla_mt = 6;   // the attention kernel is instantiated for 1-4 and 6 head tiles
   *nt = g.B <= 8 ? 1 : (g.B <= 16 ? 2 : (g.B <= 32 ? 4 : 8));
-  {
-    int chunks = sms / g.B;
-    chunks = chunks < 1 ? 1 : (chunks > 64 ? 64 : chunks);
-    int len = (g.ctx + 1 + chunks - 1) / chunks;
-    len = (len + kMlaPos - 1) / kMlaPos * kMlaPos;
-    g.mla_chunk_len = len;
-    g.mla_chunks = (g.ctx + 1 + len - 1) / len;
-  }
+  plan_mla(g, sms);
   const long long gw = (long long)sms * kWarps;
   g.fix_bank = 2ll * gw * (2 * *nt * 128);
   {
@@ -662,6 +695,7 @@ extern "C" int kk3_step_noalloc(const kk3_config* cfg, const void* const* table,
   plan_noalloc(cfg, d->sms, d->base, &a, &total, &zero, &nt, &smem);
   if (total > kNoAllocScratchBytes) return KK3_ERR_TOO_LARGE;
   if (smem > d->smem_optin) return KK3_ERR_UNSUPPORTED;
+  if (!table_complete(table, table_size, a.g)) return KK3_ERR_ARG;   // before anything is cleared or launched
   // The kernel's dynamic shared memory limit is per-function state shared with kk3_init, which sets it to its
   // own geometry's need. It is raised here when below this launch's need and never lowered, so a live context
   // keeps working and a lower value a later kk3_init left is undone.

@@ -528,9 +528,13 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         int total = 0;
         #pragma unroll 1
         for (int b = 0; b < g.B; ++b) total += reset[b] ? 1 : g.mla_chunks;
+        total *= g.mla_groups;
         #pragma unroll 1
         for (int it = blockIdx.x; it < total; it += gridDim.x) {
-          int b = 0, rem = it;
+          // item -> (batch row, chunk, head group); the groups of one chunk are adjacent items, so the second
+          // read of the chunk's cache rows comes from L2
+          const int grp = it % g.mla_groups;
+          int b = 0, rem = it / g.mla_groups;
           for (; b < g.B; ++b) {
             const int n = reset[b] ? 1 : g.mla_chunks;
             if (rem < n) break;
@@ -540,13 +544,13 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
           const int p0 = rem * g.mla_chunk_len;
           int p1 = p0 + g.mla_chunk_len;
           p1 = p1 < T ? p1 : T;
-          // one instantiation per head-tile count (hr <= 96): accumulators sized exactly, 3 stages up to 64 heads
+          const int h0 = grp * g.mla_mt * 16;
+          // one instantiation per head-tile count of a group: accumulators sized exactly, three stages
           switch (g.mla_mt) {
-            case 1: mla_attend_item<1, 3>(a, l, midx, b, rem, p0, p1, T, smem, phase); break;
-            case 2: mla_attend_item<2, 3>(a, l, midx, b, rem, p0, p1, T, smem, phase); break;
-            case 3: mla_attend_item<3, 3>(a, l, midx, b, rem, p0, p1, T, smem, phase); break;
-            case 4: mla_attend_item<4, 3>(a, l, midx, b, rem, p0, p1, T, smem, phase); break;
-            default: mla_attend_item<6, 2>(a, l, midx, b, rem, p0, p1, T, smem, phase); break;
+            case 1: mla_attend_item<1, 3>(a, l, midx, b, rem, p0, p1, T, h0, smem, phase); break;
+            case 2: mla_attend_item<2, 3>(a, l, midx, b, rem, p0, p1, T, h0, smem, phase); break;
+            case 3: mla_attend_item<3, 3>(a, l, midx, b, rem, p0, p1, T, h0, smem, phase); break;
+            default: mla_attend_item<4, 3>(a, l, midx, b, rem, p0, p1, T, h0, smem, phase); break;
           }
         }
       }

@@ -530,12 +530,12 @@ KK3_DEV void mla_stage(const MlaSrc& src, int t0, int T, bf16* dst) {
 // sub-tiles of 32 stream through an NS-deep cp.async ring; the score product S = Q K^T is split over
 // (head tile, 8 positions, k-quarter) so every warp works, and the k-partials are summed in a fixed order.
 template <int MT, int NS>
-KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int chunk, int p0, int p1, int T,
+KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int chunk, int p0, int p1, int T, int h0,
                             unsigned char* smem, int ph = -1) {
   const Geo& g = a.g;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, r = lane >> 2, c = lane & 3;
   constexpr int HR = MT * 16;
-  const bool stamp = ph >= 0 && b == 0 && chunk == 0 && tid == 0;   // sub-phase stamps of one item
+  const bool stamp = ph >= 0 && b == 0 && chunk == 0 && h0 == 0 && tid == 0;   // sub-phase stamps of one item
   if (stamp) sub_stamp(a, ph, 0);
   const int KQ = mla_kq(MT), kper = (g.kr + g.rd) / 16 / KQ;   // 36 k-steps of 16, split KQ ways
   bf16* Qs = reinterpret_cast<bf16*>(smem);                         // [HR][kRowK]
@@ -557,14 +557,14 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
   src.pol = l2_evict_first_policy();
   src.kr = g.kr;
   src.rd = g.rd;
-  // Q rows: absorbed (512) | q rope (64), copied asynchronously in the group of the first sub-tile; zero for
-  // padded heads
+  // Q rows of heads h0 .. h0 + HR - 1: absorbed (512) | q rope (64), copied asynchronously in the group of the
+  // first sub-tile; zero for padded heads
   for (int i = tid; i < HR * 72; i += kThreads) {
-    const int hh = i / 72, q = i % 72;
+    const int hh = i / 72, q = i % 72, h = h0 + hh;
     bf16* d = Qs + hh * kRowK + q * 8;
-    if (hh < g.hr) {
-      cp_async16(d, q < 64 ? a.s.absorbed + (((size_t)b * g.hr + hh) * g.kr) + q * 8
-                           : a.s.mla_q + ((size_t)b * g.hr + hh) * (g.nr + g.rd) + g.nr + (q - 64) * 8);
+    if (h < g.hr) {
+      cp_async16(d, q < 64 ? a.s.absorbed + (((size_t)b * g.hr + h) * g.kr) + q * 8
+                           : a.s.mla_q + ((size_t)b * g.hr + h) * (g.nr + g.rd) + g.nr + (q - 64) * 8);
     } else {
       *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
     }
@@ -627,7 +627,7 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
     if (stamp && s < 2) sub_stamp(a, ph, 3 + 4 * s);
     // online softmax, one warp per head row, one lane per position (k-partials summed in order)
     for (int hh = warp; hh < HR; hh += kWarps) {
-      const bool valid = (t0 + lane) < p1 && (t0 + lane) < T && hh < g.hr;
+      const bool valid = (t0 + lane) < p1 && (t0 + lane) < T && h0 + hh < g.hr;
       float sum = 0.0f;
       for (int q = 0; q < KQ; ++q) sum += Sp[((size_t)q * HR + hh) * kRowS + lane];
       const float sv = valid ? sum * scale : -INFINITY;
@@ -676,8 +676,8 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
   if (stamp) sub_stamp(a, ph, 11, (unsigned long long)nsub);
   // write the partial: [b][chunk][h] x (m, l, O[512])
   const int stride = g.kr + 2;
-  float* base = a.s.mla_part + (((size_t)b * g.mla_chunks + chunk) * g.hr) * stride;
-  for (int hh = tid; hh < g.hr; hh += kThreads) {
+  float* base = a.s.mla_part + (((size_t)b * g.mla_chunks + chunk) * g.hr + h0) * stride;
+  for (int hh = tid; hh < HR && h0 + hh < g.hr; hh += kThreads) {
     base[(size_t)hh * stride] = mrun[hh];
     base[(size_t)hh * stride + 1] = lrun[hh];
   }
@@ -689,7 +689,7 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
       for (int i = 0; i < 4; ++i) {
         const int hh = mt * 16 + r + 8 * (i >> 1);
         const int col = warp * 32 + nt * 8 + 2 * c + (i & 1);
-        if (hh < g.hr) base[(size_t)hh * stride + 2 + col] = O[mt][nt][i];
+        if (h0 + hh < g.hr) base[(size_t)hh * stride + 2 + col] = O[mt][nt][i];
       }
     }
   }

@@ -46,6 +46,34 @@ def test_error_strings_and_table_size(lib):
     assert lib.kk3_table_size(ctypes.byref(cfg)) == 32 + 8 * 32
 
 
+@pytest.mark.parametrize("cid", ["kimi-k3-dev-l4-tp1-b8-s8192", "kimi-k3-syn-l8-tp8-b8-s8192"])
+def test_check_table_requires_exactly_the_runtime_layout(lib, cid):
+    """kk3_check_table (host only, no CUDA call) accepts a table whose used slots are the runtime's layout
+    plus the outputs it binds, refuses it with KK3_ERR_ARG as soon as any one of them is NULL, and ignores
+    NULL in every other slot. Placeholder addresses are never dereferenced."""
+    case = cases.get_case(cid)
+    p = case["params"]
+    cfg = runtime.rank_config(case, 0, 0)
+    n = runtime.GLOBAL_SLOTS + p["layers"] * runtime.LAYER_SLOTS
+    vp = ctypes.c_void_p
+    lib.kk3_check_table.argtypes = [ctypes.POINTER(runtime.Config), vp, ctypes.c_int]
+    used = [slot for slot, _ in runtime.table_layout(p)]
+    for i, (name, (shape, _)) in enumerate(runtime.output_specs(case).items()):
+        if torch.Size(shape).numel():
+            used.append(runtime.OUTPUT_SLOT0 + i)
+    table = (vp * n)()
+    for s in used:
+        table[s] = 0x10000 + 16 * s
+    assert lib.kk3_check_table(ctypes.byref(cfg), table, n) == 0
+    for s in used:
+        table[s] = None
+        assert lib.kk3_check_table(ctypes.byref(cfg), table, n) == -1, s
+        table[s] = 0x10000 + 16 * s
+    table[used[-1]] = 0x10008   # misaligned
+    assert lib.kk3_check_table(ctypes.byref(cfg), table, n) == -1
+    assert lib.kk3_check_table(ctypes.byref(cfg), table, n - 1) == -1
+
+
 def test_init_rejects_unsupported_geometry_without_a_gpu(lib):
     case = cases.variant(cases.get_case("kimi-k3-dev-l4-tp1-b8-s8192"), head_dim=64)
     cfg = runtime.rank_config(case, 0, 0)

@@ -94,8 +94,11 @@ def test_noalloc_matches_context_step_twice(lib, case):
 
 @pytest.mark.gpu
 def test_noalloc_rejects_geometry_beyond_its_static_scratch(lib):
-    case = cases.get_case("kimi-k3-dev-l4-tp1-b8-s8192")   # needs ~44 MiB of scratch (the limit is 32 MiB)
+    # the dev geometry at batch 64: its stream-K partial tiles alone take ~39 MB (the limit is 32 MiB); the
+    # table is NULL, so a geometry that unexpectedly fitted would still stop at KK3_ERR_ARG, never launch
+    case = cases.get_case("kimi-k3-dev-l4-tp1-b8-s8192")
     cfg = runtime.rank_config(case, 0, 0)
+    cfg.batch = 64
     n = runtime.GLOBAL_SLOTS + case["params"]["layers"] * runtime.LAYER_SLOTS
     table = (ctypes.c_void_p * n)()
     rc = lib.kk3_step_noalloc(ctypes.byref(cfg), table, n, None, None)
