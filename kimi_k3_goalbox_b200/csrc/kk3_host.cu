@@ -272,12 +272,14 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   size_t sm_mla = mla_smem_bytes(HR);
   size_t sm_row = (512 + (size_t)(g.h > g.lh ? g.h : g.lh)) * 4 + 64;
   size_t sm_abs = ((size_t)g.B * 128 + 4 * 16 * 128) * 4;
+  size_t sm_comb = mla_combine_smem_bytes(g.B);
   size_t sm_route = kRouteSmem;
   size_t sm_gemv = (size_t)kWarps * kGemvSmemPerWarp;   // per-warp cp.async rings of the GEMV phases
   size_t sm = sm_mla;
   sm = sm_gemv > sm ? sm_gemv : sm;
   sm = sm_row > sm ? sm_row : sm;
   sm = sm_abs > sm ? sm_abs : sm;
+  sm = sm_comb > sm ? sm_comb : sm;
   sm = sm_route > sm ? sm_route : sm;
   sm = (size_t)kExpSmem > sm ? (size_t)kExpSmem : sm;   // expert rings + activation row cache
   x->smem = align_up(sm, 128);
@@ -634,11 +636,13 @@ static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, Ste
   size_t sm = mla_smem_bytes(HR);
   const size_t sm_row = (512 + (size_t)(g.h > g.lh ? g.h : g.lh)) * 4 + 64;
   const size_t sm_abs = ((size_t)g.B * 128 + 4 * 16 * 128) * 4;
+  const size_t sm_comb = mla_combine_smem_bytes(g.B);
   const size_t sm_route = kRouteSmem;
   const size_t sm_gemv = (size_t)kWarps * kGemvSmemPerWarp;
   sm = sm_gemv > sm ? sm_gemv : sm;
   sm = sm_row > sm ? sm_row : sm;
   sm = sm_abs > sm ? sm_abs : sm;
+  sm = sm_comb > sm ? sm_comb : sm;
   sm = sm_route > sm ? sm_route : sm;
   sm = (size_t)kExpSmem > sm ? (size_t)kExpSmem : sm;   // expert rings + activation row cache
   *smem = align_up(sm, 128);

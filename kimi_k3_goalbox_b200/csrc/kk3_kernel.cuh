@@ -558,7 +558,26 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
       if (KK3_RUN) {
         KK3_BUILD(o_job(a, l, sj2[0]));
         #pragma unroll 1
-        for (int it = blockIdx.x; it < g.B * g.hr; it += gridDim.x) mla_combine_item(a, l, it / g.hr, it % g.hr, fsm);
+        if (g.B * g.hr <= (int)gridDim.x) {
+          // one item per (row, head) fits one wave
+          #pragma unroll 1
+          for (int it = blockIdx.x; it < g.B * g.hr; it += gridDim.x) mla_combine_row_item(a, l, it / g.hr, it % g.hr, fsm);
+        } else {
+          const int groups = mla_combine_groups(g.hr, g.B, gridDim.x);
+          const int per = (g.B + groups - 1) / groups;   // rows per group (<= kCombRows)
+          #pragma unroll 1
+          for (int it = blockIdx.x; it < g.hr * groups; it += gridDim.x) {
+            const int hh = it / groups, r0 = (it % groups) * per;
+            const int nr = g.B - r0 < per ? g.B - r0 : per;
+            if (nr <= 0) continue;
+            switch (per) {   // rows per group: 1, 2, 4 or 8 (R >= per)
+              case 1: mla_combine_item<1>(a, l, hh, r0, nr, smem, phase); break;
+              case 2: mla_combine_item<2>(a, l, hh, r0, nr, smem, phase); break;
+              case 3: case 4: mla_combine_item<4>(a, l, hh, r0, nr, smem, phase); break;
+              default: mla_combine_item<8>(a, l, hh, r0, nr, smem, phase); break;
+            }
+          }
+        }
         prefetch_jobs(sj2, 1);
       }
       ++midx;

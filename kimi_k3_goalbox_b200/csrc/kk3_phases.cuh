@@ -426,15 +426,22 @@ KK3_FN void mla_absorb_item(const StepArgs& a, int layer, int hh, int cq, float*
     qs[i] = bf2f(a.s.mla_q[((size_t)b * g.hr + hh) * (g.nr + g.rd) + d]);
   }
   __syncthreads();
+  // this thread's 32 weights (one column c, nope dims 32dq..32dq+31), all loads in flight at once
+  float w[32];
+  {
+    const bf16* col = kb + ((size_t)hh * (g.nr + g.vd) + dq * 32) * g.kr + c;
+#pragma unroll
+    for (int d = 0; d < 32; ++d) w[d] = bf2f(col[(size_t)d * g.kr]);
+  }
   for (int b0 = 0; b0 < g.B; b0 += 16) {
     float acc[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
-    for (int d = dq * 32; d < dq * 32 + 32; ++d) {
-      const float w = bf2f(kb[((size_t)hh * (g.nr + g.vd) + d) * g.kr + c]);
+#pragma unroll
+    for (int d = 0; d < 32; ++d) {
 #pragma unroll
       for (int i = 0; i < 16; ++i)
-        if (b0 + i < g.B) acc[i] += qs[(b0 + i) * 128 + d] * w;
+        if (b0 + i < g.B) acc[i] += qs[(b0 + i) * 128 + dq * 32 + d] * w[d];
     }
 #pragma unroll
     for (int i = 0; i < 16; ++i) part[(dq * 16 + i) * 128 + (tid & 127)] = acc[i];
@@ -696,9 +703,10 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
   __syncthreads();
 }
 
-// Combine the split-K partials of (b, h), apply kb's value half and the sigmoid output gate
-// (kimi.py:280-282): out[d] = bf16(bf16(sum_c lat[c] * kb[h*256+128+d, c]) * bf16(sigmoid(og))).
-KK3_FN void mla_combine_item(const StepArgs& a, int layer, int b, int hh, float* sm) {
+// Combine of one (batch row, head): used when rows x heads items fit one wave of the grid (few heads per rank),
+// where it is faster than the per-head items below. Combines the split-K partials, applies kb's value half
+// and the sigmoid output gate (kimi.py:280-282): out[d] = bf16(bf16(sum_c lat[c] * kb[h*256+128+d, c]) * bf16(sigmoid(og))).
+KK3_FN void mla_combine_row_item(const StepArgs& a, int layer, int b, int hh, float* sm) {
   const Geo& g = a.g;
   const int tid = threadIdx.x;
   const bool keep = !reinterpret_cast<const bool*>(a.ptr[KK3_RESET])[b];
@@ -750,6 +758,161 @@ KK3_FN void mla_combine_item(const StepArgs& a, int layer, int b, int hh, float*
     const float o = round_bf(acc);
     const float gt = round_bf(sigmoidf_(bf2f(a.s.og[(size_t)b * g.hr * g.vd + hh * g.vd + dv])));
     a.s.attn_in[(size_t)b * g.hr * g.vd + hh * g.vd + dv] = f2bf(o * gt);
+  }
+  __syncthreads();
+}
+
+// Combine the split-K partials and apply kb's value half with the sigmoid output gate (kimi.py:280-282):
+// out[d] = bf16(bf16(sum_c lat[c] * kb[h*256+128+d, c]) * bf16(sigmoid(og))). One item is a head and a group of
+// batch rows (groups chosen so that heads x groups fills the grid), so every attended latent is formed once:
+//  1. per row (one warp each, all chunk loads at once): weights exp(m_i - M) and 1/L, summed in chunk order;
+//  2. lat[b][c] = bf16(sum_i w_i O_i[c] / L) into shared memory (bf16 is exact: the reference rounds it),
+//     thread = latent dim, 32 loads in flight at a time whatever the group's row count;
+//  3. out[b][d] = sum_c lat[b][c] kb[d][c] in two passes of 64 output dims: 8 threads per dim, 64 latent dims
+//     each (weights in registers), partials reduced across the 8 threads.
+constexpr int kCombRow = 72;   // bf16 per (row, 64-dim part) of the latent tile: 64 + 8 pad (bank offsets)
+constexpr int kCombRows = 8;   // rows per item at most
+__host__ __device__ inline size_t mla_combine_smem_bytes(int B) {
+  const int R = B < kCombRows ? B : kCombRows;
+  return (size_t)R * 8 * kCombRow * 2 + (size_t)R * 128 * 4 + (size_t)R * 4 + 64;
+}
+// batch-row groups per head: enough items for the grid, groups of at most kCombRows rows
+__host__ __device__ inline int mla_combine_groups(int hr, int B, int grid) {
+  int n = grid / (hr > 0 ? hr : 1);
+  const int need = (B + kCombRows - 1) / kCombRows;
+  n = n < need ? need : (n > B ? B : n);
+  return n < 1 ? 1 : n;
+}
+
+template <int R>
+KK3_FN void mla_combine_item(const StepArgs& a, int layer, int hh, int r0, int nr, unsigned char* sm, int ph = -1) {
+  const Geo& g = a.g;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // the head's value rows (vd x kr bf16) are read in step 3: bring them into L2 while steps 1-2 run
+  {
+    const unsigned char* kv = reinterpret_cast<const unsigned char*>(
+        lptr<bf16>(a, layer, KK3_MLA_KB) + ((size_t)hh * (g.nr + g.vd) + g.nr) * g.kr);
+    const int lines = g.vd * g.kr * 2 / 128;
+    for (int i = tid; i < lines; i += kThreads) asm volatile("prefetch.global.L2 [%0];" ::"l"(kv + (size_t)i * 128));
+  }
+  const bool stamp = ph >= 0 && hh == 0 && r0 == 0 && tid == 0;   // sub-phase stamps of one item
+  if (stamp) sub_stamp(a, ph, 0);
+  const bool* reset = reinterpret_cast<const bool*>(a.ptr[KK3_RESET]);
+  const int stride = g.kr + 2;
+  const size_t cstride = (size_t)g.hr * stride;
+  bf16* lat = reinterpret_cast<bf16*>(sm);                                     // [nr][8][kCombRow]
+  float* wgt = reinterpret_cast<float*>(sm + (size_t)kCombRows * 8 * kCombRow * 2);   // [nr][64]
+  float* lw = wgt + kCombRows * 64;                                            // [nr][64] w_i * l_i
+  float* inv = lw + kCombRows * 64;                                            // [nr]
+  // 1. chunk weights: every lane loads its chunks' (m, l); L is summed in chunk order by lane 0
+  for (int r = warp; r < nr; r += kWarps) {
+    const int b = r0 + r, nck = reset[b] ? 1 : g.mla_chunks;
+    const float* base = a.s.mla_part + (((size_t)b * g.mla_chunks) * g.hr + hh) * stride;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+    if (lane < nck) {
+      m0 = ld_cg_f32(base + lane * cstride);
+      l0 = ld_cg_f32(base + lane * cstride + 1);
+    }
+    if (lane + 32 < nck) {
+      m1 = ld_cg_f32(base + (lane + 32) * cstride);
+      l1 = ld_cg_f32(base + (lane + 32) * cstride + 1);
+    }
+    const float M = warp_max(fmaxf(m0, m1));
+    const float w0 = (lane < nck && m0 != -INFINITY) ? expf(m0 - M) : 0.0f;
+    const float w1 = (lane + 32 < nck && m1 != -INFINITY) ? expf(m1 - M) : 0.0f;
+    wgt[r * 64 + lane] = w0;
+    wgt[r * 64 + lane + 32] = w1;
+    lw[r * 64 + lane] = w0 * l0;
+    lw[r * 64 + lane + 32] = w1 * l1;
+    __syncwarp();
+    if (lane == 0) {
+      float L = 0.0f;
+      for (int i = 0; i < nck; ++i) L += lw[r * 64 + i];
+      inv[r] = 1.0f / L;
+    }
+  }
+  __syncthreads();
+  if (stamp) sub_stamp(a, ph, 1);
+  // 2. attended latent rows (thread = latent dim), 32 loads in flight per round (32 / R chunks of each of R
+  // rows: the partials may sit in the other die's L2, ~2 us away); chunks past a row's count have weight 0
+  // and are not read
+  constexpr int CK = 32 / R;
+  for (int cc = tid; cc < g.kr; cc += kThreads) {
+    float acc[R];
+    int nck[R];
+    const float* src[R];
+    int nmax = 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      acc[r] = 0.0f;
+      nck[r] = r < nr ? (reset[r0 + r] ? 1 : g.mla_chunks) : 0;
+      nmax = nck[r] > nmax ? nck[r] : nmax;
+      src[r] = a.s.mla_part + (((size_t)(r0 + (r < nr ? r : 0)) * g.mla_chunks) * g.hr + hh) * stride + 2 + cc;
+    }
+    for (int i0 = 0; i0 < nmax; i0 += CK) {
+      float v[R][CK];
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int k = 0; k < CK; ++k) v[r][k] = i0 + k < nck[r] ? ld_cg_f32(src[r] + (size_t)(i0 + k) * cstride) : 0.0f;
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int k = 0; k < CK; ++k)
+          if (i0 + k < nck[r]) acc[r] += wgt[r * 64 + i0 + k] * v[r][k];
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (r >= nr) break;
+      const bf16 lv = f2bf(acc[r] * inv[r]);
+      lat[(r * 8 + (cc >> 6)) * kCombRow + (cc & 63)] = lv;
+      // the attended latent (kimi.py:280) replaces the absorbed query in scratch, for diagnostics
+      a.s.absorbed[(((size_t)(r0 + r)) * g.hr + hh) * g.kr + cc] = lv;
+    }
+  }
+  __syncthreads();
+  if (stamp) sub_stamp(a, ph, 2);
+  // 3. value projection: two passes of 64 output dims, thread = (dim, 64-dim part of the latent)
+  const int t = tid & 7;
+  for (int pass = 0; pass < 2; ++pass) {
+    const int dv = pass * 64 + (tid >> 3);
+    __nv_bfloat162 w[8][4];   // this thread's 64 weights as bf16 pairs
+    {
+      const bf16* row = lptr<bf16>(a, layer, KK3_MLA_KB) + ((size_t)hh * (g.nr + g.vd) + g.nr + dv) * g.kr + t * 64;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        uint4 u = *reinterpret_cast<const uint4*>(row + e * 8);
+        w[e][0] = *reinterpret_cast<__nv_bfloat162*>(&u.x);
+        w[e][1] = *reinterpret_cast<__nv_bfloat162*>(&u.y);
+        w[e][2] = *reinterpret_cast<__nv_bfloat162*>(&u.z);
+        w[e][3] = *reinterpret_cast<__nv_bfloat162*>(&u.w);
+      }
+    }
+    for (int r = 0; r < nr; ++r) {
+      float acc = 0.0f;
+      const bf16* lr = lat + (r * 8 + t) * kCombRow;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint4 l4 = *reinterpret_cast<const uint4*>(lr + e * 8);
+        const __nv_bfloat162* lv = reinterpret_cast<const __nv_bfloat162*>(&l4);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 wf = __bfloat1622float2(w[e][q]), lf = __bfloat1622float2(lv[q]);
+          acc += wf.x * lf.x;
+          acc += wf.y * lf.y;
+        }
+      }
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+      if (t == 0) {
+        const int b = r0 + r;
+        const float o = round_bf(acc);
+        const float gt = round_bf(sigmoidf_(bf2f(a.s.og[(size_t)b * g.hr * g.vd + hh * g.vd + dv])));
+        a.s.attn_in[(size_t)b * g.hr * g.vd + hh * g.vd + dv] = f2bf(o * gt);
+      }
+    }
+    if (stamp) sub_stamp(a, ph, 3 + pass);
   }
   __syncthreads();
 }

@@ -176,6 +176,10 @@ def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[d
                 ["start", "q_ready", "t0_data", "t0_scores", "t0_softmax", "t0_pv", "t1_data", "t1_scores",
                  "t1_softmax", "t1_pv", "item_end"]) if st[i]} | {"subtiles": st[11],
                                                                   "phase_end": (ts[i + 1] - base) / 1e3}
+        if name == "mla_combine" and st[0]:
+            subinfo[f"{name}:{layer}"] = {k: (st[j] - base) / 1e3 for j, k in enumerate(
+                ["start", "weights", "latent", "values_pass0", "values_pass1"]) if st[j]} | {
+                "phase_end": (ts[i + 1] - base) / 1e3}
         if name == "experts_gate_up" and st[15]:
             subinfo[f"{name}:{layer}"] = {"raw5": st[5], "raw6": st[6], "raw7": st[7], "raw8": st[8],
                                           "staged": (st[9] - base) / 1e3, "warp0_keys": (st[10] - base) / 1e3,
@@ -240,7 +244,7 @@ def main(argv=None) -> int:
         case = cases.variant(case, batch=args.batch)
     rows = profile(case, args.reps)
     subrow, head, rows = rows[0], rows[1:3], rows[3:]
-    for k, v in [kv for kv in subrow["info"].items() if kv[0].startswith(("mla_attend", "experts_gate_up", "experts_down:1", "attn_prologue:2", "moe_in:1", "warps ")) and (not kv[0].startswith("warps ") or kv[0].endswith(":1"))]:
+    for k, v in [kv for kv in subrow["info"].items() if kv[0].startswith(("mla_attend", "mla_combine", "experts_gate_up", "experts_down:1", "attn_prologue:2", "moe_in:1", "warps ")) and (not kv[0].startswith("warps ") or kv[0].endswith(":1"))]:
         print("  sub-phase", k, {kk: (round(vv, 2) if isinstance(vv, float) else vv) for kk, vv in v.items()})
     total = sum(r["us"] for r in rows)
     print(f"{case['id']}: full step {head[0]['us']:.1f} us (events), empty launch {head[1]['us']:.1f} us, "
