@@ -21,6 +21,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = ROOT / "_build"
 LIB = PKG / "_lib" / "libkk3.so"
+CHECK = PKG / "_lib" / "kk3_tc_check"   # checker of the tensor-core expert engine (kk3_tc_check.cu)
 UNITS = ["kk3_host.cu", "kk3_kernel_nt1.cu", "kk3_kernel_nt2.cu", "kk3_kernel_nt4.cu", "kk3_kernel_nt8.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xptxas", "-v", f"-I{ROOT / 'include'}"]
@@ -69,10 +70,18 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = True) ->
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stderr}")
+    check_src = CSRC / "kk3_tc_check.cu"
+    rebuilt_check = force or _stale(CHECK, check_src)
+    if rebuilt_check:
+        cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", f"-I{ROOT / 'include'}", str(check_src), "-o", str(CHECK)]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc failed for kk3_tc_check.cu:\n{res.stderr}")
     if verbose:
         for unit, state in results:
             print(f"  {unit}: {state}")
         print(f"  {LIB.relative_to(ROOT)}: {'linked' if relink else 'up to date'}")
+        print(f"  {CHECK.relative_to(ROOT)}: {'built' if rebuilt_check else 'up to date'}")
     return LIB
 
 
