@@ -322,7 +322,7 @@ template <int NT, int MT>
 KK3_FN void run_gemv(const StepArgs& a, const GemvJob* jobs, int njobs, int cta_lo, int cta_hi, int parity,
                          int bank = 0, int ph = -1) {
   if ((int)blockIdx.x < cta_lo || (int)blockIdx.x >= cta_hi) return;
-  extern __shared__ __align__(16) unsigned char kk3_dyn_smem[];
+  extern __shared__ __align__(1024) unsigned char kk3_dyn_smem[];
   constexpr bool XS = NT <= 2;                                   // stage activations with the weights
   constexpr int kSlotVec = (MT * 4 + (XS ? NT * 2 : 0)) * 32;    // uint4 per unit slot
   constexpr int S = kGemvSmemPerWarp / (kSlotVec * 16);          // ring depth in units
@@ -613,7 +613,7 @@ KK3_DEV uint4 ld_cg16(const void* p) {
 
 template <int MT>
 KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
-  extern __shared__ __align__(16) unsigned char kk3_dyn_smem[];
+  extern __shared__ __align__(1024) unsigned char kk3_dyn_smem[];
   __shared__ unsigned long long s_mask;    // MT == 2: batch rows staged (bit b = latent row b)
   __shared__ int s_first, s_count;        // MT == 1: pairs [s_first, s_first + s_count) staged
   __shared__ int s_rowmap[kMaxBatch];     // MT == 2: cache slot i holds latent row s_rowmap[i]

@@ -437,7 +437,10 @@ KK3_DEV void lm_head_job(const StepArgs& a, GemvJob& j) {
 
 template <int NT>
 __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_constant__ StepArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
+  // dynamic shared memory on a 1024-byte boundary (checked below; ptxas pads the static variables before it):
+  // the engines' rings of 16-byte copies assume whole 128-byte lines, and rings that straddle them ran
+  // up to a third slower
+  extern __shared__ __align__(1024) unsigned char smem[];
   // GEMV job descriptors live in shared memory: built once per CTA by thread 0 from the parameter block,
   // then read by every warp (indexing a per-thread array would put it in local memory)
   __shared__ GemvJob sj[kMaxJobs];
@@ -446,6 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   __shared__ int sjn;
   for (int i = threadIdx.x; i < 256; i += kThreads) kk3_e8m0_lut[i] = e8m0_to_f32((unsigned)i);
   if (threadIdx.x == 0) kk3_cur_phase = 0;
+  if (threadIdx.x == 0 && ((unsigned)__cvta_generic_to_shared(smem) & 1023u) != 0u) set_error(a, kErrDevice);
   __syncthreads();
   const Geo& g = a.g;
   float* fsm = reinterpret_cast<float*>(smem);

@@ -1,14 +1,16 @@
 // Checker of the tensor-core expert engine (kk3_tc_experts.cuh) against the decode step's mma.sync engine
-// (run_experts, kk3_gemv.cuh) on one TP8 rank's expert geometry (batch 8, 16 of 896 experts per row, latent 3584,
-// expert intermediate 384), random MXFP4 codes and E8M0 scales, bf16-valued latent rows.
+// (run_experts, kk3_gemv.cuh) on one expert geometry (batch 8, 16 of 896 experts per row, latent 3584, expert
+// intermediate 384 for a TP8 rank by default), random MXFP4 codes and E8M0 scales, bf16-valued latent rows.
 //
 // Both engines run gate/up (kimi.py:317-319: situ(gate, up) per pair) and then down (:320-323) on the same
 // routed batch. Prints one JSON line: the fraction of bit-identical activations and slot outputs, the largest
 // difference relative to the largest value, each phase's best time over `reps` launches with the L2 flushed
 // before each, and the device error word. Routing tables are built on the host exactly as the step's routing
-// groups pairs (by expert, chunks of <= 8 pairs); experts are folded into 160 distinct ones to bound memory.
+// groups pairs (by expert, chunks of <= 8 pairs); experts are folded into `distinct_experts` ones to bound
+// memory.
 //
-//     kk3_tc_check [reps]
+//     kk3_tc_check [reps] [expert_intermediate] [distinct_experts]
+//     (intermediate 384: one TP8 rank, the default; 3072: TP1. Distinct experts: 160 by default, at most 896)
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -74,7 +76,12 @@ static float bfh2f(uint16_t b) {
 
 int main(int argc, char** argv) {
   const int reps = argc > 1 ? atoi(argv[1]) : 3;
-  const int B = 8, E = 896, K = 16, lh = 3584, inter = 384, nuse = 160;
+  const int B = 8, E = 896, K = 16, lh = 3584;
+  const int inter = argc > 2 ? atoi(argv[2]) : 384, nuse = argc > 3 ? atoi(argv[3]) : 160;
+  if (inter <= 0 || inter % 128 != 0 || nuse < 1 || nuse > E) {
+    printf("{\"error\": \"expert_intermediate must be a positive multiple of 128, distinct_experts in [1, 896]\"}\n");
+    return 1;
+  }
   int dev = 0, sms = 0;
   CK(cudaGetDevice(&dev));
   CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -188,7 +195,7 @@ int main(int argc, char** argv) {
   StepArgs a2 = a;
   a2.s.out_slot = d_out2;
 
-  const int sm_mma = kExpSmem, sm_tc = 220 * 1024;
+  const int sm_mma = kExpSmem, sm_tc = 3 * tc_stage_bytes<2>();
   CK(cudaFuncSetAttribute(mma_engine<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_mma));
   CK(cudaFuncSetAttribute(mma_engine<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_mma));
   CK(cudaFuncSetAttribute(tc_engine<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_tc));

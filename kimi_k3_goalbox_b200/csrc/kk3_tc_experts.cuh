@@ -235,7 +235,7 @@ KK3_DEV void tc_quant_pairs(const StepArgs& a, const __half* x, int K, int npair
 // ---- the engine --------------------------------------------------------------------------------------
 
 template <int MT>
-KK3_DEV int tc_stage_bytes() {
+__host__ __device__ constexpr int tc_stage_bytes() {
   // A[MT] 32 KB each | B: 2 atoms x 2 terms x 1 KB | SFA[MT][2 halves] 512 B | SFB 512 B
   return (MT * 32768 + 4096 + (2 * MT + 1) * 512 + 1023) & ~1023;
 }
@@ -247,12 +247,13 @@ struct TcIter {
 
 template <int MT>
 KK3_FN void run_experts_tc(const StepArgs& a, const TcPhase& ph, int smem_bytes) {
-  extern __shared__ __align__(16) unsigned char kk3_dyn_smem[];
+  extern __shared__ __align__(1024) unsigned char kk3_dyn_smem[];
   constexpr int kTcBars = 2 * kTcMaxStages + 5;   // full[S], empty[S], acc full[2], acc empty[2], drain
   constexpr int kEpiWarps = 8, kEpiThreads = kEpiWarps * 32;
   __shared__ __align__(8) unsigned long long tc_bar[kTcBars];
   __shared__ unsigned tc_tmem;
   __shared__ int tc_last;
+  __shared__ int tc_run;   // one decision for the whole CTA: every role runs, or none
   __shared__ int s_cexp[kTcChunkCache], s_cfp[kTcChunkCache], s_cnp[kTcChunkCache];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -327,6 +328,7 @@ KK3_FN void run_experts_tc(const StepArgs& a, const TcPhase& ph, int smem_bytes)
 
   if (threadIdx.x == 0) {
     if (S < 2) set_error(a, kErrDevice);
+    tc_run = S >= 2 && !failed(a);
     for (int s = 0; s < kTcMaxStages; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
@@ -343,7 +345,7 @@ KK3_FN void run_experts_tc(const StepArgs& a, const TcPhase& ph, int smem_bytes)
   __syncthreads();
   tc_fence_after();
   const unsigned tmem = tc_tmem;
-  const bool run = S >= 2 && !failed(a);
+  const bool run = tc_run != 0;
   // TMEM columns: D[buf][mt][half] at ((buf * MT + mt) * 2 + half) * 32, then per stage 4 columns per
   // scale block (SFA[mt][half], SFB)
   auto d_col = [&](int b, int mt, int h) { return (unsigned)(((b * MT + mt) * 2 + h) * 32); };
