@@ -6,15 +6,22 @@ Default workload: kimi-k3-dev-l4-tp1-b8-s8192 at N=1 (the only single-GPU case o
 at N>1 the same model (4 layers, full width, batch 8, context 8192) at TP=N, one rank per GPU over NCCL
 (torchrun), i.e. strong scaling of a fixed model. `--case` selects any case of the table instead
 (e.g. kimi-k3-syn-l8-tp8-b8-s8192 with --gpus 8). Synthetic seeded weights and state on the device
-(the reference's generator); inputs (>= 14 GB per GPU at the default) are larger than the 126 MB L2,
-so no flush runs between steps.
+(the reference's generator, a fresh seed per run as the reference's harness draws one per trial); inputs
+(>= 14 GB per GPU at the default) are larger than the 126 MB L2, so no flush runs between steps.
 
-`value` is the device time of one step (CUDA events on the launching stream, max over ranks): pure kernel
-time with inputs resident. `e2e` is the same metric through the public API (`submission.build(case)` ->
-`run(inputs)`), with the step's per-sequence inputs (token, reset) copied host->device from pinned memory
-and the result (next_token) copied back inside the timed region.
-`--impl reference` times the reference algorithm (the oracle restatement, BF16, torch on the host cores)
-on a bounded per-layer sample of the same workload, on rank 0 only.
+Legs of one run, in order:
+- parity (checker, untimed): one step through the public `run(inputs)` on fresh-seed inputs, graded with the
+  reference's band rule against the BF16 and FP32 oracle computed on the same device tensors, with real
+  NCCL all-reduces at N>1 (the reference's `_reduce`/`_greedy` collectives). The oracle is the checker
+  here, never the thing measured.
+- `value`: device time of K steps (CUDA events on the launching stream, max over ranks), inputs resident.
+- `e2e`: the same metric through `submission.build(case)` -> `run(inputs)`, with the step's per-sequence
+  inputs (token, reset) copied host->device from pinned memory and next_token copied back, inside the
+  timed region.
+- extras: at N=8 the north-star cases kimi-k3-syn-l8-tp8-b{1,8,64}-s8192 at real TP8 (parity + latency); at
+  N=1 the deep stack (one TP8 rank of syn b8 at the deepest layer count that fits, per layer x 93).
+- `--impl reference` times whole steps of the reference algorithm (the oracle restatement, BF16, torch on
+  the host cores) on the same workload, on rank 0 only.
 """
 
 from __future__ import annotations
@@ -22,9 +29,11 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import secrets
 import statistics
 import subprocess
 import sys
+import threading
 import time
 from datetime import timedelta
 from pathlib import Path
@@ -38,7 +47,12 @@ sys.path.insert(0, str(ROOT))
 from kimi_k3_goalbox_b200 import cases, sol  # noqa: E402
 
 DEFAULT_CASE = "kimi-k3-dev-l4-tp1-b8-s8192"
+NORTH_STAR = ["kimi-k3-syn-l8-tp8-b1-s8192", "kimi-k3-syn-l8-tp8-b8-s8192", "kimi-k3-syn-l8-tp8-b64-s8192"]
+DEEP_CASE = "kimi-k3-syn-l8-tp8-b8-s8192"
+DEEP_LAYERS = (84, 80, 76)           # deepest first; the first whose inputs fit with a margin is used
+DEEP_MARGIN = 10 << 30               # bytes left free for the CUDA context, scratch and allocator slack
 FALLBACK_HBM_GBS = 6650.0
+METRIC = "decode-step latency per rank (worst rank, CUDA events)"
 
 
 def pick_case(args, n: int) -> dict:
@@ -49,19 +63,40 @@ def pick_case(args, n: int) -> dict:
         if n != 1:
             case = cases.variant(case, tp=n)
     if getattr(args, "rank_equivalent", False) and case["tp"] > 1 and n == 1:
-        # one TP rank's shard shapes as a TP1 geometry: the same arithmetic and bytes as one rank of the case,
-        # with identity reductions
-        tp = case["tp"]
-        params = dict(case["params"])
-        for key in ("q_heads", "vocab", "intermediate", "dense_intermediate"):
-            params[key] //= tp
-        case = dict(case, id=case["id"] + "-rank-equivalent", gpus=1, tp=1, params=params)
+        case = rank_equivalent(case)
     elif args.case and case["tp"] != n:
         case = cases.variant(case, tp=n)
     if args.batch:
         case = cases.variant(case, batch=args.batch)
     case["params"].pop("checkpoint", None)
     return case
+
+
+def plain_case(case_id: str) -> dict:
+    """A case of the table with synthetic weights (the checkpoint flag dropped)."""
+    case = cases.get_case(case_id)
+    case["params"].pop("checkpoint", None)
+    return case
+
+
+def rank_equivalent(case: dict) -> dict:
+    """One TP rank's shard shapes as a TP1 geometry: the same arithmetic and bytes as one rank of the case,
+    with identity reductions (the survey's one-rank-equivalent method)."""
+    tp = case["tp"]
+    params = dict(case["params"])
+    for key in ("q_heads", "vocab", "intermediate", "dense_intermediate"):
+        params[key] //= tp
+    params.pop("checkpoint", None)
+    return dict(case, id=case["id"] + "-rank-equivalent", gpus=1, tp=1, params=params)
+
+
+def config_for(case: dict, n: int) -> dict:
+    """The `config` object of both arms (the same dict, so the two lines name the same workload)."""
+    p = case["params"]
+    nbytes = sol.floor_bytes(case)["minimum_bytes"]
+    return {"workload": case["id"], "tp": case["tp"], "batch": p["batch"], "layers": p["layers"],
+            "context": p["context"], "parallelism": f"tp{case['tp']}", "n_gpus": n,
+            "l2": "inputs %.1f GB per rank > 126 MB L2; no flush" % (nbytes / 1e9)}
 
 
 def peaks() -> tuple[float, str]:
@@ -75,37 +110,78 @@ def peaks() -> tuple[float, str]:
 
 
 def traffic_for(case_id: str):
+    """DRAM bytes (read + write) of one step-kernel launch of this workload, from the committed ncu summary
+    (profiles/step_kernel_traffic.json); None when no capture of this workload exists."""
     path = ROOT / "profiles" / "step_kernel_traffic.json"
     if path.exists():
         try:
-            return json.loads(path.read_text()).get(case_id)
+            v = json.loads(path.read_text()).get(case_id)
+            return v if isinstance(v, (int, float)) else None
         except Exception:
             return None
     return None
 
 
-class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled every 50 ms with timestamps. The sampler starts before
-    the warm-up (nvidia-smi needs a moment to start); only samples inside [mark_start, mark_end], the timed
-    region, enter the summary."""
+# ---------------------------------------------------------------------------------------------------------
+# clocks during the timed region
 
-    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+class ClockSampler:
+    """SM clock, max clock, power and clock-event (throttle) reasons of this rank's GPU, sampled during the
+    timed region. NVML is polled from a thread every ~1 ms (the steps are milliseconds long, so an
+    nvidia-smi loop at its 50 ms floor would see no sample inside a 20-step window); without NVML it falls
+    back to `nvidia-smi -lms 50`. Only samples inside [mark_start, mark_end] enter the summary."""
+
+    # nvmlClocksEventReasons bits (nvml.h)
+    REASONS = {0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
     def __init__(self, device_index: int):
         self.device_index = device_index
-        self.proc = None
+        self.samples: list[tuple[float, float, float, float, int]] = []   # (t, sm, max, power_w, reasons)
         self.t0 = self.t1 = None
-        self.lines: list[str] = []
+        self.source = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._proc = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            prop = torch.cuda.get_device_properties(self.device_index)
+            bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device_index)
+
+    def _poll(self, pynvml, handle):
+        mx = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+        while not self._stop.is_set():
+            try:
+                sm = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
+                reasons = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
+                power = pynvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+                self.samples.append((time.time(), sm, mx, power, reasons))
+            except Exception:
+                pass
+            time.sleep(0.001)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            pynvml, handle = self._nvml_handle()
+            self._thread = threading.Thread(target=self._poll, args=(pynvml, handle), daemon=True)
+            self._thread.start()
+            self.source = "nvml (1 ms poll)"
         except Exception:
-            self.proc = None
+            try:
+                fields = "timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active"
+                self._proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={fields}", "--format=csv,noheader,nounits",
+                     "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.source = "nvidia-smi (50 ms)"
+            except Exception:
+                self._proc = None
         return self
 
     def mark_start(self):
@@ -115,43 +191,54 @@ class ClockSampler:
         self.t1 = time.time()
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            time.sleep(0.1)   # let the sample that covers the end of the timed region arrive
-            self.proc.terminate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+        if self._proc is not None:
+            from datetime import datetime
+            time.sleep(0.1)
+            self._proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                out, _ = self._proc.communicate(timeout=5)
             except Exception:
-                self.proc.kill()
+                self._proc.kill()
                 out = ""
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            for line in out.splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                try:
+                    ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                    self.samples.append((ts, float(parts[1]), float(parts[2]), float(parts[3]), int(parts[4], 16)))
+                except Exception:
+                    continue
 
     def summary(self) -> dict:
-        from datetime import datetime
-        sm, mx, reasons, power = [], None, set(), []
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 10:
-                continue
-            try:
-                ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
-                clk, mxv = float(parts[2]), float(parts[3])
-            except ValueError:
-                continue
-            # a sample reports the state just before its timestamp: keep those inside the timed window
-            if self.t0 is None or self.t1 is None or not (self.t0 <= ts <= self.t1 + 0.05):
-                continue
-            sm.append(clk)
-            mx = mxv
-            try:
-                power.append(float(parts[4]))
-            except ValueError:
-                pass
-            for name, val in zip(names, parts[6:10]):
-                if val.lower() == "active":
+        inside = [s for s in self.samples if self.t0 is not None and self.t1 is not None and self.t0 <= s[0] <= self.t1]
+        reasons = set()
+        for s in inside:
+            for bit, name in self.REASONS.items():
+                if s[4] & bit:
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm), "power_w_max": max(power) if power else None}
+        return {"sm_mhz": statistics.median([s[1] for s in inside]) if inside else None,
+                "sm_max_mhz": inside[0][2] if inside else None, "reasons": sorted(reasons), "samples": len(inside),
+                "power_w_max": max(s[3] for s in inside) if inside else None, "source": self.source}
+
+
+def merge_clocks(summaries: list[dict]) -> dict:
+    """Clocks over ranks: the lowest per-rank median, every reason seen on any rank, all samples."""
+    got = [s for s in summaries if s.get("sm_mhz") is not None]
+    out = {"sm_mhz": min(s["sm_mhz"] for s in got) if got else None,
+           "sm_max_mhz": max(s["sm_max_mhz"] for s in got) if got else None,
+           "reasons": sorted({r for s in summaries for r in s.get("reasons", [])}),
+           "samples": sum(s.get("samples", 0) for s in summaries),
+           "power_w_max": max((s["power_w_max"] for s in got if s.get("power_w_max") is not None), default=None),
+           "source": summaries[0].get("source") if summaries else None}
+    if len(summaries) > 1:
+        out["per_rank_sm_mhz"] = [s.get("sm_mhz") for s in summaries]
+    return out
+
+
+# ---------------------------------------------------------------------------------------------------------
+# distributed plumbing
 
 
 def init_dist(n: int):
@@ -161,7 +248,7 @@ def init_dist(n: int):
     rank = int(os.environ["RANK"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
-    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     return rank, local
 
 
@@ -173,58 +260,214 @@ def max_over_ranks(x: float, n: int) -> float:
     return float(t.item())
 
 
+def gather(obj, n: int) -> list:
+    if n == 1:
+        return [obj]
+    out = [None] * n
+    dist.all_gather_object(out, obj)
+    return out
+
+
 def barrier(n: int):
     if n > 1:
         dist.barrier()
     torch.cuda.synchronize()
 
 
+def fresh_seed(args, n: int) -> int:
+    """The harness draws secrets.randbits(32) on rank 0 per trial and broadcasts it
+    (megabench/harness/distributed.py:33-36); --seed fixes it instead."""
+    if args.seed is not None:
+        return args.seed
+    values = [secrets.randbits(32)]
+    if n > 1:
+        dist.broadcast_object_list(values, src=0)
+    return int(values[0])
+
+
+def execution_for(case: dict, n: int, rank: int, device) -> dict | None:
+    if n == 1:
+        return None
+    return {"rank": rank, "world_size": n, "tp_rank": rank, "ep_rank": 0, "backend": "nccl", "device": str(device),
+            "tp_group": dist.group.WORLD, "ep_group": None}
+
+
+# ---------------------------------------------------------------------------------------------------------
+# the legs
+
+
+def parity_leg(case: dict, values: dict, runner, n: int, rank: int, seed: int) -> dict:
+    """Checker leg (untimed): one step through run(), graded by the reference's band rule
+    (megabench/tasks/kimi.py:370-462) against the BF16 and FP32 oracle on the same device tensors, with real
+    all-reduces over the process group at N>1 (kimi.py:343-347, :218-227). Every rank takes the same
+    collective steps; the outcome is agreed over ranks."""
+    from oracle import kimi_oracle as ko
+    t0 = time.perf_counter()
+    serial = n == 1
+    group = None if serial else dist.group.WORLD
+    error, details = None, None
+    try:
+        before = ko.snapshot(values)
+        actual = runner(values)
+        torch.cuda.synchronize()
+        runner.ctx.check()
+        actual = {k: v.clone() for k, v in actual.items()}
+        ko.check_unchanged(values, before)
+    except Exception as exc:   # the step itself failed: no grading collectives are entered by anyone
+        error = f"step: {type(exc).__name__}: {exc}"
+    errors = gather(error, n)
+    if any(errors):
+        return {"seed": seed, "pass": False, "reason": "; ".join(e for e in errors if e)[:500]}
+    try:
+        expected = ko.reference(case, values, serial=serial, tp_rank=rank, group=group)
+        details = ko.compare(case, values, expected, actual, serial=serial, tp_rank=rank, group=group)
+    except AssertionError as exc:
+        error = f"band: {exc}"
+    except Exception as exc:
+        error = f"grader: {type(exc).__name__}: {exc}"
+    errors = gather(error, n)
+    torch.cuda.synchronize()
+    out = {"seed": seed, "pass": not any(errors), "grader": "oracle band rule (kimi.py:370-462)",
+           "collectives": "none (serial)" if serial else f"NCCL all-reduce over {n} ranks", "seconds": None}
+    if any(errors):
+        out["reason"] = "; ".join(e for e in errors if e)[:500]
+    else:
+        out["worst_ratio"] = {k: round(v["worst_ratio"], 4) for k, v in details.items() if "worst_ratio" in v}
+        out["next_token"] = details["next_token"]
+        out["expert_sets_differing_from_oracle"] = details["expert_ids"]["sets_differing_from_oracle"]
+        out["cache_length_mismatches"] = details["cache_length"]["mismatched_elements"]
+    out["seconds"] = round(time.perf_counter() - t0, 1)
+    return out
+
+
+def time_steps(ctx, stream, steps: int, warmup: int, n: int, clocks: ClockSampler | None = None) -> tuple:
+    """Warm up, then time exactly `steps` launches: (total ms of the region, per-step ms list), this rank."""
+    for _ in range(warmup):
+        ctx.launch(stream.cuda_stream)
+    barrier(n)
+    ctx.check()
+    barrier(n)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if clocks:
+        clocks.mark_start()
+    t0.record(stream)
+    for i in range(steps):
+        starts[i].record(stream)
+        ctx.launch(stream.cuda_stream)
+        ends[i].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.mark_end()
+    barrier(n)
+    ctx.check()
+    return t0.elapsed_time(t1), [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+
+def build_runner(case: dict, n: int, rank: int, device):
+    from kimi_k3_goalbox_b200.submission import build
+    exec_info = execution_for(case, n, rank, device)
+    return build(dict(case, execution=exec_info) if exec_info else case)
+
+
+def measure_case(args, case: dict, n: int, rank: int, local: int, *, parity: bool, seed: int) -> dict:
+    """Extra workload: fresh inputs, optional parity leg, K timed steps (max over ranks). Returns the entry."""
+    from kimi_k3_goalbox_b200 import synthetic
+    device = torch.device("cuda", local)
+    entry = {"workload": case["id"], "tp": case["tp"], "batch": case["params"]["batch"],
+             "layers": case["params"]["layers"]}
+    with torch.inference_mode():
+        values = synthetic.make_inputs(case, seed, device, rank=rank)
+        torch.cuda.synchronize()
+        runner = build_runner(case, n, rank, device)
+        try:
+            if parity:
+                entry["parity"] = parity_leg(case, values, runner, n, rank, seed)
+            ctx = runner.ctx
+            outputs = ctx.allocate_outputs()
+            ctx._bind_inputs(values)
+            ctx.bind_outputs(outputs)
+            stream = torch.cuda.current_stream(device)
+            total_ms, per_step = time_steps(ctx, stream, args.steps, args.warmup, n)
+        finally:
+            barrier(n)
+            runner.close()
+    ms = max_over_ranks(total_ms / args.steps, n)
+    p50 = max_over_ranks(statistics.median(per_step), n)
+    nbytes = sol.floor_bytes(case)["minimum_bytes"]
+    peak, _ = peaks()
+    entry.update({"us": round(ms * 1000.0, 2), "p50_us": round(p50 * 1000.0, 2),
+                  "floor_us_at_8TBps": round(nbytes / 8.0e12 * 1e6, 1),
+                  "pct_of_floor_8TBps": round(100.0 * (nbytes / 8.0e12) / (ms * 1e-3), 1),
+                  "frac_of_measured_hbm": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4),
+                  "algorithmic_bytes": nbytes, "launches_per_step": 1, "seed": seed})
+    del values
+    torch.cuda.empty_cache()
+    return entry
+
+
+def deep_stack(args, local: int) -> dict:
+    """One TP8 rank of syn b8 (rank-equivalent TP1 geometry) at the deepest layer count whose inputs fit this
+    GPU's free memory with a margin; per-layer latency extrapolated to the full model's 93 layers
+    (megabench/sol.py:27-73 floor, README.md:157: 93 layers need ~200 GB per rank)."""
+    free, total = torch.cuda.mem_get_info(local)
+    base = cases.get_case(DEEP_CASE)
+    chosen = None
+    for L in DEEP_LAYERS:
+        case = rank_equivalent(cases.variant(base, layers=L))
+        from kimi_k3_goalbox_b200 import synthetic
+        need = sum(torch.Size(s).numel() * torch.empty(0, dtype=dt).element_size()
+                   for s, dt, _, _ in synthetic.weight_specs(case).values())
+        p = case["params"]
+        for l in range(L):
+            if cases.is_mla(p, l):
+                need += p["batch"] * p["context"] * (p["kv_lora_rank"] + p["qk_rope_dim"]) * 2
+            else:
+                need += p["batch"] * (3 * p["q_heads"] * p["head_dim"] * 4 * 2 + p["q_heads"] * 128 * 128 * 4)
+        if need + DEEP_MARGIN <= free:
+            chosen = (L, case, need)
+            break
+    if chosen is None:
+        return {"skipped": f"no layer count in {DEEP_LAYERS} fits {free / 2**30:.1f} GiB free"}
+    L, case, need = chosen
+    seed = args.seed if args.seed is not None else secrets.randbits(32)
+    e = measure_case(args, case, 1, 0, local, parity=False, seed=seed)
+    full = rank_equivalent(cases.variant(base, layers=93))
+    floor93 = sol.floor_bytes(full)["minimum_bytes"]
+    per_layer = e["us"] / L
+    e.update({"inputs_gib": round(need / 2**30, 1), "free_gib_before": round(free / 2**30, 1),
+              "per_layer_us": round(per_layer, 2), "extrapolated_93_layers_us": round(per_layer * 93, 1),
+              "floor_93_layers_us_at_8TBps": round(floor93 / 8.0e12 * 1e6, 1),
+              "pct_of_floor_93_8TBps": round(100.0 * (floor93 / 8.0e12) / (per_layer * 93 * 1e-6), 1),
+              "note": "per layer = step / L (embedding and head included); no parity leg at this depth"})
+    return e
+
+
 def run_b200(args, n: int, rank: int, local: int) -> dict | None:
     from kimi_k3_goalbox_b200 import synthetic
     from kimi_k3_goalbox_b200.runtime import StepContext
-    from kimi_k3_goalbox_b200.submission import build
 
     case = pick_case(args, n)
     p = case["params"]
     device = torch.device("cuda", local)
-    seed = args.seed
+    seed = fresh_seed(args, n)
     with torch.inference_mode():
         values = synthetic.make_inputs(case, seed, device, rank=rank)
         torch.cuda.synchronize()
+        runner = build_runner(case, n, rank, device)
+        parity = parity_leg(case, values, runner, n, rank, seed) if not args.no_parity else None
         # --- kernel-only timing (inputs resident, table bound once)
-        exec_info = None
-        if n > 1:
-            exec_info = {"rank": rank, "world_size": n, "tp_rank": rank, "ep_rank": 0, "backend": "nccl",
-                         "device": str(device), "tp_group": dist.group.WORLD, "ep_group": None}
-        runner = build(dict(case, execution=exec_info) if exec_info else case)
         ctx: StepContext = runner.ctx
         outputs = ctx.allocate_outputs()
         ctx._bind_inputs(values)
         ctx.bind_outputs(outputs)
         stream = torch.cuda.current_stream(device)
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        t_all0, t_all1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local) as clocks:
-            for _ in range(args.warmup):
-                ctx.launch(stream.cuda_stream)
-            torch.cuda.synchronize()
-            barrier(n)
-            ctx.check()
-            barrier(n)
-            clocks.mark_start()
-            t_all0.record(stream)
-            for i in range(args.steps):
-                starts[i].record(stream)
-                ctx.launch(stream.cuda_stream)
-                ends[i].record(stream)
-            t_all1.record(stream)
-            torch.cuda.synchronize()
-            clocks.mark_end()
-        barrier(n)
-        ctx.check()
-        per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-        total_ms = max_over_ranks(t_all0.elapsed_time(t_all1), n)
+            total_ms, per_step = time_steps(ctx, stream, args.steps, args.warmup, n, clocks)
+        clock_summary = merge_clocks(gather(clocks.summary(), n))
+        total_ms = max_over_ranks(total_ms, n)
         p50_ms = max_over_ranks(statistics.median(per_step), n)
         ms_per_step = total_ms / args.steps
 
@@ -252,6 +495,19 @@ def run_b200(args, n: int, rank: int, local: int) -> dict | None:
         ctx.check()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1), n) / args.steps
         runner.close()
+        host_values = None
+        if rank == 0 and n == 1 and not args.no_cpu_baseline:
+            host_values = {k: v.cpu() for k, v in values.items()}   # for the cpu_baseline leg
+        del values, outputs, out
+        torch.cuda.empty_cache()
+
+    extras = {}
+    if not args.no_extras:
+        if n == 8 and args.case is None:
+            extras["north_star_tp8"] = [measure_case(args, plain_case(cid), n, rank, local, parity=not args.no_parity,
+                                                     seed=fresh_seed(args, n)) for cid in NORTH_STAR]
+        if n == 1 and args.case is None:
+            extras["deep_stack"] = deep_stack(args, local)
 
     if rank != 0:
         return None
@@ -260,8 +516,8 @@ def run_b200(args, n: int, rank: int, local: int) -> dict | None:
     peak, peak_src = peaks()
     achieved = nbytes / (ms_per_step * 1e-3) / 1e9
     B = p["batch"]
-    return {
-        "metric": "decode-step latency per rank (worst rank, CUDA events)",
+    line = {
+        "metric": METRIC,
         "value": round(ms_per_step * 1000.0, 2),
         "unit": "us",
         "n_gpus": n,
@@ -272,10 +528,8 @@ def run_b200(args, n: int, rank: int, local: int) -> dict | None:
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16 activations, mxfp4 experts, fp32 accumulate/state",
-        "data": "synthetic (reference seeded generator, seed %d)" % seed,
-        "config": {"workload": case["id"], "tp": case["tp"], "batch": B, "layers": p["layers"],
-                   "context": p["context"], "parallelism": f"tp{case['tp']}",
-                   "l2": "inputs %.1f GB per rank > 126 MB L2; no flush" % (nbytes / 1e9)},
+        "data": "synthetic (reference seeded generator, fresh seed %d)" % seed,
+        "config": config_for(case, n),
         "p50_us": round(p50_ms * 1000.0, 2),
         "hbm_floor_us": {"at_8.0_TBps": round(nbytes / 8.0e12 * 1e6, 1),
                          f"at_{peak_src}_{peak / 1000:.3f}_TBps": round(nbytes / (peak * 1e9) * 1e6, 1)},
@@ -283,126 +537,91 @@ def run_b200(args, n: int, rank: int, local: int) -> dict | None:
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic_for(case["id"]),
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else "fallback",
-                     "algorithmic_bytes_per_launch": nbytes},
+                     "algorithmic_bytes_per_launch": nbytes,
+                     "kernel": "kk3_step_kernel (the whole step is one launch)"},
+        "parity": parity,
         "e2e": {"value": round(e2e_ms * 1000.0, 2), "unit": "us", "h2d_bytes_per_step": B * 8 + B,
                 "d2h_bytes_per_step": B * 8},
         "gpu_launches": args.steps,
-        "clocks": clocks.summary(),
+        "clocks": clock_summary,
     }
+    line.update(extras)
+    if host_values is not None:
+        line["cpu_baseline"] = cpu_baseline_line(args, n, case, host_values)
+    return line
+
+
+# ---------------------------------------------------------------------------------------------------------
+# the reference arm: whole steps of the oracle restatement on the host cores
+
+
+def host_inputs(case: dict, seed: int) -> tuple[dict, str]:
+    """The workload's inputs in host memory: generated with the reference's seeded generator on the GPU
+    when one is present (seconds) and copied to the host, else on the host (minutes)."""
+    from oracle import kimi_oracle as ko
+    if torch.cuda.is_available():
+        with torch.inference_mode():
+            vals = ko.make_inputs(case, seed, "cuda:0")
+            out = {k: v.cpu() for k, v in vals.items()}
+            del vals
+            torch.cuda.empty_cache()
+        return out, "seeded generator on cuda:0, copied to host"
+    return ko.make_inputs(case, seed, "cpu"), "seeded generator on the host"
+
+
+def time_reference_steps(case: dict, values: dict, steps: int, warmup: int) -> tuple[list[float], int]:
+    from oracle import kimi_oracle as ko
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    times = []
+    with torch.inference_mode():
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            ko.reference(case, values, serial=True)
+            dt = time.perf_counter() - t0
+            if i >= warmup:
+                times.append(dt)
+    return times, torch.get_num_threads()
 
 
 def run_reference(args, n: int) -> dict:
-    """The reference algorithm (oracle restatement) on the host cores, per-layer samples of the workload."""
+    """`--impl reference`: whole BF16 oracle steps (the reference algorithm, kimi.py:230-340) on the host cores,
+    on the arm's workload. At TP>1 one rank's arithmetic runs serially (its shard shapes, local reductions)."""
     from oracle import kimi_oracle as ko
     case = pick_case(args, n)
-    if case["tp"] != 1:
-        case = ko.serial_rank_view(case)   # one rank's arithmetic, reductions local
-    p = case["params"]
-    torch.set_num_threads(os.cpu_count() or 1)
+    serial_case = ko.serial_rank_view(case) if case["tp"] != 1 else case
+    seed = args.seed if args.seed is not None else secrets.randbits(32)
     t0 = time.perf_counter()
-    values = fast_cpu_inputs(case)
+    values, how = host_inputs(serial_case, seed)
     gen_s = time.perf_counter() - t0
-    parts = ["embed+head"] + list(range(p["layers"]))
-    times = {str(x): [] for x in parts}
-    with torch.inference_mode():
-        for i in range(args.warmup + args.steps):
-            part = parts[i % len(parts)]
-            dt = ko.timed_sample(case, values, part)
-            if i >= args.warmup:
-                times[str(part)].append(dt)
-        # parts never sampled in the timed window are sampled once more
-        for part in parts:
-            if not times[str(part)]:
-                times[str(part)].append(ko.timed_sample(case, values, part))
-    step_s = sum(statistics.median(v) for v in times.values())
+    times, cores = time_reference_steps(serial_case, values, args.steps, args.warmup)
+    total_s = sum(times)
+    step_us = total_s / len(times) * 1e6
+    sample = (f"{args.steps} whole decode steps after {args.warmup} warm-up steps, BF16 oracle restatement "
+              f"(MXFP4 decode in C, bit-identical to the reference's torch decode); inputs: {how} in {gen_s:.0f} s, "
+              "untimed" + ("; one TP rank's arithmetic serially (reductions local)" if case["tp"] != 1 else ""))
     return {
-        "metric": "decode-step latency per rank (worst rank, CUDA events)",
-        "impl": "reference",
-        "value": round(step_s * 1e6, 1),
-        "unit": "us",
-        "n_gpus": n,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(step_s * 1e3, 3),
-        "higher_is_better": False,
-        "scaling": "strong",
-        "vs_baseline": None,
+        "metric": METRIC, "impl": "reference", "value": round(step_us, 1), "unit": "us", "n_gpus": n,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_us / 1000.0, 3),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16 activations, mxfp4 experts (decoded to bf16), fp32 accumulate/state",
-        "data": "synthetic (random fill with the reference's shapes and distributions)",
-        "config": {"workload": pick_case(args, n)["id"], "tp": pick_case(args, n)["tp"], "batch": p["batch"],
-                   "layers": p["layers"], "context": p["context"], "parallelism": "cpu"},
-        "cpu_baseline": {"value": round(step_s * 1e6, 1), "unit": "us", "cores": torch.get_num_threads(),
-                         "kind": "port",
-                         "sample": "one decoder layer (or embed+head) per step, cycling; value = sum of per-part medians"
-                                   f"; input fill {gen_s:.1f} s untimed"},
-        "e2e": {"value": round(step_s * 1e6, 1), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "per_part_s": {k: round(statistics.median(v), 4) for k, v in times.items()},
+        "data": "synthetic (reference seeded generator, seed %d)" % seed,
+        "config": config_for(case, n),
+        "p50_us": round(statistics.median(times) * 1e6, 1),
+        "cpu_baseline": {"value": round(step_us, 1), "unit": "us", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(step_us, 1), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "timed_region_s": round(total_s, 1),
     }
 
 
-def fast_cpu_inputs(case: dict) -> dict:
-    """CPU inputs with the reference's shapes, dtypes and value distributions, filled by tiling one random
-    block (the oracle's cost does not depend on the exact values; seeded generation of ~15 GB on CPU would
-    take minutes)."""
-    from oracle import kimi_oracle as ko
-    g = torch.Generator().manual_seed(0)
-    block = torch.randn(1 << 22, generator=g)
-    codes = torch.randint(0, 256, (1 << 22,), generator=g, dtype=torch.uint8)
-    converted: dict = {}
-
-    def tile(t, src):
-        flat = t.view(-1)
-        for s in range(0, flat.numel(), src.numel()):
-            n = min(src.numel(), flat.numel() - s)
-            flat[s:s + n].copy_(src[:n])
-        return t
-
-    def fill(shape, std, mean, dtype):
-        key = (std, mean, dtype)
-        if key not in converted:
-            converted[key] = (block * std + mean).to(dtype)
-        return tile(torch.empty(shape, dtype=dtype), converted[key])
-
-    vals = {}
-    p = case["params"]
-    for name, (shape, dtype, fan_in, _) in ko.tensor_specs(case).items():
-        if name.endswith("_blocks"):
-            vals[name] = tile(torch.empty(shape, dtype=torch.uint8), codes)
-        elif name.endswith("_scales"):
-            e = round(-torch.log2(torch.tensor(2.93 * (p["latent_hidden"] if "down" not in name else p["intermediate"]) ** 0.5)).item())
-            vals[name] = (126 + e + torch.randint(0, 3, shape, generator=g)).to(torch.uint8)
-        elif name.endswith("A_log"):
-            vals[name] = fill(shape, 0.5, 0.0, dtype)
-        elif name.endswith("dt_bias"):
-            vals[name] = fill(shape, 1.0, -4.0, dtype)
-        elif name.endswith("router_bias"):
-            vals[name] = fill(shape, 0.01, 0.0, dtype)
-        elif fan_in == 0:
-            vals[name] = fill(shape, 0.1, 1.0, dtype)
-        else:
-            vals[name] = fill(shape, fan_in ** -0.5, 0.0, dtype)
-    state = ko.make_state(dict(case, params=dict(p, context=1)), 0, "cpu", 0)
-    B = p["batch"]
-    vals["token"] = state["token"]
-    vals["reset"] = torch.zeros(B, dtype=torch.bool)
-    hr, d = p["q_heads"] // case["tp"], p["head_dim"]
-    for l in range(p["layers"]):
-        x = f"l{l}_"
-        if ko.is_mla(case, l):
-            vals[x + "kv_cache"] = fill((B, p["context"], p["kv_lora_rank"]), 1.0, 0.0, torch.bfloat16)
-            vals[x + "pe_cache"] = fill((B, p["context"], p["qk_rope_dim"]), 1.0, 0.0, torch.bfloat16)
-        else:
-            vals[x + "conv_state"] = fill((B, 3, hr * d, p["conv_kernel"]), 1.0, 0.0, torch.bfloat16)
-            vals[x + "recurrent_state"] = fill((B, hr, d, d), 0.05, 0.0, torch.float32)
-    return vals
-
-
-def cpu_baseline_line(args, n: int) -> dict:
-    """A short reference-arm measurement attached to the b200 line (rank 0, N=1)."""
-    sub = argparse.Namespace(**vars(args))
-    sub.steps, sub.warmup = args.cpu_steps, 0
-    ref = run_reference(sub, n)
-    return ref["cpu_baseline"]
+def cpu_baseline_line(args, n: int, case: dict, host_values: dict) -> dict:
+    """The cpu_baseline object of the b200 line (rank 0, N=1): a bounded sample of whole oracle steps on the
+    same inputs (already in host memory), timed on the host cores."""
+    times, cores = time_reference_steps(case, host_values, args.cpu_steps, 1)
+    step_us = statistics.median(times) * 1e6
+    return {"value": round(step_us, 1), "unit": "us", "cores": cores, "kind": "port",
+            "sample": f"median of {args.cpu_steps} whole BF16 oracle steps (after 1 warm-up) on this run's inputs; "
+                      "MXFP4 decode in C, bit-identical to the reference's torch decode"}
 
 
 def main(argv=None) -> int:
@@ -415,9 +634,11 @@ def main(argv=None) -> int:
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--rank-equivalent", action="store_true",
                     help="N=1 only: time one TP rank of --case (its shard shapes as a TP1 geometry)")
-    ap.add_argument("--seed", type=int, default=20261201)
-    ap.add_argument("--cpu-steps", type=int, default=5, help="samples of the attached cpu_baseline (N=1)")
+    ap.add_argument("--seed", type=int, default=None, help="fixed input seed (default: a fresh one per run)")
+    ap.add_argument("--cpu-steps", type=int, default=3, help="whole oracle steps in the attached cpu_baseline (N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the checker leg")
+    ap.add_argument("--no-extras", action="store_true", help="skip the north-star (N=8) and deep-stack (N=1) keys")
     args = ap.parse_args(argv)
     n = args.gpus
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -434,8 +655,6 @@ def main(argv=None) -> int:
     try:
         line = run_b200(args, n, rank, local)
         if rank == 0 and line is not None:
-            if n == 1 and not args.no_cpu_baseline:
-                line["cpu_baseline"] = cpu_baseline_line(args, n)
             print(json.dumps(line), flush=True)
     finally:
         if n > 1:

@@ -124,7 +124,9 @@ int kk3_open_peers(kk3_ctx* ctx, const void* handles);
 int kk3_step(kk3_ctx* ctx, const void* const* table, int table_size, void* stream);
 
 /* Device-side status of the most recent steps, read from mapped host memory without synchronising:
- * KK3_OK, KK3_ERR_TIMEOUT or KK3_ERR_DEVICE. Call after the stream has been synchronised. */
+ * KK3_OK, KK3_ERR_TIMEOUT or KK3_ERR_DEVICE. Call after the stream has been synchronised. A step that fails
+ * also writes next_token = -1 and cache_length = 0 into its outputs, and every later kk3_step on the context
+ * returns KK3_ERR_FAILED. */
 int kk3_status(kk3_ctx* ctx);
 
 /* Allocation-free variant of kk3_init + kk3_step + kk3_free for one TP1 step (no counterpart in the
@@ -134,10 +136,14 @@ int kk3_status(kk3_ctx* ctx);
  * 32 MiB per device; nothing is allocated. Geometries whose scratch does not fit get KK3_ERR_TOO_LARGE,
  * tp > 1 gets KK3_ERR_UNSUPPORTED (a static device symbol cannot be exported to peers over CUDA IPC).
  * The first call on a device does set-up (symbol address, kernel attributes); make it before any stream
- * capture containing this call. Each call clears the scratch words that must start at zero on `stream`,
- * then launches the step. `error_word` (optional, device-accessible int the caller zeroed) is set to a
- * nonzero device code if an in-kernel wait times out. Calls whose steps overlap on one device share the
- * scratch and race: serialise them. Same table, outputs and arithmetic as kk3_step. */
+ * capture containing this call. Each call enqueues two device operations on `stream`: a cudaMemsetAsync of the
+ * scratch words that must start at zero (the whole planned scratch when the geometry differs from the previous
+ * call's on this device), then the step's cooperative launch. `error_word` (optional, a device-accessible int
+ * the caller zeroed) is set to a nonzero device code if an in-kernel wait times out. With error_word = NULL
+ * a failed step is visible only in its outputs (next_token = -1, cache_length = 0, as every failed step
+ * writes them), and the next call clears the internal error state: there is no status query. Calls whose
+ * steps overlap on one device share the scratch and race: serialise them. Same table, outputs and
+ * arithmetic as kk3_step. */
 int kk3_step_noalloc(const kk3_config* cfg, const void* const* table, int table_size, void* stream,
                      int* error_word);
 

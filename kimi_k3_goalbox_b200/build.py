@@ -22,6 +22,9 @@ CSRC = PKG / "csrc"
 BUILD = ROOT / "_build"
 LIB = PKG / "_lib" / "libkk3.so"
 CHECK = PKG / "_lib" / "kk3_tc_check"   # checker of the tensor-core expert engine (kk3_tc_check.cu)
+# the oracle's C restatement of the MXFP4 decode (test infrastructure: the checker and the timed CPU baseline)
+ORACLE_SRC = ROOT / "oracle" / "mxfp4.c"
+ORACLE_LIB = ROOT / "oracle" / "libkk3_oracle_mxfp4.so"
 UNITS = ["kk3_host.cu", "kk3_kernel_nt1.cu", "kk3_kernel_nt2.cu", "kk3_kernel_nt4.cu", "kk3_kernel_nt8.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xptxas", "-v", f"-I{ROOT / 'include'}"]
@@ -77,7 +80,17 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = True) ->
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"nvcc failed for kk3_tc_check.cu:\n{res.stderr}")
+    rebuilt_oracle = force or not ORACLE_LIB.exists() or ORACLE_SRC.stat().st_mtime > ORACLE_LIB.stat().st_mtime
+    if rebuilt_oracle:
+        cc = shutil.which("gcc") or shutil.which("cc")
+        if cc is None:
+            raise RuntimeError("gcc not found: needed for the oracle's C decode")
+        cmd = [cc, "-O2", "-fopenmp", "-fPIC", "-shared", str(ORACLE_SRC), "-o", str(ORACLE_LIB), "-lm"]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"gcc failed for oracle/mxfp4.c:\n{res.stderr}")
     if verbose:
+        print(f"  {ORACLE_LIB.relative_to(ROOT)}: {'built' if rebuilt_oracle else 'up to date'}")
         for unit, state in results:
             print(f"  {unit}: {state}")
         print(f"  {LIB.relative_to(ROOT)}: {'linked' if relink else 'up to date'}")

@@ -136,16 +136,29 @@ static int validate(const kk3_config* c) {
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
-  if (!out) return KK3_ERR_ARG;
-  *out = nullptr;
-  int rc = validate(cfg);
-  if (rc != KK3_OK) return rc;
-  KK3_CUDA(cudaSetDevice(cfg->device));
-  kk3_ctx* x = new (std::nothrow) kk3_ctx();
-  if (!x) return KK3_ERR_CUDA;
-  x->cfg = *cfg;
-  Geo& g = x->g;
+// One planner for both entry points (kk3_init and kk3_step_noalloc): the geometry, the batch-tile class, the
+// scratch layout and the dynamic shared memory of a step on a grid of `sms` CTAs. With base == nullptr only
+// the sizes are computed. The scratch starts with the words that must be zero when a step begins (barrier,
+// phase count, error word and its mirror, situ and stream-K counters, then the single-rank exchange block when
+// `comm_inline`); `zero_bytes` covers them, the rest is written before it is read within every step.
+// `profiling` adds the per-CTA barrier and per-warp engine stamps (context path only). `comm_inline` places a
+// single rank's exchange buffer inside the scratch (the allocation-free path, tp == 1); otherwise the exchange
+// buffer is a separate allocation, exported to peers over CUDA IPC.
+struct StepPlan {
+  Geo g;
+  Scratch s;
+  Comm comm;        // offsets always; comm.base[rank] only when comm_inline
+  int nt;           // batch in 8-row n-tiles: 1, 2, 4 or 8
+  size_t smem;      // dynamic shared memory of the step kernel
+  size_t total;     // scratch bytes
+  size_t zero;      // leading scratch bytes that must be zero at the start of a step
+  size_t comm_bytes;
+  size_t qkv_w;
+};
+
+static void plan_step(const kk3_config* cfg, int sms, unsigned char* base, bool profiling, bool comm_inline,
+                      StepPlan* pl) {
+  Geo& g = pl->g;
   memset(&g, 0, sizeof(g));
   g.L = cfg->layers; g.B = cfg->batch; g.h = cfg->hidden; g.lh = cfg->latent_hidden; g.inter = cfg->inter_shard;
   g.dinter = cfg->dense_inter_shard; g.sinter = cfg->shared_inter_shard; g.hr = cfg->heads; g.d = cfg->head_dim;
@@ -158,16 +171,13 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   }
   g.nblk = (g.L + g.bs - 1) / g.bs;
   g.timeout_ns = cfg->timeout_ns > 0 ? cfg->timeout_ns : 10000000000ll;
-  cudaDeviceProp prop;
-  if (cudaGetDeviceProperties(&prop, cfg->device) != cudaSuccess) { delete x; return KK3_ERR_CUDA; }
-  x->sms = prop.multiProcessorCount;
-  x->grid = x->sms;
-  x->nt = g.B <= 8 ? 1 : (g.B <= 16 ? 2 : (g.B <= 32 ? 4 : 8));
-  plan_mla(g, x->grid);
-  const long long gw = (long long)x->grid * kWarps;
-  g.fix_bank = 2ll * gw * (2 * x->nt * 128);
+  const int nt = g.B <= 8 ? 1 : (g.B <= 16 ? 2 : (g.B <= 32 ? 4 : 8));
+  pl->nt = nt;
+  plan_mla(g, sms);
+  const long long gw = (long long)sms * kWarps;
+  g.fix_bank = 2ll * gw * (2 * nt * 128);
   {
-    long long tiles = 0, t;
+    long long tiles = 0;
     auto mx = [&](long long v) { tiles = v > tiles ? v : tiles; };
     mx((3ll * g.qdim + g.qdim + g.d + g.hr + 15 * 6) / 16 + 6);
     mx((long long)(g.qr + g.kr + g.rd + g.hr * g.vd) / 16 + 3);
@@ -176,21 +186,45 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
     mx(2ll * ((g.dinter + 15) / 16) + 2);                                        // dense gate | up
     mx((long long)(g.E + 15) / 16 + (g.lh + 15) / 16 + 2ll * ((g.sinter + 15) / 16) + 4);   // MoE input pass
     mx((long long)(g.V + 15) / 16 + 1);
-    t = (long long)g.B * g.K * ((g.inter > g.lh ? g.inter : g.lh) / 16);
-    mx(t);
+    mx((long long)g.B * g.K * ((g.inter > g.lh ? g.inter : g.lh) / 16));
     g.cnt_bank = (int)tiles;
   }
-  // scratch layout
-  struct Item { void** p; size_t bytes; };
-  const size_t B = g.B;
-  size_t qkv_w = (size_t)3 * g.qdim > (size_t)(g.qr + g.kr + g.rd) ? (size_t)3 * g.qdim : (size_t)(g.qr + g.kr + g.rd);
-  Scratch& s = x->s;
+  const size_t B = g.B, tp = g.tp;
+  const size_t qkv_w =
+      (size_t)3 * g.qdim > (size_t)(g.qr + g.kr + g.rd) ? (size_t)3 * g.qdim : (size_t)(g.qr + g.kr + g.rd);
+  pl->qkv_w = qkv_w;
+  Scratch& s = pl->s;
+  memset(&s, 0, sizeof(s));
   // situ pairs: tiles of the larger of the dense and shared-expert intermediates, 4 * NT floats per lane
   const size_t situ_tiles = (size_t)((g.dinter > g.sinter ? g.dinter : g.sinter) + 15) / 16 + 1;
-  const size_t situ_floats = 2 * situ_tiles * 32 * 4 * (size_t)x->nt;
-  unsigned* bar = nullptr;
-  int* phase_count = nullptr;
+  const size_t situ_floats = 2 * situ_tiles * 32 * 4 * (size_t)nt;
+  // exchange buffer: flags [B][tp] u32, then two parity regions {att bf16 [tp][B][h], exp f32 [tp][B][lh],
+  // shd bf16 [tp][B][h], key u64 [tp][B]}
+  Comm& c = pl->comm;
+  memset(&c, 0, sizeof(c));
+  const size_t flag_bytes = align_up(B * tp * 4, 256);
+  c.flag_off = 0;
+  c.att_off = 0;
+  size_t r = align_up(tp * B * g.h * 2, 256);
+  c.exp_off = r;
+  r += align_up(tp * B * g.lh * 4, 256);
+  c.shd_off = r;
+  r += align_up(tp * B * g.h * 2, 256);
+  c.key_off = r;
+  r += align_up(tp * B * 8, 256);
+  c.region_bytes = r;
+  c.data_off[0] = flag_bytes;
+  c.data_off[1] = flag_bytes + r;
+  pl->comm_bytes = flag_bytes + 2 * r;
+  unsigned char* comm = nullptr;
+  int* err_mirror = nullptr;
+  struct Item { void** p; size_t bytes; };
   Item items[] = {
+      // must be zero when a step begins
+      {(void**)&s.bar, 64}, {(void**)&s.phase_count, 64}, {(void**)&s.err, 64}, {(void**)&err_mirror, 64},
+      {(void**)&s.situ_cnt, situ_tiles * 4}, {(void**)&s.fix_cnt, (size_t)g.cnt_bank * 2 * 4},
+      {(void**)&comm, comm_inline ? pl->comm_bytes : 0},
+      // written before they are read within every step
       {(void**)&s.prefix, B * g.h * 2}, {(void**)&s.blocks, (size_t)g.nblk * B * g.h * 2},
       {(void**)&s.xa, B * g.h * 2}, {(void**)&s.xm, B * g.h * 2}, {(void**)&s.qkv, B * qkv_w * 2},
       {(void**)&s.og, B * (size_t)g.qdim * 2}, {(void**)&s.fa, B * g.d * 2}, {(void**)&s.beta, B * g.hr * 2},
@@ -204,28 +238,64 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
       {(void**)&s.chunk_info, (1 + B * g.K * 3) * 4}, {(void**)&s.act_p, B * g.K * (size_t)g.inter * 2},
       {(void**)&s.out_slot, B * g.K * (size_t)g.lh * 2}, {(void**)&s.x3, B * g.lh * 2},
       {(void**)&s.shared_red, B * g.h * 2}, {(void**)&s.expert_sum, B * g.lh * 4},
-      {(void**)&s.fix_part, (size_t)g.fix_bank * 2 * 4}, {(void**)&s.fix_cnt, (size_t)g.cnt_bank * 2 * 4},
+      {(void**)&s.fix_part, (size_t)g.fix_bank * 2 * 4}, {(void**)&s.argmax_key, B * 8},
       {(void**)&s.situ_buf, situ_floats * 4},
-      {(void**)&s.argmax_key, B * 8}, {(void**)&bar, 64}, {(void**)&phase_count, 64}, {(void**)&s.err, 64},
-      {(void**)&s.situ_cnt, situ_tiles * 4},
-      {(void**)&s.phase_ts, (kMaxPhases + 1) * 8}, {(void**)&s.arrive_ts, (size_t)kArrivePhases * 1024 * 8},
-      {(void**)&s.warp_ts, (size_t)kArrivePhases * x->grid * kWarps * 8},
-      {(void**)&s.sub_ts, (size_t)kArrivePhases * 16 * 8},
+      {(void**)&s.phase_ts, (kMaxPhases + 1) * 8}, {(void**)&s.sub_ts, (size_t)kArrivePhases * 16 * 8},
+      {(void**)&s.arrive_ts, profiling ? (size_t)kArrivePhases * 1024 * 8 : 0},
+      {(void**)&s.warp_ts, profiling ? (size_t)kArrivePhases * sms * kWarps * 8 : 0},
   };
-  size_t total = 0;
-  for (auto& it : items) total += align_up(it.bytes, 256);
-  x->scratch_bytes = total;
-  if (cudaMalloc(&x->scratch, total) != cudaSuccess) { delete x; return KK3_ERR_CUDA; }
-  if (cudaMemset(x->scratch, 0, total) != cudaSuccess) { cudaFree(x->scratch); delete x; return KK3_ERR_CUDA; }
-  {
-    size_t off = 0;
-    for (auto& it : items) {
-      *it.p = (char*)x->scratch + off;
-      off += align_up(it.bytes, 256);
-    }
+  size_t off = 0;
+  for (auto& it : items) {
+    *it.p = (base && it.bytes) ? base + off : nullptr;
+    // the exchange block's data regions are written before they are read: only its flag array must be zero
+    if (it.p == (void**)&comm) pl->zero = off + (comm_inline ? flag_bytes : 0);
+    off += align_up(it.bytes, 256);
   }
-  s.bar = bar;
-  s.phase_count = phase_count;
+  pl->total = off;
+  // the mirror word stands in for mapped host memory when the caller gives none (kk3_init replaces it)
+  s.err_host = err_mirror;
+  if (comm_inline) c.base[g.rank] = comm;
+  const int HR = g.mla_mt * 16;
+  size_t sm = mla_smem_bytes(HR);
+  const size_t sm_row = (512 + (size_t)(g.h > g.lh ? g.h : g.lh)) * 4 + 64;
+  const size_t sm_abs = ((size_t)g.B * 128 + 4 * 16 * 128) * 4;
+  const size_t sm_comb = mla_combine_smem_bytes(g.B);
+  const size_t sm_route = kRouteSmem;
+  const size_t sm_gemv = (size_t)kWarps * kGemvSmemPerWarp;   // per-warp cp.async rings of the GEMV phases
+  sm = sm_gemv > sm ? sm_gemv : sm;
+  sm = sm_row > sm ? sm_row : sm;
+  sm = sm_abs > sm ? sm_abs : sm;
+  sm = sm_comb > sm ? sm_comb : sm;
+  sm = sm_route > sm ? sm_route : sm;
+  sm = (size_t)kExpSmem > sm ? (size_t)kExpSmem : sm;   // expert rings + activation row cache
+  pl->smem = align_up(sm, 128);
+}
+
+extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
+  if (!out) return KK3_ERR_ARG;
+  *out = nullptr;
+  int rc = validate(cfg);
+  if (rc != KK3_OK) return rc;
+  KK3_CUDA(cudaSetDevice(cfg->device));
+  kk3_ctx* x = new (std::nothrow) kk3_ctx();
+  if (!x) return KK3_ERR_CUDA;
+  x->cfg = *cfg;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, cfg->device) != cudaSuccess) { delete x; return KK3_ERR_CUDA; }
+  x->sms = prop.multiProcessorCount;
+  x->grid = x->sms;
+  StepPlan pl;
+  plan_step(cfg, x->grid, nullptr, true, false, &pl);   // sizes
+  x->scratch_bytes = pl.total;
+  if (cudaMalloc(&x->scratch, pl.total) != cudaSuccess) { delete x; return KK3_ERR_CUDA; }
+  if (cudaMemset(x->scratch, 0, pl.total) != cudaSuccess) { cudaFree(x->scratch); delete x; return KK3_ERR_CUDA; }
+  plan_step(cfg, x->grid, (unsigned char*)x->scratch, true, false, &pl);
+  x->g = pl.g;
+  x->s = pl.s;
+  x->nt = pl.nt;
+  const Geo& g = x->g;
+  Scratch& s = x->s;
+  const size_t B = g.B;
   // device error word in mapped host memory, readable without synchronising
   if (cudaHostAlloc((void**)&x->err_host, 64, cudaHostAllocMapped) != cudaSuccess) {
     cudaFree(x->scratch); delete x; return KK3_ERR_CUDA;
@@ -241,25 +311,10 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   }
   memset(x->trace_host, 0xff, kTraceWords * sizeof(int));
   s.trace_host = x->trace_dev;
-  // exchange buffer: flags [B][tp] u32, then two parity regions {att bf16 [tp][B][h], exp f32 [tp][B][lh],
-  // shd bf16 [tp][B][h], key u64 [tp][B]}
+  // exchange buffer: its own allocation, so that CUDA IPC can export it to the peers
+  x->comm = pl.comm;
   Comm& c = x->comm;
-  memset(&c, 0, sizeof(c));
-  const size_t tp = g.tp;
-  c.flag_off = 0;
-  size_t off = align_up(B * tp * 4, 256);
-  c.att_off = 0;
-  size_t r = align_up(tp * B * g.h * 2, 256);
-  c.exp_off = r;
-  r += align_up(tp * B * g.lh * 4, 256);
-  c.shd_off = r;
-  r += align_up(tp * B * g.h * 2, 256);
-  c.key_off = r;
-  r += align_up(tp * B * 8, 256);
-  c.region_bytes = r;
-  c.data_off[0] = off;
-  c.data_off[1] = off + r;
-  x->comm_bytes = off + 2 * r;
+  x->comm_bytes = pl.comm_bytes;
   if (cudaMalloc(&x->comm_local, x->comm_bytes) != cudaSuccess ||
       cudaMemset(x->comm_local, 0, x->comm_bytes) != cudaSuccess) {
     cudaFreeHost(x->err_host); cudaFree(x->scratch); delete x; return KK3_ERR_CUDA;
@@ -267,22 +322,7 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   for (int i = 0; i < kMaxTp; ++i) c.base[i] = nullptr;
   c.base[g.rank] = (unsigned char*)x->comm_local;
   x->peers_open = g.tp == 1;
-  // shared memory: the largest phase (MLA attention with all head tiles, or row buffers)
-  const int HR = g.mla_mt * 16;
-  size_t sm_mla = mla_smem_bytes(HR);
-  size_t sm_row = (512 + (size_t)(g.h > g.lh ? g.h : g.lh)) * 4 + 64;
-  size_t sm_abs = ((size_t)g.B * 128 + 4 * 16 * 128) * 4;
-  size_t sm_comb = mla_combine_smem_bytes(g.B);
-  size_t sm_route = kRouteSmem;
-  size_t sm_gemv = (size_t)kWarps * kGemvSmemPerWarp;   // per-warp cp.async rings of the GEMV phases
-  size_t sm = sm_mla;
-  sm = sm_gemv > sm ? sm_gemv : sm;
-  sm = sm_row > sm ? sm_row : sm;
-  sm = sm_abs > sm ? sm_abs : sm;
-  sm = sm_comb > sm ? sm_comb : sm;
-  sm = sm_route > sm ? sm_route : sm;
-  sm = (size_t)kExpSmem > sm ? (size_t)kExpSmem : sm;   // expert rings + activation row cache
-  x->smem = align_up(sm, 128);
+  x->smem = pl.smem;
   if (x->smem > (size_t)prop.sharedMemPerBlockOptin) {
     kk3_free(x);
     return KK3_ERR_UNSUPPORTED;
@@ -295,6 +335,7 @@ extern "C" int kk3_init(const kk3_config* cfg, kk3_ctx** out) {
   x->args = new (std::nothrow) StepArgs();
   if (!x->args) { kk3_free(x); return KK3_ERR_CUDA; }
   // diagnostics table
+  const size_t qkv_w = pl.qkv_w;
   void* bp[KK3_BUF_COUNT] = {s.prefix, s.xa, s.xm, s.attn_in, s.scores, s.latent, s.shared_act, s.x3, s.route_w,
                              s.qkv, s.mla_q, s.absorbed, s.absorbed, s.expert_sum, s.blocks, x->comm_local,
                              s.phase_ts, s.arrive_ts, s.sub_ts, s.warp_ts};
@@ -533,122 +574,6 @@ struct NoAllocDevice {
 static NoAllocDevice noalloc_dev[kNoAllocMaxDevices];
 static std::mutex noalloc_mu;
 
-// Geometry, scratch layout and launch shape of a TP1 step whose scratch starts at `base` (same formulas as
-// kk3_init). The layout starts with the words that must be zero when a step begins (see kk3_step_noalloc);
-// `zero_bytes` covers them.
-static int plan_noalloc(const kk3_config* cfg, int sms, unsigned char* base, StepArgs* a, size_t* total_bytes,
-                        size_t* zero_bytes, int* nt, size_t* smem) {
-  Geo& g = a->g;
-  memset(&g, 0, sizeof(g));
-  g.L = cfg->layers; g.B = cfg->batch; g.h = cfg->hidden; g.lh = cfg->latent_hidden; g.inter = cfg->inter_shard;
-  g.dinter = cfg->dense_inter_shard; g.sinter = cfg->shared_inter_shard; g.hr = cfg->heads; g.d = cfg->head_dim;
-  g.qr = cfg->q_lora_rank; g.kr = cfg->kv_lora_rank; g.nr = cfg->qk_nope_dim; g.rd = cfg->qk_rope_dim;
-  g.vd = cfg->v_head_dim; g.V = cfg->vocab_shard; g.E = cfg->experts; g.K = cfg->topk; g.ctx = cfg->context;
-  g.conv = cfg->conv_kernel; g.bs = cfg->attn_res_block_size; g.first_dense = cfg->first_dense; g.tp = 1;
-  g.rank = 0; g.qdim = g.hr * g.d;
-  for (int l = 0; l < g.L; ++l) {
-    if (((l + 1) % 4 == 0) || l == g.L - 1) ++g.nmla; else ++g.nkda;
-  }
-  g.nblk = (g.L + g.bs - 1) / g.bs;
-  g.timeout_ns = cfg->timeout_ns > 0 ? cfg->timeout_ns : 10000000000ll;
-  *nt = g.B <= 8 ? 1 : (g.B <= 16 ? 2 : (g.B <= 32 ? 4 : 8));
-  plan_mla(g, sms);
-  const long long gw = (long long)sms * kWarps;
-  g.fix_bank = 2ll * gw * (2 * *nt * 128);
-  {
-    long long tiles = 0;
-    auto mx = [&](long long v) { tiles = v > tiles ? v : tiles; };
-    mx((3ll * g.qdim + g.qdim + g.d + g.hr + 15 * 6) / 16 + 6);
-    mx((long long)(g.qr + g.kr + g.rd + g.hr * g.vd) / 16 + 3);
-    mx((long long)g.hr * (g.nr + g.rd) / 16 + 1);
-    mx(g.h / 16 + 1);
-    mx(2ll * ((g.dinter + 15) / 16) + 2);                                        // dense gate | up
-    mx((long long)(g.E + 15) / 16 + (g.lh + 15) / 16 + 2ll * ((g.sinter + 15) / 16) + 4);   // MoE input pass
-    mx((long long)(g.V + 15) / 16 + 1);
-    mx((long long)g.B * g.K * ((g.inter > g.lh ? g.inter : g.lh) / 16));
-    g.cnt_bank = (int)tiles;
-  }
-  const size_t B = g.B;
-  const size_t qkv_w =
-      (size_t)3 * g.qdim > (size_t)(g.qr + g.kr + g.rd) ? (size_t)3 * g.qdim : (size_t)(g.qr + g.kr + g.rd);
-  Scratch& s = a->s;
-  memset(&s, 0, sizeof(s));
-  const size_t situ_tiles = (size_t)((g.dinter > g.sinter ? g.dinter : g.sinter) + 15) / 16 + 1;
-  const size_t situ_floats = 2 * situ_tiles * 32 * 4 * (size_t)*nt;
-  Comm& c = a->comm;
-  memset(&c, 0, sizeof(c));
-  // exchange buffer of a single rank: flags [B][1] u32, then two parity regions {att, exp, shd, key}
-  const size_t flag_bytes = align_up(B * 4, 256);
-  c.flag_off = 0;
-  c.att_off = 0;
-  size_t r = align_up(B * g.h * 2, 256);
-  c.exp_off = r;
-  r += align_up(B * g.lh * 4, 256);
-  c.shd_off = r;
-  r += align_up(B * g.h * 2, 256);
-  c.key_off = r;
-  r += align_up(B * 8, 256);
-  c.region_bytes = r;
-  c.data_off[0] = flag_bytes;
-  c.data_off[1] = flag_bytes + r;
-  const size_t comm_bytes = flag_bytes + 2 * r;
-  unsigned char* comm = nullptr;
-  int* err_mirror = nullptr;
-  struct Item { void** p; size_t bytes; };
-  Item items[] = {
-      // must be zero when a step begins: barrier word, phase count, error word and its mirror, situ pair
-      // counters, stream-K tile counters, exchange flags (the exchange buffer's flag
-      // array comes first; its data regions after it are written before they are read)
-      {(void**)&s.bar, 64}, {(void**)&s.phase_count, 64}, {(void**)&s.err, 64}, {(void**)&err_mirror, 64},
-      {(void**)&s.situ_cnt, situ_tiles * 4},
-      {(void**)&s.fix_cnt, (size_t)g.cnt_bank * 2 * 4}, {(void**)&comm, comm_bytes},
-      // written before they are read within every step
-      {(void**)&s.prefix, B * g.h * 2}, {(void**)&s.blocks, (size_t)g.nblk * B * g.h * 2},
-      {(void**)&s.xa, B * g.h * 2}, {(void**)&s.xm, B * g.h * 2}, {(void**)&s.qkv, B * qkv_w * 2},
-      {(void**)&s.og, B * (size_t)g.qdim * 2}, {(void**)&s.fa, B * g.d * 2}, {(void**)&s.beta, B * g.hr * 2},
-      {(void**)&s.attn_in, B * (size_t)g.hr * g.vd * 2}, {(void**)&s.mla_qan, B * g.qr * 2},
-      {(void**)&s.mla_q, B * (size_t)g.hr * (g.nr + g.rd) * 2}, {(void**)&s.absorbed, B * (size_t)g.hr * g.kr * 2},
-      {(void**)&s.mla_part, B * (size_t)g.mla_chunks * g.hr * (g.kr + 2) * 4},
-      {(void**)&s.dense_act, B * (size_t)(g.dinter > 0 ? g.dinter : 64) * 2}, {(void**)&s.scores, B * g.E * 4},
-      {(void**)&s.latent, B * g.lh * 2}, {(void**)&s.latent_p, B * g.lh * 2},
-      {(void**)&s.shared_act, B * (size_t)(g.sinter > 0 ? g.sinter : 64) * 2}, {(void**)&s.route_ids, B * g.K * 4},
-      {(void**)&s.route_w, B * g.K * 4}, {(void**)&s.pair_row, B * g.K * 4}, {(void**)&s.pair_slot, B * g.K * 4},
-      {(void**)&s.chunk_info, (1 + B * g.K * 3) * 4}, {(void**)&s.act_p, B * g.K * (size_t)g.inter * 2},
-      {(void**)&s.out_slot, B * g.K * (size_t)g.lh * 2}, {(void**)&s.x3, B * g.lh * 2},
-      {(void**)&s.shared_red, B * g.h * 2}, {(void**)&s.expert_sum, B * g.lh * 4},
-      {(void**)&s.fix_part, (size_t)g.fix_bank * 2 * 4}, {(void**)&s.argmax_key, B * 8},
-      {(void**)&s.situ_buf, situ_floats * 4},
-      {(void**)&s.phase_ts, (kMaxPhases + 1) * 8}, {(void**)&s.sub_ts, (size_t)kArrivePhases * 16 * 8},
-  };
-  size_t off = 0;
-  for (auto& it : items) {
-    *it.p = base ? base + off : nullptr;
-    off += align_up(it.bytes, 256);
-    if (it.p == (void**)&comm) *zero_bytes = off - align_up(it.bytes, 256) + flag_bytes;
-  }
-  *total_bytes = off;
-  s.arrive_ts = nullptr;   // per-CTA barrier stamps are a profiling aid of the context path
-  s.warp_ts = nullptr;
-  s.trace_host = nullptr;
-  s.err_host = err_mirror;
-  c.base[0] = comm;
-  const int HR = g.mla_mt * 16;
-  size_t sm = mla_smem_bytes(HR);
-  const size_t sm_row = (512 + (size_t)(g.h > g.lh ? g.h : g.lh)) * 4 + 64;
-  const size_t sm_abs = ((size_t)g.B * 128 + 4 * 16 * 128) * 4;
-  const size_t sm_comb = mla_combine_smem_bytes(g.B);
-  const size_t sm_route = kRouteSmem;
-  const size_t sm_gemv = (size_t)kWarps * kGemvSmemPerWarp;
-  sm = sm_gemv > sm ? sm_gemv : sm;
-  sm = sm_row > sm ? sm_row : sm;
-  sm = sm_abs > sm ? sm_abs : sm;
-  sm = sm_comb > sm ? sm_comb : sm;
-  sm = sm_route > sm ? sm_route : sm;
-  sm = (size_t)kExpSmem > sm ? (size_t)kExpSmem : sm;   // expert rings + activation row cache
-  *smem = align_up(sm, 128);
-  return KK3_OK;
-}
-
 // First call on a device, with that device current: find the scratch array's device address and the SM
 // count. The first call therefore does CUDA set-up work; make it before any stream capture that contains
 // this entry point and before latency-sensitive use.
@@ -694,15 +619,18 @@ extern "C" int kk3_step_noalloc(const kk3_config* cfg, const void* const* table,
   // the argument block is ~25 KB (one pointer per table slot); it lives on this host stack until the launch
   // has copied it
   StepArgs a;
-  size_t total = 0, zero = 0, smem = 0;
-  int nt = 1;
-  plan_noalloc(cfg, d->sms, d->base, &a, &total, &zero, &nt, &smem);
+  StepPlan pl;
+  plan_step(cfg, d->sms, d->base, false, true, &pl);   // the same planner as kk3_init
+  const size_t total = pl.total, zero = pl.zero, smem = pl.smem;
+  const int nt = pl.nt;
+  a.g = pl.g;
+  a.s = pl.s;
+  a.comm = pl.comm;
   if (total > kNoAllocScratchBytes) return KK3_ERR_TOO_LARGE;
   if (smem > d->smem_optin) return KK3_ERR_UNSUPPORTED;
   if (!table_complete(table, table_size, a.g)) return KK3_ERR_ARG;   // before anything is cleared or launched
-  // The kernel's dynamic shared memory limit is per-function state shared with kk3_init, which sets it to its
-  // own geometry's need. It is raised here when below this launch's need and never lowered, so a live context
-  // keeps working and a lower value a later kk3_init left is undone.
+  // The kernel's dynamic shared memory limit is per-function state shared with kk3_init; both raise it when
+  // below the launch's need and never lower it, so every live context keeps working.
   {
     cudaError_t e = nt == 1 ? raise_smem_nt1(smem) : nt == 2 ? raise_smem_nt2(smem)
                   : nt == 4 ? raise_smem_nt4(smem) : raise_smem_nt8(smem);

@@ -435,6 +435,20 @@ KK3_DEV void lm_head_job(const StepArgs& a, GemvJob& j) {
 
 // ---- the kernel -------------------------------------------------------------------------------------
 
+// A CTA that leaves the step because a wait ran out or an error was reported marks the step's integer outputs
+// as invalid before it returns: next_token = -1 and cache_length = 0 for every row (a valid step writes a token
+// in [0, vocab) and a length of 1 or context + 1). The caller learns of the failure from the outputs it reads
+// after synchronising, not only from the status word at its next call. Every failing CTA writes the same
+// values, and no CTA runs a later phase once the error word is set.
+KK3_DEV void poison_outputs(const StepArgs& a) {
+  long long* next = gout<long long>(a, KK3_OUT_NEXT_TOKEN);
+  long long* len = gout<long long>(a, KK3_OUT_CACHE_LENGTH);
+  for (int b = threadIdx.x; b < a.g.B; b += kThreads) {
+    next[b] = -1;
+    len[b] = 0;
+  }
+}
+
 template <int NT>
 __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_constant__ StepArgs a) {
   // dynamic shared memory on a 1024-byte boundary (checked below; ptxas pads the static variables before it):
@@ -458,9 +472,14 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   const unsigned seq0 = a.epoch * 1024u;
   const bool lead = threadIdx.x == 0;
 #define KK3_RUN (phase >= a.start_phase)
+#define KK3_FAIL()        \
+  do {                    \
+    poison_outputs(a);    \
+    return;               \
+  } while (0)
 #define KK3_PHASE_END()                                                                      \
   do {                                                                                       \
-    if (KK3_RUN && !grid_sync(a, phase)) return;                                             \
+    if (KK3_RUN && !grid_sync(a, phase)) KK3_FAIL();                                         \
     ++phase;                                                                                 \
     trace_progress(a, 0, phase);                                                             \
     if (blockIdx.x == 0 && threadIdx.x == 0 && phase <= kMaxPhases) a.s.phase_ts[phase] = globaltimer(); \
@@ -489,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   for (int l = 0; l < g.L; ++l) {
     const bool mla = layer_is_mla(g, l);
     // attention prologue (kimi.py:257-262)
-    if (KK3_RUN && !phase_attn_prologue(a, l, nb, pending, pend_signal, seq0 + pend_x, pend_x & 1, fsm, phase)) return;
+    if (KK3_RUN && !phase_attn_prologue(a, l, nb, pending, pend_signal, seq0 + pend_x, pend_x & 1, fsm, phase)) KK3_FAIL();
     pending = PEND_NONE;
     if (l % g.bs == 0) ++nb;
     KK3_PHASE_END();
@@ -596,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
     }
     const unsigned x_att = xi++;
     KK3_PHASE_END();
-    if (KK3_RUN && !phase_mlp_prologue(a, l, nb, seq0 + x_att, x_att & 1, fsm)) return;
+    if (KK3_RUN && !phase_mlp_prologue(a, l, nb, seq0 + x_att, x_att & 1, fsm)) KK3_FAIL();
     KK3_PHASE_END();
     if (l < g.first_dense) {
       // dense FFN (kimi.py:304)
@@ -668,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         run_experts<1>(a, sph);
       }
       KK3_PHASE_END();
-      if (KK3_RUN && !phase_moe_combine(a, l, seq0 + x_moe, x_moe & 1, fsm)) return;
+      if (KK3_RUN && !phase_moe_combine(a, l, seq0 + x_moe, x_moe & 1, fsm)) KK3_FAIL();
       KK3_PHASE_END();
       // latent up + shared + residual (kimi.py:325-329)
       if (KK3_RUN) {
@@ -682,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   // head (kimi.py:330-334)
   if (pending != PEND_NONE) {
     // the last layer was dense: fold its exchange into prefix first
-    if (KK3_RUN && !phase_fold_pending(a, pending, pend_signal, seq0 + pend_x, pend_x & 1)) return;
+    if (KK3_RUN && !phase_fold_pending(a, pending, pend_signal, seq0 + pend_x, pend_x & 1)) KK3_FAIL();
     KK3_PHASE_END();
   }
   if (KK3_RUN) phase_head_prologue(a, nb, fsm);
@@ -693,12 +712,13 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   }
   KK3_PHASE_END();
   const unsigned x_key = xi++;
-  if (KK3_RUN && !phase_argmax(a, seq0 + x_key, x_key & 1)) return;
+  if (KK3_RUN && !phase_argmax(a, seq0 + x_key, x_key & 1)) KK3_FAIL();
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     if (phase + 1 <= kMaxPhases) a.s.phase_ts[phase + 1] = globaltimer();
     *a.s.phase_count = phase + 1;
   }
 #undef KK3_BUILD
+#undef KK3_FAIL
 #undef KK3_PHASE_END
 #undef KK3_RUN
 }

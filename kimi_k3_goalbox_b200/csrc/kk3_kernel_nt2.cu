@@ -6,20 +6,21 @@
 
 namespace kk3 {
 
-cudaError_t prepare_nt2(size_t smem, int* occupancy) {
-  cudaError_t e = cudaFuncSetAttribute(kk3_step_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occupancy, kk3_step_kernel<2>, kThreads, smem);
-}
-
-// Raise (never lower) the kernel's dynamic shared memory limit to at least `smem`; used by the allocation-free
-// entry point, which shares this per-function setting with contexts made by kk3_init.
+// Raise (never lower) the kernel's dynamic shared memory limit to at least `smem`. The limit is per-function
+// state shared by every context and by the allocation-free entry point, so lowering it for a smaller geometry
+// would make the next launch of a live context with a larger need fail.
 cudaError_t raise_smem_nt2(size_t smem) {
   cudaFuncAttributes attr;
   cudaError_t e = cudaFuncGetAttributes(&attr, kk3_step_kernel<2>);
   if (e != cudaSuccess) return e;
   if ((size_t)attr.maxDynamicSharedSizeBytes >= smem) return cudaSuccess;
   return cudaFuncSetAttribute(kk3_step_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
+cudaError_t prepare_nt2(size_t smem, int* occupancy) {
+  cudaError_t e = raise_smem_nt2(smem);
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occupancy, kk3_step_kernel<2>, kThreads, smem);
 }
 
 cudaError_t launch_nt2(const StepArgs* args, int grid, size_t smem, cudaStream_t stream) {

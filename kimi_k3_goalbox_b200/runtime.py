@@ -34,7 +34,8 @@ FFN_SLOT0 = 16
 
 ERRORS = {0: "ok", -1: "bad argument or pointer table", -2: "geometry not supported by the sm_100a kernels",
           -3: "CUDA runtime call failed", -4: "in-kernel wait exceeded its bound", -5: "in-kernel check failed",
-          -6: "tensor-parallel peers are not open", -7: "context failed earlier; rebuild it"}
+          -6: "tensor-parallel peers are not open", -7: "context failed earlier; rebuild it",
+          -8: "geometry needs more scratch than the allocation-free entry point's static buffer"}
 
 
 class Config(ctypes.Structure):
@@ -248,6 +249,10 @@ class StepContext:
             raise KK3Error(rc, "kk3_step")
 
     def step(self, values: dict, outputs: dict | None = None, stop_phase: int = -1) -> dict:
+        """Enqueue one step. Raises if an earlier step of this context reported a failure (the status word is
+        read without synchronising, so a failure of the previous step is seen once its kernel has ended). A
+        step that fails writes next_token = -1 and cache_length = 0 into its own outputs, so its failure is
+        visible in what the caller reads back after synchronising."""
         self.check()
         self._bind_inputs(values)
         out = self.allocate_outputs() if outputs is None else outputs

@@ -217,6 +217,43 @@ def decode_mxfp4(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
     return values.flatten(-2)
 
 
+_C_DECODE = None
+
+
+def _c_decode_lib():
+    """The C restatement of the decode (oracle/mxfp4.c), built in-tree by kimi_k3_goalbox_b200/build.py; None
+    when it has not been built (the torch restatement above is then used everywhere)."""
+    global _C_DECODE
+    if _C_DECODE is None:
+        import ctypes
+        from pathlib import Path
+        path = Path(__file__).resolve().parent / "libkk3_oracle_mxfp4.so"
+        _C_DECODE = False
+        if path.exists():
+            lib = ctypes.CDLL(str(path))
+            for name in ("kk3o_decode_mxfp4_f32", "kk3o_decode_mxfp4_bf16"):
+                getattr(lib, name).argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p]
+                getattr(lib, name).restype = None
+            _C_DECODE = lib
+    return _C_DECODE or None
+
+
+def decode_mxfp4_as(codes: torch.Tensor, scales: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """decode_mxfp4(codes, scales).to(dtype) for dtype FP32 or BF16. On CPU with the C decode built, the same
+    bits come from oracle/mxfp4.c in one multithreaded pass (the torch form materialises int64 indices and
+    several FP32 temporaries per value and dominates the oracle's CPU step); elsewhere the torch form."""
+    lib = _c_decode_lib()
+    if (lib is None or codes.device.type != "cpu" or dtype not in (torch.float32, torch.bfloat16)
+            or codes.dtype != torch.uint8 or scales.dtype != torch.uint8
+            or codes.shape[:-1] != scales.shape or codes.shape[-1] != 16):
+        return decode_mxfp4(codes, scales).to(dtype)
+    codes, scales = codes.contiguous(), scales.contiguous()
+    out = torch.empty(scales.shape + (32,), dtype=dtype)
+    fn = lib.kk3o_decode_mxfp4_f32 if dtype == torch.float32 else lib.kk3o_decode_mxfp4_bf16
+    fn(codes.data_ptr(), scales.data_ptr(), scales.numel(), out.data_ptr())
+    return out.flatten(-2)
+
+
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     """common.py:13-21 (plain form): FP32 normalise, cast to x's dtype, multiply by the weight in that dtype."""
     xf = x.float()
@@ -393,7 +430,7 @@ def _moe(st, layer, x):
         rows, slots = (top == expert).nonzero(as_tuple=True)
 
         def wt(kind, e=expert):
-            return decode_mxfp4(v[f"{pre}{kind}_blocks"][e], v[f"{pre}{kind}_scales"][e]).to(act)
+            return decode_mxfp4_as(v[f"{pre}{kind}_blocks"][e], v[f"{pre}{kind}_scales"][e], act)
 
         y = st.cast(st.cast(situ(latent[rows] @ wt("gate").T, latent[rows] @ wt("up").T)) @ wt("down").T)
         total.index_add_(0, rows, y.float() * w[rows, slots, None])

@@ -52,9 +52,42 @@ def test_small_geometry_with_phase_diagnostics():
     _run_and_grade(gh.small_case(3), 7, reset=[False, True, False], diagnose=True)
 
 
-@pytest.mark.parametrize("batch,seed", [(1, 3), (1, 4), (8, 11), (20, 5)])
+@pytest.mark.parametrize("batch,seed", [(1, 3), (1, 4), (8, 11), (12, 6), (16, 9), (20, 5)])
 def test_small_geometry_batches(batch, seed):
+    """Batches 1-8, 9-16, 17-32 and 33-64 run the NT = 1, 2, 4 and 8 instantiations of the step kernel."""
     _run_and_grade(gh.small_case(batch), seed)
+
+
+def test_fresh_seeds():
+    """The harness draws a fresh seed per trial (megabench/harness/distributed.py:33-36): two random seeds,
+    printed so a failure can be replayed."""
+    import secrets
+    for batch in (3, 8):
+        seed = secrets.randbits(32)
+        print(f"fresh seed {seed} (batch {batch})")
+        _run_and_grade(gh.small_case(batch), seed)
+
+
+def test_two_live_contexts_of_different_geometry():
+    """Contexts share per-function kernel attributes (the dynamic shared memory limit is raised, never
+    lowered): two live contexts of different geometry step alternately and both stay within the band."""
+    a_case, b_case = gh.small_case(3), gh.small_case(2, q_heads=4, intermediate=256)
+    with torch.inference_mode():
+        va, vb = ko.make_inputs(a_case, 21, "cuda"), ko.make_inputs(b_case, 22, "cuda")
+        ea, eb = ko.reference(a_case, va, serial=True), ko.reference(b_case, vb, serial=True)
+        ca, cb = StepContext(a_case), StepContext(b_case)
+        try:
+            for _ in range(2):
+                oa = {k: v.clone() for k, v in ca.step(va).items()}
+                ob = {k: v.clone() for k, v in cb.step(vb).items()}
+                torch.cuda.synchronize()
+                ca.check()
+                cb.check()
+                ko.compare(a_case, va, ea, oa, serial=True)
+                ko.compare(b_case, vb, eb, ob, serial=True)
+        finally:
+            ca.close()
+            cb.close()
 
 
 def test_dev_l4_tp1_b8_full_width():

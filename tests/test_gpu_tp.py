@@ -1,11 +1,12 @@
 """Tensor-parallel GPU tests: the in-kernel one-shot exchange over NVLink peer memory.
 
-- test_tp2_band_two_gpus: two ranks on two GPUs (torchrun, NCCL only for set-up), each graded with the band
-  rule against the oracle computed with real all-reduces; skipped on a box with fewer than two GPUs.
+- test_tp_band_multi_gpu: TP2, TP4 and TP8 ranks on as many GPUs (torchrun, NCCL only for set-up), each graded
+  with the band rule against the oracle computed with real all-reduces, on fresh seeds; a spec is skipped on
+  a box with fewer GPUs than its TP degree.
 - test_exchange_wait_times_out: failure detection on one GPU without a fault. A TP2 context's peer buffer is
   a zeroed allocation that no rank ever writes, so the first exchange wait runs out its (short) bound; the
-  kernel must report KK3_ERR_TIMEOUT through the status word, leave the device usable, and the context must
-  refuse further steps.
+  kernel must report KK3_ERR_TIMEOUT through the status word, write next_token = -1 and cache_length = 0 into
+  the step's outputs, leave the device usable, and the context must refuse further steps.
 """
 
 from __future__ import annotations
@@ -34,24 +35,44 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def two_gpus() -> bool:
-    return torch.cuda.is_available() and torch.cuda.device_count() >= 2
+def gpus() -> int:
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+# Every spec runs as tp ranks on tp GPUs; each rank is graded against the oracle with real all-reduces.
+TP_SPECS = [
+    ({"kind": "small", "batch": 3, "tp": 2}, "small-b3-tp2"),
+    ({"kind": "case", "case": "kimi-k3-dev-l8-tp2-b8-s8192"}, "dev-l8-tp2-b8"),
+    ({"kind": "small", "batch": 5, "tp": 4}, "small-b5-tp4"),
+    ({"kind": "case", "case": "kimi-k3-dev-l4-tp1-b8-s8192", "tp": 4}, "dev-l4-tp4-b8"),
+    ({"kind": "small", "batch": 3, "tp": 8}, "small-b3-tp8"),
+    ({"kind": "case", "case": "kimi-k3-syn-l8-tp8-b1-s8192"}, "syn-l8-tp8-b1"),
+    ({"kind": "case", "case": "kimi-k3-syn-l8-tp8-b8-s8192"}, "syn-l8-tp8-b8"),
+    ({"kind": "case", "case": "kimi-k3-syn-l8-tp8-b64-s8192"}, "syn-l8-tp8-b64"),
+]
+
+
+def spec_tp(spec: dict) -> int:
+    if "tp" in spec:
+        return spec["tp"]
+    return cases.get_case(spec["case"])["tp"]
 
 
 @pytest.mark.gpu
-@pytest.mark.skipif(not two_gpus(), reason="needs two GPUs")
-@pytest.mark.parametrize("spec", [{"kind": "small", "batch": 3, "tp": 2},
-                                  {"kind": "case", "case": "kimi-k3-dev-l8-tp2-b8-s8192", "params": {"layers": 4}}],
-                         ids=["small-b3-tp2", "dev-l4-tp2-b8"])
-def test_tp2_band_two_gpus(spec):
+@pytest.mark.parametrize("spec", [s for s, _ in TP_SPECS], ids=[i for _, i in TP_SPECS])
+def test_tp_band_multi_gpu(spec):
+    tp = spec_tp(spec)
+    if gpus() < tp:
+        pytest.skip(f"needs {tp} GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", MASTER_ADDR="127.0.0.1")
-    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
+    cmd = ["timeout", "-k", "30", "900", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={tp}", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
            str(ROOT / "tests" / "tp_worker.py"), "--spec", json.dumps(spec)]
-    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=700)
+    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=1000)
     out = r.stdout + r.stderr
     assert r.returncode == 0, out[-4000:]
-    assert out.count("ok:") == 2, out[-4000:]
+    assert out.count("ok:") == tp, out[-4000:]
+    print("\n".join(line for line in out.splitlines() if "ok:" in line))
 
 
 @pytest.mark.gpu
@@ -64,9 +85,11 @@ def test_exchange_wait_times_out():
         try:
             peer = torch.zeros(ctx.exchange_bytes(), dtype=torch.uint8, device="cuda:0")
             ctx.debug_set_peer(1, peer)
-            ctx.step(values)
+            out = ctx.step(values)
             torch.cuda.synchronize()          # the kernel must end by itself
             assert ctx.status() == KK3_ERR_TIMEOUT
+            # the failed step marks its own integer outputs as invalid
+            assert bool((out["next_token"] == -1).all()) and bool((out["cache_length"] == 0).all())
             with pytest.raises(runtime.KK3Error) as err:
                 ctx.step(values)
             assert err.value.code in (KK3_ERR_TIMEOUT, KK3_ERR_FAILED)

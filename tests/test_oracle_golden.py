@@ -106,3 +106,23 @@ def test_two_rank_gloo_matches_reference():
         for key, t in want["bf16"].items():
             assert torch.equal(got["bf16"][key], t), key
         assert got["grade"] == want["grade"]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_c_decode_matches_torch_decode_on_every_scale_byte(dtype):
+    """oracle/mxfp4.c reproduces the torch restatement of quantization.py:40-51 bit for bit, for every E8M0
+    byte (0: subnormal products, 254: overflow to inf, 255: NaN groups) and every code byte."""
+    from kimi_k3_goalbox_b200 import build
+    build.build(verbose=False)
+    assert ko._c_decode_lib() is not None, "oracle/libkk3_oracle_mxfp4.so was not built"
+    g = torch.Generator().manual_seed(5)
+    codes = torch.randint(0, 256, (256, 3, 16), generator=g, dtype=torch.uint8)
+    codes[:, 0] = torch.arange(256, dtype=torch.uint8)[:, None].expand(256, 16).flip(0)
+    scales = torch.arange(256, dtype=torch.uint8)[:, None].expand(256, 3).contiguous()
+    want = ko.decode_mxfp4(codes, scales).to(dtype)
+    got = ko.decode_mxfp4_as(codes, scales, dtype)
+    assert got.shape == want.shape and got.dtype == want.dtype
+    nan = want.isnan()
+    assert torch.equal(got.isnan(), nan)   # NaN groups agree; NaN payload bits are not part of the contract
+    view = torch.int16 if dtype == torch.bfloat16 else torch.int32
+    assert torch.equal(got.view(view)[~nan], want.view(view)[~nan])

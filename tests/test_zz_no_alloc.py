@@ -69,9 +69,9 @@ def assert_same(got: dict, want: dict) -> None:
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("case", [gh.small_case(3),
+@pytest.mark.parametrize("case", [gh.small_case(3), gh.small_case(12),
                                   gh.rank_equivalent("kimi-k3-syn-l8-tp8-b8-s8192", layers=4)],
-                         ids=["small-b3", "tp8-rank-b8-l4"])
+                         ids=["small-b3", "small-b12-nt2", "tp8-rank-b8-l4"])
 def test_noalloc_matches_context_step_twice(lib, case):
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)

@@ -12,6 +12,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import secrets
 import sys
 from datetime import timedelta
 from pathlib import Path
@@ -30,16 +31,18 @@ from tests import gpu_helpers as gh  # noqa: E402
 
 def make_case(spec: dict) -> dict:
     if spec["kind"] == "small":
-        # expert intermediate 256: 128 rows per rank (the expert engine needs shards of 128)
-        return cases.variant(gh.small_case(spec["batch"], intermediate=128 * spec["tp"]), tp=spec["tp"])
+        # per rank: 128 expert rows (the expert engine needs shards of 128), 64 dense rows, one head or more
+        tp = spec["tp"]
+        return cases.variant(gh.small_case(spec["batch"], intermediate=128 * tp, dense_intermediate=max(256, 64 * tp),
+                                           q_heads=max(2, tp)), tp=tp)
     base = cases.get_case(spec["case"])
-    return cases.variant(base, **spec.get("params", {}))
+    return cases.variant(base, tp=spec.get("tp"), **spec.get("params", {}))
 
 
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--spec", required=True, help="JSON case spec")
-    ap.add_argument("--seed", type=int, default=11)
+    ap.add_argument("--seed", type=int, default=None, help="default: a fresh seed per run (printed)")
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     device = torch.device("cuda", rank)
@@ -49,6 +52,10 @@ def main() -> int:
     case["params"].pop("checkpoint", None)
     assert case["tp"] == world, (case["tp"], world)
     group = dist.group.WORLD
+    # a fresh seed per run, drawn on rank 0 and broadcast (megabench/harness/distributed.py:33-36)
+    seed = [args.seed if args.seed is not None else secrets.randbits(32)]
+    dist.broadcast_object_list(seed, src=0)
+    args.seed = int(seed[0])
     try:
         with torch.inference_mode():
             values = ko.make_inputs(case, args.seed, device, rank)
@@ -64,7 +71,7 @@ def main() -> int:
             for key, t in first.items():
                 assert torch.equal(t, second[key]), f"rank {rank}: second step differs in {key}"
             run.close()
-        print(f"rank {rank} ok:", {k: (v.get("worst_ratio", v) if isinstance(v, dict) else v) for k, v in details.items()},
+        print(f"rank {rank} ok: seed {args.seed}", {k: (v.get("worst_ratio", v) if isinstance(v, dict) else v) for k, v in details.items()},
               flush=True)
     finally:
         dist.destroy_process_group()
