@@ -27,6 +27,7 @@ Legs of one run, in order:
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import secrets
@@ -38,8 +39,12 @@ import time
 from datetime import timedelta
 from pathlib import Path
 
-import torch
-import torch.distributed as dist
+# Inputs of tens to ~170 GB per GPU are generated, freed and generated again in one process: expandable
+# segments keep the caching allocator from pinning freed space behind live tensors (set before CUDA starts).
+os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
@@ -366,6 +371,51 @@ def time_steps(ctx, stream, steps: int, warmup: int, n: int, clocks: ClockSample
     return t0.elapsed_time(t1), [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
 
+def host_comm_leg(args, ctx, stream, n: int) -> dict:
+    """The comparison baseline at N>1: the same kernel in phase ranges with the reference's NCCL collectives
+    between them (FP32 all-reduce of each partial, kimi.py:343-347; all-gather of the argmax keys, :218-227)
+    instead of the in-kernel one-shot peer exchange. Same inputs and outputs as the timed fused steps; one step
+    is compared with a fused step first."""
+    from kimi_k3_goalbox_b200 import runtime
+    group = dist.group.WORLD
+    fused = ctx.allocate_outputs()
+    ctx.bind_outputs(fused)
+    ctx.launch(stream.cuda_stream)
+    torch.cuda.synchronize()
+    ctx.check()
+    host = ctx.allocate_outputs()
+    ctx.bind_outputs(host)
+    ctx.set_comm_mode(runtime.COMM_HOST)
+    try:
+        counts = ctx.launch_host_comm(group, stream.cuda_stream)
+        torch.cuda.synchronize()
+        ctx.check()
+        diff = float((host["logits"] - fused["logits"]).abs().max())
+        same_tokens = bool(torch.equal(host["next_token"], fused["next_token"]))
+        same_routes = bool(torch.equal(host["expert_ids"], fused["expert_ids"]))
+        for _ in range(args.warmup):
+            ctx.launch_host_comm(group, stream.cuda_stream)
+        barrier(n)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            ctx.launch_host_comm(group, stream.cuda_stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        barrier(n)
+        ctx.check()
+    finally:
+        ctx.set_comm_mode(runtime.COMM_PEER)
+    ms = max_over_ranks(t0.elapsed_time(t1), n) / args.steps
+    flags = torch.tensor([diff, float(not same_tokens), float(not same_routes)], device="cuda", dtype=torch.float64)
+    dist.all_reduce(flags, op=dist.ReduceOp.MAX)
+    return {"us": round(ms * 1000.0, 2), "launches_per_step": counts,
+            "transport": "NCCL all-reduce (FP32) per partial + all-gather of argmax keys, between phase-range launches",
+            "vs_fused": {"max_abs_logit_diff": float(flags[0]), "next_token_equal": not bool(flags[1]),
+                         "expert_ids_equal": not bool(flags[2])},
+            "note": "same kernel; exchanges by NCCL on the host instead of in-kernel NVLink peer stores"}
+
+
 def build_runner(case: dict, n: int, rank: int, device):
     from kimi_k3_goalbox_b200.submission import build
     exec_info = execution_for(case, n, rank, device)
@@ -403,7 +453,8 @@ def measure_case(args, case: dict, n: int, rank: int, local: int, *, parity: boo
                   "pct_of_floor_8TBps": round(100.0 * (nbytes / 8.0e12) / (ms * 1e-3), 1),
                   "frac_of_measured_hbm": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4),
                   "algorithmic_bytes": nbytes, "launches_per_step": 1, "seed": seed})
-    del values
+    del values, runner
+    gc.collect()
     torch.cuda.empty_cache()
     return entry
 
@@ -430,7 +481,9 @@ def deep_stack(args, local: int) -> dict:
             chosen = (L, case, need)
             break
     if chosen is None:
-        return {"skipped": f"no layer count in {DEEP_LAYERS} fits {free / 2**30:.1f} GiB free"}
+        return {"skipped": f"no layer count in {DEEP_LAYERS} fits {free / 2**30:.1f} GiB free",
+                "torch_allocated_gib": round(torch.cuda.memory_allocated(local) / 2**30, 2),
+                "torch_reserved_gib": round(torch.cuda.memory_reserved(local) / 2**30, 2)}
     L, case, need = chosen
     seed = args.seed if args.seed is not None else secrets.randbits(32)
     e = measure_case(args, case, 1, 0, local, parity=False, seed=seed)
@@ -494,11 +547,13 @@ def run_b200(args, n: int, rank: int, local: int) -> dict | None:
         barrier(n)
         ctx.check()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1), n) / args.steps
+        nccl = host_comm_leg(args, ctx, stream, n) if n > 1 and not args.no_nccl else None
         runner.close()
         host_values = None
         if rank == 0 and n == 1 and not args.no_cpu_baseline:
             host_values = {k: v.cpu() for k, v in values.items()}   # for the cpu_baseline leg
-        del values, outputs, out
+        del values, outputs, out, runner, ctx, tok_d, rst_d
+        gc.collect()
         torch.cuda.empty_cache()
 
     extras = {}
@@ -540,6 +595,7 @@ def run_b200(args, n: int, rank: int, local: int) -> dict | None:
                      "algorithmic_bytes_per_launch": nbytes,
                      "kernel": "kk3_step_kernel (the whole step is one launch)"},
         "parity": parity,
+        "nccl_allreduce_variant": nccl,
         "e2e": {"value": round(e2e_ms * 1000.0, 2), "unit": "us", "h2d_bytes_per_step": B * 8 + B,
                 "d2h_bytes_per_step": B * 8},
         "gpu_launches": args.steps,
@@ -639,6 +695,7 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the checker leg")
     ap.add_argument("--no-extras", action="store_true", help="skip the north-star (N=8) and deep-stack (N=1) keys")
+    ap.add_argument("--no-nccl", action="store_true", help="N>1: skip the plain-NCCL comparison variant")
     args = ap.parse_args(argv)
     n = args.gpus
     world = int(os.environ.get("WORLD_SIZE", "1"))

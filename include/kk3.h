@@ -186,6 +186,21 @@ int kk3_debug_copy(kk3_ctx* ctx, int id, void* dst, size_t bytes);
 /* Bytes of this rank's exchange buffer (flags + two parity regions). */
 size_t kk3_exchange_bytes(kk3_ctx* ctx);
 
+/* Byte offsets inside this rank's exchange buffer (8 values): the flag array [B][tp] u32, the two parity data
+ * regions, the bytes of one region, and inside a region the sub-regions att bf16 [tp][B][hidden],
+ * exp f32 [tp][B][latent_hidden], shd bf16 [tp][B][hidden], key u64 [tp][B]. */
+int kk3_exchange_layout(kk3_ctx* ctx, long long* offsets);
+
+/* Exchange transport of the tensor-parallel reductions (kimi.py:343-347, :218-227).
+ * KK3_COMM_PEER (default, the product): one-shot peer stores and release flags inside the one launch.
+ * KK3_COMM_HOST (comparison baseline, no counterpart in the reference's API): each rank writes its partial only
+ * into its own slot of its own buffer and never waits; the MoE combine and argmax phases each split in two
+ * (write, then read). The caller runs the step as phase ranges with kk3_debug_phases and reduces the slots with
+ * NCCL between them: all-reduce (FP32 sum) of this rank's att, exp and shd slots, all-gather of the keys. */
+#define KK3_COMM_PEER 0
+#define KK3_COMM_HOST 1
+int kk3_set_comm_mode(kk3_ctx* ctx, int mode);
+
 /* Single-process testing aid: use an existing device allocation of kk3_exchange_bytes() bytes as rank r's
  * exchange buffer instead of an IPC mapping (no counterpart in the reference). */
 int kk3_debug_set_peer(kk3_ctx* ctx, int r, void* device_ptr);

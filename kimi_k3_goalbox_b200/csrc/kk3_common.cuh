@@ -28,6 +28,10 @@ constexpr int kMaxPhases = 2048;       // phase timestamp capacity (a 96-layer s
 constexpr int kArrivePhases = 256;     // phases with per-CTA barrier arrival stamps
 constexpr int kTraceWords = 2 * 1024 + 4096;   // mapped trace: phase and progress per CTA, marker per warp
 
+// exchange transport (StepArgs::comm_mode)
+constexpr int kCommPeer = 0;   // in-kernel one-shot NVLink peer stores + per-row release flags (the product)
+constexpr int kCommHost = 1;   // comparison baseline: the host runs NCCL collectives between phase-range launches
+
 // device error word values (also the host-visible status)
 constexpr int kErrTimeout = 1;
 constexpr int kErrDevice = 2;
@@ -114,6 +118,8 @@ struct StepArgs {
   int stop_phase;       // debug: return after this many grid phases (-1: run everything)
   int start_phase;      // debug: skip the work (and barriers) of phases before this one (0: run everything)
   int trace;            // debug: publish per-CTA progress to mapped host memory (fault localisation)
+  int comm_mode;        // kCommPeer: one-shot peer stores and flags inside the kernel; kCommHost: each rank
+                        // writes only its own slot and the host reduces the slots between launches (NCCL)
   int nptr;
   const void* ptr[kMaxPtrs];
 };

@@ -123,6 +123,10 @@ KK3_DEV unsigned long long argmax_key(float v, unsigned idx) {
 KK3_DEV unsigned char* xregion(const StepArgs& a, int dst, int parity) {
   return a.comm.base[dst] + a.comm.data_off[parity];
 }
+// ranks whose regions receive this rank's partial: every rank (peer stores), or only this rank's own region
+// when the host reduces the slots with NCCL between launches
+KK3_DEV int xdst_lo(const StepArgs& a) { return a.comm_mode == kCommHost ? a.g.rank : 0; }
+KK3_DEV int xdst_hi(const StepArgs& a) { return a.comm_mode == kCommHost ? a.g.rank + 1 : a.g.tp; }
 
 // Fused epilogue for one complete 16-row tile. acc[mt][nt][i]: rows row0 + r (+8 for i >= 2), column
 // nt*8 + 2c + (i & 1).
@@ -231,7 +235,7 @@ KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const 
           // layout [src][col][ldo], src = this rank; written into every rank's region
           const bf16 b = f2bf(v);
           const size_t off = (size_t)a.g.rank * a.g.B * j.ldo + o;
-          for (int dst = 0; dst < a.g.tp; ++dst)
+          for (int dst = xdst_lo(a); dst < xdst_hi(a); ++dst)
             reinterpret_cast<bf16*>(xregion(a, dst, parity) + j.aux_off)[off] = b;
           break;
         }

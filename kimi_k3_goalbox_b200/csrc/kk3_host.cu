@@ -60,6 +60,7 @@ struct kk3_ctx {
   unsigned epoch = 0;
   int failed = 0;
   int peers_open = 0;
+  int comm_mode = kCommPeer;
   StepArgs* args = nullptr;
   size_t buf_bytes[KK3_BUF_COUNT] = {};
   void* buf_ptr[KK3_BUF_COUNT] = {};
@@ -388,6 +389,21 @@ extern "C" int kk3_debug_set_peer(kk3_ctx* x, int r, void* device_ptr) {
 
 extern "C" size_t kk3_exchange_bytes(kk3_ctx* x) { return x ? x->comm_bytes : 0; }
 
+extern "C" int kk3_exchange_layout(kk3_ctx* x, long long* offsets) {
+  if (!x || !offsets) return KK3_ERR_ARG;
+  const Comm& c = x->comm;
+  const long long v[8] = {c.flag_off, c.data_off[0], c.data_off[1], c.region_bytes,
+                          c.att_off, c.exp_off, c.shd_off, c.key_off};
+  for (int i = 0; i < 8; ++i) offsets[i] = v[i];
+  return KK3_OK;
+}
+
+extern "C" int kk3_set_comm_mode(kk3_ctx* x, int mode) {
+  if (!x || (mode != KK3_COMM_PEER && mode != KK3_COMM_HOST)) return KK3_ERR_ARG;
+  x->comm_mode = mode == KK3_COMM_HOST ? kCommHost : kCommPeer;
+  return KK3_OK;
+}
+
 // Every tensor except the token ids and reset flags is read with 16-byte vector or cp.async loads, so a
 // misaligned pointer would fault on the device: reject it here instead.
 static bool table_aligned(const void* const* table, int n) {
@@ -452,6 +468,7 @@ static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int
   a->stop_phase = stop_phase;
   a->start_phase = start_phase < 0 ? 0 : start_phase;
   a->trace = x->trace;
+  a->comm_mode = x->comm_mode;
   a->nptr = n;
   memcpy(a->ptr, table, sizeof(void*) * n);
   cudaError_t e = launch_kernel(x->nt, a, x->grid, x->smem, (cudaStream_t)stream);
@@ -650,6 +667,7 @@ extern "C" int kk3_step_noalloc(const kk3_config* cfg, const void* const* table,
   a.stop_phase = -1;
   a.start_phase = 0;
   a.trace = 0;
+  a.comm_mode = kCommPeer;
   a.nptr = table_size;
   memcpy(a.ptr, table, sizeof(void*) * table_size);
   cudaError_t e = launch_kernel(nt, &a, d->sms, smem, st);

@@ -36,7 +36,7 @@ KK3_FN void phase_embed(const StepArgs& a, unsigned seq, int parity, float* fsm)
     } else {
       const size_t off = ((size_t)g.rank * g.B + b) * g.h;
       #pragma unroll 1
-      for (int dst = 0; dst < g.tp; ++dst) {
+      for (int dst = xdst_lo(a); dst < xdst_hi(a); ++dst) {
         bf16* reg = reinterpret_cast<bf16*>(a.comm.base[dst] + a.comm.data_off[parity] + a.comm.att_off);
         #pragma unroll 1
         for (int e = threadIdx.x; e < g.h; e += kThreads) reg[off + e] = mine ? row[e] : zero;
@@ -164,8 +164,12 @@ KK3_FN void phase_mla_rows(const StepArgs& a, int layer, int midx, float* fsm) {
 }
 
 // MoE combine: expert_sum (slot order = ascending expert id, kimi.py:319-323), TP sum (:324),
-// latent_norm (:325) -> x3; shared-expert TP sum (:326) -> shared_red
-KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int parity, float* fsm) {
+// latent_norm (:325) -> x3; shared-expert TP sum (:326) -> shared_red.
+// `part`: kCombineAll runs it whole (the in-kernel exchange waits for the peers' slots in the middle). With the
+// host transport it is two phases: kCombineWrite ends after this rank's slot is written (the launch ends there
+// and the host all-reduces the slots), kCombineRead starts from the reduced slot.
+constexpr int kCombineAll = 0, kCombineWrite = 1, kCombineRead = 2;
+KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int parity, float* fsm, int part) {
   const Geo& g = a.g;
   float* red = fsm;
   const int nvec = g.lh / 8, hvec = g.h / 8;
@@ -178,7 +182,7 @@ KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int pa
       const int c = threadIdx.x + q * kThreads;
 #pragma unroll
       for (int e = 0; e < 8; ++e) tot[q][e] = 0.0f;
-      if (c >= nvec) continue;
+      if (c >= nvec || part == kCombineRead) continue;
       // 8 slots' loads in flight at a time (L2), summed in slot order
       const uint4* slot0 = reinterpret_cast<const uint4*>(a.s.out_slot + (size_t)b * g.K * g.lh) + c;
       #pragma unroll 1
@@ -206,20 +210,25 @@ KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int pa
     }
     if (g.tp > 1) {
       const size_t off = ((size_t)g.rank * g.B + b) * g.lh;
-      #pragma unroll 1
-      for (int dst = 0; dst < g.tp; ++dst) {
-        float* reg = reinterpret_cast<float*>(a.comm.base[dst] + a.comm.data_off[parity] + a.comm.exp_off) + off;
+      if (part != kCombineRead) {
+        #pragma unroll 1
+        for (int dst = xdst_lo(a); dst < xdst_hi(a); ++dst) {
+          float* reg = reinterpret_cast<float*>(a.comm.base[dst] + a.comm.data_off[parity] + a.comm.exp_off) + off;
 #pragma unroll
-        for (int q = 0; q < kRowChunks; ++q) {
-          const int c = threadIdx.x + q * kThreads;
-          if (c >= nvec) continue;
-          *reinterpret_cast<float4*>(reg + c * 8) = make_float4(tot[q][0], tot[q][1], tot[q][2], tot[q][3]);
-          *reinterpret_cast<float4*>(reg + c * 8 + 4) = make_float4(tot[q][4], tot[q][5], tot[q][6], tot[q][7]);
+          for (int q = 0; q < kRowChunks; ++q) {
+            const int c = threadIdx.x + q * kThreads;
+            if (c >= nvec) continue;
+            *reinterpret_cast<float4*>(reg + c * 8) = make_float4(tot[q][0], tot[q][1], tot[q][2], tot[q][3]);
+            *reinterpret_cast<float4*>(reg + c * 8 + 4) = make_float4(tot[q][4], tot[q][5], tot[q][6], tot[q][7]);
+          }
         }
+        if (part == kCombineWrite) continue;   // the host all-reduces the slots before kCombineRead
+        xch_signal_row(a, b, seq);
+        if (!xch_wait_row(a, b, seq)) return false;
       }
-      xch_signal_row(a, b, seq);
-      if (!xch_wait_row(a, b, seq)) return false;
       const float* reg = xlocal<float>(a, parity, a.comm.exp_off);
+      // peer stores: every rank's slot, summed in rank order; host transport: the all-reduced own slot
+      const int lo = a.comm_mode == kCommHost ? g.rank : 0, hi = a.comm_mode == kCommHost ? g.rank + 1 : g.tp;
 #pragma unroll
       for (int q = 0; q < kRowChunks; ++q) {
         const int c = threadIdx.x + q * kThreads;
@@ -227,7 +236,7 @@ KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int pa
 #pragma unroll
         for (int e = 0; e < 8; ++e) tot[q][e] = 0.0f;
         #pragma unroll 1
-        for (int src = 0; src < g.tp; ++src) {
+        for (int src = lo; src < hi; ++src) {
           const float* r = reg + ((size_t)src * g.B + b) * g.lh + c * 8;
           const float4 v0 = *reinterpret_cast<const float4*>(r), v1 = *reinterpret_cast<const float4*>(r + 4);
           tot[q][0] += v0.x; tot[q][1] += v0.y; tot[q][2] += v0.z; tot[q][3] += v0.w;
@@ -283,7 +292,10 @@ KK3_FN void phase_head_prologue(const StepArgs& a, int nb, float* fsm) {
   }
 }
 
-KK3_FN bool phase_argmax(const StepArgs& a, unsigned seq, int parity) {
+// Greedy token (kimi.py:218-227): the largest (value, lowest index) key over the ranks. `part` as in
+// phase_moe_combine: with the host transport, kCombineWrite stores this rank's key and the launch ends (the host
+// all-gathers the keys), kCombineRead takes the maximum over the gathered slots.
+KK3_FN bool phase_argmax(const StepArgs& a, unsigned seq, int parity, int part) {
   const Geo& g = a.g;
   long long* next = gout<long long>(a, KK3_OUT_NEXT_TOKEN);
   long long* len = gout<long long>(a, KK3_OUT_CACHE_LENGTH);
@@ -295,10 +307,15 @@ KK3_FN bool phase_argmax(const StepArgs& a, unsigned seq, int parity) {
     __syncthreads();
     if (g.tp > 1) {
       const size_t off = (size_t)g.rank * g.B + b;
-      if ((int)threadIdx.x < g.tp) {
+      if ((int)threadIdx.x < g.tp && part != kCombineRead &&
+          ((int)threadIdx.x >= xdst_lo(a) && (int)threadIdx.x < xdst_hi(a))) {
         unsigned long long* reg =
             reinterpret_cast<unsigned long long*>(a.comm.base[threadIdx.x] + a.comm.data_off[parity] + a.comm.key_off);
         reg[off] = best;
+      }
+      if (part == kCombineWrite) {
+        __syncthreads();
+        continue;
       }
       xch_signal_row(a, b, seq);
       if (!xch_wait_row(a, b, seq)) return false;
@@ -471,6 +488,8 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   unsigned xi = 0;
   const unsigned seq0 = a.epoch * 1024u;
   const bool lead = threadIdx.x == 0;
+  // host transport (comparison baseline): the combine and argmax phases are split at their exchange
+  const bool host_comm = a.comm_mode == kCommHost && g.tp > 1;
 #define KK3_RUN (phase >= a.start_phase)
 #define KK3_FAIL()        \
   do {                    \
@@ -687,7 +706,14 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         run_experts<1>(a, sph);
       }
       KK3_PHASE_END();
-      if (KK3_RUN && !phase_moe_combine(a, l, seq0 + x_moe, x_moe & 1, fsm)) KK3_FAIL();
+      if (host_comm) {
+        // host transport: write this rank's slots, end the phase (the host all-reduces), then read
+        if (KK3_RUN && !phase_moe_combine(a, l, seq0 + x_moe, x_moe & 1, fsm, kCombineWrite)) KK3_FAIL();
+        KK3_PHASE_END();
+        if (KK3_RUN && !phase_moe_combine(a, l, seq0 + x_moe, x_moe & 1, fsm, kCombineRead)) KK3_FAIL();
+      } else {
+        if (KK3_RUN && !phase_moe_combine(a, l, seq0 + x_moe, x_moe & 1, fsm, kCombineAll)) KK3_FAIL();
+      }
       KK3_PHASE_END();
       // latent up + shared + residual (kimi.py:325-329)
       if (KK3_RUN) {
@@ -712,7 +738,13 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   }
   KK3_PHASE_END();
   const unsigned x_key = xi++;
-  if (KK3_RUN && !phase_argmax(a, seq0 + x_key, x_key & 1)) KK3_FAIL();
+  if (host_comm) {
+    if (KK3_RUN && !phase_argmax(a, seq0 + x_key, x_key & 1, kCombineWrite)) KK3_FAIL();
+    KK3_PHASE_END();
+    if (KK3_RUN && !phase_argmax(a, seq0 + x_key, x_key & 1, kCombineRead)) KK3_FAIL();
+  } else {
+    if (KK3_RUN && !phase_argmax(a, seq0 + x_key, x_key & 1, kCombineAll)) KK3_FAIL();
+  }
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     if (phase + 1 <= kMaxPhases) a.s.phase_ts[phase + 1] = globaltimer();
     *a.s.phase_count = phase + 1;

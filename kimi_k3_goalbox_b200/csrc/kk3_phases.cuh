@@ -18,14 +18,17 @@ KK3_DEV unsigned* flag_ptr(const StepArgs& a, int dst, int b, int src) {
   return reinterpret_cast<unsigned*>(a.comm.base[dst] + a.comm.flag_off) + (size_t)b * a.g.tp + src;
 }
 
-// called by a whole CTA after its writes of row b (all threads), tp > 1 only
+// called by a whole CTA after its writes of row b (all threads), tp > 1 only. With the host transport the
+// launch ends before the slots are read and the host reduces them: nothing to signal or wait for.
 KK3_DEV void xch_signal_row(const StepArgs& a, int b, unsigned seq) {
+  if (a.comm_mode == kCommHost) return;
   __threadfence_system();
   __syncthreads();
   if ((int)threadIdx.x < a.g.tp) st_release_sys(flag_ptr(a, threadIdx.x, b, a.g.rank), seq);
 }
 
 KK3_DEV bool xch_wait_row(const StepArgs& a, int b, unsigned seq) {
+  if (a.comm_mode == kCommHost) return true;
   __shared__ int ok;
   if (threadIdx.x == 0) ok = 1;
   __syncthreads();
@@ -274,11 +277,14 @@ KK3_FN void rms_row(const bf16* in, const bf16* w, int n, float eps, bf16* out, 
 
 // Sum the tp BF16 partials of row b, 16-byte chunk c, of an exchange sub-region (FP32, rank order), rounded
 // to BF16 (kimi.py:343-347).
+// Sum of the tp bf16 slots of row b (FP32, rank order, kimi.py:343-347). With the host transport the host has
+// already all-reduced the partials into this rank's own slot (FP32 sum, cast to bf16), so that slot is read.
 KK3_DEV void xch_sum8(const StepArgs& a, int parity, long long off, int b, int width, int c, float (&out)[8]) {
   const bf16* base = xlocal<bf16>(a, parity, off);
 #pragma unroll
   for (int e = 0; e < 8; ++e) out[e] = 0.0f;
-  for (int src = 0; src < a.g.tp; ++src) {
+  const int lo = a.comm_mode == kCommHost ? a.g.rank : 0, hi = a.comm_mode == kCommHost ? a.g.rank + 1 : a.g.tp;
+  for (int src = lo; src < hi; ++src) {
     float f[8];
     unpack8(ld_act16(base + ((size_t)src * a.g.B + b) * width + c * 8), f);
 #pragma unroll

@@ -46,6 +46,48 @@ class Config(ctypes.Structure):
         "rank", "device")] + [("timeout_ns", ctypes.c_int64)]
 
 
+COMM_PEER, COMM_HOST = 0, 1   # include/kk3.h KK3_COMM_*
+
+
+def host_comm_segments(params: dict, tp: int) -> list[tuple[int, int, list[tuple[str, str, int]]]]:
+    """Phase ranges of one step under the host transport (KK3_COMM_HOST), as the kernel runs them
+    (csrc/kk3_kernel.cuh): (start_phase, stop_phase, exchanges to run after the range), stop_phase -1 = to the
+    end. An exchange is (sub-region, "sum" | "gather", parity): "sum" all-reduces this rank's slot (FP32 sum,
+    kimi.py:343-347), "gather" all-gathers the argmax keys (kimi.py:218-227). Exchanges alternate parity in
+    program order, as the kernel's exchange counter does."""
+    from .cases import is_mla
+    L, fd = params["layers"], params["first_dense"]
+    names = ["embed"]
+    for l in range(L):
+        names.append("attn_prologue")
+        names += (["mla_proj", "mla_rows", "mla_qb", "mla_absorb", "mla_attend", "mla_combine"] if is_mla(params, l)
+                  else ["kda_proj", "kda"])
+        names += ["o_proj", "mlp_prologue"]
+        names += (["dense_gate_up", "dense_down"] if l < fd else
+                  ["moe_in", "experts_gate_up", "experts_down", "moe_combine_write", "moe_combine_read", "latent_up"])
+    if L <= fd:
+        names.append("fold")
+    names += ["head_prologue", "lm_head", "argmax_write", "argmax_read"]
+    points = {"embed": [("att", "sum")], "o_proj": [("att", "sum")], "dense_down": [("att", "sum")],
+              "moe_combine_write": [("exp", "sum"), ("shd", "sum")], "argmax_write": [("key", "gather")]}
+    segs, start, xi = [], 0, 0
+    for i, name in enumerate(names):
+        if name in points and tp > 1:
+            segs.append((start, i + 1, [(region, kind, xi & 1) for region, kind in points[name]]))
+            xi += 1
+            start = i + 1
+    segs.append((start, -1, []))
+    return segs
+
+
+class _DeviceBytes:
+    """A raw device range exposed through __cuda_array_interface__, so torch can alias it without a copy."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
 class KK3Error(RuntimeError):
     def __init__(self, code: int, what: str):
         super().__init__(f"{what}: kk3 error {code} ({ERRORS.get(code, 'unknown')})")
@@ -83,6 +125,8 @@ def load_library() -> ctypes.CDLL:
         lib.kk3_debug_copy.argtypes = [vp, i32, vp, ctypes.c_size_t]
         lib.kk3_debug_trace.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_int), i32]
         lib.kk3_launch_config.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(ctypes.c_size_t)]
+        lib.kk3_exchange_layout.argtypes = [vp, ctypes.POINTER(ctypes.c_longlong)]
+        lib.kk3_set_comm_mode.argtypes = [vp, i32]
         _LIB = lib
     return _LIB
 
@@ -291,7 +335,69 @@ class StepContext:
         self.lib.kk3_launch_config(self.handle, ctypes.byref(g), ctypes.byref(t), ctypes.byref(s))
         return g.value, t.value, s.value
 
+    # --- the host-transport comparison baseline (KK3_COMM_HOST) -----------------------------------------
+    def set_comm_mode(self, mode: int) -> None:
+        rc = self.lib.kk3_set_comm_mode(self.handle, mode)
+        if rc != 0:
+            raise KK3Error(rc, "kk3_set_comm_mode")
+
+    def exchange_slots(self) -> dict:
+        """This rank's exchange buffer as torch views: {(parity, region): tensor [tp, B, width]} for the regions
+        att (bf16), exp (f32), shd (bf16) and key (int64 view of the u64 keys)."""
+        if getattr(self, "_xviews", None) is None:
+            ptr, size = ctypes.c_void_p(), ctypes.c_size_t()
+            rc = self.lib.kk3_debug_buffer(self.handle, 15, ctypes.byref(ptr), ctypes.byref(size))   # KK3_BUF_EXCHANGE
+            if rc != 0:
+                raise KK3Error(rc, "kk3_debug_buffer")
+            off = (ctypes.c_longlong * 8)()
+            rc = self.lib.kk3_exchange_layout(self.handle, off)
+            if rc != 0:
+                raise KK3Error(rc, "kk3_exchange_layout")
+            raw = torch.as_tensor(_DeviceBytes(ptr.value, size.value), device=torch.device("cuda", self.device))
+            tp, B, p = self.case["tp"], self.params["batch"], self.params
+            widths = {"att": (p["hidden"], torch.bfloat16, 4), "exp": (p["latent_hidden"], torch.float32, 5),
+                      "shd": (p["hidden"], torch.bfloat16, 6), "key": (1, torch.int64, 7)}
+            views = {}
+            for parity in (0, 1):
+                for region, (w, dt, k) in widths.items():
+                    start = off[1 + parity] + off[k]
+                    n = tp * B * w * torch.empty(0, dtype=dt).element_size()
+                    views[(parity, region)] = raw[start:start + n].view(dt).view(tp, B, w)
+            self._xraw, self._xviews = raw, views
+        return self._xviews
+
+    def launch_host_comm(self, group, stream: int | None = None) -> dict:
+        """One step with the host transport: the kernel runs in phase ranges and NCCL reduces the partials
+        between them, as the reference does (kimi.py:343-347: FP32 all-reduce of each partial, cast back;
+        :218-227: the argmax keys are all-gathered and the kernel takes their maximum). Returns the launch
+        counts of the step."""
+        import torch.distributed as dist
+        tp, rank = self.case["tp"], self.cfg.rank
+        views = self.exchange_slots()
+        segs = host_comm_segments(self.params, tp)
+        counts = {"step_kernel_segments": len(segs), "nccl_collectives": 0, "torch_glue_kernels": 0}
+        for start, stop, exchanges in segs:
+            self.launch(stream, stop_phase=stop, start_phase=start)
+            for region, kind, parity in exchanges:
+                v = views[(parity, region)]
+                if kind == "gather":
+                    flat = v.view(-1)
+                    mine = flat[rank * v.shape[1]:(rank + 1) * v.shape[1]].clone()
+                    dist.all_gather_into_tensor(flat, mine, group=group)
+                    counts["torch_glue_kernels"] += 1
+                elif v.dtype == torch.float32:
+                    dist.all_reduce(v[rank], group=group)
+                else:
+                    acc = v[rank].float()
+                    dist.all_reduce(acc, group=group)
+                    v[rank].copy_(acc)
+                    counts["torch_glue_kernels"] += 2
+                counts["nccl_collectives"] += 1
+        return counts
+
     def close(self) -> None:
+        self._cached_inputs = None   # the bound input tensors: let the caller's memory go with the context
+        self._xviews = self._xraw = None
         if getattr(self, "handle", None):
             self.lib.kk3_free(self.handle)
             self.handle = None
