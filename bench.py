@@ -371,6 +371,24 @@ def time_steps(ctx, stream, steps: int, warmup: int, n: int, clocks: ClockSample
     return t0.elapsed_time(t1), [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
 
+def phase_breakdown(ctx, stream, n: int) -> dict:
+    """One more step, then its in-step phase times (CTA 0's %globaltimer stamps after every grid barrier) on
+    every rank: per phase the slowest rank, summed by phase name over the layers (largest first). Untimed."""
+    from kimi_k3_goalbox_b200 import phase_profile
+    ctx.launch(stream.cuda_stream)
+    torch.cuda.synchronize()
+    ctx.check()
+    rows = phase_profile.step_phase_times(ctx)
+    per_rank = gather(rows, n)
+    worst = []
+    for i, r in enumerate(rows):
+        k = max(range(n), key=lambda q: per_rank[q][i]["us"])
+        worst.append(per_rank[k][i])
+    out = phase_profile.summarize(worst)
+    out["method"] = "in-step %globaltimer stamps of one step; per phase the slowest rank; work = until the last CTA arrived"
+    return out
+
+
 def host_comm_leg(args, ctx, stream, n: int) -> dict:
     """The comparison baseline at N>1: the same kernel in phase ranges with the reference's NCCL collectives
     between them (FP32 all-reduce of each partial, kimi.py:343-347; all-gather of the argmax keys, :218-227)
@@ -520,6 +538,7 @@ def run_b200(args, n: int, rank: int, local: int) -> dict | None:
         with ClockSampler(local) as clocks:
             total_ms, per_step = time_steps(ctx, stream, args.steps, args.warmup, n, clocks)
         clock_summary = merge_clocks(gather(clocks.summary(), n))
+        phases = phase_breakdown(ctx, stream, n)
         total_ms = max_over_ranks(total_ms, n)
         p50_ms = max_over_ranks(statistics.median(per_step), n)
         ms_per_step = total_ms / args.steps
@@ -595,6 +614,7 @@ def run_b200(args, n: int, rank: int, local: int) -> dict | None:
                      "algorithmic_bytes_per_launch": nbytes,
                      "kernel": "kk3_step_kernel (the whole step is one launch)"},
         "parity": parity,
+        "phase_breakdown": phases,
         "nccl_allreduce_variant": nccl,
         "e2e": {"value": round(e2e_ms * 1000.0, 2), "unit": "us", "h2d_bytes_per_step": B * 8 + B,
                 "d2h_bytes_per_step": B * 8},

@@ -580,9 +580,10 @@ KK3_DEV unsigned lds32(const unsigned char* p) { return *reinterpret_cast<const 
 // ldmatrix.x4 gives a lane the four group words of its row; each quad converts them to FP16 in hardware
 // (cvt.rn.f16x2.e2m1x2), runs mma.sync per 32-wide group and applies the group scale to the FP32 partial,
 // in the same order as a unit at a time.
-// E8M0 scale byte -> FP32 factor (2^(s - 127); s = 0 and s = 255 exactly as the reference decodes them),
-// filled at kernel start; at namespace scope so the engine's reads compile to shared-memory loads
-static __shared__ float kk3_e8m0_lut[256];
+// E8M0 byte -> 2^(s - 127) from its bits (s << 23), two integer instructions and no table: exact for s in 1..254.
+// s = 0 gives 0 instead of the reference's 2^-127 (a weight of at most 6 * 2^-127, below the resolution of any
+// FP32 sum it enters); s = 255 gives inf instead of the reference's NaN group (the output is not finite either way).
+KK3_DEV float e8m0_bits(unsigned s) { return __uint_as_float(s << 23); }
 
 constexpr int kExpRing = 10240;           // per-warp ring bytes: four MT=2 pair slots (2560 B) or six MT=1
 constexpr int kExpXCache = 56 * 1024;     // per-CTA activation row cache, after the rings
@@ -638,10 +639,13 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
   int nchunks = __ldcg(a.s.chunk_info);
   nchunks = nchunks < 0 ? 0 : (nchunks > npk ? npk : nchunks);
   const int per_chunk = tiles * ksteps;      // <= 512 tiles x 128 k-steps
-  const int U = nchunks * per_chunk;         // <= 2048 chunks: fits 32 bits
+  const int U = nchunks * per_chunk;         // <= 2048 chunks: fits 32 bits; even (ksteps is even)
   if (U == 0) return;                        // the same for every thread of the grid
+  // warps get whole unit pairs: warp w owns pairs [UP * w / GW, UP * (w + 1) / GW), so no pair is split
+  // between warps and the unit loop has no partial pairs
+  const int UP = U >> 1;
   int GW = gridDim.x * kWarps;
-  GW = GW < U ? GW : U;
+  GW = GW < UP ? GW : UP;
 
   // routing-table values are clamped so that a routing fault can never address outside the buffers
   auto chunk_expert = [&](int chunk) {
@@ -669,8 +673,8 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
     unsigned long long mask = 0ull;
     int first = 0, count = 0;
     if (cw0 < GW) {
-      const int cbeg = (int)((long long)U * cw0 / GW);
-      const int cend = (int)((long long)U * (cw0 + kWarps < GW ? cw0 + kWarps : GW) / GW);
+      const int cbeg = 2 * (int)((long long)UP * cw0 / GW);
+      const int cend = 2 * (int)((long long)UP * (cw0 + kWarps < GW ? cw0 + kWarps : GW) / GW);
       int fp_lo, np_lo, fp_hi, np_hi;
       chunk_pairs(cbeg / per_chunk, fp_lo, np_lo);
       chunk_pairs((cend - 1) / per_chunk, fp_hi, np_hi);
@@ -716,8 +720,7 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
 
   const int gw = cw0 + warp;
   if (gw >= GW) return;
-  const int ubeg = (int)((long long)U * gw / GW), uend = (int)((long long)U * (gw + 1) / GW);
-  const int nunits = uend - ubeg;
+  const int ubeg = 2 * (int)((long long)UP * gw / GW), uend = 2 * (int)((long long)UP * (gw + 1) / GW);
   unsigned char* ring = kk3_dyn_smem + (size_t)warp * kExpRing;
   if (trace) trace_warp(a, 1);
 
@@ -760,7 +763,13 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
       p_scl = ph.scales[scl_mt] + e * ph.expert_scales +
               (swin ? (size_t)(p_tile * 16 + scl_i) * sbytes : (size_t)p_tile * 16 * sbytes + scl_i * 16);
   };
-  int p_left = npairs, p_slot = 0;
+  // A scale window (the scales of 4 pairs, or of the whole tile) is copied once, with the first of its pairs the
+  // warp issues, into the scale area of window slot (window count % S); the consumer counts windows the same way.
+  // Window slot w is reused S windows later, when the consumer has left window w behind (every window holds at
+  // least one pair and the producer runs S - 1 pairs ahead).
+  const int wmask = swin ? 3 : 0x7fffffff;   // (kp & wmask) == 0: kp opens a window
+  int p_left = npairs, p_slot = 0, p_wslot = S - 1;
+  bool p_first = true;
   auto p_issue = [&]() {
     const unsigned slot = ring_s + p_slot * kSlot;
 #pragma unroll
@@ -771,9 +780,13 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
                    ::"r"(slot + mt * kCode + 512 + p_dst_code), "l"(p_code[mt] + 8 * rowbytes), "l"(pol) : "memory");
       p_code[mt] += 64;
     }
-    if (scl_lane)
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(slot + p_dst_scl),
-                   "l"(p_scl + (swin ? (p_kp >> 2) * 16 : 0)) : "memory");
+    if (p_first || (p_kp & wmask) == 0) {
+      p_wslot = p_wslot + 1 == S ? 0 : p_wslot + 1;
+      if (scl_lane)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ring_s + p_wslot * kSlot + p_dst_scl),
+                     "l"(p_scl + (swin ? (p_kp >> 2) * 16 : 0)) : "memory");
+    }
+    p_first = false;
     p_slot = p_slot + 1 == S ? 0 : p_slot + 1;
     --p_left;
     if (++p_kp == kpairs) {
@@ -854,7 +867,7 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[mt][0][i] = 0.0f;
-  const bool lo_first = (ubeg & 1) == 0, hi_last = (uend & 1) == 0;
+  int c_wslot = S - 1;   // window slot of the current pair's scales (counted as the producer counts)
   for (int n = 0; n < npairs; ++n) {
     __syncwarp();   // every lane is done with the slot the next issue overwrites
     if (p_left > 0) p_issue();
@@ -864,7 +877,6 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
     if (trace && n < 2) trace_warp(a, 5 | (n << 8));
     const unsigned slot = ring_s + c_slot * kSlot;
     c_slot = c_slot + 1 == S ? 0 : c_slot + 1;
-    const bool lo = n > 0 || lo_first, hi = n < npairs - 1 || hi_last;
     // this pair's activation pieces: k = 128 kp + 64 u + 32 g + 8c, group j = 2u + g; each next one is
     // loaded while the previous group is being multiplied
     const int xko = c_kp * 256 + c * 16;
@@ -873,12 +885,13 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
       return *reinterpret_cast<const uint4*>(xp + xko + j * 64);                              // generic
     };
     uint4 xn = ldx(0);
+    if (n == 0 || (c_kp & wmask) == 0) c_wslot = c_wslot + 1 == S ? 0 : c_wslot + 1;
     unsigned wa[MT][4], wb[MT][4], sa[MT], sb[MT];   // group words and scale words of rows r and r + 8
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
       ldsm4(wa[mt], slot + mt * kCode + c_ldsm);
       ldsm4(wb[mt], slot + mt * kCode + 512 + c_ldsm);
-      const unsigned char* sl = ring + (slot - ring_s) + mt * kScale + (c_kp & c_kmask) * 4;
+      const unsigned char* sl = ring + (size_t)c_wslot * kSlot + mt * kScale + (c_kp & c_kmask) * 4;
       sa[mt] = *reinterpret_cast<const unsigned*>(sl + c_scl_a);
       sb[mt] = *reinterpret_cast<const unsigned*>(sl + c_scl_b);
     }
@@ -886,7 +899,6 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
     for (int j = 0; j < 4; ++j) {
       const uint4 X = xn;
       if (j < 3) xn = ldx(j + 1);
-      if (j < 2 ? !lo : !hi) continue;
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
         unsigned ra[4], rb[4];
@@ -895,23 +907,25 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
         float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         mma_f16_nv(t, ra[0], rb[0], ra[1], rb[1], X.x, X.y);
         mma_f16_nv(t, ra[2], rb[2], ra[3], rb[3], X.z, X.w);
-        // 2^(s - 127) from a 256-entry table (s = 0 and s = 255 exactly as the reference decodes them)
-        const float fa = kk3_e8m0_lut[(sa[mt] >> (8 * j)) & 0xffu], fb = kk3_e8m0_lut[(sb[mt] >> (8 * j)) & 0xffu];
+        // 2^(s - 127) from the scale byte's bits (see e8m0_bits)
+        const float fa = e8m0_bits((sa[mt] >> (8 * j)) & 0xffu), fb = e8m0_bits((sb[mt] >> (8 * j)) & 0xffu);
         acc[mt][0][0] = fmaf(t[0], fa, acc[mt][0][0]);
         acc[mt][0][1] = fmaf(t[1], fa, acc[mt][0][1]);
         acc[mt][0][2] = fmaf(t[2], fb, acc[mt][0][2]);
         acc[mt][0][3] = fmaf(t[3], fb, acc[mt][0][3]);
       }
     }
-    if ((c_kp == kpairs - 1 && hi) || n == npairs - 1) {
+    if (c_kp == kpairs - 1 || n == npairs - 1) {
       const int tile_beg = c_chunk * per_chunk + c_tile * ksteps;
-      // the whole tile is this warp's: no fix-up (owners are computed only for split tiles, a 64-bit division)
+      // the whole tile is this warp's: no fix-up (owners are computed only for split tiles, a 64-bit division);
+      // ownership is by unit pairs, so the fix-up works in pairs
       bool done = tile_beg >= ubeg && tile_beg + ksteps <= uend;
       if (!done) {
-        const long long first = owner_of(tile_beg, U, GW), lastw = owner_of(tile_beg + ksteps - 1, U, GW);
+        const int pt = tile_beg >> 1;
+        const long long first = owner_of(pt, UP, GW), lastw = owner_of(pt + kpairs - 1, UP, GW);
         done = first == lastw ||
                stream_k_fixup<1, MT>(a, a.s.fix_part, a.s.fix_cnt + c_chunk * tiles + c_tile, gw, tile_beg <= ubeg,
-                                     tile_beg, first, lastw, U, GW, acc);
+                                     pt, first, lastw, UP, GW, acc);
       }
       if (done) expert_epilogue<MT>(ph.rows, c_tile, out_row, acc);
 #pragma unroll

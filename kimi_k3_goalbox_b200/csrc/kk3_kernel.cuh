@@ -478,7 +478,6 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   __shared__ GemvJob sj2[2];
   __shared__ ExpertPhase sph;
   __shared__ int sjn;
-  for (int i = threadIdx.x; i < 256; i += kThreads) kk3_e8m0_lut[i] = e8m0_to_f32((unsigned)i);
   if (threadIdx.x == 0) kk3_cur_phase = 0;
   if (threadIdx.x == 0 && ((unsigned)__cvta_generic_to_shared(smem) & 1023u) != 0u) set_error(a, kErrDevice);
   __syncthreads();

@@ -27,7 +27,6 @@ using namespace kk3;
 
 template <int MT>
 __global__ void __launch_bounds__(512, 1) mma_engine(const __grid_constant__ StepArgs a, const __grid_constant__ ExpertPhase ph) {
-  for (int i = threadIdx.x; i < 256; i += kThreads) kk3_e8m0_lut[i] = e8m0_to_f32((unsigned)i);
   if (threadIdx.x == 0) kk3_cur_phase = -1;
   __syncthreads();
   run_experts<MT>(a, ph);

@@ -97,6 +97,45 @@ def phase_bytes(case: dict, distinct_experts: float | None = None) -> list[int]:
     return out
 
 
+def step_phase_times(ctx) -> list[dict]:
+    """In-step time of every grid phase of the step that ran last on `ctx` (synchronised by the caller), from the
+    %globaltimer stamps CTA 0 writes after every grid barrier: per phase its name, layer, time, the part until
+    the last CTA arrived at the barrier ("work") and the barrier after it."""
+    prog = phase_program(ctx.params)
+    n = len(prog)
+    ts = ctx.debug_buffer(16, torch.int64, (n + 1,)).cpu().tolist()
+    grid = ctx.launch_config()[0]
+    narr = min(n - 1, 256)
+    arr = ctx.debug_buffer(17, torch.int64, (narr, grid)).cpu()
+    out = []
+    for i, (name, layer) in enumerate(prog):
+        row = {"name": name, "layer": layer, "us": (ts[i + 1] - ts[i]) / 1e3}
+        if i < narr:
+            last = int(arr[i].max())
+            row["work_us"] = (last - ts[i]) / 1e3
+            row["barrier_us"] = (ts[i + 1] - last) / 1e3
+        out.append(row)
+    return out
+
+
+def summarize(rows: list[dict], top: int = 10) -> dict:
+    """Per phase name: total in-step time over the layers (and its work / barrier split), largest first."""
+    agg: dict[str, dict] = {}
+    for r in rows:
+        a = agg.setdefault(r["name"], {"us": 0.0, "work_us": 0.0, "barrier_us": 0.0, "count": 0})
+        a["us"] += r["us"]
+        a["work_us"] += r.get("work_us") or 0.0
+        a["barrier_us"] += r.get("barrier_us") or 0.0
+        a["count"] += 1
+    total = sum(r["us"] for r in rows)
+    order = sorted(agg.items(), key=lambda kv: -kv[1]["us"])[:top]
+    return {"step_us": round(total, 1), "phases": len(rows),
+            "barrier_us_total": round(sum(r.get("barrier_us") or 0.0 for r in rows), 1),
+            "top": [{"name": k, "us": round(v["us"], 1), "share": round(v["us"] / total, 3) if total else None,
+                     "work_us": round(v["work_us"], 1), "barrier_us": round(v["barrier_us"], 1), "count": v["count"]}
+                    for k, v in order]}
+
+
 def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[dict]:
     torch.cuda.set_device(device)
     with torch.inference_mode():
