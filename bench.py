@@ -149,6 +149,7 @@ class ClockSampler:
         self._stop = threading.Event()
         self._thread = None
         self._proc = None
+        self.error = None
 
     def _nvml_handle(self):
         import pynvml
@@ -161,15 +162,19 @@ class ClockSampler:
             return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device_index)
 
     def _poll(self, pynvml, handle):
-        mx = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+        try:
+            mx = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+        except Exception as exc:   # keep polling the current clock; record why the maximum is missing
+            self.error = f"max clock: {type(exc).__name__}: {exc}"
+            mx = float("nan")
         while not self._stop.is_set():
             try:
                 sm = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
                 reasons = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
                 power = pynvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
                 self.samples.append((time.time(), sm, mx, power, reasons))
-            except Exception:
-                pass
+            except Exception as exc:
+                self.error = f"{type(exc).__name__}: {exc}"
             time.sleep(0.001)
 
     def __enter__(self):
@@ -225,7 +230,8 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median([s[1] for s in inside]) if inside else None,
                 "sm_max_mhz": inside[0][2] if inside else None, "reasons": sorted(reasons), "samples": len(inside),
-                "power_w_max": max(s[3] for s in inside) if inside else None, "source": self.source}
+                "power_w_max": max(s[3] for s in inside) if inside else None, "source": self.source,
+                "samples_total": len(self.samples), "error": self.error}
 
 
 def merge_clocks(summaries: list[dict]) -> dict:
@@ -239,6 +245,10 @@ def merge_clocks(summaries: list[dict]) -> dict:
            "source": summaries[0].get("source") if summaries else None}
     if len(summaries) > 1:
         out["per_rank_sm_mhz"] = [s.get("sm_mhz") for s in summaries]
+        out["per_rank_samples"] = [(s.get("samples"), s.get("samples_total")) for s in summaries]
+    errors = [s.get("error") for s in summaries if s.get("error")]
+    if errors:
+        out["errors"] = errors[:2]
     return out
 
 

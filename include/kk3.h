@@ -123,6 +123,21 @@ int kk3_open_peers(kk3_ctx* ctx, const void* handles);
  * (megabench/harness/runner.py:66-69) / `kimi.reference` (kimi.py:230-340) for this rank. */
 int kk3_step(kk3_ctx* ctx, const void* const* table, int table_size, void* stream);
 
+/* Multi-step decoding with in-place cache append (no counterpart in the reference's per-step API; the
+ * reference's own tools chain steps by feeding the outputs back as the next step's state,
+ * tools/verify_kimi_vs_hf.py:145-154). Same table, math and outputs as kk3_step, except:
+ *  - `lengths` (device int64 [batch], 8-byte aligned) gives each row's number of cached MLA positions; the row
+ *    attends positions [0, lengths[b]) of its cache plus the new token (only the new token after a reset), and
+ *    every lengths[b] must be below the context the context was created with (the cache capacity);
+ *  - each MLA layer's new latent and rope entries are also written into that layer's kv_cache / pe_cache input
+ *    at position lengths[b] (0 after a reset): the cache inputs are updated in place;
+ *  - cache_length = lengths[b] + 1 (1 after a reset), so the previous step's cache_length output can be passed
+ *    as the next step's `lengths`, even as the same buffer;
+ *  - the KDA state outputs may alias the state inputs (each layer's input a view of the stacked output tensor):
+ *    every state element is read before it is written, by the same thread.
+ * A row whose length is at or beyond the capacity makes the step fail (status KK3_ERR_DEVICE). */
+int kk3_step_append(kk3_ctx* ctx, const void* const* table, int table_size, const int64_t* lengths, void* stream);
+
 /* Device-side status of the most recent steps, read from mapped host memory without synchronising:
  * KK3_OK, KK3_ERR_TIMEOUT or KK3_ERR_DEVICE. Call after the stream has been synchronised. A step that fails
  * also writes next_token = -1 and cache_length = 0 into its outputs, and every later kk3_step on the context

@@ -120,6 +120,7 @@ struct StepArgs {
   int trace;            // debug: publish per-CTA progress to mapped host memory (fault localisation)
   int comm_mode;        // kCommPeer: one-shot peer stores and flags inside the kernel; kCommHost: each rank
                         // writes only its own slot and the host reduces the slots between launches (NCCL)
+  const long long* lengths;   // append mode (kk3_step_append): cached positions of each row, [B]; null otherwise
   int nptr;
   const void* ptr[kMaxPtrs];
 };
@@ -281,6 +282,19 @@ KK3_DEV const T* lptr(const StepArgs& a, int layer, int slot) {
 }
 template <typename T>
 KK3_DEV T* gout(const StepArgs& a, int slot) { return reinterpret_cast<T*>(const_cast<void*>(a.ptr[slot])); }
+
+// Cached MLA positions row b attends: 0 after a reset; in append mode its length from `lengths` (clamped to the
+// cache capacity; kk3_step_append requires lengths[b] < context); else the whole context (kimi.py:274-280).
+KK3_DEV int mla_row_len(const StepArgs& a, int b) {
+  if (reinterpret_cast<const bool*>(a.ptr[KK3_RESET])[b]) return 0;
+  if (a.lengths == nullptr) return a.g.ctx;
+  const long long n = a.lengths[b];
+  return n < 0 ? 0 : (n > a.g.ctx ? a.g.ctx : (int)n);
+}
+// split-K chunks of row b: its attended sequence (cached positions + the new token) in chunks of mla_chunk_len
+KK3_DEV int mla_row_chunks(const StepArgs& a, int b) {
+  return (mla_row_len(a, b) + 1 + a.g.mla_chunk_len - 1) / a.g.mla_chunk_len;
+}
 
 KK3_DEV void set_error(const StepArgs& a, int code) {
   if (atomicCAS(a.s.err, 0, code) == 0) {

@@ -450,7 +450,8 @@ extern "C" int kk3_check_table(const kk3_config* cfg, const void* const* table, 
   return table_complete(table, table_size, g) ? KK3_OK : KK3_ERR_ARG;
 }
 
-static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int stop_phase, int start_phase) {
+static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int stop_phase, int start_phase,
+                  const long long* lengths = nullptr) {
   if (!x || !table) return KK3_ERR_ARG;
   if (x->failed) return KK3_ERR_FAILED;
   if (!x->peers_open) return KK3_ERR_PEERS;
@@ -469,6 +470,7 @@ static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int
   a->start_phase = start_phase < 0 ? 0 : start_phase;
   a->trace = x->trace;
   a->comm_mode = x->comm_mode;
+  a->lengths = lengths;
   a->nptr = n;
   memcpy(a->ptr, table, sizeof(void*) * n);
   cudaError_t e = launch_kernel(x->nt, a, x->grid, x->smem, (cudaStream_t)stream);
@@ -477,6 +479,11 @@ static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int
 
 extern "C" int kk3_step(kk3_ctx* x, const void* const* table, int n, void* stream) {
   return launch(x, table, n, stream, -1, 0);
+}
+
+extern "C" int kk3_step_append(kk3_ctx* x, const void* const* table, int n, const int64_t* lengths, void* stream) {
+  if (!x || !lengths || (reinterpret_cast<uintptr_t>(lengths) & 7u)) return KK3_ERR_ARG;
+  return launch(x, table, n, stream, -1, 0, reinterpret_cast<const long long*>(lengths));
 }
 
 extern "C" int kk3_debug_step(kk3_ctx* x, const void* const* table, int n, void* stream, int stop_phase) {
@@ -668,6 +675,7 @@ extern "C" int kk3_step_noalloc(const kk3_config* cfg, const void* const* table,
   a.start_phase = 0;
   a.trace = 0;
   a.comm_mode = kCommPeer;
+  a.lengths = nullptr;
   a.nptr = table_size;
   memcpy(a.ptr, table, sizeof(void*) * table_size);
   cudaError_t e = launch_kernel(nt, &a, d->sms, smem, st);

@@ -160,6 +160,23 @@ KK3_FN void phase_mla_rows(const StepArgs& a, int layer, int midx, float* fsm) {
     #pragma unroll 1
     for (int e = threadIdx.x; e < g.rd; e += kThreads) pew[(size_t)b * g.rd + e] = ka[(size_t)b * (g.kr + g.rd) + g.kr + e];
     __syncthreads();
+    if (a.lengths != nullptr) {
+      // append mode: the row's new latent and rope entries also go into its cache at position `length` (0 after
+      // a reset); the attention phases read only positions below it, and the new token from kv_write/pe_write
+      const bool rst = reinterpret_cast<const bool*>(a.ptr[KK3_RESET])[b];
+      const long long n = rst ? 0 : a.lengths[b];
+      if (n < 0 || n >= g.ctx) {
+        if (threadIdx.x == 0) set_error(a, kErrDevice);   // the cache is full (or the length is invalid)
+      } else {
+        bf16* kvc = const_cast<bf16*>(lptr<bf16>(a, layer, KK3_MLA_KV_CACHE)) + ((size_t)b * g.ctx + n) * g.kr;
+        bf16* pec = const_cast<bf16*>(lptr<bf16>(a, layer, KK3_MLA_PE_CACHE)) + ((size_t)b * g.ctx + n) * g.rd;
+        #pragma unroll 1
+        for (int e = threadIdx.x; e < g.kr; e += kThreads) kvc[e] = kvw[(size_t)b * g.kr + e];
+        #pragma unroll 1
+        for (int e = threadIdx.x; e < g.rd; e += kThreads) pec[e] = pew[(size_t)b * g.rd + e];
+      }
+      __syncthreads();
+    }
   }
 }
 
@@ -333,7 +350,7 @@ KK3_FN bool phase_argmax(const StepArgs& a, unsigned seq, int parity, int part) 
     }
     if (threadIdx.x == 0) {
       next[b] = (long long)(0xffffffffu - (unsigned)(best & 0xffffffffull));
-      len[b] = reset[b] ? 1 : (long long)g.ctx + 1;
+      len[b] = reset[b] ? 1 : (long long)(a.lengths ? mla_row_len(a, b) : g.ctx) + 1;
     }
     __syncthreads();
   }
@@ -565,10 +582,9 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
       KK3_PHASE_END();
       // split-K attention over [cache, new token] (kimi.py:274-280)
       if (KK3_RUN) {
-        const bool* reset = gptr<bool>(a, KK3_RESET);
         int total = 0;
         #pragma unroll 1
-        for (int b = 0; b < g.B; ++b) total += reset[b] ? 1 : g.mla_chunks;
+        for (int b = 0; b < g.B; ++b) total += mla_row_chunks(a, b);
         total *= g.mla_groups;
         #pragma unroll 1
         for (int it = blockIdx.x; it < total; it += gridDim.x) {
@@ -577,11 +593,11 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
           const int grp = it % g.mla_groups;
           int b = 0, rem = it / g.mla_groups;
           for (; b < g.B; ++b) {
-            const int n = reset[b] ? 1 : g.mla_chunks;
+            const int n = mla_row_chunks(a, b);
             if (rem < n) break;
             rem -= n;
           }
-          const int T = reset[b] ? 1 : g.ctx + 1;
+          const int T = mla_row_len(a, b) + 1;
           const int p0 = rem * g.mla_chunk_len;
           int p1 = p0 + g.mla_chunk_len;
           p1 = p1 < T ? p1 : T;

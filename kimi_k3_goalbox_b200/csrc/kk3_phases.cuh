@@ -566,7 +566,7 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
   src.pe = lptr<bf16>(a, layer, KK3_MLA_PE_CACHE) + (size_t)b * g.ctx * g.rd;
   src.kvw = gout<bf16>(a, KK3_OUT_KV_WRITE) + ((size_t)midx * g.B + b) * g.kr;
   src.pew = gout<bf16>(a, KK3_OUT_PE_WRITE) + ((size_t)midx * g.B + b) * g.rd;
-  src.ncache = reinterpret_cast<const bool*>(a.ptr[KK3_RESET])[b] ? 0 : g.ctx;
+  src.ncache = mla_row_len(a, b);
   src.pol = l2_evict_first_policy();
   src.kr = g.kr;
   src.rd = g.rd;
@@ -716,7 +716,7 @@ KK3_FN void mla_combine_row_item(const StepArgs& a, int layer, int b, int hh, fl
   const Geo& g = a.g;
   const int tid = threadIdx.x;
   const bool keep = !reinterpret_cast<const bool*>(a.ptr[KK3_RESET])[b];
-  const int nck = keep ? g.mla_chunks : 1;
+  const int nck = mla_row_chunks(a, b);
   const int stride = g.kr + 2;
   const float* base = a.s.mla_part + (((size_t)b * g.mla_chunks) * g.hr + hh) * stride;
   const size_t cstride = (size_t)g.hr * stride;
@@ -812,7 +812,7 @@ KK3_FN void mla_combine_item(const StepArgs& a, int layer, int hh, int r0, int n
   float* inv = lw + kCombRows * 64;                                            // [nr]
   // 1. chunk weights: every lane loads its chunks' (m, l); L is summed in chunk order by lane 0
   for (int r = warp; r < nr; r += kWarps) {
-    const int b = r0 + r, nck = reset[b] ? 1 : g.mla_chunks;
+    const int b = r0 + r, nck = mla_row_chunks(a, b);
     const float* base = a.s.mla_part + (((size_t)b * g.mla_chunks) * g.hr + hh) * stride;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
     if (lane < nck) {
@@ -851,7 +851,7 @@ KK3_FN void mla_combine_item(const StepArgs& a, int layer, int hh, int r0, int n
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       acc[r] = 0.0f;
-      nck[r] = r < nr ? (reset[r0 + r] ? 1 : g.mla_chunks) : 0;
+      nck[r] = r < nr ? mla_row_chunks(a, r0 + r) : 0;
       nmax = nck[r] > nmax ? nck[r] : nmax;
       src[r] = a.s.mla_part + (((size_t)(r0 + (r < nr ? r : 0)) * g.mla_chunks) * g.hr + hh) * stride + 2 + cc;
     }

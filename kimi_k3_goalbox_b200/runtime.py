@@ -110,6 +110,7 @@ def load_library() -> ctypes.CDLL:
         lib.kk3_ipc_handle.argtypes = [vp, vp]
         lib.kk3_open_peers.argtypes = [vp, vp]
         lib.kk3_step.argtypes = [vp, vp, i32, vp]
+        lib.kk3_step_append.argtypes = [vp, vp, i32, vp, vp]
         lib.kk3_debug_step.argtypes = [vp, vp, i32, vp, i32]
         lib.kk3_debug_phases.argtypes = [vp, vp, i32, vp, i32, i32]
         lib.kk3_status.argtypes = [vp]
@@ -303,6 +304,25 @@ class StepContext:
         self.bind_outputs(out)
         self.launch(stop_phase=stop_phase)
         return out
+
+    def step_append(self, values: dict, outputs: dict, lengths: torch.Tensor) -> dict:
+        """One step that continues every sequence in place (include/kk3.h kk3_step_append): row b attends its
+        first lengths[b] cached positions plus the new token, its new MLA entries are written into the cache
+        inputs at position lengths[b] (0 after a reset), and cache_length = lengths + 1. `lengths` is a device
+        int64 [B] tensor (the previous step's cache_length output works as is). The KDA state outputs may be the
+        stacked tensor whose per-layer views are the state inputs (an in-place update)."""
+        self.check()
+        if lengths.dtype != torch.int64 or lengths.device != torch.device("cuda", self.device) or \
+                tuple(lengths.shape) != (self.params["batch"],):
+            raise ValueError("lengths must be a device int64 tensor [batch] on the context's device")
+        self._bind_inputs(values)
+        self.bind_outputs(outputs)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        rc = self.lib.kk3_step_append(self.handle, self.table, self.nslots, ctypes.c_void_p(lengths.data_ptr()),
+                                      ctypes.c_void_p(stream))
+        if rc != 0:
+            raise KK3Error(rc, "kk3_step_append")
+        return outputs
 
     def phase_count(self) -> int:
         return self.lib.kk3_phase_count(self.handle)

@@ -67,7 +67,11 @@ def main() -> int:
             torch.cuda.synchronize()
             run.ctx.check()
             expected = ko.reference(case, values, serial=False, tp_rank=rank, group=group)
-            details = ko.compare(case, values, expected, first, serial=False, tp_rank=rank, group=group)
+            try:
+                details = ko.compare(case, values, expected, first, serial=False, tp_rank=rank, group=group)
+            except AssertionError as exc:
+                print(f"rank {rank} FAIL: seed {args.seed}: {exc}", flush=True)
+                raise
             for key, t in first.items():
                 assert torch.equal(t, second[key]), f"rank {rank}: second step differs in {key}"
             run.close()
