@@ -590,6 +590,11 @@ def run_b200(args, n: int, rank: int, local: int) -> dict | None:
         if n == 8 and args.case is None:
             extras["north_star_tp8"] = [measure_case(args, plain_case(cid), n, rank, local, parity=not args.no_parity,
                                                      seed=fresh_seed(args, n)) for cid in NORTH_STAR]
+        elif args.north_star_layers and n > 1 and args.case is None:
+            # validation of the north-star leg on fewer GPUs: the same cases at TP = N with fewer layers
+            extras["north_star_reduced"] = [
+                measure_case(args, cases.variant(plain_case(cid), tp=n, layers=args.north_star_layers), n, rank, local,
+                             parity=not args.no_parity, seed=fresh_seed(args, n)) for cid in NORTH_STAR]
         if n == 1 and args.case is None:
             extras["deep_stack"] = deep_stack(args, local)
 
@@ -726,6 +731,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-parity", action="store_true", help="skip the checker leg")
     ap.add_argument("--no-extras", action="store_true", help="skip the north-star (N=8) and deep-stack (N=1) keys")
     ap.add_argument("--no-nccl", action="store_true", help="N>1: skip the plain-NCCL comparison variant")
+    ap.add_argument("--north-star-layers", type=int, default=0,
+                    help="N in 2..7: also run the north-star cases at TP = N with this many layers (validation)")
     args = ap.parse_args(argv)
     n = args.gpus
     world = int(os.environ.get("WORLD_SIZE", "1"))

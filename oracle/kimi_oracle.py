@@ -414,6 +414,7 @@ def _moe(st, layer, x):
     p, v, pre, act = st.p, st.values, f"l{layer}_", st.act
     B = p["batch"]
     scores = (x.float() @ v[pre + "router"].float().T).sigmoid()
+    st.rec(pre + "scores", scores)
     biased = scores + v[pre + "router_bias"].float()
     top = biased.topk(p["topk"], -1).indices
     if st.routes is not None:
