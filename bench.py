@@ -382,10 +382,13 @@ def time_steps(ctx, stream, steps: int, warmup: int, n: int, clocks: ClockSample
 
 
 def phase_breakdown(ctx, stream, n: int) -> dict:
-    """One more step, then its in-step phase times (CTA 0's %globaltimer stamps after every grid barrier) on
-    every rank: per phase the slowest rank, summed by phase name over the layers (largest first). Untimed."""
+    """In-step phase times (CTA 0's %globaltimer stamps after every grid barrier) of the last of three
+    back-to-back steps after a barrier, so that the ranks' launch skew does not land in the first exchange
+    wait: per phase the slowest rank, summed by phase name over the layers (largest first). Untimed."""
     from kimi_k3_goalbox_b200 import phase_profile
-    ctx.launch(stream.cuda_stream)
+    barrier(n)
+    for _ in range(3):
+        ctx.launch(stream.cuda_stream)
     torch.cuda.synchronize()
     ctx.check()
     rows = phase_profile.step_phase_times(ctx)
@@ -395,7 +398,8 @@ def phase_breakdown(ctx, stream, n: int) -> dict:
         k = max(range(n), key=lambda q: per_rank[q][i]["us"])
         worst.append(per_rank[k][i])
     out = phase_profile.summarize(worst)
-    out["method"] = "in-step %globaltimer stamps of one step; per phase the slowest rank; work = until the last CTA arrived"
+    out["method"] = ("in-step %globaltimer stamps of the last of 3 back-to-back steps; per phase the slowest rank; "
+                     "work = until the last CTA arrived")
     return out
 
 
