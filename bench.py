@@ -34,7 +34,6 @@ import secrets
 import statistics
 import subprocess
 import sys
-import threading
 import time
 from datetime import timedelta
 from pathlib import Path
@@ -131,11 +130,43 @@ def traffic_for(case_id: str):
 # clocks during the timed region
 
 
+# The sampler loop, run as its own process: it polls NVML every ~1 ms and prints one line per sample
+# (time, SM MHz, max SM MHz, power W, clock-event reason bits) until its stdin closes. A process, not a thread:
+# in torchrun ranks a polling thread starved (no sample in a whole run), and a process shares nothing with the
+# rank's interpreter.
+_POLL_SRC = r"""
+import sys, time, select
+import pynvml
+pynvml.nvmlInit()
+bus = sys.argv[1]
+try:
+    h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+except Exception:
+    h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[2]))
+try:
+    mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+except Exception:
+    mx = float("nan")
+print("ready", flush=True)
+while True:
+    r, _, _ = select.select([sys.stdin], [], [], 0.001)
+    if r:
+        break
+    try:
+        sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+        rs = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+        pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+        print(f"{time.time():.6f},{sm},{mx},{pw},{rs}", flush=True)
+    except Exception as exc:
+        print(f"error,{type(exc).__name__}: {exc}", flush=True)
+"""
+
+
 class ClockSampler:
     """SM clock, max clock, power and clock-event (throttle) reasons of this rank's GPU, sampled during the
-    timed region. NVML is polled from a thread every ~1 ms (the steps are milliseconds long, so an
-    nvidia-smi loop at its 50 ms floor would see no sample inside a 20-step window); without NVML it falls
-    back to `nvidia-smi -lms 50`. Only samples inside [mark_start, mark_end] enter the summary."""
+    timed region by a separate process that polls NVML every ~1 ms (the steps are milliseconds long, so an
+    nvidia-smi loop at its 50 ms floor would see no sample inside a 20-step window); without NVML it falls back
+    to `nvidia-smi -lms 50`. Only samples inside [mark_start, mark_end] enter the summary."""
 
     # nvmlClocksEventReasons bits (nvml.h)
     REASONS = {0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
@@ -146,49 +177,32 @@ class ClockSampler:
         self.samples: list[tuple[float, float, float, float, int]] = []   # (t, sm, max, power_w, reasons)
         self.t0 = self.t1 = None
         self.source = None
-        self._stop = threading.Event()
-        self._thread = None
         self._proc = None
+        self._smi = False
         self.error = None
-
-    def _nvml_handle(self):
-        import pynvml
-        pynvml.nvmlInit()
-        try:
-            prop = torch.cuda.get_device_properties(self.device_index)
-            bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
-            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
-        except Exception:
-            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device_index)
-
-    def _poll(self, pynvml, handle):
-        try:
-            mx = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
-        except Exception as exc:   # keep polling the current clock; record why the maximum is missing
-            self.error = f"max clock: {type(exc).__name__}: {exc}"
-            mx = float("nan")
-        while not self._stop.is_set():
-            try:
-                sm = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
-                reasons = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
-                power = pynvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
-                self.samples.append((time.time(), sm, mx, power, reasons))
-            except Exception as exc:
-                self.error = f"{type(exc).__name__}: {exc}"
-            time.sleep(0.001)
 
     def __enter__(self):
         try:
-            pynvml, handle = self._nvml_handle()
-            self._thread = threading.Thread(target=self._poll, args=(pynvml, handle), daemon=True)
-            self._thread.start()
-            self.source = "nvml (1 ms poll)"
-        except Exception:
+            import pynvml  # noqa: F401  (the poller needs it)
+            prop = torch.cuda.get_device_properties(self.device_index)
+            bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+            self._proc = subprocess.Popen([sys.executable, "-c", _POLL_SRC, bus, str(self.device_index)],
+                                          stdin=subprocess.PIPE, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                          text=True)
+            first = self._proc.stdout.readline().strip()   # NVML up before the timed region starts
+            if first != "ready":
+                raise RuntimeError(f"poller did not start: {first!r}")
+            self.source = "nvml process (1 ms poll)"
+        except Exception as exc:
+            self.error = f"nvml poller: {type(exc).__name__}: {exc}"
+            if self._proc is not None:
+                self._proc.kill()
             try:
                 fields = "timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active"
                 self._proc = subprocess.Popen(
                     ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={fields}", "--format=csv,noheader,nounits",
                      "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self._smi = True
                 self.source = "nvidia-smi (50 ms)"
             except Exception:
                 self._proc = None
@@ -201,25 +215,32 @@ class ClockSampler:
         self.t1 = time.time()
 
     def __exit__(self, *exc):
-        if self._thread is not None:
-            self._stop.set()
-            self._thread.join(timeout=5)
-        if self._proc is not None:
-            from datetime import datetime
-            time.sleep(0.1)
-            self._proc.terminate()
+        if self._proc is None:
+            return
+        time.sleep(0.01)
+        out = ""
+        try:
+            if self._smi:
+                time.sleep(0.1)
+                self._proc.terminate()
+            else:
+                self._proc.stdin.close()   # the poller's stop signal
+            out, _ = self._proc.communicate(timeout=10)
+        except Exception:
+            self._proc.kill()
+        from datetime import datetime
+        for line in out.splitlines():
+            parts = [x.strip() for x in line.split(",")]
             try:
-                out, _ = self._proc.communicate(timeout=5)
-            except Exception:
-                self._proc.kill()
-                out = ""
-            for line in out.splitlines():
-                parts = [x.strip() for x in line.split(",")]
-                try:
-                    ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
-                    self.samples.append((ts, float(parts[1]), float(parts[2]), float(parts[3]), int(parts[4], 16)))
-                except Exception:
+                if parts[0] == "error":
+                    self.error = ",".join(parts[1:])[:200]
                     continue
+                ts = (datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp() if self._smi
+                      else float(parts[0]))
+                rs = int(parts[4], 16) if self._smi else int(parts[4])
+                self.samples.append((ts, float(parts[1]), float(parts[2]), float(parts[3]), rs))
+            except Exception:
+                continue
 
     def summary(self) -> dict:
         inside = [s for s in self.samples if self.t0 is not None and self.t1 is not None and self.t0 <= s[0] <= self.t1]
