@@ -34,6 +34,7 @@ import secrets
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from datetime import timedelta
 from pathlib import Path
@@ -138,27 +139,28 @@ _POLL_SRC = r"""
 import sys, time, select
 import pynvml
 pynvml.nvmlInit()
-bus = sys.argv[1]
+bus, index, path = sys.argv[1], int(sys.argv[2]), sys.argv[3]
 try:
     h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
 except Exception:
-    h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[2]))
+    h = pynvml.nvmlDeviceGetHandleByIndex(index)
 try:
     mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
 except Exception:
     mx = float("nan")
-print("ready", flush=True)
-while True:
-    r, _, _ = select.select([sys.stdin], [], [], 0.001)
-    if r:
-        break
-    try:
-        sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
-        rs = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
-        pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
-        print(f"{time.time():.6f},{sm},{mx},{pw},{rs}", flush=True)
-    except Exception as exc:
-        print(f"error,{type(exc).__name__}: {exc}", flush=True)
+with open(path, "w") as out:
+    print("ready", flush=True)
+    while True:
+        r, _, _ = select.select([sys.stdin], [], [], 0.001)
+        if r:
+            break
+        try:
+            sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+            rs = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+            pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+            out.write(f"{time.time():.6f},{sm},{mx},{pw},{rs}\n")
+        except Exception as exc:
+            out.write(f"error,{type(exc).__name__}: {exc}\n")
 """
 
 
@@ -166,27 +168,35 @@ class ClockSampler:
     """SM clock, max clock, power and clock-event (throttle) reasons of this rank's GPU, sampled during the
     timed region by a separate process that polls NVML every ~1 ms (the steps are milliseconds long, so an
     nvidia-smi loop at its 50 ms floor would see no sample inside a 20-step window); without NVML it falls back
-    to `nvidia-smi -lms 50`. Only samples inside [mark_start, mark_end] enter the summary."""
+    to `nvidia-smi -lms 50`. The poller writes its samples to a file (a pipe that nobody reads while the steps
+    run would fill up and stall it) and stops when its standard input closes. Only samples inside
+    [mark_start, mark_end] enter the summary."""
 
     # nvmlClocksEventReasons bits (nvml.h)
     REASONS = {0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
                0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, bus: str | None = None):
         self.device_index = device_index
+        self.bus = bus   # PCI bus id of the GPU (default: from torch's device properties)
         self.samples: list[tuple[float, float, float, float, int]] = []   # (t, sm, max, power_w, reasons)
         self.t0 = self.t1 = None
         self.source = None
         self._proc = None
         self._smi = False
+        self._path = None
         self.error = None
 
     def __enter__(self):
         try:
             import pynvml  # noqa: F401  (the poller needs it)
-            prop = torch.cuda.get_device_properties(self.device_index)
-            bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
-            self._proc = subprocess.Popen([sys.executable, "-c", _POLL_SRC, bus, str(self.device_index)],
+            bus = self.bus
+            if bus is None:
+                prop = torch.cuda.get_device_properties(self.device_index)
+                bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+            fd, self._path = tempfile.mkstemp(prefix="kk3_clocks_", suffix=".csv")
+            os.close(fd)
+            self._proc = subprocess.Popen([sys.executable, "-c", _POLL_SRC, bus, str(self.device_index), self._path],
                                           stdin=subprocess.PIPE, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                                           text=True)
             first = self._proc.stdout.readline().strip()   # NVML up before the timed region starts
@@ -223,11 +233,17 @@ class ClockSampler:
             if self._smi:
                 time.sleep(0.1)
                 self._proc.terminate()
-            else:
-                self._proc.stdin.close()   # the poller's stop signal
-            out, _ = self._proc.communicate(timeout=10)
-        except Exception:
+            out, _ = self._proc.communicate(timeout=10)   # closes the poller's standard input: its stop signal
+        except Exception as exc:
+            self.error = f"clock sampler stop: {type(exc).__name__}: {exc}"
             self._proc.kill()
+            self._proc.communicate()
+        if self._path is not None:
+            try:
+                with open(self._path) as f:
+                    out = f.read()
+            finally:
+                os.unlink(self._path)
         from datetime import datetime
         for line in out.splitlines():
             parts = [x.strip() for x in line.split(",")]
@@ -430,12 +446,16 @@ def host_comm_leg(args, ctx, stream, n: int) -> dict:
     instead of the in-kernel one-shot peer exchange. Same inputs and outputs as the timed fused steps; one step
     is compared with a fused step first."""
     from kimi_k3_goalbox_b200 import runtime
+    from kimi_k3_goalbox_b200 import phase_profile
     group = dist.group.WORLD
     fused = ctx.allocate_outputs()
     ctx.bind_outputs(fused)
-    ctx.launch(stream.cuda_stream)
+    barrier(n)
+    for _ in range(3):
+        ctx.launch(stream.cuda_stream)
     torch.cuda.synchronize()
     ctx.check()
+    fused_rows = phase_profile.step_phase_times(ctx)
     host = ctx.allocate_outputs()
     ctx.bind_outputs(host)
     ctx.set_comm_mode(runtime.COMM_HOST)
@@ -457,16 +477,39 @@ def host_comm_leg(args, ctx, stream, n: int) -> dict:
         torch.cuda.synchronize()
         barrier(n)
         ctx.check()
+        host_rows = host_phase_times(ctx, runtime)
     finally:
         ctx.set_comm_mode(runtime.COMM_PEER)
     ms = max_over_ranks(t0.elapsed_time(t1), n) / args.steps
+    # the phases whose epilogue stores the partial into every rank's slot (fused) or only into its own (host):
+    # their in-step time with each transport (slowest rank), the store cost of the peer exchange
+    compare = {}
+    for name in ("o_proj", "dense_down", "experts_down", "embed"):
+        f = [r["us"] for r in fused_rows if r["name"] == name]
+        h = [r["us"] for r in host_rows if r["name"] == name and r["us"] is not None]
+        if f and h:
+            compare[name] = {"fused_us": round(sum(f), 1), "host_us": round(sum(h), 1), "count": len(f)}
+    per_rank = gather(compare, n)
+    for name in compare:
+        for k in ("fused_us", "host_us"):
+            compare[name][k] = max(pr[name][k] for pr in per_rank)
     flags = torch.tensor([diff, float(not same_tokens), float(not same_routes)], device="cuda", dtype=torch.float64)
     dist.all_reduce(flags, op=dist.ReduceOp.MAX)
     return {"us": round(ms * 1000.0, 2), "launches_per_step": counts,
             "transport": "NCCL all-reduce (FP32) per partial + all-gather of argmax keys, between phase-range launches",
             "vs_fused": {"max_abs_logit_diff": float(flags[0]), "next_token_equal": not bool(flags[1]),
                          "expert_ids_equal": not bool(flags[2])},
+            "exchange_store_phases": compare,
             "note": "same kernel; exchanges by NCCL on the host instead of in-kernel NVLink peer stores"}
+
+
+def host_phase_times(ctx, runtime) -> list[dict]:
+    """In-step phase times of the last host-transport step: the phases inside a launch range (a range's first
+    phase is left out, its stamp difference spans the NCCL collective before it)."""
+    names = runtime.host_comm_program(ctx.params)
+    ts = ctx.debug_buffer(16, torch.int64, (len(names) + 1,)).cpu().tolist()
+    starts = {start for start, _, _ in runtime.host_comm_segments(ctx.params, ctx.case["tp"])}
+    return [{"name": nm, "us": None if i in starts else (ts[i + 1] - ts[i]) / 1e3} for i, nm in enumerate(names)]
 
 
 def build_runner(case: dict, n: int, rank: int, device):

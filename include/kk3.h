@@ -202,8 +202,10 @@ int kk3_debug_copy(kk3_ctx* ctx, int id, void* dst, size_t bytes);
 size_t kk3_exchange_bytes(kk3_ctx* ctx);
 
 /* Byte offsets inside this rank's exchange buffer (8 values): the flag array [B][tp] u32, the two parity data
- * regions, the bytes of one region, and inside a region the sub-regions att bf16 [tp][B][hidden],
- * exp f32 [tp][B][latent_hidden], shd bf16 [tp][B][hidden], key u64 [tp][B]. */
+ * regions, the bytes of one region, and inside a region the sub-regions att bf16 [tp][hidden/16][bp][16],
+ * exp f32 [tp][B][latent_hidden], shd bf16 [tp][hidden/16][bp][16], key u64 [tp][B]. bp is the batch padded to
+ * 8, 16, 32 or 64 (the kernel's n-tile width); channel ch of batch row b is element
+ * ((ch / 16) * bp + b) * 16 + ch % 16 of a source's slot, so that one 16-channel tile of a source is contiguous. */
 int kk3_exchange_layout(kk3_ctx* ctx, long long* offsets);
 
 /* Exchange transport of the tensor-parallel reductions (kimi.py:343-347, :218-227).
@@ -215,6 +217,15 @@ int kk3_exchange_layout(kk3_ctx* ctx, long long* offsets);
 #define KK3_COMM_PEER 0
 #define KK3_COMM_HOST 1
 int kk3_set_comm_mode(kk3_ctx* ctx, int mode);
+
+/* The engine of the BF16 projections. KK3_GEMV_AUTO (the default): tcgen05.mma kind::f16 on the tensor cores
+ * (M = 128 weight rows, N = the batch padded to 32 or 64, FP32 accumulators in TMEM) for batches above 16, the
+ * warp-level mma.sync engine for batches up to 16. KK3_GEMV_MMA: mma.sync for every batch (the comparison
+ * engine). Both sum in FP32; results may differ in the last bit of a rounded value. No counterpart in the
+ * reference. Takes effect at the next step. */
+#define KK3_GEMV_AUTO 0
+#define KK3_GEMV_MMA 1
+int kk3_set_gemv_engine(kk3_ctx* ctx, int engine);
 
 /* Single-process testing aid: use an existing device allocation of kk3_exchange_bytes() bytes as rank r's
  * exchange buffer instead of an IPC mapping (no counterpart in the reference). */

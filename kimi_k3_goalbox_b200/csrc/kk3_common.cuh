@@ -52,6 +52,7 @@ struct Geo {
   int cnt_bank;       // counters per stream-K counter bank
   int mla_mt;         // 16-row head tiles per head group of the MLA attention (<= 4)
   int mla_groups;     // head groups: ceil(ceil(hr / 16) / mla_mt)
+  int bp;             // batch padded to the step's n-tile width (8 * NT): the bf16 exchange regions' batch stride
 };
 
 // scratch buffers (device pointers owned by the context)
@@ -110,6 +111,8 @@ struct Comm {
   long long att_off, exp_off, shd_off, key_off;
 };
 
+constexpr int kGemvAuto = 0, kGemvMma = 1;
+
 struct StepArgs {
   Geo g;
   Scratch s;
@@ -121,6 +124,8 @@ struct StepArgs {
   int comm_mode;        // kCommPeer: one-shot peer stores and flags inside the kernel; kCommHost: each rank
                         // writes only its own slot and the host reduces the slots between launches (NCCL)
   const long long* lengths;   // append mode (kk3_step_append): cached positions of each row, [B]; null otherwise
+  int gemv_engine;      // kGemvAuto: tcgen05 projections for batches above 16, mma.sync below; kGemvMma: mma.sync
+                        // for every batch (the comparison engine)
   int nptr;
   const void* ptr[kMaxPtrs];
 };

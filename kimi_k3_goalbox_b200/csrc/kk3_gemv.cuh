@@ -109,6 +109,12 @@ KK3_DEV void mma_step_bf16(const uint4* __restrict__ slot, const bf16* __restric
   }
 }
 
+// two floats as a bf16 pair (round to nearest even), lo in the low half (the lower address)
+KK3_DEV unsigned pack_bf2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const unsigned*>(&v);
+}
+
 KK3_DEV float situ_f(float g, float u) {
   return 4.0f * tanhf(g / 4.0f) * sigmoidf_(g) * (25.0f * tanhf(u / 25.0f));
 }
@@ -123,6 +129,14 @@ KK3_DEV unsigned long long argmax_key(float v, unsigned idx) {
 KK3_DEV unsigned char* xregion(const StepArgs& a, int dst, int parity) {
   return a.comm.base[dst] + a.comm.data_off[parity];
 }
+// Element index of (source rank, batch row b, channel ch) in a bf16 exchange region (att, shd) of `width`
+// channels: [src][width / 16][bp][16]. One 16-row GEMV tile of one source is one contiguous block of bp * 32
+// bytes, so the exchange epilogue writes whole 128-byte lines over NVLink; a reader's 8 consecutive channels of
+// one row are one 16-byte piece.
+KK3_DEV size_t xch_index(const Geo& g, int src, int b, int ch, int width) {
+  return (((size_t)src * (width >> 4) + (ch >> 4)) * g.bp + b) * 16 + (ch & 15);
+}
+
 // ranks whose regions receive this rank's partial: every rank (peer stores), or only this rank's own region
 // when the host reduces the slots with NCCL between launches
 KK3_DEV int xdst_lo(const StepArgs& a) { return a.comm_mode == kCommHost ? a.g.rank : 0; }
@@ -197,6 +211,34 @@ KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const 
     if (lane == 0) atomicExch(cnt, 0);
     return;
   }
+  if (j.epi == EPI_EXCHANGE) {
+    // bf16(acc) into every rank's region at this rank's slot, layout xch_index (rows = ldo channels, a
+    // multiple of 16; padding columns carry the zero products of the zero activation columns). Two shuffles
+    // regroup the MMA fragment so that each lane holds 8 contiguous bytes of the n-tile's 256-byte block
+    // (column-major, 16 rows per column): one 8-byte store per lane and destination covers the block.
+    const int col_l = 2 * c + (r & 1);                     // this lane's column within the n-tile
+    const int rw = r >> 1;                                 // row pair R = 2 rw (and R + 8)
+    const int woff = col_l * 8 + ((rw & 1) ? 3 + rw : rw); // 4-byte word of the lane's 8-byte piece
+    const size_t blk = ((size_t)a.g.rank * (j.ldo >> 4) + tile) * a.g.bp * 16;   // elements
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const float* v = acc[0][nt];
+      const bool even = (r & 1) == 0;
+      // step 1 (partner r ^ 1): even lanes gather column 2c, odd lanes column 2c + 1, rows R, R + 1 (+ 8)
+      const float s0 = even ? v[1] : v[0], s1 = even ? v[3] : v[2];
+      const float t0 = __shfl_xor_sync(0xffffffffu, s0, 4), t1 = __shfl_xor_sync(0xffffffffu, s1, 4);
+      const unsigned w0 = even ? pack_bf2(v[0], t0) : pack_bf2(t0, v[1]);   // rows R, R + 1
+      const unsigned w1 = even ? pack_bf2(v[2], t1) : pack_bf2(t1, v[3]);   // rows R + 8, R + 9
+      // step 2 (partner rw ^ 1): rw even keeps words (rw, rw + 1), rw odd keeps (rw + 3, rw + 4)
+      const unsigned send = (rw & 1) ? w0 : w1;
+      const unsigned got = __shfl_xor_sync(0xffffffffu, send, 8);
+      const uint2 piece = (rw & 1) ? make_uint2(got, w1) : make_uint2(w0, got);
+      const size_t e = blk + (size_t)nt * 128 + (size_t)woff * 2;
+      for (int dst = xdst_lo(a); dst < xdst_hi(a); ++dst)
+        *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(xregion(a, dst, parity) + j.aux_off) + e) = piece;
+    }
+    return;
+  }
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -229,14 +271,6 @@ KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const 
           const bf16* shared = reinterpret_cast<const bf16*>(j.aux);
           const float out = round_bf(round_bf(v) + bf2f(shared[o]));
           prefix[o] = f2bf(bf2f(prefix[o]) + out);
-          break;
-        }
-        case EPI_EXCHANGE: {
-          // layout [src][col][ldo], src = this rank; written into every rank's region
-          const bf16 b = f2bf(v);
-          const size_t off = (size_t)a.g.rank * a.g.B * j.ldo + o;
-          for (int dst = xdst_lo(a); dst < xdst_hi(a); ++dst)
-            reinterpret_cast<bf16*>(xregion(a, dst, parity) + j.aux_off)[off] = b;
           break;
         }
         default:
@@ -493,7 +527,10 @@ KK3_FN void prefetch_jobs(const GemvJob* jobs, int njobs) {
   const long long pieces = (total + kPrefetchPiece - 1) / kPrefetchPiece;
   const long long nthreads = (long long)gridDim.x * 32;
   if (threadIdx.x >= 32) return;
-  for (long long piece = (long long)blockIdx.x * 32 + threadIdx.x; piece < pieces; piece += nthreads) {
+  // lane-major over the CTAs (piece = lane * G + CTA), so every CTA issues pieces / G of them: each bulk
+  // prefetch holds the issuing SM's copy engine for a while, and CTA-major pieces made the first few CTAs of
+  // the grid (32 pieces each) arrive late at the phase's barrier
+  for (long long piece = (long long)threadIdx.x * gridDim.x + blockIdx.x; piece < pieces; piece += nthreads) {
     long long off = piece * kPrefetchPiece;
     for (int i = 0; i < njobs; ++i) {
       for (int m = 0; m < (jobs[i].w2 ? 2 : 1); ++m) {

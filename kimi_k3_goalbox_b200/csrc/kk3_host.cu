@@ -61,6 +61,7 @@ struct kk3_ctx {
   int failed = 0;
   int peers_open = 0;
   int comm_mode = kCommPeer;
+  int gemv_engine = kGemvAuto;
   StepArgs* args = nullptr;
   size_t buf_bytes[KK3_BUF_COUNT] = {};
   void* buf_ptr[KK3_BUF_COUNT] = {};
@@ -174,6 +175,7 @@ static void plan_step(const kk3_config* cfg, int sms, unsigned char* base, bool 
   g.timeout_ns = cfg->timeout_ns > 0 ? cfg->timeout_ns : 10000000000ll;
   const int nt = g.B <= 8 ? 1 : (g.B <= 16 ? 2 : (g.B <= 32 ? 4 : 8));
   pl->nt = nt;
+  g.bp = 8 * nt;
   plan_mla(g, sms);
   const long long gw = (long long)sms * kWarps;
   g.fix_bank = 2ll * gw * (2 * nt * 128);
@@ -199,18 +201,19 @@ static void plan_step(const kk3_config* cfg, int sms, unsigned char* base, bool 
   // situ pairs: tiles of the larger of the dense and shared-expert intermediates, 4 * NT floats per lane
   const size_t situ_tiles = (size_t)((g.dinter > g.sinter ? g.dinter : g.sinter) + 15) / 16 + 1;
   const size_t situ_floats = 2 * situ_tiles * 32 * 4 * (size_t)nt;
-  // exchange buffer: flags [B][tp] u32, then two parity regions {att bf16 [tp][B][h], exp f32 [tp][B][lh],
-  // shd bf16 [tp][B][h], key u64 [tp][B]}
+  // exchange buffer: flags [B][tp] u32, then two parity regions {att bf16 [tp][h/16][bp][16], exp f32
+  // [tp][B][lh], shd bf16 [tp][h/16][bp][16], key u64 [tp][B]}; bp = 8 * nt, so that one 16-row GEMV tile of a
+  // source is one contiguous block of the bf16 regions
   Comm& c = pl->comm;
   memset(&c, 0, sizeof(c));
   const size_t flag_bytes = align_up(B * tp * 4, 256);
   c.flag_off = 0;
   c.att_off = 0;
-  size_t r = align_up(tp * B * g.h * 2, 256);
+  size_t r = align_up(tp * (size_t)g.bp * g.h * 2, 256);
   c.exp_off = r;
   r += align_up(tp * B * g.lh * 4, 256);
   c.shd_off = r;
-  r += align_up(tp * B * g.h * 2, 256);
+  r += align_up(tp * (size_t)g.bp * g.h * 2, 256);
   c.key_off = r;
   r += align_up(tp * B * 8, 256);
   c.region_bytes = r;
@@ -404,6 +407,12 @@ extern "C" int kk3_set_comm_mode(kk3_ctx* x, int mode) {
   return KK3_OK;
 }
 
+extern "C" int kk3_set_gemv_engine(kk3_ctx* x, int engine) {
+  if (!x || (engine != KK3_GEMV_AUTO && engine != KK3_GEMV_MMA)) return KK3_ERR_ARG;
+  x->gemv_engine = engine == KK3_GEMV_MMA ? kGemvMma : kGemvAuto;
+  return KK3_OK;
+}
+
 // Every tensor except the token ids and reset flags is read with 16-byte vector or cp.async loads, so a
 // misaligned pointer would fault on the device: reject it here instead.
 static bool table_aligned(const void* const* table, int n) {
@@ -470,6 +479,7 @@ static int launch(kk3_ctx* x, const void* const* table, int n, void* stream, int
   a->start_phase = start_phase < 0 ? 0 : start_phase;
   a->trace = x->trace;
   a->comm_mode = x->comm_mode;
+  a->gemv_engine = x->gemv_engine;
   a->lengths = lengths;
   a->nptr = n;
   memcpy(a->ptr, table, sizeof(void*) * n);
@@ -675,6 +685,7 @@ extern "C" int kk3_step_noalloc(const kk3_config* cfg, const void* const* table,
   a.start_phase = 0;
   a.trace = 0;
   a.comm_mode = kCommPeer;
+  a.gemv_engine = kGemvAuto;
   a.lengths = nullptr;
   a.nptr = table_size;
   memcpy(a.ptr, table, sizeof(void*) * table_size);

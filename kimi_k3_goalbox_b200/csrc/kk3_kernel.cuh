@@ -10,6 +10,7 @@
 #pragma once
 
 #include "kk3_phases.cuh"
+#include "kk3_tc_gemv.cuh"
 
 namespace kk3 {
 
@@ -34,12 +35,14 @@ KK3_FN void phase_embed(const StepArgs& a, unsigned seq, int parity, float* fsm)
       #pragma unroll 1
       for (int e = threadIdx.x; e < g.h; e += kThreads) a.s.prefix[(size_t)b * g.h + e] = mine ? row[e] : zero;
     } else {
-      const size_t off = ((size_t)g.rank * g.B + b) * g.h;
+      // 16-byte pieces of the row into every rank's att region (layout xch_index)
       #pragma unroll 1
-      for (int dst = xdst_lo(a); dst < xdst_hi(a); ++dst) {
-        bf16* reg = reinterpret_cast<bf16*>(a.comm.base[dst] + a.comm.data_off[parity] + a.comm.att_off);
+      for (int c = threadIdx.x; c < g.h / 8; c += kThreads) {
+        const uint4 v = mine ? *reinterpret_cast<const uint4*>(row + (size_t)c * 8) : make_uint4(0, 0, 0, 0);
+        const size_t e = xch_index(g, g.rank, b, c * 8, g.h);
         #pragma unroll 1
-        for (int e = threadIdx.x; e < g.h; e += kThreads) reg[off + e] = mine ? row[e] : zero;
+        for (int dst = xdst_lo(a); dst < xdst_hi(a); ++dst)
+          *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(a.comm.base[dst] + a.comm.data_off[parity] + a.comm.att_off) + e) = v;
       }
       xch_signal_row(a, b, seq);
     }
@@ -349,8 +352,11 @@ KK3_FN bool phase_argmax(const StepArgs& a, unsigned seq, int parity, int part) 
       __syncthreads();
     }
     if (threadIdx.x == 0) {
-      next[b] = (long long)(0xffffffffu - (unsigned)(best & 0xffffffffull));
-      len[b] = reset[b] ? 1 : (long long)(a.lengths ? mla_row_len(a, b) : g.ctx) + 1;
+      // an error raised earlier in the step (a full append cache, for one) is visible here through the grid
+      // barriers since: the step's outputs are then marked invalid instead of written
+      const bool bad = failed(a);
+      next[b] = bad ? -1 : (long long)(0xffffffffu - (unsigned)(best & 0xffffffffull));
+      len[b] = bad ? 0 : (reset[b] ? 1 : (long long)(a.lengths ? mla_row_len(a, b) : g.ctx) + 1);
     }
     __syncthreads();
   }
@@ -380,6 +386,18 @@ KK3_DEV void prefetch_row_inputs(const StepArgs& a, int which, int l) {
                      gptr<bf16>(a, which ? KK3_MLP_RES_PROJ : KK3_ATTENTION_RES_PROJ) + o,
                      gptr<bf16>(a, which ? KK3_LN2 : KK3_LN1) + o, g.h * 2);
   }
+}
+
+// One BF16 GEMV pass over all CTAs: the tcgen05 engine for the batch classes above 16 rows (NT >= 4), the
+// warp-level mma.sync engine below (and for every batch when the context asks for it). False when a bounded
+// wait of the tcgen05 engine gave up.
+template <int NT>
+KK3_DEV bool gemv_pass(const StepArgs& a, const GemvJob* jobs, int njobs, int parity, int bank = 0, int ph = -1) {
+  if constexpr (NT >= 4) {
+    if (a.gemv_engine == kGemvAuto) return run_gemv_tc<NT>(a, jobs, njobs, parity, bank);
+  }
+  run_gemv<NT, 1>(a, jobs, njobs, 0, gridDim.x, parity, bank, ph);
+  return true;
 }
 
 // ---- job lists of the GEMV phases (built identically by every thread) ---------------------------------
@@ -517,7 +535,8 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
     if (KK3_RUN && !grid_sync(a, phase)) KK3_FAIL();                                         \
     ++phase;                                                                                 \
     trace_progress(a, 0, phase);                                                             \
-    if (blockIdx.x == 0 && threadIdx.x == 0 && phase <= kMaxPhases) a.s.phase_ts[phase] = globaltimer(); \
+    if (blockIdx.x == 0 && threadIdx.x == 0 && phase <= kMaxPhases && phase > a.start_phase)             \
+      a.s.phase_ts[phase] = globaltimer(); /* stamped only after phases that ran: launch ranges keep theirs */ \
     if (phase == a.stop_phase) return;                                                       \
   } while (0)
 #define KK3_BUILD(stmt)   \
@@ -549,7 +568,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
     KK3_PHASE_END();
     if (KK3_RUN) {
       KK3_BUILD(sjn = attn_proj_jobs(a, l, mla, sj));
-      run_gemv<NT, 1>(a, sj, sjn, 0, gridDim.x, 0, 0, phase);
+      if (!gemv_pass<NT>(a, sj, sjn, 0, 0, phase)) KK3_FAIL();
     }
     KK3_PHASE_END();
     if (!mla) {
@@ -572,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
                    EPI_STORE_BF16, a.s.mla_q, g.hr * (g.nr + g.rd));
           prepare_jobs(sj, 1);
         });
-        run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, 0);
+        if (!gemv_pass<NT>(a, sj, 1, 0)) KK3_FAIL();
       }
       KK3_PHASE_END();
       // absorbed query (kimi.py:271-272)
@@ -644,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
     if (KK3_RUN) {
       KK3_BUILD(o_job(a, l, sj[0]));
       prefetch_row_inputs(a, 1, l);
-      run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, xi & 1);
+      if (!gemv_pass<NT>(a, sj, 1, xi & 1)) KK3_FAIL();
       if (g.tp > 1) __threadfence_system();
     }
     const unsigned x_att = xi++;
@@ -655,7 +674,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
       // dense FFN (kimi.py:304)
       if (KK3_RUN) {
         KK3_BUILD(sjn = mlp_in_jobs(a, l, sj));
-        run_gemv<NT, 1>(a, sj, sjn, 0, gridDim.x, 0);
+        if (!gemv_pass<NT>(a, sj, sjn, 0)) KK3_FAIL();
       }
       KK3_PHASE_END();
       if (KK3_RUN) {
@@ -666,7 +685,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
           prepare_jobs(sj, 1);
         });
         prefetch_row_inputs(a, 0, l + 1);
-        run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, xi & 1);
+        if (!gemv_pass<NT>(a, sj, 1, xi & 1)) KK3_FAIL();
         if (g.tp > 1) __threadfence_system();
       }
       pending = PEND_DENSE;
@@ -682,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
           const float* rb = lptr<float>(a, l, KK3_MOE_ROUTER_BIAS);
           if ((reinterpret_cast<uintptr_t>(rb) & 15u) == 0) prefetch_l2(rb, (unsigned)(g.E * 4) & ~15u);
         }
-        run_gemv<NT, 1>(a, sj, sjn, 0, gridDim.x, 0, 0, phase);
+        if (!gemv_pass<NT>(a, sj, sjn, 0, 0, phase)) KK3_FAIL();
       }
       KK3_PHASE_END();
       const unsigned x_moe = xi++;
@@ -715,7 +734,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         // the shared expert's down projection first (kimi.py:326), then the routed experts' (:320-323); the
         // routed experts' fix-up uses counter bank 0, so this one takes bank 1
         prefetch_row_inputs(a, 2, l);
-        run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, x_moe & 1, 1);
+        if (!gemv_pass<NT>(a, sj, 1, x_moe & 1, 1)) KK3_FAIL();
         if (g.tp > 1) __threadfence_system();
         if (blockIdx.x == 0 && threadIdx.x == 0) sub_stamp(a, phase, 0);
         run_experts<1>(a, sph);
@@ -734,7 +753,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
       if (KK3_RUN) {
         KK3_BUILD(latent_up_job(a, l, sj[0]));
         prefetch_row_inputs(a, 0, l + 1);
-        run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, 0);
+        if (!gemv_pass<NT>(a, sj, 1, 0)) KK3_FAIL();
       }
       KK3_PHASE_END();
     }
@@ -749,7 +768,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
   KK3_PHASE_END();
   if (KK3_RUN) {
     KK3_BUILD(lm_head_job(a, sj[0]));
-    run_gemv<NT, 1>(a, sj, 1, 0, gridDim.x, 0);
+    if (!gemv_pass<NT>(a, sj, 1, 0)) KK3_FAIL();
   }
   KK3_PHASE_END();
   const unsigned x_key = xi++;

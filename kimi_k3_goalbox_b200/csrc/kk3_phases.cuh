@@ -275,9 +275,8 @@ KK3_FN void rms_row(const bf16* in, const bf16* w, int n, float eps, bf16* out, 
   __syncthreads();
 }
 
-// Sum the tp BF16 partials of row b, 16-byte chunk c, of an exchange sub-region (FP32, rank order), rounded
-// to BF16 (kimi.py:343-347).
-// Sum of the tp bf16 slots of row b (FP32, rank order, kimi.py:343-347). With the host transport the host has
+// Sum of the tp bf16 slots of row b, 16-byte chunk c (channels 8c .. 8c + 7, layout xch_index), in FP32 and
+// rank order, rounded to BF16 (kimi.py:343-347). With the host transport the host has
 // already all-reduced the partials into this rank's own slot (FP32 sum, cast to bf16), so that slot is read.
 KK3_DEV void xch_sum8(const StepArgs& a, int parity, long long off, int b, int width, int c, float (&out)[8]) {
   const bf16* base = xlocal<bf16>(a, parity, off);
@@ -286,7 +285,7 @@ KK3_DEV void xch_sum8(const StepArgs& a, int parity, long long off, int b, int w
   const int lo = a.comm_mode == kCommHost ? a.g.rank : 0, hi = a.comm_mode == kCommHost ? a.g.rank + 1 : a.g.tp;
   for (int src = lo; src < hi; ++src) {
     float f[8];
-    unpack8(ld_act16(base + ((size_t)src * a.g.B + b) * width + c * 8), f);
+    unpack8(ld_act16(base + xch_index(a.g, src, b, c * 8, width)), f);
 #pragma unroll
     for (int e = 0; e < 8; ++e) out[e] += f[e];
   }
@@ -311,47 +310,81 @@ KK3_FN void kda_item(const StepArgs& a, int layer, int kidx, int b, int hh, floa
   float* outv = sm + 768;    // [128]
   float* fa = sm + 896;      // [128]
   float* misc = sm + 1024;   // [32]
+  const bool stamp = blockIdx.x == 0 && tid == 0;   // profiling stamps of CTA 0's first item (sub 0-5)
+  if (stamp) sub_stamp(a, kk3_cur_phase, 0);
   const bool keep = !reinterpret_cast<const bool*>(a.ptr[KK3_RESET])[b];
   const bf16* conv_in = lptr<bf16>(a, layer, KK3_KDA_CONV_STATE);
   const float* cw = lptr<float>(a, layer, KK3_KDA_CONV_WEIGHT);
   bf16* conv_out = gout<bf16>(a, KK3_OUT_CONV_STATE) + (size_t)kidx * g.B * 3 * D * 4;
+  const float* st_in = lptr<float>(a, layer, KK3_KDA_RECURRENT_STATE) + (((size_t)b * g.hr + hh) * dh) * dh;
+  float* st_out = gout<float>(a, KK3_OUT_RECURRENT_STATE) + ((((size_t)kidx * g.B + b) * g.hr + hh) * dh) * dh;
+
+  // An item is a chain of short dependent steps, so every global load that needs no result of this item is
+  // issued first and their latencies overlap: this warp's eight state rows, this thread's quarter of an f_b
+  // row, the conv inputs and weights, the decay parameters and the output gate.
+  float4 rows[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    rows[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (keep) rows[i] = *reinterpret_cast<const float4*>(st_in + (size_t)(warp * 8 + i) * dh + lane * 4);
+  }
+  // f_b (kimi.py:290): output channel gd = tid / 4; part gp sums the 8-wide input chunks gp, gp + 4, gp + 8 and
+  // gp + 12, so the four parts of a channel read 64 contiguous bytes per load and distinct shared-memory banks
+  const int gd = tid >> 2, gp = tid & 3;
+  const uint4* fbp = reinterpret_cast<const uint4*>(lptr<bf16>(a, layer, KK3_KDA_FB) + (size_t)(hh * dh + gd) * dh);
+  uint4 fbw[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) fbw[q] = fbp[q * 4 + gp];
+  const float A = gp == 0 ? expf(lptr<float>(a, layer, KK3_KDA_A_LOG)[hh]) : 0.0f;
+  const float dtb = gp == 0 ? lptr<float>(a, layer, KK3_KDA_DT_BIAS)[hh * dh + gd] : 0.0f;
+  // conv (kimi.py:286-289): thread (i, dd) of the first 384 holds channel dd of q, k or v
+  const int ci = tid >> 7, cd = tid & 127;
+  const size_t coff = (((size_t)b * 3 + ci) * D + hh * dh + cd) * 4;
+  float raw = 0.0f, w1 = 0.0f, w2 = 0.0f, w3 = 0.0f;
+  float4 cwv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (tid < 384) {
+    raw = bf2f(a.s.qkv[((size_t)b * 3 + ci) * D + hh * dh + cd]);
+    if (keep) {
+      w1 = bf2f(conv_in[coff + 1]);
+      w2 = bf2f(conv_in[coff + 2]);
+      w3 = bf2f(conv_in[coff + 3]);
+    }
+    cwv = *reinterpret_cast<const float4*>(cw + ((size_t)ci * D + hh * dh + cd) * 4);
+  }
+  float ogt[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // warp 0: output gate of value channels 4 lane .. 4 lane + 3
+  if (warp == 0) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) ogt[q] = bf2f(a.s.og[(size_t)b * D + hh * dh + lane * 4 + q]);
+  }
   if (tid < 128) fa[tid] = bf2f(a.s.fa[(size_t)b * dh + tid]);
   __syncthreads();
-  if (tid < 384) {
-    const int i = tid >> 7, dd = tid & 127, ch = hh * dh + dd;
-    const float raw = bf2f(a.s.qkv[((size_t)b * 3 + i) * D + ch]);
-    const size_t off = (((size_t)b * 3 + i) * D + ch) * 4;
-    float w1 = 0.0f, w2 = 0.0f, w3 = 0.0f;
-    if (keep) {
-      w1 = bf2f(conv_in[off + 1]);
-      w2 = bf2f(conv_in[off + 2]);
-      w3 = bf2f(conv_in[off + 3]);
+  if (stamp) sub_stamp(a, kk3_cur_phase, 1);
+  {
+    float acc = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const bf16* wv = reinterpret_cast<const bf16*>(&fbw[q]);
+      const float4 f0 = *reinterpret_cast<const float4*>(fa + (q * 4 + gp) * 8);
+      const float4 f1 = *reinterpret_cast<const float4*>(fa + (q * 4 + gp) * 8 + 4);
+      acc += bf2f(wv[0]) * f0.x + bf2f(wv[1]) * f0.y + bf2f(wv[2]) * f0.z + bf2f(wv[3]) * f0.w +
+             bf2f(wv[4]) * f1.x + bf2f(wv[5]) * f1.y + bf2f(wv[6]) * f1.z + bf2f(wv[7]) * f1.w;
     }
-    bf16* co = conv_out + off;
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (gp == 0) decay[gd] = expf(-5.0f * sigmoidf_(A * (round_bf(acc) + dtb)));
+  }
+  if (tid < 384) {
+    bf16* co = conv_out + coff;
     co[0] = f2bf(w1);
     co[1] = f2bf(w2);
     co[2] = f2bf(w3);
     co[3] = f2bf(raw);
-    const float* cwi = cw + ((size_t)i * D + ch) * 4;
-    const float s = w1 * cwi[0] + w2 * cwi[1] + w3 * cwi[2] + raw * cwi[3];
+    const float s = w1 * cwv.x + w2 * cwv.y + w3 * cwv.z + raw * cwv.w;
     const float act = round_bf(s * sigmoidf_(s));
-    (i == 0 ? sq : (i == 1 ? sk : sv))[dd] = act;
-  } else {
-    const int dd = tid - 384, ch = hh * dh + dd;
-    const bf16* fb = lptr<bf16>(a, layer, KK3_KDA_FB) + (size_t)ch * dh;
-    float acc = 0.0f;
-    for (int e = 0; e < dh; e += 8) {
-      const uint4 w = *reinterpret_cast<const uint4*>(fb + e);
-      const bf16* wv = reinterpret_cast<const bf16*>(&w);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) acc += bf2f(wv[q]) * fa[e + q];
-    }
-    const float gate = round_bf(acc);
-    const float A = expf(lptr<float>(a, layer, KK3_KDA_A_LOG)[hh]);
-    const float dtb = lptr<float>(a, layer, KK3_KDA_DT_BIAS)[ch];
-    decay[dd] = expf(-5.0f * sigmoidf_(A * (gate + dtb)));
+    (ci == 0 ? sq : (ci == 1 ? sk : sv))[cd] = act;
   }
   __syncthreads();
+  if (stamp) sub_stamp(a, kk3_cur_phase, 2);
   if (warp < 2) {
     const float* src = warp == 0 ? sq : sk;
     float v[4], ss = 0.0f;
@@ -371,18 +404,11 @@ KK3_FN void kda_item(const StepArgs& a, int layer, int kidx, int b, int hh, floa
     misc[0] = sigmoidf_(bf2f(a.s.beta[(size_t)b * g.hr + hh]));
   }
   __syncthreads();
+  if (stamp) sub_stamp(a, kk3_cur_phase, 3);
   const float sb = misc[0];
   const float4 dk = *reinterpret_cast<const float4*>(decay + lane * 4);
   const float4 kk = *reinterpret_cast<const float4*>(kn + lane * 4);
   const float4 qq = *reinterpret_cast<const float4*>(qn + lane * 4);
-  const float* st_in = lptr<float>(a, layer, KK3_KDA_RECURRENT_STATE) + (((size_t)b * g.hr + hh) * dh) * dh;
-  float* st_out = gout<float>(a, KK3_OUT_RECURRENT_STATE) + ((((size_t)kidx * g.B + b) * g.hr + hh) * dh) * dh;
-  float4 rows[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    rows[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (keep) rows[i] = *reinterpret_cast<const float4*>(st_in + (size_t)(warp * 8 + i) * dh + lane * 4);
-  }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int v = warp * 8 + i;
@@ -396,6 +422,7 @@ KK3_FN void kda_item(const StepArgs& a, int layer, int kidx, int b, int hh, floa
     if (lane == 0) outv[v] = o;
   }
   __syncthreads();
+  if (stamp) sub_stamp(a, kk3_cur_phase, 4);
   if (warp == 0) {
     float o[4], ss = 0.0f;
 #pragma unroll
@@ -409,11 +436,11 @@ KK3_FN void kda_item(const StepArgs& a, int layer, int kidx, int b, int hh, floa
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int v = lane * 4 + q;
-      const float gt = sigmoidf_(bf2f(a.s.og[(size_t)b * D + hh * dh + v]));
-      a.s.attn_in[(size_t)b * D + hh * dh + v] = f2bf(o[q] * rs * onorm[v] * gt);
+      a.s.attn_in[(size_t)b * D + hh * dh + v] = f2bf(o[q] * rs * onorm[v] * sigmoidf_(ogt[q]));
     }
   }
   __syncthreads();
+  if (stamp) sub_stamp(a, kk3_cur_phase, 5);
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -42,6 +42,7 @@
 #pragma once
 #include <cuda.h>
 #include "kk3_phases.cuh"
+#include "kk3_tcgen05.cuh"
 
 namespace kk3 {
 
@@ -68,38 +69,7 @@ struct TcPhase {
   __half* act_dbg;               // MT == 2: optional FP16 copy of the activations [pairs, rows]
 };
 
-// ---- PTX wrappers ----------------------------------------------------------------------------------
-
-KK3_DEV void mbar_init(unsigned bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-KK3_DEV void mbar_inval(unsigned bar) { asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(bar) : "memory"); }
-KK3_DEV void mbar_arrive(unsigned bar) {
-  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-KK3_DEV void mbar_arrive_tx(unsigned bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-KK3_DEV bool mbar_test(unsigned bar, unsigned parity) {
-  unsigned ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-  return ok != 0;
-}
-// Bounded wait for the phase of parity `parity` to complete; false (error raised) on timeout or error.
-KK3_DEV bool mbar_wait(const StepArgs& a, unsigned bar, unsigned parity) {
-  if (mbar_test(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  for (unsigned spin = 0;; ++spin) {
-    if (mbar_test(bar, parity)) return true;
-    if ((spin & 15) == 15 && (failed(a) || globaltimer() - t0 > (unsigned long long)a.g.timeout_ns)) {
-      set_error(a, kErrTimeout);
-      return false;
-    }
-  }
-}
+// ---- PTX wrappers (the shared ones are in kk3_tcgen05.cuh) -------------------------------------------
 
 KK3_DEV void tma_load_3d(unsigned dst, const CUtensorMap* map, unsigned bar, int x, int y, int z,
                          unsigned long long pol) {
@@ -112,18 +82,6 @@ KK3_DEV void bulk_load(unsigned dst, const void* src, unsigned bytes, unsigned b
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
-KK3_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-KK3_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
-
-KK3_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-KK3_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-KK3_DEV void tmem_alloc(unsigned dst_smem, unsigned ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
-               : "memory");
-}
-KK3_DEV void tmem_dealloc(unsigned taddr, unsigned ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
 // 32 rows x 16 bytes of shared memory -> TMEM lanes 32w + row (every w), 4 columns
 KK3_DEV void tmem_cp_32x128b_x4(unsigned taddr, unsigned long long sdesc) {
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
@@ -134,21 +92,6 @@ KK3_DEV void umma_mxf8f6f4(unsigned d, unsigned long long adesc, unsigned long l
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n}"
       ::"r"(d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb) : "memory");
-}
-KK3_DEV void umma_commit(unsigned bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-KK3_DEV float tmem_ld1(unsigned taddr) {
-  unsigned v;
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(v) : "r"(taddr) : "memory");
-  return __uint_as_float(v);
-}
-KK3_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// Shared-memory matrix descriptors (tcgen05): K-major, 128-byte swizzle, 8-row atoms of 1024 bytes
-KK3_DEV unsigned long long sdesc_sw128(unsigned addr) {
-  return (unsigned long long)((addr & 0x3ffffu) >> 4) | (1ull << 16) | ((unsigned long long)(1024 >> 4) << 32) |
-         (1ull << 46) | (2ull << 61);
 }
 // no swizzle, 16-byte rows, 8-row core matrices 128 bytes apart (the 32x128b scale-factor source)
 KK3_DEV unsigned long long sdesc_rows16(unsigned addr) {

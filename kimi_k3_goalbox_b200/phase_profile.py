@@ -225,6 +225,10 @@ def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[d
                                           "warp0_threshold": (st[12] - base) / 1e3, "warp0_row": (st[13] - base) / 1e3,
                                           "all_rows": (st[14] - base) / 1e3, "grouped": (st[15] - base) / 1e3,
                                           "phase_end": (ts[i + 1] - base) / 1e3}
+        if name == "kda" and st[0]:
+            subinfo[f"{name}:{layer}"] = {k: (st[j] - base) / 1e3 for j, k in enumerate(
+                ["item_start", "loads_fa", "conv_gate", "norms", "state", "item_end"]) if st[j]} | {
+                "phase_end": (ts[i + 1] - base) / 1e3}
         if name == "experts_down" and st[0]:
             subinfo[f"{name}:{layer}"] = {"shared_down_cta0": (st[0] - base) / 1e3, "staged_cta0": (st[1] - base) / 1e3,
                                           "phase_end": (ts[i + 1] - base) / 1e3}
@@ -283,7 +287,7 @@ def main(argv=None) -> int:
         case = cases.variant(case, batch=args.batch)
     rows = profile(case, args.reps)
     subrow, head, rows = rows[0], rows[1:3], rows[3:]
-    for k, v in [kv for kv in subrow["info"].items() if kv[0].startswith(("mla_attend", "mla_combine", "experts_gate_up", "experts_down:1", "attn_prologue:2", "moe_in:1", "warps ")) and (not kv[0].startswith("warps ") or kv[0].endswith(":1"))]:
+    for k, v in [kv for kv in subrow["info"].items() if kv[0].startswith(("mla_attend", "mla_combine", "experts_gate_up", "experts_down:1", "attn_prologue:2", "moe_in:1", "kda:", "warps ")) and (not kv[0].startswith("warps ") or kv[0].endswith(":1"))]:
         print("  sub-phase", k, {kk: (round(vv, 2) if isinstance(vv, float) else vv) for kk, vv in v.items()})
     total = sum(r["us"] for r in rows)
     print(f"{case['id']}: full step {head[0]['us']:.1f} us (events), empty launch {head[1]['us']:.1f} us, "

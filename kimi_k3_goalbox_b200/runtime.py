@@ -47,6 +47,7 @@ class Config(ctypes.Structure):
 
 
 COMM_PEER, COMM_HOST = 0, 1   # include/kk3.h KK3_COMM_*
+GEMV_AUTO, GEMV_MMA = 0, 1     # include/kk3.h KK3_GEMV_*
 
 
 def host_comm_segments(params: dict, tp: int) -> list[tuple[int, int, list[tuple[str, str, int]]]]:
@@ -55,6 +56,22 @@ def host_comm_segments(params: dict, tp: int) -> list[tuple[int, int, list[tuple
     end. An exchange is (sub-region, "sum" | "gather", parity): "sum" all-reduces this rank's slot (FP32 sum,
     kimi.py:343-347), "gather" all-gathers the argmax keys (kimi.py:218-227). Exchanges alternate parity in
     program order, as the kernel's exchange counter does."""
+    names = host_comm_program(params)
+    points = {"embed": [("att", "sum")], "o_proj": [("att", "sum")], "dense_down": [("att", "sum")],
+              "moe_combine_write": [("exp", "sum"), ("shd", "sum")], "argmax_write": [("key", "gather")]}
+    segs, start, xi = [], 0, 0
+    for i, name in enumerate(names):
+        if name in points and tp > 1:
+            segs.append((start, i + 1, [(region, kind, xi & 1) for region, kind in points[name]]))
+            xi += 1
+            start = i + 1
+    segs.append((start, -1, []))
+    return segs
+
+
+def host_comm_program(params: dict) -> list[str]:
+    """Grid phases of one step under the host transport, in kernel order: the peer program with the MoE
+    combine and the argmax each split at their exchange (csrc/kk3_kernel.cuh)."""
     from .cases import is_mla
     L, fd = params["layers"], params["first_dense"]
     names = ["embed"]
@@ -68,16 +85,7 @@ def host_comm_segments(params: dict, tp: int) -> list[tuple[int, int, list[tuple
     if L <= fd:
         names.append("fold")
     names += ["head_prologue", "lm_head", "argmax_write", "argmax_read"]
-    points = {"embed": [("att", "sum")], "o_proj": [("att", "sum")], "dense_down": [("att", "sum")],
-              "moe_combine_write": [("exp", "sum"), ("shd", "sum")], "argmax_write": [("key", "gather")]}
-    segs, start, xi = [], 0, 0
-    for i, name in enumerate(names):
-        if name in points and tp > 1:
-            segs.append((start, i + 1, [(region, kind, xi & 1) for region, kind in points[name]]))
-            xi += 1
-            start = i + 1
-    segs.append((start, -1, []))
-    return segs
+    return names
 
 
 class _DeviceBytes:
@@ -128,8 +136,14 @@ def load_library() -> ctypes.CDLL:
         lib.kk3_launch_config.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(ctypes.c_size_t)]
         lib.kk3_exchange_layout.argtypes = [vp, ctypes.POINTER(ctypes.c_longlong)]
         lib.kk3_set_comm_mode.argtypes = [vp, i32]
+        lib.kk3_set_gemv_engine.argtypes = [vp, i32]
         _LIB = lib
     return _LIB
+
+
+def padded_tiles(batch: int) -> int:
+    """The step kernel's batch class: 8-column MMA n-tiles per batch (1, 2, 4 or 8 for B <= 8, 16, 32, 64)."""
+    return 1 if batch <= 8 else 2 if batch <= 16 else 4 if batch <= 32 else 8
 
 
 def rank_config(case: dict, rank: int, device: int, timeout_ns: int = 0) -> Config:
@@ -356,14 +370,23 @@ class StepContext:
         return g.value, t.value, s.value
 
     # --- the host-transport comparison baseline (KK3_COMM_HOST) -----------------------------------------
+    def set_gemv_engine(self, engine: int) -> None:
+        """GEMV_AUTO (tcgen05 projections above batch 16) or GEMV_MMA (mma.sync for every batch), include/kk3.h."""
+        rc = self.lib.kk3_set_gemv_engine(self.handle, engine)
+        if rc != 0:
+            raise KK3Error(rc, "kk3_set_gemv_engine")
+
     def set_comm_mode(self, mode: int) -> None:
         rc = self.lib.kk3_set_comm_mode(self.handle, mode)
         if rc != 0:
             raise KK3Error(rc, "kk3_set_comm_mode")
 
     def exchange_slots(self) -> dict:
-        """This rank's exchange buffer as torch views: {(parity, region): tensor [tp, B, width]} for the regions
-        att (bf16), exp (f32), shd (bf16) and key (int64 view of the u64 keys)."""
+        """This rank's exchange buffer as torch views: {(parity, region): tensor [tp, n]}, one row per source
+        rank, for the regions att (bf16, n = hidden x bp), exp (f32, n = batch x latent_hidden), shd (bf16, as
+        att) and key (int64 view of the u64 keys, n = batch). bp is the batch padded to the kernel's n-tile width
+        (8, 16, 32 or 64); the bf16 regions are channel-tiled ([hidden / 16][bp][16] per source), which the
+        elementwise NCCL reductions of the host transport do not need to know."""
         if getattr(self, "_xviews", None) is None:
             ptr, size = ctypes.c_void_p(), ctypes.c_size_t()
             rc = self.lib.kk3_debug_buffer(self.handle, 15, ctypes.byref(ptr), ctypes.byref(size))   # KK3_BUF_EXCHANGE
@@ -375,14 +398,15 @@ class StepContext:
                 raise KK3Error(rc, "kk3_exchange_layout")
             raw = torch.as_tensor(_DeviceBytes(ptr.value, size.value), device=torch.device("cuda", self.device))
             tp, B, p = self.case["tp"], self.params["batch"], self.params
-            widths = {"att": (p["hidden"], torch.bfloat16, 4), "exp": (p["latent_hidden"], torch.float32, 5),
-                      "shd": (p["hidden"], torch.bfloat16, 6), "key": (1, torch.int64, 7)}
+            bp = 8 * padded_tiles(B)
+            sizes = {"att": (p["hidden"] * bp, torch.bfloat16, 4), "exp": (B * p["latent_hidden"], torch.float32, 5),
+                     "shd": (p["hidden"] * bp, torch.bfloat16, 6), "key": (B, torch.int64, 7)}
             views = {}
             for parity in (0, 1):
-                for region, (w, dt, k) in widths.items():
+                for region, (n, dt, k) in sizes.items():
                     start = off[1 + parity] + off[k]
-                    n = tp * B * w * torch.empty(0, dtype=dt).element_size()
-                    views[(parity, region)] = raw[start:start + n].view(dt).view(tp, B, w)
+                    nbytes = tp * n * torch.empty(0, dtype=dt).element_size()
+                    views[(parity, region)] = raw[start:start + nbytes].view(dt).view(tp, n)
             self._xraw, self._xviews = raw, views
         return self._xviews
 

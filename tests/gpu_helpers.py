@@ -95,3 +95,36 @@ def diagnose(ctx, case: dict, values: dict, trace: dict, limit: float = 0.05, ve
         if verbose:
             print(f"  {label:22s} rel_l2 = {err:.3e}{'   <-- large' if err > limit else ''}")
     return rows
+
+
+def load_submission(path, contract: dict):
+    """Import the candidate file by path and call its build(contract), as the reference harness does
+    (megabench/harness/runner.py:53-69): a fresh module named megabench_candidate, the file's folder first on
+    sys.path, build must be callable and must return a callable."""
+    import importlib.util
+    import sys
+    from pathlib import Path
+
+    path = Path(path).resolve()
+    spec = importlib.util.spec_from_file_location("megabench_candidate", path)
+    module = importlib.util.module_from_spec(spec)
+    sys.path.insert(0, str(path.parent))
+    spec.loader.exec_module(module)
+    assert callable(getattr(module, "build", None)), "submission must export build(case)"
+    runner = module.build(contract)
+    assert callable(runner), "build(case) must return a callable run(inputs)"
+    return runner
+
+
+def audit_launches(fn, inputs: dict) -> list[str]:
+    """Names of the GPU activities one call of fn(inputs) produces, recorded with torch.profiler the way the
+    reference harness audits a candidate's launch budget (megabench/harness/benchmark.py:49-74)."""
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+        fn(inputs)
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    if not names:   # diagnostics for the assertion that follows: what the profiler did record
+        print("profiler events:", [(e.name, str(e.device_type)) for e in prof.events()][:40])
+    return names

@@ -49,3 +49,29 @@ def test_host_comm_segments_cover_the_program_with_exchanges_in_kernel_order():
         # embedding, 2 per layer, argmax
         assert len(parities) == 1 + 2 * p["layers"] + 1
         assert runtime.host_comm_segments(p, 1) == [(0, -1, [])]
+
+
+def test_clock_poller_process_records_samples_in_the_window(tmp_path, monkeypatch):
+    """The NVML poller runs as its own process (a fake pynvml module stands in for the driver here); it must
+    record samples while the parent is busy, stop when the sampler exits and hand every sample back."""
+    (tmp_path / "pynvml.py").write_text(
+        "NVML_CLOCK_SM = 1\n"
+        "def nvmlInit(): pass\n"
+        "def nvmlDeviceGetHandleByPciBusId(bus): return 0\n"
+        "def nvmlDeviceGetHandleByIndex(i): return 0\n"
+        "def nvmlDeviceGetMaxClockInfo(h, kind): return 1965\n"
+        "def nvmlDeviceGetClockInfo(h, kind): return 1920\n"
+        "def nvmlDeviceGetCurrentClocksEventReasons(h): return 0x4\n"
+        "def nvmlDeviceGetPowerUsage(h): return 700000\n")
+    monkeypatch.setenv("PYTHONPATH", str(tmp_path))
+    with bench.ClockSampler(0, bus="00000000:01:00.0") as c:
+        time.sleep(0.05)
+        c.mark_start()
+        busy = time.time() + 0.3
+        while time.time() < busy:   # the parent does not read anything while the steps run
+            pass
+        c.mark_end()
+    s = c.summary()
+    assert c.source.startswith("nvml"), c.error
+    assert s["samples"] >= 10 and s["sm_mhz"] == 1920.0 and s["sm_max_mhz"] == 1965.0, s
+    assert s["reasons"] == ["sw_power_cap"] and s["power_w_max"] == 700.0 and s["error"] is None

@@ -104,3 +104,29 @@ def test_syn_l8_tp8_rank_equivalent(batch):
     """One TP8 rank of kimi-k3-syn-l8-tp8-b{1,8,64}-s8192 (shard shapes, reductions local)."""
     case = gh.rank_equivalent("kimi-k3-syn-l8-tp8-b8-s8192", batch=batch)
     _run_and_grade(case, 100 + batch)
+
+
+@pytest.mark.parametrize("batch,seed", [(20, 5), (64, 41)])
+def test_tensor_core_projections_against_the_mma_engine(batch, seed):
+    """Batches above 16 run the BF16 projections on tcgen05 (M = 128 weight rows, N = the padded batch, TMEM
+    accumulators). The same inputs through the warp-level mma.sync engine (kk3_set_gemv_engine): both within the
+    band, and the two steps' logits close (FP32 sums in another order, so not bit-identical)."""
+    from kimi_k3_goalbox_b200 import runtime
+    case = gh.small_case(batch)
+    with torch.inference_mode():
+        values = ko.make_inputs(case, seed, "cuda")
+        expected = ko.reference(case, values, serial=True)
+        outs = {}
+        for engine in (runtime.GEMV_AUTO, runtime.GEMV_MMA):
+            ctx = StepContext(case)
+            try:
+                ctx.set_gemv_engine(engine)
+                outs[engine] = {k: v.clone() for k, v in ctx.step(values).items()}
+                torch.cuda.synchronize()
+                ctx.check()
+            finally:
+                ctx.close()
+            ko.compare(case, values, expected, outs[engine], serial=True)
+        d = gh.rel_l2(outs[runtime.GEMV_AUTO]["logits"], outs[runtime.GEMV_MMA]["logits"])
+        print(f"batch {batch}: logits rel-L2 tcgen05 vs mma.sync {d:.2e}")
+        assert d < 1e-2, d

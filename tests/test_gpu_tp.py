@@ -54,6 +54,14 @@ TP_SPECS = [
 ]
 
 
+def worker_report(out: str) -> str:
+    """The workers' own output (FAIL lines with their seed, tracebacks) without torchrun's per-rank failure
+    summaries, which would otherwise fill the assertion message."""
+    noise = ("torch/distributed/elastic", "error_file", "traceback :", "elastic/errors.html", "Sending process",
+             "ChildFailedError", "exitcode", "<N/A>", "[1]:", "[2]:", "[3]:", "[4]:", "[5]:", "[6]:", "[7]:", "====")
+    return "\n".join(line for line in out.splitlines() if not any(n in line for n in noise))[-8000:]
+
+
 def spec_tp(spec: dict) -> int:
     if "tp" in spec:
         return spec["tp"]
@@ -73,8 +81,8 @@ def test_tp_band_multi_gpu(spec):
           (["--seed", str(spec["seed"])] if "seed" in spec else [])
     r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=1000)
     out = r.stdout + r.stderr
-    assert r.returncode == 0, out[-4000:]
-    assert out.count("ok:") == tp, out[-4000:]
+    assert r.returncode == 0, worker_report(out)
+    assert out.count("ok:") == tp, worker_report(out)
     print("\n".join(line for line in out.splitlines() if "ok:" in line))
 
 

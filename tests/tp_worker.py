@@ -1,10 +1,11 @@
 """One rank of the tensor-parallel GPU parity test (launched by tests/test_gpu_tp.py through torchrun).
 
-Each rank builds the submission with the reference's execution context (rank, tp_rank, device, tp_group;
-megabench/harness/distributed.py:67-69), runs the step twice, and grades its outputs with the oracle's band
-rule against the BF16 and FP32 oracle computed with real all-reduces over the same process group
-(megabench/tasks/kimi.py:343-347). The second step must reproduce the first bit for bit: the in-kernel
-exchange alternates parity regions and sequence numbers between steps.
+Each rank imports submission.py by path and builds it with the reference's execution context (rank, tp_rank,
+device, tp_group; megabench/harness/distributed.py:67-69, runner.py:53-69), runs the step twice, checks that
+the inputs are unchanged, audits one call's GPU launches (exactly one kernel; harness/benchmark.py:49-74), and
+grades its outputs with the oracle's band rule against the BF16 and FP32 oracle computed with real all-reduces
+over the same process group (megabench/tasks/kimi.py:343-347). The second step must reproduce the first bit
+for bit: the in-kernel exchange alternates parity regions and sequence numbers between steps.
 """
 
 from __future__ import annotations
@@ -24,7 +25,6 @@ ROOT = Path(__file__).resolve().parents[1]
 sys.path.insert(0, str(ROOT))
 
 from kimi_k3_goalbox_b200 import cases  # noqa: E402
-from kimi_k3_goalbox_b200.submission import build  # noqa: E402
 from oracle import kimi_oracle as ko  # noqa: E402
 from tests import gpu_helpers as gh  # noqa: E402
 
@@ -61,11 +61,16 @@ def main() -> int:
             values = ko.make_inputs(case, args.seed, device, rank)
             execution = {"rank": rank, "world_size": world, "tp_rank": rank, "ep_rank": 0, "backend": "nccl",
                          "device": str(device), "tp_group": group, "ep_group": None}
-            run = build(dict(case, execution=execution))
+            run = gh.load_submission(ROOT / "submission.py", dict(case, execution=execution))
+            originals = ko.snapshot(values)
             first = {k: v.clone() for k, v in run(values).items()}
             second = run(values)
             torch.cuda.synchronize()
             run.ctx.check()
+            ko.check_unchanged(values, originals)
+            # one call is one GPU launch on every rank (megabench/harness/benchmark.py:49-74, budget 1)
+            launches = gh.audit_launches(run, values)
+            assert len(launches) == case["max_gpu_launches"] == 1 and "kk3_step_kernel" in launches[0], launches
             expected = ko.reference(case, values, serial=False, tp_rank=rank, group=group)
             try:
                 details = ko.compare(case, values, expected, first, serial=False, tp_rank=rank, group=group)
