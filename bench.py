@@ -503,6 +503,36 @@ def host_comm_leg(args, ctx, stream, n: int) -> dict:
             "note": "same kernel; exchanges by NCCL on the host instead of in-kernel NVLink peer stores"}
 
 
+def push_comm_leg(args, ctx, stream, n: int) -> dict:
+    """The in-kernel push transport (include/kk3.h KK3_COMM_PUSH) on the same inputs: one step compared with a
+    fused (peer-transport) step, K timed steps (max over ranks) and its in-step phase breakdown. One launch per
+    step, no host collective."""
+    from kimi_k3_goalbox_b200 import runtime
+    fused = ctx.allocate_outputs()
+    ctx.bind_outputs(fused)
+    ctx.launch(stream.cuda_stream)
+    torch.cuda.synchronize()
+    ctx.check()
+    pushed = ctx.allocate_outputs()
+    ctx.bind_outputs(pushed)
+    ctx.set_comm_mode(runtime.COMM_PUSH)
+    try:
+        ctx.launch(stream.cuda_stream)
+        torch.cuda.synchronize()
+        ctx.check()
+        same = all(torch.equal(pushed[k], fused[k]) for k in fused)
+        total_ms, _ = time_steps(ctx, stream, args.steps, args.warmup, n, None)
+        phases = phase_breakdown(ctx, stream, n)
+    finally:
+        ctx.set_comm_mode(runtime.COMM_PEER)
+    flag = torch.tensor([0.0 if same else 1.0], device="cuda", dtype=torch.float64)
+    dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+    return {"us": round(max_over_ranks(total_ms, n) / args.steps * 1000.0, 2), "launches_per_step": 1,
+            "outputs_identical_to_fused": not bool(flag[0]), "phase_breakdown": phases,
+            "transport": "partials of the projections stored locally, pushed by every CTA at the start of the "
+                         "reading phase (coalesced 16-byte pieces, one flag per source and CTA)"}
+
+
 def host_phase_times(ctx, runtime) -> list[dict]:
     """In-step phase times of the last host-transport step: the phases inside a launch range (a range's first
     phase is left out, its stamp difference spans the NCCL collective before it)."""
@@ -645,6 +675,7 @@ def run_b200(args, n: int, rank: int, local: int) -> dict | None:
         ctx.check()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1), n) / args.steps
         nccl = host_comm_leg(args, ctx, stream, n) if n > 1 and not args.no_nccl else None
+        push = push_comm_leg(args, ctx, stream, n) if n > 1 else None
         runner.close()
         host_values = None
         if rank == 0 and n == 1 and not args.no_cpu_baseline:
@@ -699,6 +730,7 @@ def run_b200(args, n: int, rank: int, local: int) -> dict | None:
         "parity": parity,
         "phase_breakdown": phases,
         "nccl_allreduce_variant": nccl,
+        "push_exchange_variant": push,
         "e2e": {"value": round(e2e_ms * 1000.0, 2), "unit": "us", "h2d_bytes_per_step": B * 8 + B,
                 "d2h_bytes_per_step": B * 8},
         "gpu_launches": args.steps,

@@ -213,9 +213,14 @@ int kk3_exchange_layout(kk3_ctx* ctx, long long* offsets);
  * KK3_COMM_HOST (comparison baseline, no counterpart in the reference's API): each rank writes its partial only
  * into its own slot of its own buffer and never waits; the MoE combine and argmax phases each split in two
  * (write, then read). The caller runs the step as phase ranges with kk3_debug_phases and reduces the slots with
- * NCCL between them: all-reduce (FP32 sum) of this rank's att, exp and shd slots, all-gather of the keys. */
+ * NCCL between them: all-reduce (FP32 sum) of this rank's att, exp and shd slots, all-gather of the keys.
+ * KK3_COMM_PUSH (in-kernel alternative, one launch): the projections' partials (att, shd) are stored only into
+ * this rank's own slot; at the start of the phase that reads them every CTA copies its 1/G share of that slot to
+ * every peer in 16-byte pieces and raises one release flag per (source, CTA). The routed-expert sums, the
+ * embedding rows and the argmax keys go as with KK3_COMM_PEER. */
 #define KK3_COMM_PEER 0
 #define KK3_COMM_HOST 1
+#define KK3_COMM_PUSH 2
 int kk3_set_comm_mode(kk3_ctx* ctx, int mode);
 
 /* The engine of the BF16 projections. KK3_GEMV_AUTO (the default): tcgen05.mma kind::f16 on the tensor cores

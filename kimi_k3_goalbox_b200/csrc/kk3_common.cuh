@@ -31,6 +31,8 @@ constexpr int kTraceWords = 2 * 1024 + 4096;   // mapped trace: phase and progre
 // exchange transport (StepArgs::comm_mode)
 constexpr int kCommPeer = 0;   // in-kernel one-shot NVLink peer stores + per-row release flags (the product)
 constexpr int kCommHost = 1;   // comparison baseline: the host runs NCCL collectives between phase-range launches
+constexpr int kCommPush = 2;   // in-kernel, with the GEMV partials stored locally and pushed to the peers in coalesced
+                               // per-CTA chunks at the start of the phase that reads them (release flag per chunk)
 
 // device error word values (also the host-visible status)
 constexpr int kErrTimeout = 1;
@@ -105,6 +107,7 @@ struct Scratch {
 struct Comm {
   unsigned char* base[kMaxTp];   // per rank, this rank's view of rank r's exchange buffer
   long long flag_off;            // byte offset of the flag array [B][tp] (u32)
+  long long push_flag_off;       // byte offset of the chunk-push flag array [tp][grid] (u32), push transport
   long long data_off[2];         // byte offset of the two parity data regions
   long long region_bytes;        // bytes per parity region
   // sub-regions inside a parity region, byte offsets (each [tp][B][width])

@@ -141,6 +141,10 @@ KK3_DEV size_t xch_index(const Geo& g, int src, int b, int ch, int width) {
 // when the host reduces the slots with NCCL between launches
 KK3_DEV int xdst_lo(const StepArgs& a) { return a.comm_mode == kCommHost ? a.g.rank : 0; }
 KK3_DEV int xdst_hi(const StepArgs& a) { return a.comm_mode == kCommHost ? a.g.rank + 1 : a.g.tp; }
+// the same for the GEMV epilogues' partials (att, shd): under the push transport they stay local until the
+// reading phase pushes them (xch_push)
+KK3_DEV int xdst_gemv_lo(const StepArgs& a) { return a.comm_mode == kCommPeer ? 0 : a.g.rank; }
+KK3_DEV int xdst_gemv_hi(const StepArgs& a) { return a.comm_mode == kCommPeer ? a.g.tp : a.g.rank + 1; }
 
 // Fused epilogue for one complete 16-row tile. acc[mt][nt][i]: rows row0 + r (+8 for i >= 2), column
 // nt*8 + 2c + (i & 1).
@@ -234,7 +238,7 @@ KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const 
       const unsigned got = __shfl_xor_sync(0xffffffffu, send, 8);
       const uint2 piece = (rw & 1) ? make_uint2(got, w1) : make_uint2(w0, got);
       const size_t e = blk + (size_t)nt * 128 + (size_t)woff * 2;
-      for (int dst = xdst_lo(a); dst < xdst_hi(a); ++dst)
+      for (int dst = xdst_gemv_lo(a); dst < xdst_gemv_hi(a); ++dst)
         *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(xregion(a, dst, parity) + j.aux_off) + e) = piece;
     }
     return;

@@ -206,8 +206,10 @@ static void plan_step(const kk3_config* cfg, int sms, unsigned char* base, bool 
   // source is one contiguous block of the bf16 regions
   Comm& c = pl->comm;
   memset(&c, 0, sizeof(c));
-  const size_t flag_bytes = align_up(B * tp * 4, 256);
+  // flags: per-row flags [B][tp], then the push transport's per-chunk flags [tp][sms] (both start at zero)
+  const size_t flag_bytes = align_up(B * tp * 4, 256) + align_up(tp * (size_t)sms * 4, 256);
   c.flag_off = 0;
+  c.push_flag_off = (long long)align_up(B * tp * 4, 256);
   c.att_off = 0;
   size_t r = align_up(tp * (size_t)g.bp * g.h * 2, 256);
   c.exp_off = r;
@@ -402,8 +404,8 @@ extern "C" int kk3_exchange_layout(kk3_ctx* x, long long* offsets) {
 }
 
 extern "C" int kk3_set_comm_mode(kk3_ctx* x, int mode) {
-  if (!x || (mode != KK3_COMM_PEER && mode != KK3_COMM_HOST)) return KK3_ERR_ARG;
-  x->comm_mode = mode == KK3_COMM_HOST ? kCommHost : kCommPeer;
+  if (!x || (mode != KK3_COMM_PEER && mode != KK3_COMM_HOST && mode != KK3_COMM_PUSH)) return KK3_ERR_ARG;
+  x->comm_mode = mode == KK3_COMM_HOST ? kCommHost : (mode == KK3_COMM_PUSH ? kCommPush : kCommPeer);
   return KK3_OK;
 }
 

@@ -94,11 +94,16 @@ KK3_DEV void store_row(bf16* dst, const uint4 (&v)[kRowChunks], int nvec) {
 KK3_FN bool phase_attn_prologue(const StepArgs& a, int layer, int nb, int pending, bool need_signal, unsigned seq,
                                  int parity, float* fsm, int ph = -1) {
   const Geo& g = a.g;
+  // push transport: the dense FFN's partial is pushed here (the embedding rows were stored directly)
+  const bool push = a.comm_mode == kCommPush && g.tp > 1 && pending == PEND_DENSE;
+  if (push) xch_push(a, parity, a.comm.att_off, (long long)g.h * g.bp * 2, seq);
   #pragma unroll 1
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
     if (b == 0 && threadIdx.x == 0) sub_stamp(a, ph, 0);
     const bool fold = pending != PEND_NONE && !(g.tp == 1 && pending == PEND_EMBED);
-    if (pending != PEND_NONE && g.tp > 1) {
+    if (push) {
+      if (!xch_wait_push(a, seq)) return false;
+    } else if (pending != PEND_NONE && g.tp > 1) {
       if (need_signal) xch_signal_row(a, b, seq);
       if (!xch_wait_row(a, b, seq)) return false;
     }
@@ -117,9 +122,13 @@ KK3_FN bool phase_attn_prologue(const StepArgs& a, int layer, int nb, int pendin
 // fold a pending exchange into prefix without a following norm (only when the last layer is dense)
 KK3_FN bool phase_fold_pending(const StepArgs& a, int pending, bool need_signal, unsigned seq, int parity) {
   const Geo& g = a.g;
+  const bool push = a.comm_mode == kCommPush && g.tp > 1 && pending == PEND_DENSE;
+  if (push) xch_push(a, parity, a.comm.att_off, (long long)g.h * g.bp * 2, seq);
   #pragma unroll 1
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
-    if (g.tp > 1) {
+    if (push) {
+      if (!xch_wait_push(a, seq)) return false;
+    } else if (g.tp > 1) {
       if (need_signal) xch_signal_row(a, b, seq);
       if (!xch_wait_row(a, b, seq)) return false;
     }
@@ -133,9 +142,13 @@ KK3_FN bool phase_fold_pending(const StepArgs& a, int pending, bool need_signal,
 // attention exchange -> prefix (assign right after a block push, else add), then the MLP prologue
 KK3_FN bool phase_mlp_prologue(const StepArgs& a, int layer, int nb_after, unsigned seq, int parity, float* fsm) {
   const Geo& g = a.g;
+  const bool push = a.comm_mode == kCommPush && g.tp > 1;
+  if (push) xch_push(a, parity, a.comm.att_off, (long long)g.h * g.bp * 2, seq);
   #pragma unroll 1
   for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
-    if (g.tp > 1) {
+    if (push) {
+      if (!xch_wait_push(a, seq)) return false;
+    } else if (g.tp > 1) {
       xch_signal_row(a, b, seq);
       if (!xch_wait_row(a, b, seq)) return false;
     }
@@ -189,7 +202,7 @@ KK3_FN void phase_mla_rows(const StepArgs& a, int layer, int midx, float* fsm) {
 // host transport it is two phases: kCombineWrite ends after this rank's slot is written (the launch ends there
 // and the host all-reduces the slots), kCombineRead starts from the reduced slot.
 constexpr int kCombineAll = 0, kCombineWrite = 1, kCombineRead = 2;
-KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int parity, float* fsm, int part) {
+KK3_FN bool phase_moe_combine_rows(const StepArgs& a, int layer, unsigned seq, int parity, float* fsm, int part) {
   const Geo& g = a.g;
   float* red = fsm;
   const int nvec = g.lh / 8, hvec = g.h / 8;
@@ -297,6 +310,126 @@ KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int pa
     __syncthreads();
   }
   return true;
+}
+
+// Weighted sum of the K pair outputs of row b, channels 8v .. 8v + 7, in slot order (kimi.py:320-323: each
+// pair's output times its routing weight, accumulated in FP32)
+KK3_DEV void routed_sum8(const StepArgs& a, int b, int v, float (&tot)[8]) {
+  const Geo& g = a.g;
+  const int nvec = g.lh / 8;
+  const float* w = a.s.route_w + (size_t)b * g.K;
+  const uint4* slot0 = reinterpret_cast<const uint4*>(a.s.out_slot + (size_t)b * g.K * g.lh) + v;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) tot[e] = 0.0f;
+  #pragma unroll 1
+  for (int j0 = 0; j0 < g.K; j0 += 8) {
+    uint4 x[8];
+    float wj[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const bool live = j0 + u < g.K;
+      x[u] = live ? __ldcg(slot0 + (size_t)(j0 + u) * nvec) : make_uint4(0, 0, 0, 0);
+      wj[u] = live ? __ldcg(w + j0 + u) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (j0 + u >= g.K) break;
+      float f[8];
+      unpack8(x[u], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) tot[e] += f[e] * wj[u];
+    }
+  }
+}
+
+// MoE combine with the in-kernel transports at TP > 1. The routed sums are computed in B x Q chunk items (Q =
+// min(G / B, lh / 32) per row), item i on CTA i, and every item stores its FP32 chunk into the exp slot of this
+// rank in every rank's buffer (own included); under the push transport every CTA also pushes its share of the
+// shared expert's partial. Then every CTA raises flag [rank][cta] = seq in every buffer, so each SM sends a few
+// KB instead of the row CTAs sending whole rows. The row CTAs wait for all flags and finish as the row path does:
+// FP32 sum of the tp slots in rank order (kimi.py:343-347), latent norm, shared-expert sum.
+KK3_FN bool phase_moe_combine_chunked(const StepArgs& a, int layer, unsigned seq, int parity, float* fsm) {
+  const Geo& g = a.g;
+  float* red = fsm;
+  const int nvec = g.lh / 8, hvec = g.h / 8;
+  if (a.comm_mode == kCommPush) xch_push_stores(a, parity, a.comm.shd_off, (long long)g.h * g.bp * 2);
+  int Q = (int)gridDim.x / g.B;
+  Q = Q < nvec / 4 ? Q : nvec / 4;
+  Q = Q < 1 ? 1 : Q;
+  if ((int)blockIdx.x < g.B * Q) {
+    const int b = blockIdx.x / Q, q = blockIdx.x - b * Q;
+    const int v0 = nvec * q / Q, v1 = nvec * (q + 1) / Q;
+    const size_t off = ((size_t)g.rank * g.B + b) * g.lh;
+    for (int v = v0 + threadIdx.x; v < v1; v += kThreads) {
+      float tot[8];
+      routed_sum8(a, b, v, tot);
+      const float4 lo = make_float4(tot[0], tot[1], tot[2], tot[3]), hi = make_float4(tot[4], tot[5], tot[6], tot[7]);
+      #pragma unroll 1
+      for (int dst = 0; dst < g.tp; ++dst) {
+        float* reg = reinterpret_cast<float*>(a.comm.base[dst] + a.comm.data_off[parity] + a.comm.exp_off) + off + v * 8;
+        *reinterpret_cast<float4*>(reg) = lo;
+        *reinterpret_cast<float4*>(reg + 4) = hi;
+      }
+    }
+  }
+  xch_push_flags(a, seq, false);
+  #pragma unroll 1
+  for (int b = blockIdx.x; b < g.B; b += gridDim.x) {
+    if (!xch_wait_push(a, seq, true)) return false;
+    const float* reg = xlocal<float>(a, parity, a.comm.exp_off);
+    float tot[kRowChunks][8];
+#pragma unroll
+    for (int q = 0; q < kRowChunks; ++q) {
+      const int c = threadIdx.x + q * kThreads;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) tot[q][e] = 0.0f;
+      if (c >= nvec) continue;
+      #pragma unroll 1
+      for (int src = 0; src < g.tp; ++src) {
+        const float* r = reg + ((size_t)src * g.B + b) * g.lh + c * 8;
+        const float4 v0 = __ldcg(reinterpret_cast<const float4*>(r)), v1 = __ldcg(reinterpret_cast<const float4*>(r + 4));
+        tot[q][0] += v0.x; tot[q][1] += v0.y; tot[q][2] += v0.z; tot[q][3] += v0.w;
+        tot[q][4] += v1.x; tot[q][5] += v1.y; tot[q][6] += v1.z; tot[q][7] += v1.w;
+      }
+    }
+    // x3 = rms(bf16(total), latent_norm)
+    float ss[1] = {0.0f};
+#pragma unroll
+    for (int q = 0; q < kRowChunks; ++q)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        tot[q][e] = round_bf(tot[q][e]);
+        ss[0] += tot[q][e] * tot[q][e];
+      }
+    block_sums<1>(ss, red);
+    const float rs = rsqrtf(ss[0] / (float)g.lh + 1e-5f);
+    const bf16* ln = lptr<bf16>(a, layer, KK3_MOE_LATENT_NORM);
+#pragma unroll
+    for (int q = 0; q < kRowChunks; ++q) {
+      const int c = threadIdx.x + q * kThreads;
+      if (c >= nvec) continue;
+      float wf[8], o[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(ln) + c), wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = round_bf(round_bf(tot[q][e] * rs) * wf[e]);
+      *reinterpret_cast<uint4*>(a.s.x3 + (size_t)b * g.lh + c * 8) = pack8(o);
+    }
+#pragma unroll
+    for (int q = 0; q < kRowChunks; ++q) {
+      const int c = threadIdx.x + q * kThreads;
+      if (c >= hvec) continue;
+      float x[8];
+      xch_sum8(a, parity, a.comm.shd_off, b, g.h, c, x);
+      *reinterpret_cast<uint4*>(a.s.shared_red + (size_t)b * g.h + c * 8) = pack8(x);
+    }
+    __syncthreads();
+  }
+  return true;
+}
+
+KK3_FN bool phase_moe_combine(const StepArgs& a, int layer, unsigned seq, int parity, float* fsm, int part) {
+  if (a.g.tp > 1 && a.comm_mode != kCommHost) return phase_moe_combine_chunked(a, layer, seq, parity, fsm);
+  return phase_moe_combine_rows(a, layer, seq, parity, fsm, part);
 }
 
 KK3_FN void phase_head_prologue(const StepArgs& a, int nb, float* fsm) {

@@ -39,6 +39,55 @@ KK3_DEV bool xch_wait_row(const StepArgs& a, int b, unsigned seq) {
   return ok != 0;
 }
 
+// Push transport (kCommPush). The GEMV epilogue stored this rank's partial only into its own slot of its own
+// buffer; at the start of the phase that reads it every CTA copies its 1/G share of that slot (contiguous 16-byte
+// pieces, read from L2) into the same slot of every peer's buffer, fences, and raises flag [rank][cta] = seq in
+// each peer's chunk-push flag array. A reader waits for all G flags of every peer. Many SMs each send a few KB,
+// instead of the epilogues' stores going out from whichever warps finish tiles.
+KK3_DEV unsigned* push_flag_ptr(const StepArgs& a, int dst, int src, int cta) {
+  return reinterpret_cast<unsigned*>(a.comm.base[dst] + a.comm.push_flag_off) + (size_t)src * gridDim.x + cta;
+}
+// this CTA's 1/G share of this rank's slot (sub-region `off`, slot_bytes a multiple of 16) into every peer
+KK3_DEV void xch_push_stores(const StepArgs& a, int parity, long long off, long long slot_bytes) {
+  const Geo& g = a.g;
+  const long long n16 = slot_bytes >> 4;
+  const long long c0 = n16 * blockIdx.x / gridDim.x, c1 = n16 * (blockIdx.x + 1) / gridDim.x;
+  const size_t mine = (size_t)a.comm.data_off[parity] + off + (size_t)g.rank * slot_bytes;
+  const uint4* src = reinterpret_cast<const uint4*>(a.comm.base[g.rank] + mine);
+  for (long long i = c0 + threadIdx.x; i < c1; i += kThreads) {
+    const uint4 v = __ldcg(src + i);
+    #pragma unroll 1
+    for (int dst = 0; dst < g.tp; ++dst)
+      if (dst != g.rank) reinterpret_cast<uint4*>(a.comm.base[dst] + mine)[i] = v;
+  }
+}
+// a whole CTA, after its stores: flag [rank][cta] = seq in the chunk flag array of every rank in [lo, hi) except
+// (when skip_self) this one
+KK3_DEV void xch_push_flags(const StepArgs& a, unsigned seq, bool skip_self) {
+  __threadfence_system();
+  __syncthreads();
+  if ((int)threadIdx.x < a.g.tp && !(skip_self && (int)threadIdx.x == a.g.rank))
+    st_release_sys(push_flag_ptr(a, threadIdx.x, a.g.rank, blockIdx.x), seq);
+}
+// all CTAs: push this rank's slot of sub-region `off` and flag it
+KK3_DEV void xch_push(const StepArgs& a, int parity, long long off, long long slot_bytes, unsigned seq) {
+  xch_push_stores(a, parity, off, slot_bytes);
+  xch_push_flags(a, seq, true);
+}
+// a whole CTA: wait until every peer's (and with self, this rank's too) every CTA flagged exchange `seq`
+KK3_DEV bool xch_wait_push(const StepArgs& a, unsigned seq, bool self = false) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  const int n = a.g.tp * (int)gridDim.x;
+  for (int i = threadIdx.x; i < n; i += kThreads) {
+    const int src = i / (int)gridDim.x, cta = i - src * (int)gridDim.x;
+    if ((self || src != a.g.rank) && !wait_flag_sys(a, push_flag_ptr(a, a.g.rank, src, cta), seq)) ok = 0;
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
 // local region (this rank's buffer), parity p, byte offset `off`
 template <typename T>
 KK3_DEV const T* xlocal(const StepArgs& a, int parity, long long off) {

@@ -120,7 +120,7 @@ KK3_DEV TcPos tc_locate(const TcPlan& p, long long u) {
 constexpr int kTcgLag = 3;   // a stage is refilled once the MMAs of 3 k-steps ago completed
 
 // Run a list of BF16 jobs on the tensor cores (all CTAs, all threads). CTA-level stream-K: CTA c takes k-steps
-// [U c / G, U (c + 1) / G) of the pass (U k-steps, G CTAs), so every CTA streams the same number of weight
+// [U c / G, U (c + 1) / G) of the pass (U k-steps, G = min(CTAs, U)), so every CTA streams the same number of weight
 // bytes; a block whose k-steps span several CTAs is finished by the last of them to arrive, which adds the
 // partials in CTA order (each CTA keeps at most two: its first and its last block). Returns false when a
 // bounded wait gave up (the error word is set; TMEM is released before returning).
@@ -149,8 +149,11 @@ KK3_FN bool run_gemv_tc(const StepArgs& a, const GemvJob* jobs, int njobs, int p
     flags[1] = 1;
   }
   __syncthreads();
-  const long long U = plan.total, G = gridDim.x;
-  const long long rbeg = U * blockIdx.x / G, rend = U * (blockIdx.x + 1) / G;
+  // G = min(grid, U) participating CTAs, so that every range is non-empty: the CTAs between a block's first and
+  // last owner are then exactly its contributors (an empty range would be counted but never arrive)
+  const long long U = plan.total, G = (long long)gridDim.x < U ? (long long)gridDim.x : U;
+  const long long rbeg = (long long)blockIdx.x < G ? U * blockIdx.x / G : U;
+  const long long rend = (long long)blockIdx.x < G ? U * (blockIdx.x + 1) / G : U;
   const long long total_steps = rend - rbeg;
   if (total_steps <= 0) {
     __syncthreads();

@@ -46,7 +46,7 @@ class Config(ctypes.Structure):
         "rank", "device")] + [("timeout_ns", ctypes.c_int64)]
 
 
-COMM_PEER, COMM_HOST = 0, 1   # include/kk3.h KK3_COMM_*
+COMM_PEER, COMM_HOST, COMM_PUSH = 0, 1, 2   # include/kk3.h KK3_COMM_*
 GEMV_AUTO, GEMV_MMA = 0, 1     # include/kk3.h KK3_GEMV_*
 
 

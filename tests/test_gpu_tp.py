@@ -51,6 +51,10 @@ TP_SPECS = [
     ({"kind": "case", "case": "kimi-k3-syn-l8-tp8-b1-s8192"}, "syn-l8-tp8-b1"),
     ({"kind": "case", "case": "kimi-k3-syn-l8-tp8-b8-s8192"}, "syn-l8-tp8-b8"),
     ({"kind": "case", "case": "kimi-k3-syn-l8-tp8-b64-s8192"}, "syn-l8-tp8-b64"),
+    # the push transport (KK3_COMM_PUSH = 2): the projections' partials pushed in per-CTA chunks
+    ({"kind": "small", "batch": 3, "tp": 2, "seed": 11, "comm": 2}, "small-b3-tp2-push"),
+    ({"kind": "case", "case": "kimi-k3-dev-l8-tp2-b8-s8192", "comm": 2}, "dev-l8-tp2-b8-push"),
+    ({"kind": "case", "case": "kimi-k3-syn-l8-tp8-b8-s8192", "comm": 2}, "syn-l8-tp8-b8-push"),
 ]
 
 

@@ -48,7 +48,8 @@ def main() -> int:
     device = torch.device("cuda", rank)
     torch.cuda.set_device(device)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
-    case = make_case(json.loads(args.spec))
+    spec = json.loads(args.spec)
+    case = make_case(spec)
     case["params"].pop("checkpoint", None)
     assert case["tp"] == world, (case["tp"], world)
     group = dist.group.WORLD
@@ -62,6 +63,8 @@ def main() -> int:
             execution = {"rank": rank, "world_size": world, "tp_rank": rank, "ep_rank": 0, "backend": "nccl",
                          "device": str(device), "tp_group": group, "ep_group": None}
             run = gh.load_submission(ROOT / "submission.py", dict(case, execution=execution))
+            if spec.get("comm"):   # another in-kernel exchange transport (include/kk3.h KK3_COMM_*)
+                run.ctx.set_comm_mode(spec["comm"])
             originals = ko.snapshot(values)
             first = {k: v.clone() for k, v in run(values).items()}
             second = run(values)
