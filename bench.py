@@ -149,18 +149,23 @@ try:
 except Exception:
     mx = float("nan")
 with open(path, "w") as out:
-    print("ready", flush=True)
+    i, pw, ready = 0, float("nan"), False
     while True:
-        r, _, _ = select.select([sys.stdin], [], [], 0.001)
-        if r:
-            break
         try:
             sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
             rs = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
-            pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+            if i % 8 == 0:   # power is the slowest query: every 8th sample
+                pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
             out.write(f"{time.time():.6f},{sm},{mx},{pw},{rs}\n")
         except Exception as exc:
             out.write(f"error,{type(exc).__name__}: {exc}\n")
+        i += 1
+        if not ready:   # NVML is warm once the first sample is written
+            print("ready", flush=True)
+            ready = True
+        r, _, _ = select.select([sys.stdin], [], [], 0.001)
+        if r:
+            break
 """
 
 
@@ -267,7 +272,7 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median([s[1] for s in inside]) if inside else None,
                 "sm_max_mhz": inside[0][2] if inside else None, "reasons": sorted(reasons), "samples": len(inside),
-                "power_w_max": max(s[3] for s in inside) if inside else None, "source": self.source,
+                "power_w_max": max((s[3] for s in inside if s[3] == s[3]), default=None), "source": self.source,
                 "samples_total": len(self.samples), "error": self.error}
 
 
@@ -818,7 +823,7 @@ def cpu_baseline_line(args, n: int, case: dict, host_values: dict) -> dict:
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--case", default=None)

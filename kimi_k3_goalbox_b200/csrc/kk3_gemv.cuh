@@ -200,19 +200,63 @@ KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const 
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old != 1) return;
     __syncwarp();   // lane 0's acquire before every lane's loads of the other half
+    // the other half's loads of two n-tiles at a time before their stores: a load after a store through another
+    // pointer cannot be hoisted by the compiler, which made each element one dependent L2 round trip
+    constexpr int C = NT < 2 ? NT : 2;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+    for (int n0 = 0; n0 < NT; n0 += C) {
+      float ov[C][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int row = row0 + r + 8 * (i >> 1);
-        const int col = nt * 8 + 2 * c + (i & 1);
-        if (row >= j.rows || col >= j.ncols) continue;
-        const float mv = round_bf(acc[0][nt][i]), ov = ld_cg_f32(other + nt * 4 + i);
-        const float g = half ? ov : mv, u = half ? mv : ov;
-        reinterpret_cast<bf16*>(j.out)[(size_t)col * j.ldo + row] = f2bf(situ_f(g, u));
+      for (int k = 0; k < C; ++k) {
+        const float4 t = __ldcg(reinterpret_cast<const float4*>(other + (n0 + k) * 4));   // L2: another SM wrote it
+        ov[k][0] = t.x; ov[k][1] = t.y; ov[k][2] = t.z; ov[k][3] = t.w;
+      }
+#pragma unroll
+      for (int k = 0; k < C; ++k) {
+        const int nt = n0 + k;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = row0 + r + 8 * (i >> 1);
+          const int col = nt * 8 + 2 * c + (i & 1);
+          if (row >= j.rows || col >= j.ncols) continue;
+          const float mv = round_bf(acc[0][nt][i]);
+          const float g = half ? ov[k][i] : mv, u = half ? mv : ov[k][i];
+          reinterpret_cast<bf16*>(j.out)[(size_t)col * j.ldo + row] = f2bf(situ_f(g, u));
+        }
       }
     }
     if (lane == 0) atomicExch(cnt, 0);
+    return;
+  }
+  if (j.epi == EPI_ROUTED) {
+    // prefix[col, row] += bf16(bf16(acc) + shared_red[col, row]) (kimi.py:325-329): all loads first (see the
+    // situ pair above), then the stores
+    bf16* prefix = reinterpret_cast<bf16*>(j.out);
+    const bf16* shared = reinterpret_cast<const bf16*>(j.aux);
+    constexpr int C = NT < 2 ? NT : 2;   // n-tiles whose loads are issued together
+#pragma unroll
+    for (int n0 = 0; n0 < NT; n0 += C) {
+      float pv[C][4], sv[C][4];
+#pragma unroll
+      for (int k = 0; k < C; ++k)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = row0 + r + 8 * (i >> 1), col = (n0 + k) * 8 + 2 * c + (i & 1);
+          const bool ok = row < j.rows && col < j.ncols;
+          const size_t o = (size_t)col * j.ldo + row;
+          pv[k][i] = ok ? bf2f(prefix[o]) : 0.0f;
+          sv[k][i] = ok ? bf2f(shared[o]) : 0.0f;
+        }
+#pragma unroll
+      for (int k = 0; k < C; ++k)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = row0 + r + 8 * (i >> 1), col = (n0 + k) * 8 + 2 * c + (i & 1);
+          if (row >= j.rows || col >= j.ncols) continue;
+          const float out = round_bf(round_bf(acc[0][n0 + k][i]) + sv[k][i]);
+          prefix[(size_t)col * j.ldo + row] = f2bf(pv[k][i] + out);
+        }
+    }
     return;
   }
   if (j.epi == EPI_EXCHANGE) {
@@ -268,13 +312,6 @@ KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const 
           const bf16 b = f2bf(v);
           reinterpret_cast<bf16*>(j.out)[o] = b;
           reinterpret_cast<__half*>(j.out2)[(size_t)col * j.ldo + row] = __float2half_rn(bf2f(b));
-          break;
-        }
-        case EPI_ROUTED: {
-          bf16* prefix = reinterpret_cast<bf16*>(j.out);
-          const bf16* shared = reinterpret_cast<const bf16*>(j.aux);
-          const float out = round_bf(round_bf(v) + bf2f(shared[o]));
-          prefix[o] = f2bf(bf2f(prefix[o]) + out);
           break;
         }
         default:

@@ -78,6 +78,11 @@ def test_tp_band_multi_gpu(spec):
     tp = spec_tp(spec)
     if gpus() < tp:
         pytest.skip(f"needs {tp} GPUs")
+    # the ranks run in child processes on GPUs 0..tp-1: give back what earlier tests of this process cached on
+    # GPU 0 (the full-width cases leave ~120 GB in torch's allocator cache)
+    import gc
+    gc.collect()
+    torch.cuda.empty_cache()
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", MASTER_ADDR="127.0.0.1")
     cmd = ["timeout", "-k", "30", "900", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={tp}", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
