@@ -148,7 +148,9 @@ KK3_DEV int xdst_gemv_hi(const StepArgs& a) { return a.comm_mode == kCommPeer ? 
 
 // Fused epilogue for one complete 16-row tile. acc[mt][nt][i]: rows row0 + r (+8 for i >= 2), column
 // nt*8 + 2c + (i & 1).
-template <int NT, int MT>
+// LD: n-tiles whose epilogue loads (the other situ half, the residual operands) are issued together (the warp
+// engine keeps it at 2 for its register budget).
+template <int NT, int MT, int LD = (NT < 2 ? NT : 2)>
 KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const float (&acc)[MT][NT][4], int parity) {
   const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
   const int row0 = tile * 16;
@@ -202,7 +204,7 @@ KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const 
     __syncwarp();   // lane 0's acquire before every lane's loads of the other half
     // the other half's loads of two n-tiles at a time before their stores: a load after a store through another
     // pointer cannot be hoisted by the compiler, which made each element one dependent L2 round trip
-    constexpr int C = NT < 2 ? NT : 2;
+    constexpr int C = LD;
 #pragma unroll
     for (int n0 = 0; n0 < NT; n0 += C) {
       float ov[C][4];
@@ -233,7 +235,7 @@ KK3_DEV void gemv_epilogue(const StepArgs& a, const GemvJob& j, int tile, const 
     // situ pair above), then the stores
     bf16* prefix = reinterpret_cast<bf16*>(j.out);
     const bf16* shared = reinterpret_cast<const bf16*>(j.aux);
-    constexpr int C = NT < 2 ? NT : 2;   // n-tiles whose loads are issued together
+    constexpr int C = LD;   // n-tiles whose loads are issued together
 #pragma unroll
     for (int n0 = 0; n0 < NT; n0 += C) {
       float pv[C][4], sv[C][4];

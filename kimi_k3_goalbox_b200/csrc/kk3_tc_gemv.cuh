@@ -20,10 +20,11 @@
 // At the end of a segment (the CTA's k-steps of one block) warps 0-3 read the accumulator (TMEM lane = block
 // row) with tcgen05.ld. A block done by one CTA goes straight to the epilogue; otherwise each contributor
 // writes its FP32 partial to the stream-K bank and the last to arrive sums them in CTA order (deterministic)
-// before the epilogue. The epilogue
-// is the GEMV engine's: the 128 x N block is staged in shared memory and eight warps each run
-// gemv_epilogue on one 16-row tile in the mma.sync fragment layout, so every fused epilogue (exchange
-// stores, situ pairs, logits keys, ...) is shared with the mma.sync path.
+// before the epilogue. The 128 x N block is staged column-major in shared memory. Plain stores (bf16, FP32 sigmoid, latent) go out
+// column by column in 16-byte pieces; every other epilogue is the GEMV engine's gemv_epilogue, run by eight
+// warps on one 16-row tile each in the mma.sync fragment layout, so the fused epilogues (exchange stores,
+// situ pairs, logits keys, residual update) are shared with the mma.sync path. The reduction and the epilogue
+// are separate (not inlined) functions, so their registers do not spill in the streaming loop.
 #pragma once
 #include "kk3_tcgen05.cuh"
 
@@ -37,8 +38,8 @@ struct TcGemvShape {
   static constexpr int N = NT * 8;                               // batch columns of the MMA
   static constexpr int kStageB = N * 128;                        // bytes of one activation stage
   static constexpr int kStage = kTcgStageA + kStageB;            // a multiple of 1024: stages stay swizzle-aligned
-  static constexpr int kStagingStride = N + 4;                   // floats per staged result row
-  static constexpr int kStaging = kTcgRows * kStagingStride * 4;
+  static constexpr int kStagingStride = kTcgRows + 4;            // floats per staged result column (column-major)
+  static constexpr int kStaging = N * kStagingStride * 4;
   static constexpr int kCtl = 1024;                              // mbarriers, TMEM address, pass plan
   static constexpr int kStagesFit = (kExpSmem - kStaging - kCtl) / kStage;   // within the step's dynamic smem
   static constexpr int S = kStagesFit > 8 ? 8 : kStagesFit;
@@ -119,6 +120,214 @@ KK3_DEV TcPos tc_locate(const TcPlan& p, long long u) {
 
 constexpr int kTcgLag = 3;   // a stage is refilled once the MMAs of 3 k-steps ago completed
 
+// Profiling contexts only (warp_ts allocated): CTA-level event k of this pass into the per-warp stamp slot k of
+// the CTA (0 start, 1 first k-step's data landed, 2 last k-step's MMAs issued, 3 last segment's MMAs done,
+// 4 its partial published or staged, 5 after its reduction, 6 after its epilogue, 7 pass end).
+KK3_DEV void tc_stamp(const StepArgs& a, int k) {
+  if (a.s.warp_ts && threadIdx.x == 0) {
+    const int ph = kk3_cur_phase;
+    if (ph >= 0 && ph < kArrivePhases) a.s.warp_ts[((size_t)ph * gridDim.x + blockIdx.x) * kWarps + k] = globaltimer();
+  }
+}
+
+// Sum of a split block's partials into the staging block (all threads; CTA order, deterministic). Not inlined, so
+// that its registers (all loads of four contributors in flight per thread) never spill in the streaming loop.
+template <int NT>
+KK3_FN void tc_reduce_block(const float* part_base, float* staging, long long first, long long lastc,
+                            long long bstart, long long U, long long G) {
+  constexpr int N = NT * 8, E = kTcgRows * N / 4 / kThreads;   // float4 elements per thread
+  static_assert(E * kThreads == kTcgRows * N / 4, "reduction elements per thread");
+  const int ncon = (int)(lastc - first) + 1;
+  float4 acc[E];
+#pragma unroll
+  for (int k = 0; k < E; ++k) acc[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int k0 = 0; k0 < ncon; k0 += 4) {
+    float4 v[4][E];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const long long c = first + k0 + t;
+      const float4* src = reinterpret_cast<const float4*>(
+          part_base + ((size_t)c * 2 + ((U * c / G >= bstart) ? 0 : 1)) * kTcgRows * N);
+#pragma unroll
+      for (int k = 0; k < E; ++k)
+        v[t][k] = k0 + t < ncon ? __ldcg(src + threadIdx.x + k * kThreads) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+#pragma unroll
+      for (int k = 0; k < E; ++k) {
+        acc[k].x += v[t][k].x; acc[k].y += v[t][k].y; acc[k].z += v[t][k].z; acc[k].w += v[t][k].w;
+      }
+  }
+#pragma unroll
+  for (int k = 0; k < E; ++k) {
+    const int e = threadIdx.x + k * kThreads, q = e / kTcgRows, row = e - q * kTcgRows;   // partial: [N/4][128]
+    float* col = staging + (4 * q) * TcGemvShape<NT>::kStagingStride + row;   // staging: [N][128 + 4]
+    col[0] = acc[k].x;
+    col[TcGemvShape<NT>::kStagingStride] = acc[k].y;
+    col[2 * TcGemvShape<NT>::kStagingStride] = acc[k].z;
+    col[3 * TcGemvShape<NT>::kStagingStride] = acc[k].w;
+  }
+}
+
+// Epilogue of one finished 128 x N block from the staging buffer (all threads). Each kind of epilogue has its own
+// compact loop over 8-row pieces of one output column (16-byte stores where the row stride allows): the block
+// is finished once per pass by whichever CTA completes it, so its code runs cold from the instruction cache,
+// and the GEMV engine's per-tile gemv_epilogue (every kind, fully unrolled for the fragment layout) took up to
+// ~25 us there. The arithmetic and rounding are the same as gemv_epilogue's (kimi.py:304, :308, :317, :325-331,
+// :343-347). sflags: 8 ints of shared memory for the situ pairing. Not inlined, like tc_reduce_block.
+template <int NT>
+KK3_FN void tc_epilogue_block(const StepArgs& a, const GemvJob& j, int block, const float* staging, int parity,
+                              volatile int* sflags) {
+  constexpr int N = NT * 8, SS = TcGemvShape<NT>::kStagingStride;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row0 = block * kTcgRows;
+  const int nrows = j.rows - row0 < kTcgRows ? j.rows - row0 : kTcgRows;
+  const bool vec = (j.ldo & 7) == 0;   // 8-row pieces are 16-byte aligned in the output
+  const int epi = j.epi;
+  if (epi == EPI_SITU_GATE || epi == EPI_SITU_UP) {
+    // publish this half's bf16-rounded tiles ([N][16] floats per 16-row tile), count the halves of each tile;
+    // the second half to arrive forms situ(gate, up) (kimi.py:194-196)
+    const int half = epi == EPI_SITU_UP ? 1 : 0;
+    const int ntiles = (nrows + 15) >> 4;
+    float* buf = reinterpret_cast<float*>(const_cast<void*>(j.aux));
+    const size_t tf = (size_t)16 * N;
+    #pragma unroll 1
+    for (int e = tid; e < ntiles * N * 4; e += kThreads) {   // float4 of rows 4q .. 4q + 3 of column n, tile t
+      const int t = e / (N * 4), rem = e - t * N * 4, n = rem >> 2, q = rem & 3;
+      const float4 v = *reinterpret_cast<const float4*>(staging + n * SS + t * 16 + q * 4);
+      *reinterpret_cast<float4*>(buf + ((size_t)half * j.tiles + block * 8 + t) * tf + n * 16 + q * 4) =
+          make_float4(round_bf(v.x), round_bf(v.y), round_bf(v.z), round_bf(v.w));
+    }
+    __syncthreads();
+    int* cnt = reinterpret_cast<int*>(j.out2) + block * 8;
+    if (tid < ntiles) {
+      __threadfence();
+      sflags[tid] = atom_add_acq_rel_gpu(cnt + tid, 1) == 1;
+    }
+    __syncthreads();
+    __threadfence();
+    #pragma unroll 1
+    for (int p = tid; p < ntiles * N * 2; p += kThreads) {   // 8-row piece h of column n, tile t
+      const int t = p / (N * 2), rem = p - t * N * 2, n = rem >> 1, h = rem & 1;
+      if (!sflags[t] || n >= j.ncols) continue;
+      const int rr = t * 16 + h * 8;
+      const float* oth = buf + ((size_t)(1 - half) * j.tiles + block * 8 + t) * tf + n * 16 + h * 8;
+      const float4 o0 = __ldcg(reinterpret_cast<const float4*>(oth)), o1 = __ldcg(reinterpret_cast<const float4*>(oth + 4));
+      const float ov[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
+      float res[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float mv = round_bf(staging[n * SS + rr + e]);
+        res[e] = situ_f(half ? ov[e] : mv, half ? mv : ov[e]);
+      }
+      bf16* out = reinterpret_cast<bf16*>(j.out) + (size_t)n * j.ldo + row0 + rr;
+      if (vec && rr + 8 <= nrows) {
+        *reinterpret_cast<uint4*>(out) = pack8(res);
+      } else {
+        for (int e = 0; e < 8 && rr + e < nrows; ++e) out[e] = f2bf(res[e]);
+      }
+    }
+    __syncthreads();
+    if (tid < ntiles && sflags[tid]) atomicExch(cnt + tid, 0);
+    __syncthreads();
+    return;
+  }
+  if (epi == EPI_LOGITS) {
+    // argmax keys: warp w takes columns w, w + 16, ...; per column the largest (value, lowest index) key of the
+    // block's rows, one atomicMax per column (kimi.py:218-227, :331)
+    #pragma unroll 1
+    for (int n = warp; n < N; n += kWarps) {
+      unsigned long long best = 0ull;
+      #pragma unroll 1
+      for (int r = lane; r < nrows; r += 32) {
+        const unsigned long long k = argmax_key(round_bf(staging[n * SS + r]), (unsigned)(row0 + r + j.aux_off));
+        best = k > best ? k : best;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+      }
+      if (lane == 0 && n < j.ncols && best != 0ull)
+        atomicMax(reinterpret_cast<unsigned long long*>(const_cast<void*>(j.aux)) + n, best);
+    }
+  }
+  #pragma unroll 1
+  for (int p = tid; p < N * 16; p += kThreads) {   // 8-row piece of column n
+    const int n = p >> 4, rr = (p & 15) * 8;
+    if (rr >= nrows || (n >= j.ncols && epi != EPI_EXCHANGE)) continue;
+    float v[8];
+    const float4 s0 = *reinterpret_cast<const float4*>(staging + n * SS + rr);
+    const float4 s1 = *reinterpret_cast<const float4*>(staging + n * SS + rr + 4);
+    v[0] = s0.x; v[1] = s0.y; v[2] = s0.z; v[3] = s0.w; v[4] = s1.x; v[5] = s1.y; v[6] = s1.z; v[7] = s1.w;
+    const size_t o = (size_t)n * j.ldo + row0 + rr;
+    const bool full = vec && rr + 8 <= nrows;
+    if (epi == EPI_EXCHANGE) {
+      // this rank's slot of every destination's region (xch_index layout; rows = ldo channels, a multiple of
+      // 16); padding columns carry the zero products of the zero activation columns
+      const uint4 b = pack8(v);
+      const size_t e = xch_index(a.g, a.g.rank, n, row0 + rr, j.ldo);
+      for (int dst = xdst_gemv_lo(a); dst < xdst_gemv_hi(a); ++dst)
+        *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(xregion(a, dst, parity) + j.aux_off) + e) = b;
+    } else if (epi == EPI_ROUTED) {
+      // prefix += bf16(bf16(acc) + shared) (kimi.py:325-329)
+      bf16* prefix = reinterpret_cast<bf16*>(j.out) + o;
+      const bf16* shared = reinterpret_cast<const bf16*>(j.aux) + o;
+      float pv[8], sv[8], res[8];
+      if (full) {
+        unpack8(*reinterpret_cast<const uint4*>(prefix), pv);
+        unpack8(*reinterpret_cast<const uint4*>(shared), sv);
+      } else {
+        for (int e = 0; e < 8; ++e) {
+          pv[e] = rr + e < nrows ? bf2f(prefix[e]) : 0.0f;
+          sv[e] = rr + e < nrows ? bf2f(shared[e]) : 0.0f;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) res[e] = pv[e] + round_bf(round_bf(v[e]) + sv[e]);
+      if (full) {
+        *reinterpret_cast<uint4*>(prefix) = pack8(res);
+      } else {
+        for (int e = 0; e < 8 && rr + e < nrows; ++e) prefix[e] = f2bf(res[e]);
+      }
+    } else if (epi == EPI_SIGMOID_F32 || epi == EPI_LOGITS) {
+      float* d = reinterpret_cast<float*>(j.out) + o;
+      float r[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) r[e] = epi == EPI_LOGITS ? round_bf(v[e]) : sigmoidf_(v[e]);
+      if (full) {
+        *reinterpret_cast<float4*>(d) = make_float4(r[0], r[1], r[2], r[3]);
+        *reinterpret_cast<float4*>(d + 4) = make_float4(r[4], r[5], r[6], r[7]);
+      } else {
+        for (int e = 0; e < 8 && rr + e < nrows; ++e) d[e] = r[e];
+      }
+    } else if (epi == EPI_STORE_BF16 || epi == EPI_LATENT) {
+      bf16* d = reinterpret_cast<bf16*>(j.out) + o;
+      const uint4 b = pack8(v);
+      float r[8];
+      unpack8(b, r);
+      if (full) {
+        *reinterpret_cast<uint4*>(d) = b;
+      } else {
+        for (int e = 0; e < 8 && rr + e < nrows; ++e) d[e] = f2bf(r[e]);
+      }
+      if (epi == EPI_LATENT) {   // FP16 copy of the bf16-rounded latent for the MXFP4 path
+        __half* h = reinterpret_cast<__half*>(j.out2) + o;
+        if (full) {
+          __half2 hh[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) hh[e] = __floats2half2_rn(r[2 * e], r[2 * e + 1]);
+          *reinterpret_cast<uint4*>(h) = *reinterpret_cast<const uint4*>(hh);
+        } else {
+          for (int e = 0; e < 8 && rr + e < nrows; ++e) h[e] = __float2half_rn(r[e]);
+        }
+      }
+    }
+  }
+  __syncthreads();   // staging is rewritten by the next segment
+}
+
 // Run a list of BF16 jobs on the tensor cores (all CTAs, all threads). CTA-level stream-K: CTA c takes k-steps
 // [U c / G, U (c + 1) / G) of the pass (U k-steps, G = min(CTAs, U)), so every CTA streams the same number of weight
 // bytes; a block whose k-steps span several CTAs is finished by the last of them to arrive, which adds the
@@ -170,6 +379,7 @@ KK3_FN bool run_gemv_tc(const StepArgs& a, const GemvJob* jobs, int njobs, int p
   const unsigned tmem = *reinterpret_cast<volatile unsigned*>(ctl + 8 * S);
   const unsigned idesc = idesc_bf16_f32(N);
   const unsigned long long pol = l2_evict_first_policy();
+  tc_stamp(a, 0);
 
   // ---- producer cursor over k-steps [rbeg, rend)
   TcPos pp = tc_locate(plan, rbeg);
@@ -231,6 +441,8 @@ KK3_FN bool run_gemv_tc(const StepArgs& a, const GemvJob* jobs, int njobs, int p
     cp_async_wait_g<P>();   // this thread's copies of `step` landed
     fence_async_smem();
     __syncthreads();
+    if (step == 0) tc_stamp(a, 1);
+    if (step + 1 == total_steps) tc_stamp(a, 2);
     const int st = (int)(step % S);
     if (tid == 0 && ok) {
       tc_fence_after();
@@ -247,6 +459,8 @@ KK3_FN bool run_gemv_tc(const StepArgs& a, const GemvJob* jobs, int njobs, int p
       // end of a segment: wait for its MMAs, read the accumulator (warps 0-3: TMEM lanes = block rows)
       if (!mbar_wait(a, bar0 + 8 * st, (unsigned)((step / S) & 1))) ok = false;
       tc_fence_after();
+      const bool last_seg = step + 1 == total_steps;
+      if (last_seg) tc_stamp(a, 3);
       const GemvJob& j = jobs[cp.job];
       const long long bstart = plan.ubase[cp.job] + (long long)cp.block * kend;
       const long long first = owner_of(bstart, U, G), lastc = owner_of(bstart + kend - 1, U, G);
@@ -259,11 +473,9 @@ KK3_FN bool run_gemv_tc(const StepArgs& a, const GemvJob* jobs, int njobs, int p
           float v[16];
           tmem_ld16(tmem + ((unsigned)(warp * 32) << 16) + h * 16, v);
           tmem_ld_wait();
-          if (whole) {
-            float* srow = staging + row * Sh::kStagingStride + h * 16;
+          if (whole) {   // staging is column-major: lanes (consecutive rows) hit consecutive banks
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              *reinterpret_cast<float4*>(srow + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            for (int q = 0; q < 16; ++q) staging[(h * 16 + q) * Sh::kStagingStride + row] = v[q];
           } else {
 #pragma unroll
             for (int q = 0; q < 4; ++q)   // lanes write consecutive rows
@@ -275,6 +487,7 @@ KK3_FN bool run_gemv_tc(const StepArgs& a, const GemvJob* jobs, int njobs, int p
       // the accumulator is free for the next segment and the partial / staging is written; a wait that gave up
       // on any thread stops the pass on every thread
       ok = __syncthreads_and(ok) != 0;
+      if (last_seg) tc_stamp(a, 4);
       bool run_epi = ok && whole;
       if (ok && !whole) {
         const int blk_id = plan.bbase[cp.job] + cp.block;
@@ -287,48 +500,15 @@ KK3_FN bool run_gemv_tc(const StepArgs& a, const GemvJob* jobs, int njobs, int p
         run_epi = flags[0] != 0;
         if (run_epi) {
           __threadfence();
-          // sum the contributors' partials in CTA order (their first or last segment)
-          const int ncon = (int)(lastc - first) + 1;
-          for (int e = tid; e < kTcgRows * N / 4; e += kThreads) {
-            const int q = e / kTcgRows, row = e - q * kTcgRows;
-            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            for (int k0 = 0; k0 < ncon; k0 += 4) {
-              float4 v[4];
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                v[t] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (k0 + t < ncon) {
-                  const long long c = first + k0 + t;
-                  const int slot = (U * c / G >= bstart) ? 0 : 1;
-                  v[t] = __ldcg(reinterpret_cast<const float4*>(part_base + ((size_t)c * 2 + slot) * kTcgRows * N) +
-                                (size_t)q * kTcgRows + row);
-                }
-              }
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                acc.x += v[t].x; acc.y += v[t].y; acc.z += v[t].z; acc.w += v[t].w;
-              }
-            }
-            *reinterpret_cast<float4*>(staging + row * Sh::kStagingStride + 4 * q) = acc;
-          }
+          tc_reduce_block<NT>(part_base, staging, first, lastc, bstart, U, G);
           if (tid == 0) atomicExch(cnt_base + blk_id, 0);
           __syncthreads();
+          if (last_seg) tc_stamp(a, 5);
         }
       }
       if (run_epi) {
-        // eight warps, one 16-row tile each, in the mma.sync fragment layout of gemv_epilogue
-        const int wt = warp & 7, tile = cp.block * 8 + wt;
-        if (warp < 8 && tile * 16 < j.rows) {
-          const int r = lane >> 2, c = lane & 3;
-          float acc[1][NT][4];
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              acc[0][nt][i] = staging[(wt * 16 + r + 8 * (i >> 1)) * Sh::kStagingStride + nt * 8 + 2 * c + (i & 1)];
-          gemv_epilogue<NT, 1>(a, j, tile, acc, parity);
-        }
-        __syncthreads();   // staging is rewritten by the next segment
+        tc_epilogue_block<NT>(a, j, cp.block, staging, parity, reinterpret_cast<volatile int*>(ctl + Sh::kCtl - 64));
+        if (last_seg) tc_stamp(a, 6);
       }
       seg_first = false;
       // next segment
@@ -355,6 +535,7 @@ KK3_FN bool run_gemv_tc(const StepArgs& a, const GemvJob* jobs, int njobs, int p
   if (tid == 0)
     for (int i = 0; i < S; ++i) mbar_inval(bar0 + 8 * i);
   __syncthreads();
+  tc_stamp(a, 7);
   return flags[1] != 0;
 }
 
