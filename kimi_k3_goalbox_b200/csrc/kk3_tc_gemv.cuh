@@ -15,8 +15,9 @@
 //  - each thread waits for its own copies, makes them visible to the async proxy (fence.proxy.async: the
 //    copies are generic-proxy writes and the tensor core reads through the async proxy), then the CTA
 //    synchronises and thread 0 issues four K = 16 MMAs and commits them to the stage's mbarrier;
-//  - a stage is refilled only after the mbarrier of the MMAs that read it completed, three k-steps later, so
-//    the MMA latency stays off the copy path; the copies run S - 3 k-steps ahead of the MMAs, across blocks.
+//  - a stage is refilled only after the mbarrier of the MMAs that read it completed, two k-steps later, so
+//    the MMA latency stays off the copy path; the copies run S - 2 k-steps ahead of the MMAs, across blocks
+//    (a k-step streams in ~1 us while its four MMAs finish in well under that).
 // At the end of a segment (the CTA's k-steps of one block) warps 0-3 read the accumulator (TMEM lane = block
 // row) with tcgen05.ld. A block done by one CTA goes straight to the epilogue; otherwise each contributor
 // writes its FP32 partial to the stream-K bank and the last to arrive sums them in CTA order (deterministic)
@@ -118,7 +119,7 @@ KK3_DEV TcPos tc_locate(const TcPlan& p, long long u) {
   return t;
 }
 
-constexpr int kTcgLag = 3;   // a stage is refilled once the MMAs of 3 k-steps ago completed
+constexpr int kTcgLag = 2;   // a stage is refilled once the MMAs of 2 k-steps ago completed
 
 // Profiling contexts only (warp_ts allocated): CTA-level event k of this pass into the per-warp stamp slot k of
 // the CTA (0 start, 1 first k-step's data landed, 2 last k-step's MMAs issued, 3 last segment's MMAs done,
