@@ -618,22 +618,28 @@ struct ExpertPhase {
   long long expert_scales;   // bytes of scales per expert (rows * K / 32)
 };
 
-// Expert epilogue for one complete 16-row tile. `dst[e]` is the output row of this lane's column 2c + e in
-// the chunk (null when the chunk has fewer pairs): the FP16 activation row of the pair (MT == 2) or the
-// pair's bf16 slot-output row (MT == 1); it is resolved once per chunk, not per tile.
-template <int MT>
+// Expert epilogue for one complete tile. `dst[e]` is the output row of this lane's column 2c + e in the chunk
+// (null when the chunk has fewer pairs), resolved once per chunk, not per tile. Gate/up (DOWN false, MT == 2):
+// rows tile*16 + ..., the FP16 activation row of the pair gets situ(gate, up). Down: the pair's bf16 slot-output
+// row; with MT == 2 the tile is two 16-row halves (rows tile*32 + 16 mt + ...), one per "matrix".
+template <int MT, bool DOWN>
 KK3_DEV void expert_epilogue(int rows, int tile, void* const (&dst)[2], const float (&acc)[MT][1][4]) {
   const int lane = threadIdx.x & 31, r = lane >> 2;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int row = tile * 16 + r + 8 * (i >> 1);
     void* d = dst[i & 1];
-    if (d == nullptr || row >= rows) continue;
-    if (MT == 2) {
+    if (d == nullptr) continue;
+    if (!DOWN) {
+      const int row = tile * 16 + r + 8 * (i >> 1);
+      if (row >= rows) continue;
       const float g = round_bf(acc[0][0][i]), u = round_bf(acc[MT - 1][0][i]);
       reinterpret_cast<__half*>(d)[row] = __float2half_rn(round_bf(situ_f(g, u)));
     } else {
-      reinterpret_cast<bf16*>(d)[row] = f2bf(acc[0][0][i]);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const int row = tile * 16 * MT + mt * 16 + r + 8 * (i >> 1);
+        if (row < rows) reinterpret_cast<bf16*>(d)[row] = f2bf(acc[mt][0][i]);
+      }
     }
   }
 }
@@ -696,16 +702,20 @@ KK3_DEV uint4 ld_cg16(const void* p) {
   return v;
 }
 
-template <int MT>
+// MT matrices per unit: gate and up (DOWN false), or the down projection as one matrix (MT == 1) or as two
+// adjacent 16-row tiles streamed together (MT == 2, "row pairs": codes[1] / scales[1] point 16 rows further,
+// tiles count 32-row pairs), which shares each activation load and each unit's fixed costs between two tiles.
+template <int MT, bool DOWN = (MT == 1)>
 KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
   extern __shared__ __align__(1024) unsigned char kk3_dyn_smem[];
-  __shared__ unsigned long long s_mask;    // MT == 2: batch rows staged (bit b = latent row b)
-  __shared__ int s_first, s_count;        // MT == 1: pairs [s_first, s_first + s_count) staged
-  __shared__ int s_rowmap[kMaxBatch];     // MT == 2: cache slot i holds latent row s_rowmap[i]
+  __shared__ unsigned long long s_mask;    // gate/up: batch rows staged (bit b = latent row b)
+  __shared__ int s_first, s_count;        // down: pairs [s_first, s_first + s_count) staged
+  __shared__ int s_rowmap[kMaxBatch];     // gate/up: cache slot i holds latent row s_rowmap[i]
   constexpr int kCode = 16 * 64;                  // code bytes per matrix and unit pair
   // scale bytes per matrix and unit pair: the 16-byte window (four pairs) of every row, or, when a row's scales
   // are not a multiple of 16 bytes, the tile's whole scale block (16 rows x K/32 bytes, contiguous)
   constexpr int kScale = MT == 2 ? 256 : 512;
+  constexpr int kTileRows = DOWN ? 16 * MT : 16;   // weight rows a tile index advances by
   constexpr int kSlot = MT * (kCode + kScale);
   constexpr int S = (kExpRing / kSlot) > 12 ? 12 : (kExpRing / kSlot);
   static_assert(S >= 4, "ring too shallow");
@@ -759,7 +769,7 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
       chunk_pairs(cbeg / per_chunk, fp_lo, np_lo);
       chunk_pairs((cend - 1) / per_chunk, fp_hi, np_hi);
       const int p_lo = fp_lo, p_hi = fp_hi + np_hi > p_lo ? fp_hi + np_hi : p_lo;
-      if (MT == 2) {
+      if (!DOWN) {
         for (int p = p_lo; p < p_hi; ++p) mask |= 1ull << pair_batch_row(p);
         int n = 0;
         for (int b = 0; b < a.g.B; ++b) {
@@ -786,7 +796,7 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
     const int total = s_count * pieces_per_row;
     for (int q = threadIdx.x; q < total; q += kThreads) {
       const int i = q / pieces_per_row, col = q - i * pieces_per_row;
-      const __half* src = (MT == 2) ? a.s.latent_p + (size_t)s_rowmap[i] * a.g.lh
+      const __half* src = !DOWN ? a.s.latent_p + (size_t)s_rowmap[i] * a.g.lh
                                     : a.s.act_p + (size_t)(s_first + i) * a.g.inter;
       cp_async16_g(xcache + i * xstride + col * 16, src + col * 8);
     }
@@ -838,10 +848,10 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
     const size_t e = p_e;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
-      p_code[mt] = ph.codes[mt] + e * ph.expert_codes + (size_t)(p_tile * 16 + prow) * rowbytes + p_kp * 64 + pq * 16;
+      p_code[mt] = ph.codes[mt] + e * ph.expert_codes + (size_t)(p_tile * kTileRows + prow) * rowbytes + p_kp * 64 + pq * 16;
     if (scl_lane)
       p_scl = ph.scales[scl_mt] + e * ph.expert_scales +
-              (swin ? (size_t)(p_tile * 16 + scl_i) * sbytes : (size_t)p_tile * 16 * sbytes + scl_i * 16);
+              (swin ? (size_t)(p_tile * kTileRows + scl_i) * sbytes : (size_t)p_tile * kTileRows * sbytes + scl_i * 16);
   };
   // A scale window (the scales of 4 pairs, or of the whole tile) is copied once, with the first of its pairs the
   // warp issues, into the scale area of window slot (window count % S); the consumer counts windows the same way.
@@ -892,7 +902,7 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
   int c_fp = 0, c_np = 0;
   // lanes without a pair read a cached row (or a real global row when nothing fits the cache)
   const unsigned char* xdead = cap > 0 ? xcache
-                                       : reinterpret_cast<const unsigned char*>(MT == 2 ? a.s.latent_p : a.s.act_p);
+                                       : reinterpret_cast<const unsigned char*>(!DOWN ? a.s.latent_p : a.s.act_p);
   const unsigned char* xp = xdead;
   int x_off = 0;             // byte offset of this lane's row in the cache (when cached)
   bool x_shared = cap > 0;   // every lane's row of the current chunk is in the cache (shared-memory loads)
@@ -905,7 +915,7 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
       out_row[e] = nullptr;
       if (col >= c_np) continue;
       const int pc = c_fp + col;
-      if (MT == 2) {
+      if (!DOWN) {
         out_row[e] = a.s.act_p + (size_t)pc * a.g.inter;
       } else {
         int slot = __ldcg(a.s.pair_slot + pc);
@@ -918,7 +928,7 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
     bool cached = cap > 0;
     if (r < c_np) {
       const int p = c_fp + r;
-      if (MT == 2) {
+      if (!DOWN) {
         const int b = pair_batch_row(p);
         cached = (xmask >> b) & 1ull;
         x_off = cached ? __popcll(xmask & ((1ull << b) - 1ull)) * xstride : 0;
@@ -1007,7 +1017,7 @@ KK3_FN void run_experts(const StepArgs& a, const ExpertPhase& ph) {
                stream_k_fixup<1, MT>(a, a.s.fix_part, a.s.fix_cnt + c_chunk * tiles + c_tile, gw, tile_beg <= ubeg,
                                      pt, first, lastw, UP, GW, acc);
       }
-      if (done) expert_epilogue<MT>(ph.rows, c_tile, out_row, acc);
+      if (done) expert_epilogue<MT, DOWN>(ph.rows, c_tile, out_row, acc);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll

@@ -533,6 +533,11 @@ KK3_DEV bool gemv_pass(const StepArgs& a, const GemvJob* jobs, int njobs, int pa
   return true;
 }
 
+// the MXFP4 down projection runs as row pairs (run_experts<2, true>) when its 32-row tiles and scale layout fit
+KK3_DEV bool down_row_pairs(const Geo& g) {
+  return g.lh % 32 == 0 && (g.inter % 512 == 0 || g.inter <= 512);
+}
+
 // ---- job lists of the GEMV phases (built identically by every thread) ---------------------------------
 
 KK3_DEV void job_init(GemvJob& j, const bf16* w, int rows, int K, const bf16* x, int ldx, int ncols, int epi, void* out,
@@ -855,9 +860,16 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
       KK3_PHASE_END();
       if (KK3_RUN) {
         KK3_BUILD({
+          // row pairs (two 16-row tiles per unit) where the pair's scales fit the two-matrix scale layout: a
+          // 16-byte window per row (K % 512 == 0) or the tile's whole block (K <= 512)
+          const bool rp = down_row_pairs(g);
           sph.codes[0] = sph.codes[1] = lptr<uint8_t>(a, l, KK3_MOE_DOWN_BLOCKS);
           sph.scales[0] = sph.scales[1] = lptr<uint8_t>(a, l, KK3_MOE_DOWN_SCALES);
-          sph.rows = g.lh; sph.K = g.inter; sph.tiles = g.lh / 16; sph.ksteps = g.inter / 64;
+          if (rp) {
+            sph.codes[1] += (size_t)16 * (g.inter / 2);
+            sph.scales[1] += (size_t)16 * (g.inter / 32);
+          }
+          sph.rows = g.lh; sph.K = g.inter; sph.tiles = g.lh / (rp ? 32 : 16); sph.ksteps = g.inter / 64;
           sph.expert_codes = (long long)g.lh * g.inter / 2; sph.expert_scales = (long long)g.lh * g.inter / 32;
           job_init(sj[0], lptr<bf16>(a, l, KK3_MOE_SHARED_DOWN), g.h, g.sinter, a.s.shared_act, g.sinter, g.B,
                    EPI_EXCHANGE, nullptr, g.h);
@@ -870,7 +882,8 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         if (!gemv_pass<NT>(a, sj, 1, x_moe & 1, 1)) KK3_FAIL();
         if (g.tp > 1) __threadfence_system();
         if (blockIdx.x == 0 && threadIdx.x == 0) sub_stamp(a, phase, 0);
-        run_experts<1>(a, sph);
+        if (down_row_pairs(g)) run_experts<2, true>(a, sph);
+        else run_experts<1>(a, sph);
       }
       KK3_PHASE_END();
       if (host_comm) {

@@ -67,14 +67,14 @@ def test_harness_protocol(which, seeds):
             perf_inputs = ko.make_inputs(case, 99, "cuda")
             times = _measure(run, perf_inputs, warmup=2, reps=5)
             assert all(t > 0 for t in times)
+            # CUPTI records kernel activity into device buffers it allocates when a profiler session starts. With
+            # torch's allocator cache holding nearly all of the GPU after the full-width oracle and the earlier
+            # tests, the sessions recorded no GPU activity at all (the launch API call itself was recorded), so the
+            # cache is released first
+            import gc
+            gc.collect()
+            torch.cuda.empty_cache()
             names = gh.audit_launches(run, perf_inputs)
-            if not names:
-                # profiler sessions that recorded no GPU activity at all (not only none of ours), with the launch
-                # API call itself recorded, were seen on the full-width case when it ran after the other GPU tests
-                # of the suite, never when it ran first; the audit is repeated once so that the test reports a
-                # missing kernel, not a missing trace
-                names = gh.audit_launches(run, perf_inputs)
-                print(f"[{case['id']}] first profiler session recorded no GPU activity; second session: {names}")
             print(f"[{case['id']}] cuda-event p50 {statistics.median(times) * 1e3:.1f} us, launches {names}")
             assert 1 <= len(names) <= case["max_gpu_launches"], names
             assert "kk3_step_kernel" in names[0], names
