@@ -118,7 +118,7 @@ struct Comm {
 };
 
 constexpr int kGemvAuto = 0, kGemvMma = 1;
-constexpr int kAttnAuto = 0, kAttnMma = 1;   // MLA attention engine (kk3_set_attn_engine)
+constexpr int kAttnMma = 0, kAttnTc = 1;   // MLA attention engine (kk3_set_attn_engine)
 
 struct StepArgs {
   Geo g;

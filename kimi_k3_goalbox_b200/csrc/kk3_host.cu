@@ -111,7 +111,7 @@ static bool plan_mla_tc(Geo& g, int grid) {
 }
 
 static void plan_mla(Geo& g, int grid, int engine) {
-  if (engine == kAttnAuto && plan_mla_tc(g, grid)) return;
+  if (engine == kAttnTc && plan_mla_tc(g, grid)) return;
   plan_mla_mma(g, grid);
 }
 
@@ -209,12 +209,12 @@ static void plan_step(const kk3_config* cfg, int sms, unsigned char* base, bool 
   const int nt = g.B <= 8 ? 1 : (g.B <= 16 ? 2 : (g.B <= 32 ? 4 : 8));
   pl->nt = nt;
   g.bp = 8 * nt;
-  // the default plan (tensor cores where the geometry allows), and the warp-level plan kk3_set_attn_engine can
-  // switch to: the partials buffer holds the larger chunk count, the shared memory the warp-level item's
-  Geo gm = g;
-  plan_mla(gm, sms, kAttnMma);
-  plan_mla(g, sms, kAttnAuto);
-  const int part_chunks = g.mla_chunks > gm.mla_chunks ? g.mla_chunks : gm.mla_chunks;
+  // the default plan (the warp-level engine), and the tensor-core plan kk3_set_attn_engine can switch to: the
+  // partials buffer holds the larger chunk count
+  Geo gt = g;
+  plan_mla(gt, sms, kAttnTc);
+  plan_mla(g, sms, kAttnMma);
+  const int part_chunks = g.mla_chunks > gt.mla_chunks ? g.mla_chunks : gt.mla_chunks;
   const long long gw = (long long)sms * kWarps;
   g.fix_bank = 2ll * gw * (2 * nt * 128);
   {
@@ -299,7 +299,7 @@ static void plan_step(const kk3_config* cfg, int sms, unsigned char* base, bool 
   // the mirror word stands in for mapped host memory when the caller gives none (kk3_init replaces it)
   s.err_host = err_mirror;
   if (comm_inline) c.base[g.rank] = comm;
-  const int HR = gm.mla_mt * 16;
+  const int HR = g.mla_mt * 16;
   size_t sm = mla_smem_bytes(HR);
   const size_t sm_row = (512 + (size_t)(g.h > g.lh ? g.h : g.lh)) * 4 + 64;
   const size_t sm_abs = ((size_t)g.B * 128 + 4 * 16 * 128) * 4;
@@ -448,9 +448,9 @@ extern "C" int kk3_set_comm_mode(kk3_ctx* x, int mode) {
 }
 
 extern "C" int kk3_set_attn_engine(kk3_ctx* x, int engine) {
-  if (!x || (engine != KK3_ATTN_AUTO && engine != KK3_ATTN_MMA)) return KK3_ERR_ARG;
+  if (!x || (engine != KK3_ATTN_MMA && engine != KK3_ATTN_TC)) return KK3_ERR_ARG;
   // both plans were sized at kk3_init (the partials buffer holds the larger chunk count)
-  plan_mla(x->g, x->grid, engine == KK3_ATTN_MMA ? kAttnMma : kAttnAuto);
+  plan_mla(x->g, x->grid, engine == KK3_ATTN_TC ? kAttnTc : kAttnMma);
   return KK3_OK;
 }
 

@@ -19,6 +19,12 @@
 // The 512 FP32 columns of a whole O do not fit in TMEM next to S, so the two halves of the value dims are
 // separate, adjacent items (the second CTA's copies of the same cache rows come from L2); both compute the same S.
 // Every wait is bounded; TMEM is held for the phase and released at its end.
+//
+// Selected with kk3_set_attn_engine(KK3_ATTN_TC); the warp-level engine stays the default because it is faster at
+// this step's head counts (12-96 per rank). Measured in the step (B200): a sub-tile takes ~4.7 us, of which the 36
+// N = 32 products of S take ~1.8 us (each instruction re-reads the 4 KB query block from shared memory, so small N
+// runs far below the tensor pipe's rate) and the serial softmax ~1.9 us; with the value halves an item also walks
+// twice the sub-tiles. mla_attend at dev-l4: 329 us against 146 us for the warp-level engine.
 #pragma once
 #include "kk3_phases.cuh"
 #include "kk3_tc_gemv.cuh"

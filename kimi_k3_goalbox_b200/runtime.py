@@ -48,7 +48,7 @@ class Config(ctypes.Structure):
 
 COMM_PEER, COMM_HOST, COMM_PUSH = 0, 1, 2   # include/kk3.h KK3_COMM_*
 GEMV_AUTO, GEMV_MMA = 0, 1     # include/kk3.h KK3_GEMV_*
-ATTN_AUTO, ATTN_MMA = 0, 1     # include/kk3.h KK3_ATTN_*
+ATTN_MMA, ATTN_TC = 0, 1       # include/kk3.h KK3_ATTN_*
 BUF_ABSORBED = 11              # include/kk3.h KK3_BUF_ABSORBED (after a step: the last MLA layer's attended latent)
 
 
@@ -380,7 +380,7 @@ class StepContext:
             raise KK3Error(rc, "kk3_set_gemv_engine")
 
     def set_attn_engine(self, engine: int) -> None:
-        """ATTN_AUTO (the MLA attention on tcgen05) or ATTN_MMA (the warp-level mma.sync engine), include/kk3.h."""
+        """ATTN_MMA (the warp-level mma.sync MLA attention, the default) or ATTN_TC (tcgen05), include/kk3.h."""
         rc = self.lib.kk3_set_attn_engine(self.handle, engine)
         if rc != 0:
             raise KK3Error(rc, "kk3_set_attn_engine")

@@ -165,8 +165,8 @@ def _grade_floats(case, values, expected, out, label):
     ("kimi-k3-dev-l4-tp1-b8-s8192", 23, None),            # 96 heads: two groups of 48, 4-stage ring
 ])
 def test_tensor_core_attention_against_the_mma_engine(which, seed, reset):
-    """The MLA attention on tcgen05 (kk3_set_attn_engine KK3_ATTN_AUTO: S and O in TMEM, one thread per head row
-    for the softmax) against the warp-level mma.sync engine on the same inputs: both steps within the band, and
+    """The MLA attention on tcgen05 (kk3_set_attn_engine KK3_ATTN_TC: S and O in TMEM, one thread per head row for
+    the softmax) against the default warp-level mma.sync engine on the same inputs: both steps within the band, and
     the attended latents (the combine's bf16 output, scratch KK3_BUF_ABSORBED) close. They are not bit-identical:
     the engines sum in FP32 in different orders and round the probabilities to bf16 against different running
     maxima."""
@@ -185,7 +185,7 @@ def test_tensor_core_attention_against_the_mma_engine(which, seed, reset):
             values["reset"] = torch.tensor(reset, device="cuda")
         expected = ko.reference(case, values, serial=True)
         outs, lat = {}, {}
-        for engine in (runtime.ATTN_AUTO, runtime.ATTN_MMA):
+        for engine in (runtime.ATTN_TC, runtime.ATTN_MMA):
             ctx = StepContext(case)
             try:
                 ctx.set_attn_engine(engine)
@@ -196,8 +196,8 @@ def test_tensor_core_attention_against_the_mma_engine(which, seed, reset):
             finally:
                 ctx.close()
             _grade_floats(case, values, expected, outs[engine], f"{which} engine {engine}")
-        d_lat = gh.rel_l2(lat[runtime.ATTN_AUTO], lat[runtime.ATTN_MMA])
-        d_log = gh.rel_l2(outs[runtime.ATTN_AUTO]["logits"], outs[runtime.ATTN_MMA]["logits"])
+        d_lat = gh.rel_l2(lat[runtime.ATTN_TC], lat[runtime.ATTN_MMA])
+        d_log = gh.rel_l2(outs[runtime.ATTN_TC]["logits"], outs[runtime.ATTN_MMA]["logits"])
         print(f"{which}: attended latent rel-L2 tcgen05 vs mma.sync {d_lat:.2e}, logits {d_log:.2e}")
         assert d_lat < 1e-2, d_lat
         assert d_log < 1e-2, d_log
