@@ -707,6 +707,7 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
     KK3_PHASE_END();
     if (KK3_RUN) {
       KK3_BUILD(sjn = attn_proj_jobs(a, l, mla, sj));
+      if (!mla) kda_state_prefetch(a, l);   // the next phase's recurrent states into L2
       if (!gemv_pass<NT>(a, sj, sjn, 0, 0, phase)) KK3_FAIL();
     }
     KK3_PHASE_END();

@@ -458,17 +458,34 @@ KK3_FN void kda_item(const StepArgs& a, int layer, int kidx, int b, int hh, floa
   const float4 dk = *reinterpret_cast<const float4*>(decay + lane * 4);
   const float4 kk = *reinterpret_cast<const float4*>(kn + lane * 4);
   const float4 qq = *reinterpret_cast<const float4*>(qn + lane * 4);
+  // The warp's eight value rows are independent: their two reductions each run as one interleaved butterfly
+  // (the same xor order as warp_sum), so the shuffle latencies of the rows overlap instead of adding up.
+  float pred[8], o[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int v = warp * 8 + i;
-    float4 s = rows[i];
+    float4& s = rows[i];
     s.x *= dk.x; s.y *= dk.y; s.z *= dk.z; s.w *= dk.w;
-    const float pred = warp_sum(s.x * kk.x + s.y * kk.y + s.z * kk.z + s.w * kk.w);
-    const float err = (sv[v] - pred) * sb;
+    pred[i] = s.x * kk.x + s.y * kk.y + s.z * kk.z + s.w * kk.w;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pred[i] += __shfl_xor_sync(0xffffffffu, pred[i], off);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float4& s = rows[i];
+    const float err = (sv[warp * 8 + i] - pred[i]) * sb;
     s.x += err * kk.x; s.y += err * kk.y; s.z += err * kk.z; s.w += err * kk.w;
-    const float o = warp_sum(s.x * qq.x + s.y * qq.y + s.z * qq.z + s.w * qq.w);
-    *reinterpret_cast<float4*>(st_out + (size_t)v * dh + lane * 4) = s;
-    if (lane == 0) outv[v] = o;
+    o[i] = s.x * qq.x + s.y * qq.y + s.z * qq.z + s.w * qq.w;
+    *reinterpret_cast<float4*>(st_out + (size_t)(warp * 8 + i) * dh + lane * 4) = s;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] += __shfl_xor_sync(0xffffffffu, o[i], off);
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) outv[warp * 8 + i] = o[i];
   }
   __syncthreads();
   if (stamp) sub_stamp(a, kk3_cur_phase, 4);
@@ -490,6 +507,22 @@ KK3_FN void kda_item(const StepArgs& a, int layer, int kidx, int b, int hh, floa
   }
   __syncthreads();
   if (stamp) sub_stamp(a, kk3_cur_phase, 5);
+}
+
+// Issued by thread 0 of every CTA at the start of the KDA layer's projection phase: an L2 prefetch of the FP32
+// recurrent state (64 KB per (row, head)) of each item this CTA will run in the next phase (items it =
+// blockIdx + k * grid, state index it = b * hr + head), so the items' first loads hit L2 instead of HBM. Rows
+// that are reset read no state.
+// Only when the phase's items fit one wave: with several waves the prefetch measured no gain in the KDA phase and
+// slowed the projection phase it runs in (dev-l4: +18 us per step).
+KK3_DEV void kda_state_prefetch(const StepArgs& a, int layer) {
+  const Geo& g = a.g;
+  if (threadIdx.x != 0 || g.B * g.hr > (int)gridDim.x) return;
+  const float* st = lptr<float>(a, layer, KK3_KDA_RECURRENT_STATE);
+  const bool* reset = reinterpret_cast<const bool*>(a.ptr[KK3_RESET]);
+  #pragma unroll 1
+  for (int it = blockIdx.x; it < g.B * g.hr; it += gridDim.x)
+    if (!reset[it / g.hr]) prefetch_l2(st + (size_t)it * 128 * 128, 128u * 128u * 4u);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -540,18 +573,18 @@ KK3_FN void mla_absorb_item(const StepArgs& a, int layer, int hh, int cq, float*
 }
 
 // shared-memory layout of one attention item
+constexpr int kRowDims = 576;   // 512 latent + 64 rope dims of a cached position (kv_lora_rank 512, rope 64)
 constexpr int kRowK = 584;   // padded row (elements) of a cached position: 512 latent + 64 rope + 8 pad
 constexpr int kRowP = 40;    // padded row of the BF16 probability tile (32 positions + 8)
 constexpr int kRowS = 33;    // padded row of the FP32 score tile
 
 // Pipeline depth (position sub-tiles in flight) and k-split of the score product for a head-tile count:
-// three stages while they fit next to the query tile, the 576-wide score dot products split over up to four
-// warps per (head tile, 8 positions) so that all 16 warps take part.
+// three stages while they fit next to the query tile; the 576-wide score dot products of each (head tile,
+// 8 positions) split KQ ways so that the MT x 4 x KQ score items use the 16 warps (MT = 1: 16 items of 9
+// k-steps, 2: 16 of 18, 3: 12 of 36, 4: 16 of 36). Splitting MT = 3 four ways (48 items of 9, three per warp)
+// measured slower (score sub-phase 2.7 against 1.7 us per 32 positions).
 __host__ __device__ inline int mla_stages(int HR) { return HR <= 64 ? 3 : 2; }
-__host__ __device__ inline int mla_kq(int MT) {
-  const int q = kWarps / (MT * 4);
-  return q < 1 ? 1 : (q > 4 ? 4 : q);
-}
+__host__ __device__ constexpr int mla_kq(int MT) { return MT == 1 ? 4 : (MT == 2 ? 2 : 1); }
 __host__ __device__ inline size_t mla_smem_bytes(int HR) {
   return (size_t)(HR + mla_stages(HR) * kMlaPos) * kRowK * 2 + (size_t)mla_kq(HR / 16) * HR * kRowS * 4 +
          (size_t)HR * kRowP * 2 + 3 * HR * 4 + 64;
@@ -626,7 +659,7 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
   constexpr int HR = MT * 16;
   const bool stamp = ph >= 0 && b == 0 && chunk == 0 && h0 == 0 && tid == 0;   // sub-phase stamps of one item
   if (stamp) sub_stamp(a, ph, 0);
-  const int KQ = mla_kq(MT), kper = (g.kr + g.rd) / 16 / KQ;   // 36 k-steps of 16, split KQ ways
+  constexpr int KQ = mla_kq(MT), KPER = kRowDims / 16 / KQ;   // 36 k-steps of 16, split KQ ways
   bf16* Qs = reinterpret_cast<bf16*>(smem);                         // [HR][kRowK]
   bf16* Ks = Qs + HR * kRowK;                                       // [NS][32][kRowK]
   float* Sp = reinterpret_cast<float*>(Ks + NS * kMlaPos * kRowK);   // [KQ][HR][kRowS] k-partial scores
@@ -689,23 +722,46 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
     __syncthreads();
     if (stamp && s < 2) sub_stamp(a, ph, 2 + 4 * s);
     // k-partial scores: items (k-quarter, head tile, 8-position n-tile)
+#pragma unroll 1
     for (int it = warp; it < MT * 4 * KQ; it += kWarps) {
       const int kq = it % KQ, mt = (it / KQ) >> 2, nt = (it / KQ) & 3;
-      // two accumulators (even / odd k-steps) so consecutive MMAs do not wait on each other
-      float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sacc2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      for (int ks = kq * kper; ks < (kq + 1) * kper; ks += 2) {
-        unsigned af[4], bfr[2];
-        ldsm_x4(af, Qs + (mt * 16 + (lane & 15)) * kRowK + ks * 16 + (lane >> 4) * 8);
-        ldsm_x2(bfr, Kc + (nt * 8 + (lane & 7)) * kRowK + ks * 16 + ((lane >> 3) & 1) * 8);
-        mma_bf16(sacc, af[0], af[1], af[2], af[3], bfr[0], bfr[1]);
-        if (ks + 1 < (kq + 1) * kper) {
-          ldsm_x4(af, Qs + (mt * 16 + (lane & 15)) * kRowK + (ks + 1) * 16 + (lane >> 4) * 8);
-          ldsm_x2(bfr, Kc + (nt * 8 + (lane & 7)) * kRowK + (ks + 1) * 16 + ((lane >> 3) & 1) * 8);
-          mma_bf16(sacc2, af[0], af[1], af[2], af[3], bfr[0], bfr[1]);
-        }
-      }
+      const bf16* qrow = Qs + (mt * 16 + (lane & 15)) * kRowK + kq * KPER * 16 + (lane >> 4) * 8;
+      const bf16* krow = Kc + (nt * 8 + (lane & 7)) * kRowK + kq * KPER * 16 + ((lane >> 3) & 1) * 8;
+      float sacc[4];
+      if constexpr (MT <= 2) {
+        // 9 or 18 k-steps, fully unrolled over four accumulators: the shared-memory loads of later k-steps are
+        // issued while earlier MMAs run (score sub-phase 1.0 -> 0.6 us per 32 positions at MT = 1)
+        float acc4[4][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) sacc[i] += sacc2[i];
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc4[c][i] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < KPER; ++k) {
+          unsigned af[4], bfr[2];
+          ldsm_x4(af, qrow + k * 16);
+          ldsm_x2(bfr, krow + k * 16);
+          mma_bf16(acc4[k & 3], af[0], af[1], af[2], af[3], bfr[0], bfr[1]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sacc[i] = (acc4[0][i] + acc4[1][i]) + (acc4[2][i] + acc4[3][i]);
+      } else {
+        // 36 k-steps with the O accumulators of MT >= 3 head tiles live: two accumulators (even / odd k-steps),
+        // not unrolled (unrolled, the registers spill)
+        float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
+        for (int k = 0; k < KPER; k += 2) {
+          unsigned af[4], bfr[2];
+          ldsm_x4(af, qrow + k * 16);
+          ldsm_x2(bfr, krow + k * 16);
+          mma_bf16(s0, af[0], af[1], af[2], af[3], bfr[0], bfr[1]);
+          ldsm_x4(af, qrow + (k + 1) * 16);
+          ldsm_x2(bfr, krow + (k + 1) * 16);
+          mma_bf16(s1, af[0], af[1], af[2], af[3], bfr[0], bfr[1]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sacc[i] = s0[i] + s1[i];
+      }
       float* sp = Sp + (size_t)kq * HR * kRowS;
       sp[(mt * 16 + r) * kRowS + nt * 8 + 2 * c] = sacc[0];
       sp[(mt * 16 + r) * kRowS + nt * 8 + 2 * c + 1] = sacc[1];
@@ -714,23 +770,46 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
     }
     __syncthreads();
     if (stamp && s < 2) sub_stamp(a, ph, 3 + 4 * s);
-    // online softmax, one warp per head row, one lane per position (k-partials summed in order)
-    for (int hh = warp; hh < HR; hh += kWarps) {
-      const bool valid = (t0 + lane) < p1 && (t0 + lane) < T && h0 + hh < g.hr;
-      float sum = 0.0f;
-      for (int q = 0; q < KQ; ++q) sum += Sp[((size_t)q * HR + hh) * kRowS + lane];
-      const float sv = valid ? sum * scale : -INFINITY;
-      const float mt_ = warp_max(sv);
-      const float mold = mrun[hh];
-      const float mnew = fmaxf(mold, mt_);
-      const float p = valid ? expf(sv - mnew) : 0.0f;
-      const float ps = warp_sum(p);
-      Ps[hh * kRowP + lane] = f2bf(p);
+    // online softmax: warp w takes head rows w, w + 16, ... (MT of them, HR = 16 MT), one lane per position; the
+    // rows' reductions are interleaved so that their shuffle chains overlap (k-partials summed in order)
+    {
+      float sv[MT], mx[MT];
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        const int hh = warp + kWarps * i;
+        const bool valid = (t0 + lane) < p1 && (t0 + lane) < T && h0 + hh < g.hr;
+        float sum = 0.0f;
+#pragma unroll
+        for (int q = 0; q < KQ; ++q) sum += Sp[((size_t)q * HR + hh) * kRowS + lane];
+        sv[i] = valid ? sum * scale : -INFINITY;
+        mx[i] = sv[i];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < MT; ++i) mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], o));
+      float mnew[MT], pv[MT];
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        const int hh = warp + kWarps * i;
+        mnew[i] = fmaxf(mrun[hh], mx[i]);
+        pv[i] = sv[i] == -INFINITY ? 0.0f : expf(sv[i] - mnew[i]);
+        Ps[hh * kRowP + lane] = f2bf(pv[i]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < MT; ++i) pv[i] += __shfl_xor_sync(0xffffffffu, pv[i], o);
       if (lane == 0) {
-        const float al = (mold == -INFINITY) ? 0.0f : expf(mold - mnew);
-        alpha[hh] = (mnew == -INFINITY) ? 1.0f : al;
-        lrun[hh] = lrun[hh] * alpha[hh] + ps;
-        mrun[hh] = mnew;
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+          const int hh = warp + kWarps * i;
+          const float mold = mrun[hh];
+          const float al = (mold == -INFINITY) ? 0.0f : expf(mold - mnew[i]);
+          alpha[hh] = (mnew[i] == -INFINITY) ? 1.0f : al;
+          lrun[hh] = lrun[hh] * alpha[hh] + pv[i];
+          mrun[hh] = mnew[i];
+        }
       }
     }
     __syncthreads();
