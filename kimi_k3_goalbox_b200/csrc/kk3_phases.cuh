@@ -875,25 +875,44 @@ KK3_FN void mla_combine_row_item(const StepArgs& a, int layer, int b, int hh, fl
   const int stride = g.kr + 2;
   const float* base = a.s.mla_part + (((size_t)b * g.mla_chunks) * g.hr + hh) * stride;
   const size_t cstride = (size_t)g.hr * stride;
-  float* lat = sm;              // [512]
-  float* wgt = sm + 512;        // [chunks]
-  float* misc = sm + 512 + 64;  // [2]
-  if (tid == 0) {
-    float M = -INFINITY;
-    for (int i = 0; i < nck; ++i) M = fmaxf(M, ld_cg_f32(base + i * cstride));
-    float Lsum = 0.0f;
-    for (int i = 0; i < nck; ++i) {
-      const float m = ld_cg_f32(base + i * cstride);
-      const float w = (m == -INFINITY) ? 0.0f : expf(m - M);
-      wgt[i] = w;
-      Lsum += w * ld_cg_f32(base + i * cstride + 1);
+  float* lat = sm;                // [512]
+  float* wgt = sm + 512;          // [chunks <= 64]
+  float* misc = sm + 512 + 64;    // [2]
+  float* lsum = sm + 512 + 128;   // [chunks <= 64]: l of each chunk
+  if (tid < 32) {
+    // warp 0: every lane loads the (m, l) of chunks lane and lane + 32 at once (a loop of dependent loads by one
+    // thread took most of the item at 65 chunks); L is summed in chunk order by lane 0
+    float m0 = -INFINITY, m1 = -INFINITY;
+    if (tid < nck) {
+      m0 = ld_cg_f32(base + tid * cstride);
+      lsum[tid] = ld_cg_f32(base + tid * cstride + 1);
     }
-    misc[0] = 1.0f / Lsum;
+    if (tid + 32 < nck) {
+      m1 = ld_cg_f32(base + (tid + 32) * cstride);
+      lsum[tid + 32] = ld_cg_f32(base + (tid + 32) * cstride + 1);
+    }
+    const float M = warp_max(fmaxf(m0, m1));
+    if (tid < nck) wgt[tid] = (m0 == -INFINITY) ? 0.0f : expf(m0 - M);
+    if (tid + 32 < nck) wgt[tid + 32] = (m1 == -INFINITY) ? 0.0f : expf(m1 - M);
+    __syncwarp();
+    if (tid == 0) {
+      float Lsum = 0.0f;
+      for (int i = 0; i < nck; ++i) Lsum += wgt[i] * lsum[i];
+      misc[0] = 1.0f / Lsum;
+    }
   }
   __syncthreads();
   for (int cc = tid; cc < g.kr; cc += kThreads) {
+    // 16 chunk loads in flight, summed in chunk order
     float acc = 0.0f;
-    for (int i = 0; i < nck; ++i) acc += wgt[i] * ld_cg_f32(base + i * cstride + 2 + cc);
+    for (int i0 = 0; i0 < nck; i0 += 16) {
+      float v[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) v[k] = i0 + k < nck ? ld_cg_f32(base + (size_t)(i0 + k) * cstride + 2 + cc) : 0.0f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        if (i0 + k < nck) acc += wgt[i0 + k] * v[k];
+    }
     lat[cc] = round_bf(acc * misc[0]);
   }
   __syncthreads();
