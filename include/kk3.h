@@ -232,16 +232,6 @@ int kk3_set_comm_mode(kk3_ctx* ctx, int mode);
 #define KK3_GEMV_MMA 1
 int kk3_set_gemv_engine(kk3_ctx* ctx, int engine);
 
-/* The engine of the MLA split-K attention (kimi.py:274-280). KK3_ATTN_MMA (the default): the warp-level
- * mma.sync engine (items of up to 64 heads, accumulators in registers). KK3_ATTN_TC: tcgen05.mma kind::f16 on the
- * tensor cores (M = 128 head rows, S and the FP32 accumulator O in TMEM, items split by head group and value
- * half); measured slower at this step's head counts and kept as the comparison engine. The two sum in FP32 in
- * different orders and round the probabilities against different running maxima, so their outputs are close but
- * not bit-identical. No counterpart in the reference. Takes effect at the next step. */
-#define KK3_ATTN_MMA 0
-#define KK3_ATTN_TC 1
-int kk3_set_attn_engine(kk3_ctx* ctx, int engine);
-
 /* Single-process testing aid: use an existing device allocation of kk3_exchange_bytes() bytes as rank r's
  * exchange buffer instead of an IPC mapping (no counterpart in the reference). */
 int kk3_debug_set_peer(kk3_ctx* ctx, int r, void* device_ptr);

@@ -55,9 +55,6 @@ struct Geo {
   int mla_mt;         // 16-row head tiles per head group of the MLA attention (<= 4)
   int mla_groups;     // head groups: ceil(ceil(hr / 16) / mla_mt)
   int bp;             // batch padded to the step's n-tile width (8 * NT): the bf16 exchange regions' batch stride
-  int mla_tc;         // 1: the MLA attention runs on the tensor cores (kk3_tc_attn.cuh), 0: the warp-level engine
-  int mla_hg;         // tensor-core attention: head rows per group (a multiple of 8; mla_groups groups)
-  int mla_ns;         // tensor-core attention: ring stages of 32-position sub-tiles
 };
 
 // scratch buffers (device pointers owned by the context)
@@ -118,7 +115,6 @@ struct Comm {
 };
 
 constexpr int kGemvAuto = 0, kGemvMma = 1;
-constexpr int kAttnMma = 0, kAttnTc = 1;   // MLA attention engine (kk3_set_attn_engine)
 
 struct StepArgs {
   Geo g;

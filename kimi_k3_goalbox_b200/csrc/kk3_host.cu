@@ -8,7 +8,6 @@
 #include <new>
 
 #include "kk3_phases.cuh"
-#include "kk3_tc_attn.cuh"
 
 namespace kk3 {
 // one instantiation per batch tile count, each in its own translation unit (kk3_kernel_nt*.cu)
@@ -68,11 +67,10 @@ struct kk3_ctx {
   void* buf_ptr[KK3_BUF_COUNT] = {};
 };
 
-// MLA attention work split of the warp-level engine: heads in groups of at most four 16-row tiles (the
-// accumulators of a group stay in registers), and each batch row's attended positions in chunks so that
-// rows x chunks x groups items fill one wave of the grid.
-static void plan_mla_mma(Geo& g, int grid) {
-  g.mla_tc = 0;
+// MLA attention work split: heads in groups of at most four 16-row tiles (the accumulators of a group stay
+// in registers), and each batch row's attended positions in chunks so that rows x chunks x groups items fill
+// one wave of the grid.
+static void plan_mla(Geo& g, int grid) {
   const int tiles = (g.hr + 15) / 16;
   g.mla_groups = (tiles + 3) / 4;
   g.mla_mt = (tiles + g.mla_groups - 1) / g.mla_groups;
@@ -82,37 +80,6 @@ static void plan_mla_mma(Geo& g, int grid) {
   len = (len + kMlaPos - 1) / kMlaPos * kMlaPos;
   g.mla_chunk_len = len;
   g.mla_chunks = (g.ctx + 1 + len - 1) / len;
-}
-
-// The tensor-core engine's split (kk3_tc_attn.cuh): the heads in as few groups of at most 128 rows as leave a ring
-// of at least four 32-position sub-tiles next to the group's query rows in shared memory, two value halves per
-// (row, chunk, group), and chunks so that rows x chunks x groups x 2 items fill one wave of the grid. False when
-// the geometry has no such plan (the latent and rope widths are the item's fixed shapes).
-static bool plan_mla_tc(Geo& g, int grid) {
-  if (g.kr != 512 || g.rd != 64 || g.hr < 1) return false;
-  int groups = 1, hg = 0;
-  for (; groups <= 8; ++groups) {
-    const int per = (g.hr + groups - 1) / groups;
-    hg = (per + 7) / 8 * 8;
-    if (hg <= 128 && ta_stages(hg) >= 4) break;
-  }
-  if (groups > 8) return false;
-  g.mla_tc = 1;
-  g.mla_groups = groups;
-  g.mla_hg = hg;
-  g.mla_ns = ta_stages(hg);
-  int chunks = grid / (g.B * groups * 2);
-  chunks = chunks < 1 ? 1 : (chunks > 64 ? 64 : chunks);
-  int len = (g.ctx + 1 + chunks - 1) / chunks;
-  len = (len + kMlaPos - 1) / kMlaPos * kMlaPos;
-  g.mla_chunk_len = len;
-  g.mla_chunks = (g.ctx + 1 + len - 1) / len;
-  return true;
-}
-
-static void plan_mla(Geo& g, int grid, int engine) {
-  if (engine == kAttnTc && plan_mla_tc(g, grid)) return;
-  plan_mla_mma(g, grid);
 }
 
 static int cuda_fail(cudaError_t e, const char* what) {
@@ -209,12 +176,7 @@ static void plan_step(const kk3_config* cfg, int sms, unsigned char* base, bool 
   const int nt = g.B <= 8 ? 1 : (g.B <= 16 ? 2 : (g.B <= 32 ? 4 : 8));
   pl->nt = nt;
   g.bp = 8 * nt;
-  // the default plan (the warp-level engine), and the tensor-core plan kk3_set_attn_engine can switch to: the
-  // partials buffer holds the larger chunk count
-  Geo gt = g;
-  plan_mla(gt, sms, kAttnTc);
-  plan_mla(g, sms, kAttnMma);
-  const int part_chunks = g.mla_chunks > gt.mla_chunks ? g.mla_chunks : gt.mla_chunks;
+  plan_mla(g, sms);
   const long long gw = (long long)sms * kWarps;
   g.fix_bank = 2ll * gw * (2 * nt * 128);
   {
@@ -274,7 +236,7 @@ static void plan_step(const kk3_config* cfg, int sms, unsigned char* base, bool 
       {(void**)&s.og, B * (size_t)g.qdim * 2}, {(void**)&s.fa, B * g.d * 2}, {(void**)&s.beta, B * g.hr * 2},
       {(void**)&s.attn_in, B * (size_t)g.hr * g.vd * 2}, {(void**)&s.mla_qan, B * g.qr * 2},
       {(void**)&s.mla_q, B * (size_t)g.hr * (g.nr + g.rd) * 2}, {(void**)&s.absorbed, B * (size_t)g.hr * g.kr * 2},
-      {(void**)&s.mla_part, B * (size_t)part_chunks * g.hr * (g.kr + 2) * 4},
+      {(void**)&s.mla_part, B * (size_t)g.mla_chunks * g.hr * (g.kr + 2) * 4},
       {(void**)&s.dense_act, B * (size_t)(g.dinter > 0 ? g.dinter : 64) * 2}, {(void**)&s.scores, B * g.E * 4},
       {(void**)&s.latent, B * g.lh * 2}, {(void**)&s.latent_p, B * g.lh * 2},
       {(void**)&s.shared_act, B * (size_t)(g.sinter > 0 ? g.sinter : 64) * 2}, {(void**)&s.route_ids, B * g.K * 4},
@@ -444,13 +406,6 @@ extern "C" int kk3_exchange_layout(kk3_ctx* x, long long* offsets) {
 extern "C" int kk3_set_comm_mode(kk3_ctx* x, int mode) {
   if (!x || (mode != KK3_COMM_PEER && mode != KK3_COMM_HOST && mode != KK3_COMM_PUSH)) return KK3_ERR_ARG;
   x->comm_mode = mode == KK3_COMM_HOST ? kCommHost : (mode == KK3_COMM_PUSH ? kCommPush : kCommPeer);
-  return KK3_OK;
-}
-
-extern "C" int kk3_set_attn_engine(kk3_ctx* x, int engine) {
-  if (!x || (engine != KK3_ATTN_MMA && engine != KK3_ATTN_TC)) return KK3_ERR_ARG;
-  // both plans were sized at kk3_init (the partials buffer holds the larger chunk count)
-  plan_mla(x->g, x->grid, engine == KK3_ATTN_TC ? kAttnTc : kAttnMma);
   return KK3_OK;
 }
 

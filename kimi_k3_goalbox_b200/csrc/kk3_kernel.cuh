@@ -11,7 +11,6 @@
 
 #include "kk3_phases.cuh"
 #include "kk3_tc_gemv.cuh"
-#include "kk3_tc_attn.cuh"
 
 namespace kk3 {
 
@@ -739,10 +738,8 @@ __global__ void __launch_bounds__(kThreads, 1) kk3_step_kernel(const __grid_cons
         #pragma unroll 1
         for (int it = blockIdx.x; it < g.hr * 4; it += gridDim.x) mla_absorb_item(a, l, it / 4, it % 4, fsm);
       KK3_PHASE_END();
-      // split-K attention over [cache, new token] (kimi.py:274-280): on the tensor cores, or the warp-level engine
-      if (KK3_RUN && g.mla_tc) {
-        if (!mla_attend_tc(a, l, midx, phase)) KK3_FAIL();
-      } else if (KK3_RUN) {
+      // split-K attention over [cache, new token] (kimi.py:274-280)
+      if (KK3_RUN) {
         int total = 0;
         #pragma unroll 1
         for (int b = 0; b < g.B; ++b) total += mla_row_chunks(a, b);

@@ -515,7 +515,7 @@ KK3_FN void kda_item(const StepArgs& a, int layer, int kidx, int b, int hh, floa
 // that are reset read no state.
 // Only when the phase's items fit one wave: with several waves the prefetch measured no gain in the KDA phase and
 // slowed the projection phase it runs in (dev-l4: +18 us per step).
-KK3_DEV void kda_state_prefetch(const StepArgs& a, int layer) {
+KK3_FN void kda_state_prefetch(const StepArgs& a, int layer) {
   const Geo& g = a.g;
   if (threadIdx.x != 0 || g.B * g.hr > (int)gridDim.x) return;
   const float* st = lptr<float>(a, layer, KK3_KDA_RECURRENT_STATE);
@@ -770,46 +770,23 @@ KK3_FN void mla_attend_item(const StepArgs& a, int layer, int midx, int b, int c
     }
     __syncthreads();
     if (stamp && s < 2) sub_stamp(a, ph, 3 + 4 * s);
-    // online softmax: warp w takes head rows w, w + 16, ... (MT of them, HR = 16 MT), one lane per position; the
-    // rows' reductions are interleaved so that their shuffle chains overlap (k-partials summed in order)
-    {
-      float sv[MT], mx[MT];
-#pragma unroll
-      for (int i = 0; i < MT; ++i) {
-        const int hh = warp + kWarps * i;
-        const bool valid = (t0 + lane) < p1 && (t0 + lane) < T && h0 + hh < g.hr;
-        float sum = 0.0f;
-#pragma unroll
-        for (int q = 0; q < KQ; ++q) sum += Sp[((size_t)q * HR + hh) * kRowS + lane];
-        sv[i] = valid ? sum * scale : -INFINITY;
-        mx[i] = sv[i];
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int i = 0; i < MT; ++i) mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], o));
-      float mnew[MT], pv[MT];
-#pragma unroll
-      for (int i = 0; i < MT; ++i) {
-        const int hh = warp + kWarps * i;
-        mnew[i] = fmaxf(mrun[hh], mx[i]);
-        pv[i] = sv[i] == -INFINITY ? 0.0f : expf(sv[i] - mnew[i]);
-        Ps[hh * kRowP + lane] = f2bf(pv[i]);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int i = 0; i < MT; ++i) pv[i] += __shfl_xor_sync(0xffffffffu, pv[i], o);
+    // online softmax, one warp per head row, one lane per position (k-partials summed in order)
+    for (int hh = warp; hh < HR; hh += kWarps) {
+      const bool valid = (t0 + lane) < p1 && (t0 + lane) < T && h0 + hh < g.hr;
+      float sum = 0.0f;
+      for (int q = 0; q < KQ; ++q) sum += Sp[((size_t)q * HR + hh) * kRowS + lane];
+      const float sv = valid ? sum * scale : -INFINITY;
+      const float mt_ = warp_max(sv);
+      const float mold = mrun[hh];
+      const float mnew = fmaxf(mold, mt_);
+      const float p = valid ? expf(sv - mnew) : 0.0f;
+      const float ps = warp_sum(p);
+      Ps[hh * kRowP + lane] = f2bf(p);
       if (lane == 0) {
-#pragma unroll
-        for (int i = 0; i < MT; ++i) {
-          const int hh = warp + kWarps * i;
-          const float mold = mrun[hh];
-          const float al = (mold == -INFINITY) ? 0.0f : expf(mold - mnew[i]);
-          alpha[hh] = (mnew[i] == -INFINITY) ? 1.0f : al;
-          lrun[hh] = lrun[hh] * alpha[hh] + pv[i];
-          mrun[hh] = mnew[i];
-        }
+        const float al = (mold == -INFINITY) ? 0.0f : expf(mold - mnew);
+        alpha[hh] = (mnew == -INFINITY) ? 1.0f : al;
+        lrun[hh] = lrun[hh] * alpha[hh] + ps;
+        mrun[hh] = mnew;
       }
     }
     __syncthreads();

@@ -136,13 +136,12 @@ def summarize(rows: list[dict], top: int = 10) -> dict:
                     for k, v in order]}
 
 
-def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0, attn_engine: int = 0) -> list[dict]:
+def profile(case: dict, reps: int = 5, seed: int = 1, device: int = 0) -> list[dict]:
     torch.cuda.set_device(device)
     with torch.inference_mode():
         values = synthetic.make_inputs(case, seed, torch.device("cuda", device))
         ctx = StepContext(case, device=device)
         try:
-            ctx.set_attn_engine(attn_engine)   # include/kk3.h KK3_ATTN_MMA (default) or KK3_ATTN_TC
             out = ctx.allocate_outputs()
             ctx._bind_inputs(values)
             ctx.bind_outputs(out)
@@ -274,8 +273,6 @@ def main(argv=None) -> int:
     ap.add_argument("--rank-equivalent", action="store_true", help="one TP rank of --case as a TP1 geometry")
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--json", default=None)
-    ap.add_argument("--attn-engine", choices=["mma", "tc"], default="mma",
-                    help="MLA attention engine (include/kk3.h KK3_ATTN_MMA, the default, or KK3_ATTN_TC)")
     args = ap.parse_args(argv)
     case = cases.get_case(args.case)
     case["params"].pop("checkpoint", None)
@@ -288,7 +285,7 @@ def main(argv=None) -> int:
         raise SystemExit("multi-rank cases: pass --rank-equivalent (one rank's shapes on one GPU)")
     if args.batch:
         case = cases.variant(case, batch=args.batch)
-    rows = profile(case, args.reps, attn_engine=1 if args.attn_engine == "tc" else 0)
+    rows = profile(case, args.reps)
     subrow, head, rows = rows[0], rows[1:3], rows[3:]
     for k, v in [kv for kv in subrow["info"].items() if kv[0].startswith(("mla_attend", "mla_combine", "experts_gate_up", "experts_down:1", "attn_prologue:2", "moe_in:1", "kda:", "warps ")) and (not kv[0].startswith("warps ") or kv[0].endswith(":1"))]:
         print("  sub-phase", k, {kk: (round(vv, 2) if isinstance(vv, float) else vv) for kk, vv in v.items()})

@@ -48,8 +48,6 @@ class Config(ctypes.Structure):
 
 COMM_PEER, COMM_HOST, COMM_PUSH = 0, 1, 2   # include/kk3.h KK3_COMM_*
 GEMV_AUTO, GEMV_MMA = 0, 1     # include/kk3.h KK3_GEMV_*
-ATTN_MMA, ATTN_TC = 0, 1       # include/kk3.h KK3_ATTN_*
-BUF_ABSORBED = 11              # include/kk3.h KK3_BUF_ABSORBED (after a step: the last MLA layer's attended latent)
 
 
 def host_comm_segments(params: dict, tp: int) -> list[tuple[int, int, list[tuple[str, str, int]]]]:
@@ -139,7 +137,6 @@ def load_library() -> ctypes.CDLL:
         lib.kk3_exchange_layout.argtypes = [vp, ctypes.POINTER(ctypes.c_longlong)]
         lib.kk3_set_comm_mode.argtypes = [vp, i32]
         lib.kk3_set_gemv_engine.argtypes = [vp, i32]
-        lib.kk3_set_attn_engine.argtypes = [vp, i32]
         _LIB = lib
     return _LIB
 
@@ -378,12 +375,6 @@ class StepContext:
         rc = self.lib.kk3_set_gemv_engine(self.handle, engine)
         if rc != 0:
             raise KK3Error(rc, "kk3_set_gemv_engine")
-
-    def set_attn_engine(self, engine: int) -> None:
-        """ATTN_MMA (the warp-level mma.sync MLA attention, the default) or ATTN_TC (tcgen05), include/kk3.h."""
-        rc = self.lib.kk3_set_attn_engine(self.handle, engine)
-        if rc != 0:
-            raise KK3Error(rc, "kk3_set_attn_engine")
 
     def set_comm_mode(self, mode: int) -> None:
         rc = self.lib.kk3_set_comm_mode(self.handle, mode)

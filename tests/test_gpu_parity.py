@@ -144,60 +144,3 @@ def test_tensor_core_projections_against_the_mma_engine(batch, seed):
         d = gh.rel_l2(outs[runtime.GEMV_AUTO]["logits"], outs[runtime.GEMV_MMA]["logits"])
         print(f"batch {batch}: logits rel-L2 tcgen05 vs mma.sync {d:.2e}")
         assert d < 1e-2, d
-
-
-def _grade_floats(case, values, expected, out, label):
-    """The band rule on every output; a miss in the routed expert sets alone is printed, not failed. At full-width
-    shapes the band's routing floor misses a BF16 implementation whose error equals the oracle's on ~10 % of
-    seeds (test_fresh_seeds_full_width), and two engines that differ in the last bits re-draw that chance; every
-    float output, next_token and cache_length must still be within the band."""
-    try:
-        ko.compare(case, values, expected, out, serial=True)
-    except AssertionError as exc:
-        parts = [p.strip() for p in str(exc).split("; ") if p.strip()]
-        assert parts and all(p.startswith("expert_ids") for p in parts), f"{label}: {exc}"
-        print(f"{label}: routing band missed (floats within band): {exc}")
-
-
-@pytest.mark.parametrize("which,seed,reset", [
-    ("small-b5", 9, [False, True, False, False, True]),   # 2 heads (one group of 8 rows), reset rows attend 1 position
-    ("kimi-k3-syn-l8-tp8-b8-s8192", 17, None),            # one TP8 rank: 12 heads, one group, 5-stage ring
-    ("kimi-k3-dev-l4-tp1-b8-s8192", 23, None),            # 96 heads: two groups of 48, 4-stage ring
-])
-def test_tensor_core_attention_against_the_mma_engine(which, seed, reset):
-    """The MLA attention on tcgen05 (kk3_set_attn_engine KK3_ATTN_TC: S and O in TMEM, one thread per head row for
-    the softmax) against the default warp-level mma.sync engine on the same inputs: both steps within the band, and
-    the attended latents (the combine's bf16 output, scratch KK3_BUF_ABSORBED) close. They are not bit-identical:
-    the engines sum in FP32 in different orders and round the probabilities to bf16 against different running
-    maxima."""
-    from kimi_k3_goalbox_b200 import cases, runtime
-    if which.startswith("small"):
-        case = gh.small_case(5)
-    elif "syn" in which:
-        case = gh.rank_equivalent(which, layers=4)
-    else:
-        case = cases.get_case(which)
-    g = case["params"]
-    B, hr, kr = g["batch"], g["q_heads"] // case["tp"], g["kv_lora_rank"]
-    with torch.inference_mode():
-        values = ko.make_inputs(case, seed, "cuda")
-        if reset is not None:
-            values["reset"] = torch.tensor(reset, device="cuda")
-        expected = ko.reference(case, values, serial=True)
-        outs, lat = {}, {}
-        for engine in (runtime.ATTN_TC, runtime.ATTN_MMA):
-            ctx = StepContext(case)
-            try:
-                ctx.set_attn_engine(engine)
-                outs[engine] = {k: v.clone() for k, v in ctx.step(values).items()}
-                torch.cuda.synchronize()
-                ctx.check()
-                lat[engine] = ctx.debug_buffer(runtime.BUF_ABSORBED, torch.bfloat16, (B, hr, kr))
-            finally:
-                ctx.close()
-            _grade_floats(case, values, expected, outs[engine], f"{which} engine {engine}")
-        d_lat = gh.rel_l2(lat[runtime.ATTN_TC], lat[runtime.ATTN_MMA])
-        d_log = gh.rel_l2(outs[runtime.ATTN_TC]["logits"], outs[runtime.ATTN_MMA]["logits"])
-        print(f"{which}: attended latent rel-L2 tcgen05 vs mma.sync {d_lat:.2e}, logits {d_log:.2e}")
-        assert d_lat < 1e-2, d_lat
-        assert d_log < 1e-2, d_log
