@@ -458,8 +458,8 @@ KK3_FN void kda_item(const StepArgs& a, int layer, int kidx, int b, int hh, floa
   const float4 dk = *reinterpret_cast<const float4*>(decay + lane * 4);
   const float4 kk = *reinterpret_cast<const float4*>(kn + lane * 4);
   const float4 qq = *reinterpret_cast<const float4*>(qn + lane * 4);
-  // The warp's eight value rows are independent: their two reductions each run as one interleaved butterfly
-  // (the same xor order as warp_sum), so the shuffle latencies of the rows overlap instead of adding up.
+  // The warp's eight value rows are independent: their two reductions each run as one interleaved butterfly,
+  // in warp_sum's xor order, so the sums are those of a row at a time.
   float pred[8], o[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
